@@ -1,0 +1,434 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 MoE FFN layer (BASELINE.json metric: MoE-layer
+tokens/s and achieved HBM TB/s).
+
+Default workload = BASELINE config 0: one OLMoE-1B-7B-shaped MoE FFN layer
+(d_model 2048, 64 experts, top-8 without renormalisation, d_ff 1024 SwiGLU,
+Q8_0 experts, fp32 router) on T = 32 tokens.  A step is one layer forward
+over the T tokens.  Weights are synthetic (seeded N(0, 0.02) through the
+shared generator, quantized to Q8_0 on the device); NL distinct layers are
+rotated so that every step streams 428 MB of experts that are not in the
+126 MB L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload config0|config1] [--tokens T]
+
+Prints one JSON line (rank 0).  Under torchrun each rank runs its own
+replica of the layer on its own tokens (weak scaling); the time is the max
+over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+EXPERT_BYTES_Q8 = 3 * 1024 * 2048 // 32 * 34  # 6,684,672 B per OLMoE expert
+
+
+def load_package():
+    if "moe_b200" in sys.modules:
+        return sys.modules["moe_b200"]
+    spec = importlib.util.spec_from_file_location(
+        "moe_b200", os.path.join(ROOT, "llm.c_b200", "__init__.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["moe_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        rows = []
+        with open(self.out.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- ours
+def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream):
+    """NL device-resident layers generated on the GPU (generator tags: router
+    1, gate 2, up 3, down 4; layer l uses seed seed0 + l)."""
+    import torch
+    rb_d = moe.row_bytes(qtype, d)
+    rb_f = moe.row_bytes(qtype, F)
+    layers, keep = [], []
+    tmp = torch.empty(NE * F * d, dtype=torch.float32, device="cuda")
+    for l in range(nl):
+        seed = seed0 + l
+        wr = torch.empty(NE * d, dtype=torch.float32, device="cuda")
+        moe.check(moe.lib().moe_synth_gauss(wr.data_ptr(), seed, 1, 0, NE * d, 0.02, stream))
+        mats = []
+        for tag, rows, cols, rb in ((2, F, d, rb_d), (3, F, d, rb_d), (4, d, F, rb_f)):
+            q = torch.empty(NE * rows * rb, dtype=torch.uint8, device="cuda")
+            moe.check(moe.lib().moe_synth_gauss(tmp.data_ptr(), seed, tag, 0, NE * rows * cols,
+                                                0.02, stream))
+            moe.check(moe.lib().moe_quantize_device(tmp.data_ptr(), NE * rows, cols, qtype,
+                                                    q.data_ptr(), stream))
+            mats.append(q)
+        torch.cuda.synchronize()
+        ptrs = [[m.data_ptr() + e * (m.numel() // NE) for e in range(NE)] for m in mats]
+        lay = moe.Layer(d, F, NE, K, qtype, wr.data_ptr(), ptrs[0], ptrs[1], ptrs[2])
+        layers.append(lay)
+        keep.append((wr, mats))
+    del tmp
+    return layers, keep
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    moe = load_package()
+    moe.init(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    stream = torch.cuda.current_stream().cuda_stream
+    d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
+    T = args.tokens
+    NL = args.layers
+    layers, keep = build_layers(moe, NL, 0, d, F, NE, K, qtype, stream)
+    # tokens: config-0 input seed 0, tag 5 (rank r uses element offset r*T*d)
+    x = torch.empty(T * d, dtype=torch.float32, device="cuda")
+    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 5, rank * T * d, T * d, 1.0, stream))
+    out = torch.empty(T * d, dtype=torch.float32, device="cuda")
+
+    def step(i, flags=0):
+        layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), T, flags, stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # routing of the layers (distinct experts touched = algorithmic bytes)
+    uniq = []
+    for l in range(NL):
+        step(l)
+        ids = layers[l].routing(T)[0]
+        uniq.append(len(np.unique(ids)))
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        step(i, moe.PROFILE)
+    ev1.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ms_total = ev0.elapsed_time(ev1)
+    stage = np.zeros(5)
+    nprof = 0
+    for lay in layers:
+        try:
+            s, c = lay.stage_ms()
+            stage += np.array(s)
+            nprof += c
+        except moe.MoeError:
+            pass
+    if dist:
+        t = torch.tensor([ms_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    tokens_per_s = world * T * args.steps / (ms_total / 1e3)
+
+    # ---- e2e: reference-facing tensor_t call with host buffers (H2D + D2H inside)
+    e2e = run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist)
+
+    # ---- roofline of the dominant kernel (gate/up + SwiGLU)
+    hbm_peak, _, peak_kind = measured_peaks()
+    U = np.array([uniq[i % NL] for i in range(args.steps)], float)
+    gu_bytes = float(np.mean(U)) * 2 * F * moe.row_bytes(qtype, d) + T * K * F * 4 + T * d * 4
+    gu_ms = stage[2] / max(nprof, 1)
+    layer_bytes = float(np.mean(U)) * EXPERT_BYTES_Q8 + NE * d * 4 + 2 * T * d * 4
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None
+    roof = {"bound": "hbm", "kernel": "expert_gemv_kernel<Q8_0,dual> (gate/up + SwiGLU)",
+            "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+            "frac": achieved / hbm_peak if achieved else None, "traffic": None,
+            "peak_source": peak_kind,
+            "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
+            "layer_achieved_gbs": layer_bytes / (ms_step / 1e3) / 1e9,
+            "layer_frac": layer_bytes / (ms_step / 1e3) / 1e9 / hbm_peak,
+            "stage_ms_avg": {n: float(v / max(nprof, 1)) for n, v in
+                             zip(["router", "dispatch", "gate_up", "down", "combine"], stage)}}
+    traffic = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(traffic):
+        with open(traffic) as f:
+            tj = json.load(f)
+        roof["traffic"] = tj.get("gate_up_bytes_per_launch")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(moe, keep[0], x, T, d, F, NE, K, qtype)
+
+    line = {
+        "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d)" % T,
+        "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x Q8_0 weights",
+        "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) tokens)",
+        "config": {"workload": "config0: OLMoE-1B-7B MoE FFN layer, d 2048, 64 experts top-8, "
+                               "d_ff 1024 SwiGLU, Q8_0, T=%d tokens" % T,
+                   "tokens_per_rank": T, "layers_rotated": NL,
+                   "l2": f"{NL} distinct layers rotated; each step streams "
+                         f"{np.mean(U) * EXPERT_BYTES_Q8 / 1e6:.0f} MB of experts > 126 MB L2",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+        "gpu_launches": 6 * args.steps,
+        "distinct_experts_per_step": float(np.mean(U)),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for lay in layers:
+        lay.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist):
+    """Same metric through moe_ffn_forward (tensor_t drop-in, host buffers):
+    every step copies the tokens host->device and the output device->host."""
+    import torch
+    import ctypes as C
+    nl = min(len(keep), 2)
+    hosts = []
+    for l in range(nl):
+        wr, mats = keep[l]
+        hw = wr.cpu().numpy()
+        hm = [m.cpu().numpy() for m in mats]
+        ts = [moe.tensor(hw, moe.F32, (NE, d)), moe.tensor(hm[0], qtype, (NE, F, d)),
+              moe.tensor(hm[1], qtype, (NE, F, d)), moe.tensor(hm[2], qtype, (NE, d, F))]
+        for t in ts:
+            moe.check(moe.lib().moe_register_weights(C.byref(t)))
+        hosts.append(ts)
+    xin_p = moe.lib().moe_host_alloc(T * d * 4)
+    xout_p = moe.lib().moe_host_alloc(T * d * 4)
+    xin = np.ctypeslib.as_array((C.c_float * (T * d)).from_address(xin_p))
+    xout = np.ctypeslib.as_array((C.c_float * (T * d)).from_address(xout_p))
+    rng = np.random.default_rng(rank)
+    xin[:] = rng.standard_normal(T * d).astype(np.float32)
+    ti = moe.MoeTensor()
+    ti.data = xin_p
+    ti.type = moe.F32
+    ti.ndim = 2
+    ti.dim[0], ti.dim[1] = T, d
+    ti.totlen = ti.maxcap = T * d
+    to = moe.MoeTensor()
+    to.data = xout_p
+    to.type = moe.F32
+    to.ndim = 2
+    to.dim[0], to.dim[1] = T, d
+    to.totlen = to.maxcap = T * d
+
+    def call(i):
+        h = hosts[i % nl]
+        moe.check(moe.lib().moe_ffn_forward(C.byref(ti), C.byref(to), C.byref(h[0]),
+                                            C.byref(h[1]), C.byref(h[2]), C.byref(h[3]), K, 0))
+
+    for i in range(max(args.warmup, 2)):
+        call(i)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        call(i)
+    sec = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([sec], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t.item())
+    world = dist.get_world_size() if dist else 1
+    for h in hosts:
+        for t in h:
+            moe.lib().moe_unregister_weights(C.byref(t))
+    moe.lib().moe_host_free(xin_p)
+    moe.lib().moe_host_free(xout_p)
+    return {"value": world * T * args.steps / sec, "unit": "tokens/s",
+            "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
+            "api": "moe_ffn_forward (tensor_t drop-in, pageable->device copies inside)",
+            "timer": "host wall clock around synchronous calls"}
+
+
+def physical_cores():
+    seen = set()
+    n = os.cpu_count() or 1
+    for c in range(n):
+        try:
+            with open(f"/sys/devices/system/cpu/cpu{c}/topology/core_id") as f:
+                core = f.read().strip()
+            pkg = "0"
+            p = f"/sys/devices/system/cpu/cpu{c}/topology/physical_package_id"
+            if os.path.exists(p):
+                with open(p) as f:
+                    pkg = f.read().strip()
+            seen.add((pkg, core))
+        except OSError:
+            return n
+    return len(seen) or n
+
+
+def ref_variant():
+    flags = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = f.read()
+    except OSError:
+        pass
+    return "avx512" if " avx512f" in flags else "avx2"
+
+
+def cpu_baseline(moe, layer0, x_dev, T, d, F, NE, K, qtype, sample_tokens=8, reps=3):
+    """The reference's own CPU path (oracle/_ref, compiled from its sources)
+    on the SAME bytes as the GPU run, on a bounded sample of tokens."""
+    from oracle import oracle as orc
+    variant = ref_variant()
+    if not orc.ref_available(variant):
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                "sample": f"oracle/_ref/libref_{variant}.so not built"}
+    wr, mats = layer0
+    xs = x_dev.view(T, d)[:sample_tokens].cpu().numpy()
+    r = orc.ref_call("bench", variant, x=xs, router_w=wr.view(NE, d).cpu().numpy(),
+                     gate=mats[0].cpu().numpy(), up=mats[1].cpu().numpy(),
+                     down=mats[2].cpu().numpy(), qtype=qtype, d_ff=F, top_k=K, renorm=0,
+                     reps=reps)
+    sec = float(np.median(r["seconds"]))
+    return {"value": sample_tokens / sec, "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "variant": variant, "host_physical_cores": physical_cores(),
+            "sample": f"{sample_tokens} of the {T} config-0 tokens through ref_moe_ffn "
+                      f"(reference sources, -march=x86-64-{'v4' if variant == 'avx512' else 'v3'}), "
+                      f"median of {reps} calls after 1 warm-up, identical bytes to the GPU run; "
+                      "the reference runs these expert GEMVs on one thread (below its 16 MFLOP "
+                      "threading threshold) while its pool spins on every physical core"}
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    variant = ref_variant()
+    if not orc.ref_available(variant):
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"oracle/_ref/libref_{variant}.so not built"}), flush=True)
+        return
+    d, F, NE, K = 2048, 1024, 64, 8
+    L = orc.make_layer(0, d, F, NE, K, orc.Q8_0)
+    x = orc.make_tokens(0, args.tokens, d)
+    S = min(8, args.tokens)
+    r = orc.ref_call("bench", variant, timeout=3600, x=x[:S], router_w=L["router_w"],
+                     gate=L["gate"], up=L["up"], down=L["down"], qtype=orc.Q8_0, d_ff=F,
+                     top_k=K, renorm=0, reps=args.steps + args.warmup)
+    secs = np.array(r["seconds"])[args.warmup:]
+    tot = float(secs.sum())
+    val = S * len(secs) / tot
+    cpu = {"value": val, "unit": "tokens/s", "cores": 1, "kind": "reference",
+           "variant": variant, "host_physical_cores": physical_cores(),
+           "sample": f"{S} of the {args.tokens} config-0 tokens per step through ref_moe_ffn"}
+    print(json.dumps({
+        "impl": "reference", "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d)" % args.tokens,
+        "value": val, "unit": "tokens/s", "n_gpus": world, "steps": len(secs),
+        "warmup": args.warmup, "ms_per_step": tot / len(secs) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x Q8_0 weights",
+        "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) tokens)",
+        "config": {"workload": "config0: OLMoE-1B-7B MoE FFN layer on the reference CPU path"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

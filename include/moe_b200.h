@@ -1,0 +1,230 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) mixture-of-experts FFN path.
+ *
+ * libmoe_b200.so replaces, behind plain C calls, the CPU hot path of the
+ * llm.c engine (hoathienvu8x/llm.c): the router GEMM + softmax + top-k,
+ * token-to-expert dispatch, the grouped Q8_0/Q4_0 SwiGLU expert products
+ * and the weighted combine.  No PyTorch and no C++ types cross this
+ * boundary: only pointers, sizes and a tensor struct whose layout equals
+ * the reference's tensor_t.
+ *
+ * Threading: one caller thread at a time (the reference's own model code
+ * is single-threaded).  The library owns one CUDA stream per device.
+ * Errors: functions returning int return MOE_OK (0) or a negative
+ * moe_status; moe_last_error() describes the last failure.  The void
+ * drop-ins abort with a message, like the reference's asserts.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* Tensor carrier                                                       */
+/* ------------------------------------------------------------------ */
+
+/* Same memory layout as the reference's tensor_t (tensor.h:19-31) in the
+ * build the reference Makefile makes (FEATURES has -DQ8_DOT, so the two
+ * scratch fields are present).  A caller holding a tensor_t* passes it
+ * cast to moe_tensor_t*. */
+typedef struct moe_tensor {
+	float *data;          /* MOE_F32 payload                       */
+	void *qdata;          /* quantized payload (GGUF block layout) */
+	int type;             /* enum tensor_dtype                     */
+	uint64_t totlen;
+	uint64_t maxcap;
+	uint64_t dim[4];
+	uint32_t ndim;
+	void *scratch;        /* reference's Q8_K scratch (unused here) */
+	size_t scratch_size;
+} moe_tensor_t;
+
+/* enum tensor_dtype (tensor.h:10-17); only these three are supported */
+enum { MOE_F32 = 0, MOE_Q8_0 = 1, MOE_Q4_0 = 2 };
+
+enum moe_status {
+	MOE_OK = 0,
+	MOE_ERR_INVALID = -1,     /* bad argument / shape          */
+	MOE_ERR_UNSUPPORTED = -2, /* dtype or shape not handled    */
+	MOE_ERR_CUDA = -3,        /* CUDA runtime error            */
+	MOE_ERR_NOMEM = -4,       /* device allocation failed      */
+	MOE_ERR_NOT_INIT = -5,    /* moe_init not called           */
+	MOE_ERR_COMM = -6,        /* NCCL / expert-parallel error  */
+	MOE_ERR_TIMEOUT = -7      /* bounded wait expired          */
+};
+
+/* flags for the layer entry points */
+#define MOE_TOPK_EXACT  0x01 /* true top-k; default reproduces nn.c:276-308  */
+#define MOE_DEVICE_IO   0x02 /* input/output pointers are device pointers    */
+#define MOE_LANES_AVX2  0x04 /* router sums follow the AVX2 build (8 lanes); */
+                             /* default follows the AVX-512 build (16 lanes) */
+#define MOE_RENORM      0x08 /* Mixtral: renormalise the top-k weights       */
+                             /* (llama.c:422-427); OLMoE does not            */
+#define MOE_FORCE_GEMV  0x10 /* always use the decode (GEMV) expert kernels  */
+#define MOE_FORCE_GEMM  0x20 /* always use the grouped tensor-core kernels   */
+#define MOE_PROFILE     0x40 /* record CUDA events between the layer's stages */
+                             /* (read back with moe_layer_stage_ms)          */
+
+/* ------------------------------------------------------------------ */
+/* Library lifetime                                                     */
+/* ------------------------------------------------------------------ */
+
+/* Select CUDA device `device`, create the stream.  Idempotent. */
+MOE_API int moe_init(int device);
+/* Free every device buffer and registered weight; safe to call twice. */
+MOE_API int moe_shutdown(void);
+/* Text of the last error on this thread ("" if none). */
+MOE_API const char *moe_last_error(void);
+/* Library build/version string. */
+MOE_API const char *moe_version(void);
+
+/* ------------------------------------------------------------------ */
+/* Weight residency                                                     */
+/* ------------------------------------------------------------------ */
+
+/* Upload a weight tensor (fp32 router or Q8_0/Q4_0 blocks, 1-3 dims) to
+ * HBM once, keeping its GGUF byte layout.  Keyed by the host pointer
+ * (qdata or data): any later call that passes this tensor, or a view into
+ * it (tensor_at_q, olmoe.c:20-60), uses the device copy.  Unregistered
+ * weights passed to a compute call are uploaded on first sight.
+ * Replaces: nothing (the reference reads weights from the mmap'd GGUF,
+ * gguf.c:490-530); this is the residency hook a caller adds after
+ * gguf_tensor_3d (olmoe.c:180-182). */
+MOE_API int moe_register_weights(const moe_tensor_t *t);
+MOE_API int moe_unregister_weights(const moe_tensor_t *t);
+/* Bytes of weights resident on the current device. */
+MOE_API size_t moe_resident_bytes(void);
+
+/* ------------------------------------------------------------------ */
+/* Same-signature drop-ins (host fp32 in/out, synchronous)              */
+/* ------------------------------------------------------------------ */
+
+/* Replaces tensor_mma_transposed_2x2 (matmul.h:30-31, matmul.c:451-462):
+ * ret[m,n] = lhs[m,k] . rhs[n,k]^T (+ add), rhs fp32, Q8_0 or Q4_0.
+ * lhs/ret/add are host fp32.  Aborts on error (the reference asserts). */
+MOE_API void moe_tensor_mma_transposed_2x2(moe_tensor_t *ret, const moe_tensor_t *lhs,
+				   const moe_tensor_t *rhs, const moe_tensor_t *add);
+/* Same, returning a status instead of aborting. */
+MOE_API int moe_tensor_mma_transposed_2x2_status(moe_tensor_t *ret, const moe_tensor_t *lhs,
+					 const moe_tensor_t *rhs, const moe_tensor_t *add);
+
+/* Replaces fused_ffn_silu (nn.h:35-39, nn.c:496-539): one token through a
+ * SwiGLU FFN with quantized weights.  Returns 1 when done, 0 when not
+ * applicable (in->dim[0] != 1 or fp32 weights), exactly like the
+ * reference; aborts on a device error.  gate/up receive the gate and up
+ * activations (gate holds silu(g)*u afterwards, as in the reference). */
+MOE_API int moe_fused_ffn_silu(const moe_tensor_t *in, moe_tensor_t *out,
+		       moe_tensor_t *gate, const moe_tensor_t *gate_w,
+		       moe_tensor_t *up, const moe_tensor_t *up_w,
+		       const moe_tensor_t *down_w);
+
+/* ------------------------------------------------------------------ */
+/* Layer entry points                                                   */
+/* ------------------------------------------------------------------ */
+
+/* The whole moe_ffn of olmoe.c:343-407 (or, with MOE_RENORM, the
+ * Mixtral flavour of llama.c:393-457) in one call:
+ *   input [T, d] fp32, output [T, d] fp32 (host, or device with
+ *   MOE_DEVICE_IO); gate_inp [NE, d] fp32 router;
+ *   gate_exps/up_exps [NE, d_ff, d] and down_exps [NE, d, d_ff]
+ *   Q8_0/Q4_0 3-D tensors as gguf_tensor_3d returns them.
+ * The caller's one-line change in moe_ffn is to call this instead. */
+MOE_API int moe_ffn_forward(const moe_tensor_t *input, moe_tensor_t *output,
+		    const moe_tensor_t *gate_inp, const moe_tensor_t *gate_exps,
+		    const moe_tensor_t *up_exps, const moe_tensor_t *down_exps,
+		    size_t topk, int flags);
+
+/* Mixtral layout: per-expert 2-D tensors blk.L.ffn_{gate,up,down}.E.weight
+ * (llama.c:157-166); arrays of n_experts pointers. */
+MOE_API int moe_ffn_forward_split(const moe_tensor_t *input, moe_tensor_t *output,
+			  const moe_tensor_t *gate_inp,
+			  const moe_tensor_t *const *gate_exp,
+			  const moe_tensor_t *const *up_exp,
+			  const moe_tensor_t *const *down_exp,
+			  size_t n_experts, size_t topk, int flags);
+
+/* ------------------------------------------------------------------ */
+/* Device-level API (plain device pointers; used by engines and tests)  */
+/* ------------------------------------------------------------------ */
+
+typedef struct moe_layer moe_layer; /* opaque */
+
+typedef struct moe_layer_desc {
+	int64_t d_model, d_ff, n_experts, top_k;
+	int qtype;                   /* MOE_Q8_0 or MOE_Q4_0              */
+	int flags;                   /* default flags for forward calls   */
+	const float *router_w;       /* device [n_experts, d_model] fp32  */
+	const float *router_bias;    /* device [n_experts] or NULL        */
+	/* host arrays of n_experts DEVICE pointers to each expert's
+	 * [d_ff,d] gate/up and [d,d_ff] down block matrices */
+	const void *const *gate;
+	const void *const *up;
+	const void *const *down;
+	/* expert parallelism: this rank computes experts
+	 * [first_expert, first_expert + n_local); 0/0 means all */
+	int64_t first_expert, n_local;
+} moe_layer_desc;
+
+MOE_API int moe_layer_create(moe_layer **out, const moe_layer_desc *desc);
+MOE_API int moe_layer_destroy(moe_layer *layer);
+/* out[T,d] = MoE(x[T,d]); x/out device fp32; stream = cudaStream_t or
+ * NULL for the library stream.  Asynchronous. */
+MOE_API int moe_layer_forward(moe_layer *layer, const float *x, float *out, int64_t T,
+		      int flags, void *stream);
+/* Routing of the last forward, copied to HOST buffers (any may be NULL):
+ * ids/weights [T,k] in top-k output order, counts [NE], offsets [NE+1],
+ * perm [T*k] (pair p = t*k + slot, stably sorted by expert). */
+MOE_API int moe_layer_routing(moe_layer *layer, int32_t *ids, float *weights, int32_t *counts,
+		      int32_t *offsets, int32_t *perm);
+
+/* Device time of each stage, summed over the MOE_PROFILE forwards since
+ * the last call, in ms, from CUDA events recorded on the launching stream:
+ * [0] router (logits + softmax/top-k), [1] dispatch, [2] gate/up + SwiGLU,
+ * [3] down, [4] combine; [5] (if n >= 6) the number of forwards summed.
+ * Synchronises on the last event and resets the sums. */
+MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
+
+/* y[m, rows] = x[m, cols] . W[rows, cols]^T with W in Q8_0/Q4_0 blocks on
+ * the device (config-1 dense decode GEMV when m == 1).  Asynchronous. */
+MOE_API int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols,
+		    const float *x, int64_t m, float *y, void *stream);
+
+/* Synchronise the library stream. */
+MOE_API int moe_sync(void);
+
+/* ------------------------------------------------------------------ */
+/* Device memory helpers (so C callers need no CUDA headers)            */
+/* ------------------------------------------------------------------ */
+MOE_API void *moe_device_alloc(size_t bytes);
+MOE_API int moe_device_free(void *p);
+MOE_API int moe_memcpy_h2d(void *dst, const void *src, size_t bytes);
+MOE_API int moe_memcpy_d2h(void *dst, const void *src, size_t bytes);
+MOE_API void *moe_host_alloc(size_t bytes);     /* pinned */
+MOE_API int moe_host_free(void *p);
+
+/* Seeded synthetic inputs generated on the device (bench / tests).
+ * Fills n values sd*N(0,1) of generator stream (seed, tag) starting at
+ * element `offset`; same formula as the CPU generator.  And quantizes
+ * rows*cols fp32 (device) into Q8_0/Q4_0 blocks (device) with the
+ * reference quantizers' rounding rules. */
+MOE_API int moe_synth_gauss(float *dst, uint64_t seed, uint64_t tag, uint64_t offset,
+		    int64_t n, float sd, void *stream);
+MOE_API int moe_quantize_device(const float *src, int64_t rows, int64_t cols, int qtype,
+			void *dst, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

@@ -1,0 +1,336 @@
+"""Python binding of libmoe_b200.so (the B200 MoE FFN C ABI, include/moe_b200.h).
+
+The product is the C ABI; this module is the thin ctypes mirror that the
+tests and bench.py use.  It never computes anything itself and never falls
+back to the CPU: if the shared library is missing it raises.
+
+The directory name (llm.c_b200) is not a valid Python identifier, so load
+it with `load_package()` from bench.py / tests/conftest.py, or by path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
+
+F32, Q8_0, Q4_0 = 0, 1, 2
+TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE = (
+    0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40)
+
+ERRORS = {0: "MOE_OK", -1: "MOE_ERR_INVALID", -2: "MOE_ERR_UNSUPPORTED", -3: "MOE_ERR_CUDA",
+          -4: "MOE_ERR_NOMEM", -5: "MOE_ERR_NOT_INIT", -6: "MOE_ERR_COMM", -7: "MOE_ERR_TIMEOUT"}
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class MoeTensor(C.Structure):
+    """Layout of the reference's tensor_t (tensor.h:19-31, -DQ8_DOT build)."""
+    _fields_ = [("data", C.c_void_p), ("qdata", C.c_void_p), ("type", C.c_int),
+                ("totlen", C.c_uint64), ("maxcap", C.c_uint64), ("dim", C.c_uint64 * 4),
+                ("ndim", C.c_uint32), ("scratch", C.c_void_p), ("scratch_size", C.c_size_t)]
+
+
+class LayerDesc(C.Structure):
+    _fields_ = [("d_model", C.c_int64), ("d_ff", C.c_int64), ("n_experts", C.c_int64),
+                ("top_k", C.c_int64), ("qtype", C.c_int), ("flags", C.c_int),
+                ("router_w", C.c_void_p), ("router_bias", C.c_void_p),
+                ("gate", C.POINTER(C.c_void_p)), ("up", C.POINTER(C.c_void_p)),
+                ("down", C.POINTER(C.c_void_p)),
+                ("first_expert", C.c_int64), ("n_local", C.c_int64)]
+
+
+_lib = None
+
+# every symbol include/moe_b200.h declares, with (restype, argtypes)
+_P, _I, _SZ, _I64, _U64, _F = C.c_void_p, C.c_int, C.c_size_t, C.c_int64, C.c_uint64, C.c_float
+_TP = C.POINTER(MoeTensor)
+SIGNATURES = {
+    "moe_init": (_I, [_I]),
+    "moe_shutdown": (_I, []),
+    "moe_last_error": (C.c_char_p, []),
+    "moe_version": (C.c_char_p, []),
+    "moe_register_weights": (_I, [_TP]),
+    "moe_unregister_weights": (_I, [_TP]),
+    "moe_resident_bytes": (_SZ, []),
+    "moe_tensor_mma_transposed_2x2": (None, [_TP, _TP, _TP, _TP]),
+    "moe_tensor_mma_transposed_2x2_status": (_I, [_TP, _TP, _TP, _TP]),
+    "moe_fused_ffn_silu": (_I, [_TP, _TP, _TP, _TP, _TP, _TP, _TP]),
+    "moe_ffn_forward": (_I, [_TP, _TP, _TP, _TP, _TP, _TP, _SZ, _I]),
+    "moe_ffn_forward_split": (_I, [_TP, _TP, _TP, C.POINTER(_TP), C.POINTER(_TP),
+                                   C.POINTER(_TP), _SZ, _SZ, _I]),
+    "moe_layer_create": (_I, [C.POINTER(_P), C.POINTER(LayerDesc)]),
+    "moe_layer_destroy": (_I, [_P]),
+    "moe_layer_forward": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "moe_layer_routing": (_I, [_P, _P, _P, _P, _P, _P]),
+    "moe_layer_stage_ms": (_I, [_P, C.POINTER(C.c_float), _I]),
+    "moe_gemv_device": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
+    "moe_sync": (_I, []),
+    "moe_device_alloc": (_P, [_SZ]),
+    "moe_device_free": (_I, [_P]),
+    "moe_memcpy_h2d": (_I, [_P, _P, _SZ]),
+    "moe_memcpy_d2h": (_I, [_P, _P, _SZ]),
+    "moe_host_alloc": (_P, [_SZ]),
+    "moe_host_free": (_I, [_P]),
+    "moe_synth_gauss": (_I, [_P, _U64, _U64, _U64, _I64, _F, _P]),
+    "moe_quantize_device": (_I, [_P, _I64, _I64, _I, _P, _P]),
+}
+
+
+def lib():
+    """Load libmoe_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `make -C llm.c_b200` "
+                              "(or __graft_entry__.build()); there is no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int):
+    if rc != 0:
+        raise MoeError(rc, lib().moe_last_error().decode())
+    return rc
+
+
+def init(device: int = 0):
+    check(lib().moe_init(device))
+
+
+def shutdown():
+    check(lib().moe_shutdown())
+
+
+# ------------------------------------------------------------------ tensors
+def row_bytes(qtype: int, cols: int) -> int:
+    return {Q8_0: cols // 32 * 34, Q4_0: cols // 32 * 18, F32: cols * 4}[qtype]
+
+
+def tensor(arr: np.ndarray, qtype: int = F32, dims=None) -> MoeTensor:
+    """tensor_t view of a numpy array: fp32 data, or uint8 GGUF blocks with
+    logical dims (outermost first, innermost = columns)."""
+    t = MoeTensor()
+    if qtype == F32:
+        dims = arr.shape if dims is None else dims
+        t.data = arr.ctypes.data
+    else:
+        assert dims is not None
+        t.qdata = arr.ctypes.data
+    t.type = qtype
+    t.ndim = len(dims)
+    n = 1
+    for i, dd in enumerate(dims):
+        t.dim[i] = dd
+        n *= dd
+    t.totlen = n
+    t.maxcap = n
+    t._keep = arr
+    return t
+
+
+# ------------------------------------------------------------------ device memory
+class DeviceBuffer:
+    def __init__(self, nbytes: int):
+        self.nbytes = nbytes
+        self.ptr = lib().moe_device_alloc(max(nbytes, 1))
+        if not self.ptr:
+            raise MoeError(-4, lib().moe_last_error().decode())
+
+    @classmethod
+    def from_numpy(cls, a: np.ndarray) -> "DeviceBuffer":
+        a = np.ascontiguousarray(a)
+        b = cls(a.nbytes)
+        if a.nbytes:
+            check(lib().moe_memcpy_h2d(b.ptr, a.ctypes.data, a.nbytes))
+        return b
+
+    def to_numpy(self, dtype, shape) -> np.ndarray:
+        out = np.empty(shape, dtype)
+        if out.nbytes:
+            check(lib().moe_memcpy_d2h(out.ctypes.data, self.ptr, out.nbytes))
+        return out
+
+    def free(self):
+        if self.ptr:
+            lib().moe_device_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ layer
+class Layer:
+    """Device-resident MoE layer (moe_layer_create).  `gate`/`up` are uint8
+    [NE, d_ff, rb] and `down` uint8 [NE, d, rb] GGUF blocks, or device
+    pointer lists when built from device data."""
+
+    def __init__(self, d_model, d_ff, n_experts, top_k, qtype, router_w, gate, up, down,
+                 router_bias=None, flags=0, first_expert=0, n_local=0):
+        self.bufs = []
+        self.d_model, self.d_ff, self.n_experts, self.top_k = d_model, d_ff, n_experts, top_k
+
+        def dev(a):
+            if isinstance(a, int):
+                return a
+            b = DeviceBuffer.from_numpy(a)
+            self.bufs.append(b)
+            return b.ptr
+
+        f32 = lambda a: a if isinstance(a, int) else np.ascontiguousarray(a, np.float32)  # noqa: E731
+        self.router_w = dev(f32(router_w))
+        self.router_bias = None if router_bias is None else dev(f32(router_bias))
+
+        def ptrs(m):
+            if isinstance(m, (list, tuple)):
+                return [int(p) for p in m]
+            base = dev(np.ascontiguousarray(m))
+            stride = m[0].nbytes
+            return [base + e * stride for e in range(n_experts)]
+
+        self._g = (C.c_void_p * n_experts)(*ptrs(gate))
+        self._u = (C.c_void_p * n_experts)(*ptrs(up))
+        self._d = (C.c_void_p * n_experts)(*ptrs(down))
+        desc = LayerDesc(d_model, d_ff, n_experts, top_k, qtype, flags, self.router_w,
+                         self.router_bias, C.cast(self._g, C.POINTER(C.c_void_p)),
+                         C.cast(self._u, C.POINTER(C.c_void_p)),
+                         C.cast(self._d, C.POINTER(C.c_void_p)), first_expert, n_local)
+        h = C.c_void_p()
+        check(lib().moe_layer_create(C.byref(h), C.byref(desc)))
+        self.handle = h.value
+
+    def forward_device(self, x_ptr: int, out_ptr: int, T: int, flags=0, stream=None):
+        check(lib().moe_layer_forward(self.handle, x_ptr, out_ptr, T, flags, stream))
+
+    def forward(self, x: np.ndarray, flags=0) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        bx = DeviceBuffer.from_numpy(x)
+        bo = DeviceBuffer(x.nbytes)
+        self.forward_device(bx.ptr, bo.ptr, T, flags)
+        check(lib().moe_sync())
+        self.last_T = T
+        return bo.to_numpy(np.float32, x.shape)
+
+    def stage_ms(self):
+        """(per-stage ms summed over profiled forwards, number of forwards)"""
+        ms = (C.c_float * 6)()
+        check(lib().moe_layer_stage_ms(self.handle, ms, 6))
+        return list(ms)[:5], int(ms[5])
+
+    def routing(self, T: int):
+        K, NE = self.top_k, self.n_experts
+        ids = np.empty((T, K), np.int32)
+        w = np.empty((T, K), np.float32)
+        counts = np.empty(NE, np.int32)
+        offsets = np.empty(NE + 1, np.int32)
+        perm = np.empty(T * K, np.int32)
+        check(lib().moe_layer_routing(self.handle, ids.ctypes.data, w.ctypes.data,
+                                      counts.ctypes.data, offsets.ctypes.data, perm.ctypes.data))
+        return ids, w, counts, offsets, perm
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().moe_layer_destroy(self.handle)
+            self.handle = None
+        for b in self.bufs:
+            b.free()
+        self.bufs = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ drop-ins
+def ffn_forward(x, router_w, gate, up, down, qtype, top_k, flags=0):
+    """moe_ffn_forward through tensor_t views of host arrays (OLMoE 3-D layout)."""
+    x = np.ascontiguousarray(x, np.float32)
+    T, d = x.shape
+    NE, F = gate.shape[0], gate.shape[1]
+    out = np.zeros((T, d), np.float32)
+    ti, to = tensor(x), tensor(out)
+    tr = tensor(np.ascontiguousarray(router_w, np.float32))
+    tg = tensor(gate, qtype, (NE, F, d))
+    tu = tensor(up, qtype, (NE, F, d))
+    td = tensor(down, qtype, (NE, d, F))
+    check(lib().moe_ffn_forward(C.byref(ti), C.byref(to), C.byref(tr), C.byref(tg),
+                                C.byref(tu), C.byref(td), top_k, flags))
+    return out
+
+
+def ffn_forward_split(x, router_w, gates, ups, downs, qtype, top_k, flags=0):
+    """moe_ffn_forward_split: Mixtral per-expert 2-D tensors."""
+    x = np.ascontiguousarray(x, np.float32)
+    T, d = x.shape
+    NE = len(gates)
+    F = gates[0].shape[0]
+    out = np.zeros((T, d), np.float32)
+    ti, to = tensor(x), tensor(out)
+    tr = tensor(np.ascontiguousarray(router_w, np.float32))
+    tg = [tensor(np.ascontiguousarray(g), qtype, (F, d)) for g in gates]
+    tu = [tensor(np.ascontiguousarray(u), qtype, (F, d)) for u in ups]
+    tdn = [tensor(np.ascontiguousarray(dn), qtype, (d, F)) for dn in downs]
+    arr = lambda ts: (C.POINTER(MoeTensor) * NE)(*[C.pointer(t) for t in ts])  # noqa: E731
+    check(lib().moe_ffn_forward_split(C.byref(ti), C.byref(to), C.byref(tr), arr(tg), arr(tu),
+                                      arr(tdn), NE, top_k, flags))
+    return out
+
+
+def mma_transposed(lhs: np.ndarray, rhs: np.ndarray, qtype: int, n: int, k: int, add=None):
+    """moe_tensor_mma_transposed_2x2_status: lhs [m,k] fp32 . rhs[n,k]^T (+ add)."""
+    lhs = np.ascontiguousarray(lhs, np.float32)
+    m = lhs.shape[0]
+    ret = np.zeros((m, n), np.float32)
+    tr = tensor(ret)
+    tl = tensor(lhs)
+    trh = tensor(rhs, qtype, (n, k)) if qtype != F32 else tensor(np.ascontiguousarray(rhs, np.float32))
+    ta = tensor(np.ascontiguousarray(add, np.float32)) if add is not None else None
+    check(lib().moe_tensor_mma_transposed_2x2_status(C.byref(tr), C.byref(tl), C.byref(trh),
+                                                     C.byref(ta) if ta is not None else None))
+    return ret
+
+
+def fused_ffn_silu(x: np.ndarray, gate, up, down, qtype, d_ff):
+    """moe_fused_ffn_silu on one token; returns (out [d], hidden [d_ff], rc)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(1, -1)
+    d = x.shape[1]
+    out = np.zeros((1, d), np.float32)
+    g = np.zeros((1, d_ff), np.float32)
+    u = np.zeros((1, d_ff), np.float32)
+    ts = [tensor(x), tensor(out), tensor(g), tensor(gate, qtype, (d_ff, d)), tensor(u),
+          tensor(up, qtype, (d_ff, d)), tensor(down, qtype, (d, d_ff))]
+    rc = lib().moe_fused_ffn_silu(*[C.byref(t) for t in ts])
+    return out[0], g[0], rc
+
+
+def gemv_device(w_ptr, qtype, rows, cols, x_ptr, m, y_ptr, stream=None):
+    check(lib().moe_gemv_device(w_ptr, qtype, rows, cols, x_ptr, m, y_ptr, stream))
+
+
+def gemv(w: np.ndarray, qtype: int, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+    bw = DeviceBuffer.from_numpy(w)
+    bx = DeviceBuffer.from_numpy(x)
+    by = DeviceBuffer(x.shape[0] * rows * 4)
+    gemv_device(bw.ptr, qtype, rows, cols, bx.ptr, x.shape[0], by.ptr)
+    check(lib().moe_sync())
+    return by.to_numpy(np.float32, (x.shape[0], rows))

@@ -1,0 +1,970 @@
+// capi.cu — the C ABI of libmoe_b200.so (declared in include/moe_b200.h).
+//
+// Host-side runtime: one CUDA stream per process, a weight registry that
+// keeps each uploaded tensor's GGUF bytes resident in HBM keyed by its
+// host address, cached layer objects for the tensor_t entry points, and a
+// grow-only scratch arena per layer.  Every entry point validates shapes,
+// returns a moe_status and records a message for moe_last_error().
+#include "moe_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <array>
+#include <map>
+#include <string>
+#include <vector>
+
+#ifndef MOE_B200_VERSION
+#define MOE_B200_VERSION "moe_b200 0.1 sm_100a"
+#endif
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...)
+{
+	char buf[512];
+	va_list ap;
+	va_start(ap, fmt);
+	vsnprintf(buf, sizeof(buf), fmt, ap);
+	va_end(ap);
+	g_err = buf;
+	return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what)
+{
+	return fail(e == cudaErrorMemoryAllocation ? MOE_ERR_NOMEM : MOE_ERR_CUDA, "%s: %s", what,
+		    cudaGetErrorString(e));
+}
+
+#define CK(call)                                                   \
+	do {                                                       \
+		cudaError_t e_ = (call);                           \
+		if (e_ != cudaSuccess)                             \
+			return cuda_fail(e_, #call);               \
+	} while (0)
+
+struct Reg {
+	uintptr_t host;
+	size_t bytes;
+	void *dev;
+};
+
+struct Ctx {
+	bool init = false;
+	int device = -1;
+	cudaStream_t stream = nullptr;
+	std::map<uintptr_t, Reg> regs;  // keyed by host start address
+	size_t resident = 0;
+	// host-IO staging for the drop-ins
+	void *pin = nullptr;
+	size_t pin_bytes = 0;
+	void *dev_io = nullptr;
+	size_t dev_io_bytes = 0;
+	std::map<std::vector<uintptr_t>, moe_layer *> layers;
+};
+
+Ctx g;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int64_t qrow_bytes(int type, int64_t cols)
+{
+	if (type == MOE_Q8_0)
+		return cols / QK * Q8_0_BYTES;
+	if (type == MOE_Q4_0)
+		return cols / QK * Q4_0_BYTES;
+	return cols * 4;
+}
+
+// bytes of a tensor's payload from its dims (innermost dim = columns)
+size_t tensor_bytes(const moe_tensor_t *t)
+{
+	if (t->ndim == 0)
+		return 0;
+	uint64_t cols = t->dim[t->ndim - 1];
+	uint64_t rows = 1;
+	for (uint32_t i = 0; i + 1 < t->ndim; i++)
+		rows *= t->dim[i];
+	return (size_t)(rows * (uint64_t)qrow_bytes(t->type, (int64_t)cols));
+}
+
+const void *tensor_host_ptr(const moe_tensor_t *t)
+{
+	return t->type == MOE_F32 ? (const void *)t->data : t->qdata;
+}
+
+int ensure_init()
+{
+	if (g.init)
+		return MOE_OK;
+	return moe_init(0) == MOE_OK ? MOE_OK : MOE_ERR_NOT_INIT;
+}
+
+// device address for host range [p, p+bytes): a registered range that
+// contains it, else upload it now as a new registration.
+int resolve(const void *hp, size_t bytes, const void **dev)
+{
+	uintptr_t p = (uintptr_t)hp;
+	auto it = g.regs.upper_bound(p);
+	if (it != g.regs.begin()) {
+		--it;
+		const Reg &r = it->second;
+		if (p >= r.host && p + bytes <= r.host + r.bytes) {
+			*dev = (const char *)r.dev + (p - r.host);
+			return MOE_OK;
+		}
+	}
+	void *d = nullptr;
+	CK(cudaMalloc(&d, bytes));
+	cudaError_t e = cudaMemcpy(d, hp, bytes, cudaMemcpyHostToDevice);
+	if (e != cudaSuccess) {
+		cudaFree(d);
+		return cuda_fail(e, "weight upload");
+	}
+	g.regs[p] = Reg{p, bytes, d};
+	g.resident += bytes;
+	*dev = d;
+	return MOE_OK;
+}
+
+int ensure_pinned(size_t bytes)
+{
+	if (g.pin_bytes >= bytes)
+		return MOE_OK;
+	if (g.pin)
+		cudaFreeHost(g.pin);
+	g.pin = nullptr;
+	g.pin_bytes = 0;
+	size_t want = align_up(bytes, 1 << 20);
+	CK(cudaMallocHost(&g.pin, want));
+	g.pin_bytes = want;
+	return MOE_OK;
+}
+
+int ensure_dev_io(size_t bytes)
+{
+	if (g.dev_io_bytes >= bytes)
+		return MOE_OK;
+	CK(cudaStreamSynchronize(g.stream));
+	if (g.dev_io)
+		cudaFree(g.dev_io);
+	g.dev_io = nullptr;
+	g.dev_io_bytes = 0;
+	size_t want = align_up(bytes, 1 << 20);
+	CK(cudaMalloc(&g.dev_io, want));
+	g.dev_io_bytes = want;
+	return MOE_OK;
+}
+
+}  // namespace
+
+// -------------------------------------------------------------------------
+// layer object
+// -------------------------------------------------------------------------
+struct moe_layer {
+	moe_layer_desc d;
+	const void **dptrs = nullptr;  // device [3][NE]: gate, up, down
+	void *scratch = nullptr;
+	size_t scratch_bytes = 0;
+	int64_t capT = -1;
+	int64_t lastT = 0;
+	// MOE_PROFILE: one set of 6 events per profiled forward since the last
+	// moe_layer_stage_ms (stage boundaries on the launching stream)
+	std::vector<std::array<cudaEvent_t, 6>> prof;
+	size_t prof_used = 0;
+	// slices of scratch
+	float *logits, *wts, *h, *Y;
+	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
+};
+
+namespace {
+
+int layer_scratch(moe_layer *L, int64_t T)
+{
+	if (T <= L->capT)
+		return MOE_OK;
+	const int64_t NE = L->d.n_experts, K = L->d.top_k, F = L->d.d_ff, D = L->d.d_model;
+	const int64_t cap = T < 64 ? 64 : T;
+	size_t off = 0;
+	auto take = [&](size_t bytes) {
+		size_t o = off;
+		off = align_up(off + bytes, 256);
+		return o;
+	};
+	size_t o_logits = take(cap * NE * 4), o_ids = take(cap * K * 4), o_wts = take(cap * K * 4);
+	size_t o_counts = take(NE * 4), o_offsets = take((NE + 1) * 4), o_perm = take(cap * K * 4);
+	size_t o_pos = take(cap * K * 4), o_err = take(4);
+	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
+	if (L->scratch) {
+		CK(cudaStreamSynchronize(g.stream));
+		cudaFree(L->scratch);
+		L->scratch = nullptr;
+		L->capT = -1;
+	}
+	CK(cudaMalloc(&L->scratch, off));
+	L->scratch_bytes = off;
+	char *b = static_cast<char *>(L->scratch);
+	L->logits = (float *)(b + o_logits);
+	L->ids = (int32_t *)(b + o_ids);
+	L->wts = (float *)(b + o_wts);
+	L->counts = (int32_t *)(b + o_counts);
+	L->offsets = (int32_t *)(b + o_offsets);
+	L->perm = (int32_t *)(b + o_perm);
+	L->pos_of = (int32_t *)(b + o_pos);
+	L->err = (int32_t *)(b + o_err);
+	L->h = (float *)(b + o_h);
+	L->Y = (float *)(b + o_Y);
+	L->capT = cap;
+	return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_init(int device)
+{
+	if (g.init) {
+		if (device == g.device)
+			return MOE_OK;
+		return fail(MOE_ERR_INVALID, "moe_init: already initialised on device %d", g.device);
+	}
+	int n = 0;
+	CK(cudaGetDeviceCount(&n));
+	if (device < 0 || device >= n)
+		return fail(MOE_ERR_INVALID, "moe_init: device %d of %d", device, n);
+	CK(cudaSetDevice(device));
+	CK(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking));
+	g.device = device;
+	g.init = true;
+	g_err.clear();
+	return MOE_OK;
+}
+
+int moe_shutdown(void)
+{
+	if (!g.init)
+		return MOE_OK;
+	cudaStreamSynchronize(g.stream);
+	for (auto &kv : g.layers)
+		moe_layer_destroy(kv.second);
+	g.layers.clear();
+	for (auto &kv : g.regs)
+		cudaFree(kv.second.dev);
+	g.regs.clear();
+	g.resident = 0;
+	if (g.pin)
+		cudaFreeHost(g.pin);
+	if (g.dev_io)
+		cudaFree(g.dev_io);
+	g.pin = g.dev_io = nullptr;
+	g.pin_bytes = g.dev_io_bytes = 0;
+	cudaStreamDestroy(g.stream);
+	g.stream = nullptr;
+	g.init = false;
+	g.device = -1;
+	return MOE_OK;
+}
+
+const char *moe_last_error(void) { return g_err.c_str(); }
+
+const char *moe_version(void) { return MOE_B200_VERSION; }
+
+int moe_sync(void)
+{
+	if (!g.init)
+		return fail(MOE_ERR_NOT_INIT, "moe_sync: not initialised");
+	CK(cudaStreamSynchronize(g.stream));
+	return MOE_OK;
+}
+
+// ---------------------------------------------------------------- registry
+int moe_register_weights(const moe_tensor_t *t)
+{
+	if (!t || !tensor_host_ptr(t))
+		return fail(MOE_ERR_INVALID, "moe_register_weights: null tensor");
+	if (t->type != MOE_F32 && t->type != MOE_Q8_0 && t->type != MOE_Q4_0)
+		return fail(MOE_ERR_UNSUPPORTED, "moe_register_weights: dtype %d", t->type);
+	if (int rc = ensure_init())
+		return rc;
+	const void *dev;
+	return resolve(tensor_host_ptr(t), tensor_bytes(t), &dev);
+}
+
+int moe_unregister_weights(const moe_tensor_t *t)
+{
+	if (!t || !g.init)
+		return fail(MOE_ERR_INVALID, "moe_unregister_weights: nothing registered");
+	auto it = g.regs.find((uintptr_t)tensor_host_ptr(t));
+	if (it == g.regs.end())
+		return fail(MOE_ERR_INVALID, "moe_unregister_weights: tensor not registered");
+	CK(cudaStreamSynchronize(g.stream));
+	// drop cached layers that point into this range
+	for (auto lt = g.layers.begin(); lt != g.layers.end();) {
+		bool hit = false;
+		for (uintptr_t k : lt->first)
+			hit |= k >= it->second.host && k < it->second.host + it->second.bytes;
+		if (hit) {
+			moe_layer_destroy(lt->second);
+			lt = g.layers.erase(lt);
+		} else {
+			++lt;
+		}
+	}
+	cudaFree(it->second.dev);
+	g.resident -= it->second.bytes;
+	g.regs.erase(it);
+	return MOE_OK;
+}
+
+size_t moe_resident_bytes(void) { return g.resident; }
+
+// ---------------------------------------------------------------- memory
+void *moe_device_alloc(size_t bytes)
+{
+	if (ensure_init())
+		return nullptr;
+	void *p = nullptr;
+	cudaError_t e = cudaMalloc(&p, bytes ? bytes : 1);
+	if (e != cudaSuccess) {
+		cuda_fail(e, "moe_device_alloc");
+		return nullptr;
+	}
+	return p;
+}
+
+int moe_device_free(void *p)
+{
+	if (p)
+		CK(cudaFree(p));
+	return MOE_OK;
+}
+
+int moe_memcpy_h2d(void *dst, const void *src, size_t bytes)
+{
+	CK(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+	return MOE_OK;
+}
+
+int moe_memcpy_d2h(void *dst, const void *src, size_t bytes)
+{
+	CK(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+	return MOE_OK;
+}
+
+void *moe_host_alloc(size_t bytes)
+{
+	if (ensure_init())
+		return nullptr;
+	void *p = nullptr;
+	cudaError_t e = cudaMallocHost(&p, bytes ? bytes : 1);
+	if (e != cudaSuccess) {
+		cuda_fail(e, "moe_host_alloc");
+		return nullptr;
+	}
+	return p;
+}
+
+int moe_host_free(void *p)
+{
+	if (p)
+		CK(cudaFreeHost(p));
+	return MOE_OK;
+}
+
+// ---------------------------------------------------------------- synth
+int moe_synth_gauss(float *dst, uint64_t seed, uint64_t tag, uint64_t offset, int64_t n,
+		    float sd, void *stream)
+{
+	if (int rc = ensure_init())
+		return rc;
+	// stream seed: mix64(mix64(seed) ^ tag * 0xD1B54A32D192ED03)
+	auto mix = [](uint64_t z) {
+		z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+		z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+		return z ^ (z >> 31);
+	};
+	uint64_t s = mix(mix(seed) ^ (tag * 0xD1B54A32D192ED03ULL));
+	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+	CK(moe::launch_synth_gauss(dst, s, offset, n, sd, st));
+	return MOE_OK;
+}
+
+int moe_quantize_device(const float *src, int64_t rows, int64_t cols, int qtype, void *dst,
+			void *stream)
+{
+	if (int rc = ensure_init())
+		return rc;
+	if ((qtype != MOE_Q8_0 && qtype != MOE_Q4_0) || cols % QK)
+		return fail(MOE_ERR_INVALID, "moe_quantize_device: qtype %d cols %lld", qtype,
+			    (long long)cols);
+	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+	CK(moe::launch_quantize(src, rows, cols, qtype, dst, st));
+	return MOE_OK;
+}
+
+// ---------------------------------------------------------------- layers
+int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
+{
+	if (!out || !desc)
+		return fail(MOE_ERR_INVALID, "moe_layer_create: null argument");
+	if (int rc = ensure_init())
+		return rc;
+	const moe_layer_desc &d = *desc;
+	if (d.qtype != MOE_Q8_0 && d.qtype != MOE_Q4_0)
+		return fail(MOE_ERR_UNSUPPORTED, "moe_layer_create: qtype %d (Q8_0/Q4_0 only)",
+			    d.qtype);
+	if (d.d_model <= 0 || d.d_ff <= 0 || d.d_model % QK || d.d_ff % QK)
+		return fail(MOE_ERR_INVALID, "moe_layer_create: d_model %lld / d_ff %lld must be "
+			    "positive multiples of 32", (long long)d.d_model, (long long)d.d_ff);
+	if (d.n_experts <= 0 || d.n_experts > 256 || d.top_k <= 0 || d.top_k > d.n_experts ||
+	    d.top_k > 64)
+		return fail(MOE_ERR_INVALID, "moe_layer_create: n_experts %lld top_k %lld",
+			    (long long)d.n_experts, (long long)d.top_k);
+	if (!d.router_w || !d.gate || !d.up || !d.down)
+		return fail(MOE_ERR_INVALID, "moe_layer_create: missing weight pointers");
+	int64_t first = d.first_expert, nl = d.n_local;
+	if (nl == 0 && first == 0)
+		nl = d.n_experts;
+	if (first < 0 || nl <= 0 || first + nl > d.n_experts)
+		return fail(MOE_ERR_INVALID, "moe_layer_create: experts [%lld, +%lld) of %lld",
+			    (long long)first, (long long)nl, (long long)d.n_experts);
+	for (int64_t e = first; e < first + nl; e++)
+		if (!d.gate[e] || !d.up[e] || !d.down[e])
+			return fail(MOE_ERR_INVALID, "moe_layer_create: expert %lld has no weights",
+				    (long long)e);
+	moe_layer *L = new moe_layer();
+	L->d = d;
+	L->d.first_expert = first;
+	L->d.n_local = nl;
+	L->d.gate = L->d.up = L->d.down = nullptr;
+	std::vector<const void *> host(3 * d.n_experts);
+	for (int64_t e = 0; e < d.n_experts; e++) {
+		host[e] = d.gate[e];
+		host[d.n_experts + e] = d.up[e];
+		host[2 * d.n_experts + e] = d.down[e];
+	}
+	cudaError_t e = cudaMalloc(&L->dptrs, host.size() * sizeof(void *));
+	if (e == cudaSuccess)
+		e = cudaMemcpy(L->dptrs, host.data(), host.size() * sizeof(void *),
+			       cudaMemcpyHostToDevice);
+	if (e != cudaSuccess) {
+		cudaFree(L->dptrs);
+		delete L;
+		return cuda_fail(e, "moe_layer_create");
+	}
+	*out = L;
+	return MOE_OK;
+}
+
+int moe_layer_destroy(moe_layer *L)
+{
+	if (!L)
+		return MOE_OK;
+	if (g.init)
+		cudaStreamSynchronize(g.stream);
+	cudaFree(L->dptrs);
+	cudaFree(L->scratch);
+	for (auto &set : L->prof)
+		for (auto ev : set)
+			cudaEventDestroy(ev);
+	delete L;
+	return MOE_OK;
+}
+
+int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int flags,
+		      void *stream)
+{
+	if (!L)
+		return fail(MOE_ERR_INVALID, "moe_layer_forward: null layer");
+	if (T < 0 || T > (1 << 22))
+		return fail(MOE_ERR_INVALID, "moe_layer_forward: T = %lld", (long long)T);
+	L->lastT = T;
+	if (T == 0)
+		return MOE_OK;
+	if (!x || !out)
+		return fail(MOE_ERR_INVALID, "moe_layer_forward: null x/out");
+	if (int rc = layer_scratch(L, T))
+		return rc;
+	const moe_layer_desc &d = L->d;
+	flags |= d.flags;
+	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+	const int NE = (int)d.n_experts, K = (int)d.top_k, D = (int)d.d_model, F = (int)d.d_ff;
+	const int lanes = (flags & MOE_LANES_AVX2) ? 8 : 16;
+	const bool prof = (flags & MOE_PROFILE) != 0;
+	cudaEvent_t *ev = nullptr;
+	if (prof) {
+		if (L->prof_used == L->prof.size()) {
+			std::array<cudaEvent_t, 6> set{};
+			for (auto &e : set)
+				CK(cudaEventCreate(&e));
+			L->prof.push_back(set);
+		}
+		ev = L->prof[L->prof_used++].data();
+		CK(cudaEventRecord(ev[0], st));
+	}
+
+	CK(moe::launch_router(x, d.router_w, d.router_bias, (int)T, D, NE, K, lanes,
+			      (flags & MOE_TOPK_EXACT) ? 1 : 0, (flags & MOE_RENORM) ? 1 : 0,
+			      L->logits, L->ids, L->wts, nullptr, st));
+	if (prof)
+		CK(cudaEventRecord(ev[1], st));
+	CK(cudaMemsetAsync(L->err, 0, sizeof(int32_t), st));
+	CK(moe::launch_dispatch(L->ids, (int)(T * K), NE, L->counts, L->offsets, L->perm,
+				L->pos_of, L->err, st));
+	if (d.n_local < d.n_experts)
+		CK(cudaMemsetAsync(L->Y, 0, (size_t)T * K * D * sizeof(float), st));
+
+	const void *const *dp = L->dptrs;
+	moe::GemvArgs gu{};
+	gu.w1 = dp;
+	gu.w2 = dp + NE;
+	gu.qtype = d.qtype;
+	gu.rows = F;
+	gu.cols = D;
+	gu.NE = NE;
+	gu.K = K;
+	gu.first_expert = (int)d.first_expert;
+	gu.n_local = (int)d.n_local;
+	gu.counts = L->counts;
+	gu.offsets = L->offsets;
+	gu.perm = L->perm;
+	gu.in_perm = 1;
+	gu.out_perm = 0;
+	gu.in = x;
+	gu.out = L->h;
+	gu.dual = 1;
+	if (prof)
+		CK(cudaEventRecord(ev[2], st));
+	CK(moe::launch_expert_gemv(gu, st));
+	if (prof)
+		CK(cudaEventRecord(ev[3], st));
+
+	moe::GemvArgs dn = gu;
+	dn.w1 = dp + 2 * NE;
+	dn.w2 = nullptr;
+	dn.rows = D;
+	dn.cols = F;
+	dn.in_perm = 0;
+	dn.out_perm = 1;
+	dn.in = L->h;
+	dn.out = L->Y;
+	dn.dual = 0;
+	CK(moe::launch_expert_gemv(dn, st));
+	if (prof)
+		CK(cudaEventRecord(ev[4], st));
+
+	CK(moe::launch_combine(L->Y, L->wts, (int)T, K, D, out, st));
+	if (prof)
+		CK(cudaEventRecord(ev[5], st));
+	return MOE_OK;
+}
+
+int moe_layer_stage_ms(moe_layer *L, float *ms, int n)
+{
+	if (!L || !ms || n < 5)
+		return fail(MOE_ERR_INVALID, "moe_layer_stage_ms: need a layer and 5 floats");
+	if (L->prof_used == 0)
+		return fail(MOE_ERR_INVALID, "moe_layer_stage_ms: no MOE_PROFILE forward to report");
+	for (int i = 0; i < 5; i++)
+		ms[i] = 0.0f;
+	CK(cudaEventSynchronize(L->prof[L->prof_used - 1][5]));
+	for (size_t c = 0; c < L->prof_used; c++)
+		for (int i = 0; i < 5; i++) {
+			float t = 0.0f;
+			CK(cudaEventElapsedTime(&t, L->prof[c][i], L->prof[c][i + 1]));
+			ms[i] += t;
+		}
+	if (n >= 6)
+		ms[5] = (float)L->prof_used;
+	L->prof_used = 0;
+	return MOE_OK;
+}
+
+int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *counts,
+		      int32_t *offsets, int32_t *perm)
+{
+	if (!L)
+		return fail(MOE_ERR_INVALID, "moe_layer_routing: null layer");
+	CK(cudaStreamSynchronize(g.stream));
+	const int64_t T = L->lastT, K = L->d.top_k, NE = L->d.n_experts;
+	if (T == 0)
+		return MOE_OK;
+	int32_t err = 0;
+	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
+	if (err)
+		return fail(MOE_ERR_INVALID, "dispatch saw an expert id out of range");
+	if (ids)
+		CK(cudaMemcpy(ids, L->ids, T * K * 4, cudaMemcpyDeviceToHost));
+	if (weights)
+		CK(cudaMemcpy(weights, L->wts, T * K * 4, cudaMemcpyDeviceToHost));
+	if (counts)
+		CK(cudaMemcpy(counts, L->counts, NE * 4, cudaMemcpyDeviceToHost));
+	if (offsets)
+		CK(cudaMemcpy(offsets, L->offsets, (NE + 1) * 4, cudaMemcpyDeviceToHost));
+	if (perm)
+		CK(cudaMemcpy(perm, L->perm, T * K * 4, cudaMemcpyDeviceToHost));
+	return MOE_OK;
+}
+
+// ---------------------------------------------------------------- dense GEMV
+int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
+		    int64_t m, float *y, void *stream)
+{
+	if (int rc = ensure_init())
+		return rc;
+	if ((qtype != MOE_Q8_0 && qtype != MOE_Q4_0) || cols % QK || rows <= 0 || m < 0)
+		return fail(MOE_ERR_INVALID, "moe_gemv_device: qtype %d rows %lld cols %lld", qtype,
+			    (long long)rows, (long long)cols);
+	if (m == 0)
+		return MOE_OK;
+	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+	// one "expert" holding all m rows of x: counts = {m}, offsets = {0, m}
+	struct Meta {
+		const void *w;
+		int32_t counts[1], offsets[2];
+	};
+	static thread_local Meta *dmeta = nullptr;
+	if (!dmeta)
+		CK(cudaMalloc(&dmeta, sizeof(Meta)));
+	Meta h{w, {(int32_t)m}, {0, (int32_t)m}};
+	CK(cudaMemcpyAsync(dmeta, &h, sizeof(Meta), cudaMemcpyHostToDevice, st));
+	moe::GemvArgs a{};
+	a.w1 = reinterpret_cast<const void *const *>(&dmeta->w);
+	a.qtype = qtype;
+	a.rows = (int)rows;
+	a.cols = (int)cols;
+	a.NE = 1;
+	a.K = 1;
+	a.first_expert = 0;
+	a.n_local = 1;
+	a.counts = dmeta->counts;
+	a.offsets = dmeta->offsets;
+	a.perm = nullptr;
+	a.in_perm = a.out_perm = 0;
+	a.in = x;
+	a.out = y;
+	a.dual = 0;
+	CK(moe::launch_expert_gemv(a, st));
+	return MOE_OK;
+}
+
+// ---------------------------------------------------------------- drop-ins
+int moe_tensor_mma_transposed_2x2_status(moe_tensor_t *ret, const moe_tensor_t *lhs,
+					 const moe_tensor_t *rhs, const moe_tensor_t *add)
+{
+	if (!ret || !lhs || !rhs)
+		return fail(MOE_ERR_INVALID, "tensor_mma_transposed_2x2: null tensor");
+	if (lhs->ndim != 2 || rhs->ndim != 2 || lhs->dim[1] != rhs->dim[1] ||
+	    lhs->type != MOE_F32 || !lhs->data || !ret->data)
+		return fail(MOE_ERR_INVALID, "tensor_mma_transposed_2x2: shape/type mismatch "
+			    "(matmul.c:277-279 asserts)");
+	if (rhs->type != MOE_F32 && rhs->type != MOE_Q8_0 && rhs->type != MOE_Q4_0)
+		return fail(MOE_ERR_UNSUPPORTED, "tensor_mma_transposed_2x2: rhs dtype %d",
+			    rhs->type);
+	const int64_t m = (int64_t)lhs->dim[0], k = (int64_t)lhs->dim[1], n = (int64_t)rhs->dim[0];
+	if (ret->maxcap < (uint64_t)(m * n))
+		return fail(MOE_ERR_INVALID, "tensor_mma_transposed_2x2: ret maxcap %llu < %lld",
+			    (unsigned long long)ret->maxcap, (long long)(m * n));
+	if (add && add->totlen != (uint64_t)(m * n) && add->totlen != (uint64_t)n)
+		return fail(MOE_ERR_INVALID, "tensor_mma_transposed_2x2: add length %llu",
+			    (unsigned long long)add->totlen);
+	if (rhs->type != MOE_F32 && k % QK)
+		return fail(MOE_ERR_INVALID, "tensor_mma_transposed_2x2: k %% 32 != 0");
+	if (int rc = ensure_init())
+		return rc;
+	const void *dw;
+	if (int rc = resolve(tensor_host_ptr(rhs), tensor_bytes(rhs), &dw))
+		return rc;
+	// mma_init (matmul.c:13-33) reshapes ret to [m, n]
+	ret->ndim = 2;
+	ret->dim[0] = (uint64_t)m;
+	ret->dim[1] = (uint64_t)n;
+	ret->totlen = (uint64_t)(m * n);
+	if (m == 0 || n == 0)
+		return MOE_OK;
+	const size_t xin = align_up(m * k * 4, 256), yout = align_up(m * n * 4, 256);
+	const size_t addb = add ? align_up(add->totlen * 4, 256) : 0;
+	if (int rc = ensure_dev_io(xin + yout + addb))
+		return rc;
+	if (int rc = ensure_pinned(std::max(m * k * 4, m * n * 4)))
+		return rc;
+	char *db = static_cast<char *>(g.dev_io);
+	float *dx = (float *)db, *dy = (float *)(db + xin), *dadd = (float *)(db + xin + yout);
+	CK(cudaMemcpyAsync(dx, lhs->data, m * k * 4, cudaMemcpyHostToDevice, g.stream));
+	if (add)
+		CK(cudaMemcpyAsync(dadd, add->data, add->totlen * 4, cudaMemcpyHostToDevice,
+				   g.stream));
+	if (rhs->type == MOE_F32) {
+		// fp32 rhs: the exact lane-chain kernel of the router (matmul.c:169-245)
+		CK(moe::launch_router_logits(dx, (const float *)dw, (int)m, (int)k, (int)n, 16, dy,
+					     g.stream));
+	} else {
+		if (int rc = moe_gemv_device(dw, rhs->type, n, k, dx, m, dy, g.stream))
+			return rc;
+	}
+	if (add)
+		CK(moe::launch_add_bias(dy, dadd, m * n, (int64_t)add->totlen, g.stream));
+	CK(cudaMemcpyAsync(g.pin, dy, m * n * 4, cudaMemcpyDeviceToHost, g.stream));
+	CK(cudaStreamSynchronize(g.stream));
+	memcpy(ret->data, g.pin, m * n * 4);
+	return MOE_OK;
+}
+
+void moe_tensor_mma_transposed_2x2(moe_tensor_t *ret, const moe_tensor_t *lhs,
+				   const moe_tensor_t *rhs, const moe_tensor_t *add)
+{
+	int rc = moe_tensor_mma_transposed_2x2_status(ret, lhs, rhs, add);
+	if (rc) {
+		fprintf(stderr, "moe_tensor_mma_transposed_2x2: %s\n", g_err.c_str());
+		abort();
+	}
+}
+
+int moe_fused_ffn_silu(const moe_tensor_t *in, moe_tensor_t *out, moe_tensor_t *gate,
+		       const moe_tensor_t *gate_w, moe_tensor_t *up, const moe_tensor_t *up_w,
+		       const moe_tensor_t *down_w)
+{
+	(void)up;
+	// nn.c:503-507: applicable only to one token with quantized weights
+	if (in->dim[0] != 1)
+		return 0;
+	if (gate_w->type == MOE_F32 || up_w->type == MOE_F32 || down_w->type == MOE_F32)
+		return 0;
+	auto die = [](const char *msg) {
+		fprintf(stderr, "moe_fused_ffn_silu: %s\n", msg);
+		abort();
+	};
+	if (gate_w->type != up_w->type || gate_w->type != down_w->type ||
+	    (gate_w->type != MOE_Q8_0 && gate_w->type != MOE_Q4_0))
+		die("unsupported weight types (Q8_0/Q4_0, all equal)");
+	const int64_t k = (int64_t)in->dim[1];
+	const int64_t inter = (int64_t)gate_w->dim[0];
+	const int64_t out_n = (int64_t)down_w->dim[0];
+	if (gate_w->dim[1] != (uint64_t)k || up_w->dim[0] != (uint64_t)inter ||
+	    down_w->dim[1] != (uint64_t)inter || k % QK || inter % QK)
+		die("shape mismatch");
+	if (ensure_init())
+		die(g_err.c_str());
+	const void *dg, *du, *dd;
+	if (resolve(gate_w->qdata, tensor_bytes(gate_w), &dg) ||
+	    resolve(up_w->qdata, tensor_bytes(up_w), &du) ||
+	    resolve(down_w->qdata, tensor_bytes(down_w), &dd))
+		die(g_err.c_str());
+	// a one-token, one-expert layer: counts {1}, offsets {0,1}, perm {0}
+	struct Meta {
+		const void *w[3];
+		int32_t counts[1], offsets[2], perm[1];
+	};
+	const size_t xin = align_up(k * 4, 256), hb = align_up(inter * 4, 256);
+	const size_t yb = align_up(out_n * 4, 256), mb = align_up(sizeof(Meta), 256);
+	if (ensure_dev_io(xin + hb + yb + mb) || ensure_pinned(std::max(out_n, inter) * 4))
+		die(g_err.c_str());
+	char *db = static_cast<char *>(g.dev_io);
+	float *dx = (float *)db, *dh = (float *)(db + xin), *dy = (float *)(db + xin + hb);
+	Meta *dm = (Meta *)(db + xin + hb + yb);
+	Meta hm{{dg, du, dd}, {1}, {0, 1}, {0}};
+	if (cudaMemcpyAsync(dm, &hm, sizeof(Meta), cudaMemcpyHostToDevice, g.stream) ||
+	    cudaMemcpyAsync(dx, in->data, k * 4, cudaMemcpyHostToDevice, g.stream))
+		die("copy in failed");
+	moe::GemvArgs a{};
+	a.w1 = reinterpret_cast<const void *const *>(&dm->w[0]);
+	a.w2 = reinterpret_cast<const void *const *>(&dm->w[1]);
+	a.qtype = gate_w->type;
+	a.rows = (int)inter;
+	a.cols = (int)k;
+	a.NE = 1;
+	a.K = 1;
+	a.first_expert = 0;
+	a.n_local = 1;
+	a.counts = dm->counts;
+	a.offsets = dm->offsets;
+	a.perm = dm->perm;
+	a.in_perm = 0;
+	a.out_perm = 0;
+	a.in = dx;
+	a.out = dh;
+	a.dual = 1;
+	if (moe::launch_expert_gemv(a, g.stream) != cudaSuccess)
+		die("gate/up launch failed");
+	moe::GemvArgs b = a;
+	b.w1 = reinterpret_cast<const void *const *>(&dm->w[2]);
+	b.w2 = nullptr;
+	b.rows = (int)out_n;
+	b.cols = (int)inter;
+	b.in = dh;
+	b.out = dy;
+	b.dual = 0;
+	if (moe::launch_expert_gemv(b, g.stream) != cudaSuccess)
+		die("down launch failed");
+	if (cudaMemcpyAsync(g.pin, dy, out_n * 4, cudaMemcpyDeviceToHost, g.stream) ||
+	    cudaStreamSynchronize(g.stream))
+		die("device error");
+	memcpy(out->data, g.pin, out_n * 4);
+	if (gate && gate->data) {
+		if (cudaMemcpy(g.pin, dh, inter * 4, cudaMemcpyDeviceToHost))
+			die("device error");
+		memcpy(gate->data, g.pin, inter * 4);
+	}
+	return 1;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- layer drop-ins
+namespace {
+
+int forward_common(const moe_tensor_t *input, moe_tensor_t *output, const moe_tensor_t *gate_inp,
+		   int qtype, int64_t NE, int64_t F, const std::vector<const void *> &hg,
+		   const std::vector<const void *> &hu, const std::vector<const void *> &hd,
+		   size_t gbytes, size_t dbytes, size_t topk, int flags)
+{
+	if (!input || !output || !gate_inp)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: null tensor");
+	if (input->type != MOE_F32 || gate_inp->type != MOE_F32 || input->ndim != 2 ||
+	    gate_inp->ndim != 2)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: input/router must be 2-D fp32");
+	const int64_t T = (int64_t)input->dim[0], D = (int64_t)input->dim[1];
+	if ((int64_t)gate_inp->dim[0] != NE || (int64_t)gate_inp->dim[1] != D)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: router is [%llu,%llu], want [%lld,%lld]",
+			    (unsigned long long)gate_inp->dim[0], (unsigned long long)gate_inp->dim[1],
+			    (long long)NE, (long long)D);
+	if (output->maxcap < (uint64_t)(T * D) && !(flags & MOE_DEVICE_IO))
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: output too small");
+	if (int rc = ensure_init())
+		return rc;
+	// resolve device weights (upload on first sight)
+	const void *dr;
+	if (int rc = resolve(gate_inp->data, (size_t)NE * D * 4, &dr))
+		return rc;
+	std::vector<const void *> dg(NE), du(NE), dd(NE);
+	for (int64_t e = 0; e < NE; e++) {
+		if (int rc = resolve(hg[e], gbytes, &dg[e]))
+			return rc;
+		if (int rc = resolve(hu[e], gbytes, &du[e]))
+			return rc;
+		if (int rc = resolve(hd[e], dbytes, &dd[e]))
+			return rc;
+	}
+	std::vector<uintptr_t> key{(uintptr_t)gate_inp->data, (uintptr_t)qtype, (uintptr_t)NE,
+				   (uintptr_t)F, (uintptr_t)topk, (uintptr_t)D};
+	for (int64_t e = 0; e < NE; e++) {
+		key.push_back((uintptr_t)hg[e]);
+		key.push_back((uintptr_t)hu[e]);
+		key.push_back((uintptr_t)hd[e]);
+	}
+	moe_layer *L;
+	auto it = g.layers.find(key);
+	if (it != g.layers.end()) {
+		L = it->second;
+	} else {
+		moe_layer_desc desc{};
+		desc.d_model = D;
+		desc.d_ff = F;
+		desc.n_experts = NE;
+		desc.top_k = (int64_t)topk;
+		desc.qtype = qtype;
+		desc.flags = 0;
+		desc.router_w = (const float *)dr;
+		desc.router_bias = nullptr;
+		desc.gate = dg.data();
+		desc.up = du.data();
+		desc.down = dd.data();
+		if (int rc = moe_layer_create(&L, &desc))
+			return rc;
+		g.layers[key] = L;
+	}
+	if (flags & MOE_DEVICE_IO)
+		return moe_layer_forward(L, input->data, output->data, T, flags, nullptr);
+	const size_t xb = align_up(T * D * 4, 256);
+	if (int rc = ensure_dev_io(2 * xb))
+		return rc;
+	float *dx = (float *)g.dev_io, *dy = (float *)((char *)g.dev_io + xb);
+	CK(cudaMemcpyAsync(dx, input->data, T * D * 4, cudaMemcpyHostToDevice, g.stream));
+	if (int rc = moe_layer_forward(L, dx, dy, T, flags, nullptr))
+		return rc;
+	CK(cudaMemcpyAsync(output->data, dy, T * D * 4, cudaMemcpyDeviceToHost, g.stream));
+	CK(cudaStreamSynchronize(g.stream));
+	return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_ffn_forward(const moe_tensor_t *input, moe_tensor_t *output, const moe_tensor_t *gate_inp,
+		    const moe_tensor_t *gate_exps, const moe_tensor_t *up_exps,
+		    const moe_tensor_t *down_exps, size_t topk, int flags)
+{
+	if (!gate_exps || !up_exps || !down_exps)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: null expert tensor");
+	if (gate_exps->ndim != 3 || up_exps->ndim != 3 || down_exps->ndim != 3)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: expert tensors must be 3-D");
+	const int qt = gate_exps->type;
+	if (up_exps->type != qt || down_exps->type != qt)
+		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward: mixed expert dtypes");
+	const int64_t NE = (int64_t)gate_exps->dim[0], F = (int64_t)gate_exps->dim[1];
+	const int64_t D = (int64_t)gate_exps->dim[2];
+	if ((int64_t)up_exps->dim[0] != NE || (int64_t)up_exps->dim[1] != F ||
+	    (int64_t)up_exps->dim[2] != D || (int64_t)down_exps->dim[0] != NE ||
+	    (int64_t)down_exps->dim[1] != D || (int64_t)down_exps->dim[2] != F)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: expert shapes disagree");
+	if (qt != MOE_Q8_0 && qt != MOE_Q4_0)
+		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward: expert dtype %d", qt);
+	// tensor_at_q (olmoe.c:20-60): expert e starts e*rows*(cols/32)*bsz bytes in
+	const size_t gb = (size_t)(F * qrow_bytes(qt, D)), db = (size_t)(D * qrow_bytes(qt, F));
+	if (int rc = ensure_init())
+		return rc;
+	const void *tmp;
+	// register each 3-D tensor as one range so every expert view resolves into it
+	if (int rc = resolve(gate_exps->qdata, gb * NE, &tmp))
+		return rc;
+	if (int rc = resolve(up_exps->qdata, gb * NE, &tmp))
+		return rc;
+	if (int rc = resolve(down_exps->qdata, db * NE, &tmp))
+		return rc;
+	std::vector<const void *> hg(NE), hu(NE), hd(NE);
+	for (int64_t e = 0; e < NE; e++) {
+		hg[e] = (const char *)gate_exps->qdata + e * gb;
+		hu[e] = (const char *)up_exps->qdata + e * gb;
+		hd[e] = (const char *)down_exps->qdata + e * db;
+	}
+	return forward_common(input, output, gate_inp, qt, NE, F, hg, hu, hd, gb, db, topk, flags);
+}
+
+int moe_ffn_forward_split(const moe_tensor_t *input, moe_tensor_t *output,
+			  const moe_tensor_t *gate_inp, const moe_tensor_t *const *gate_exp,
+			  const moe_tensor_t *const *up_exp, const moe_tensor_t *const *down_exp,
+			  size_t n_experts, size_t topk, int flags)
+{
+	if (!gate_exp || !up_exp || !down_exp || n_experts == 0)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward_split: no experts");
+	const int qt = gate_exp[0]->type;
+	const int64_t F = (int64_t)gate_exp[0]->dim[0], D = (int64_t)gate_exp[0]->dim[1];
+	if (qt != MOE_Q8_0 && qt != MOE_Q4_0)
+		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward_split: expert dtype %d", qt);
+	std::vector<const void *> hg(n_experts), hu(n_experts), hd(n_experts);
+	for (size_t e = 0; e < n_experts; e++) {
+		const moe_tensor_t *a = gate_exp[e], *b = up_exp[e], *c = down_exp[e];
+		if (!a || !b || !c || a->type != qt || b->type != qt || c->type != qt ||
+		    (int64_t)a->dim[0] != F || (int64_t)a->dim[1] != D || (int64_t)b->dim[0] != F ||
+		    (int64_t)b->dim[1] != D || (int64_t)c->dim[0] != D || (int64_t)c->dim[1] != F)
+			return fail(MOE_ERR_INVALID, "moe_ffn_forward_split: expert %zu shape/type", e);
+		hg[e] = a->qdata;
+		hu[e] = b->qdata;
+		hd[e] = c->qdata;
+	}
+	const size_t gb = (size_t)(F * qrow_bytes(qt, D)), db = (size_t)(D * qrow_bytes(qt, F));
+	return forward_common(input, output, gate_inp, qt, (int64_t)n_experts, F, hg, hu, hd, gb,
+			      db, topk, flags);
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// common.cuh — shared device helpers for the B200 MoE FFN kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define QK 32            // elements per Q8_0 / Q4_0 block (quant.h:11)
+#define Q8_0_BYTES 34    // {fp16 d; int8 qs[32]}      (quant.h:14-17)
+#define Q4_0_BYTES 18    // {fp16 d; uint8 qs[16]}     (quant.h:20-23)
+
+namespace moe {
+
+enum QType { kF32 = 0, kQ8_0 = 1, kQ4_0 = 2 };
+
+__host__ __device__ inline int64_t block_bytes(int qtype)
+{
+	return qtype == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES;
+}
+
+__host__ __device__ inline int64_t row_bytes(int qtype, int64_t cols)
+{
+	return cols / QK * block_bytes(qtype);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h)
+{
+	return __half2float(__ushort_as_half(h));
+}
+
+// exp(x) rounded once to fp32: evaluated in double precision and rounded,
+// which is the correctly rounded result except within ~2^-29 ulp of a
+// rounding midpoint.  glibc's expf (used by the reference, nn.c:475 and
+// vector_avx512.h:50-63) is accurate to about 0.502 ulp, so the two agree
+// except in rare near-midpoint cases.
+__device__ __forceinline__ float exp_rn(float x)
+{
+	return (float)exp((double)x);
+}
+
+// reference's vector_reduce_sum (vector_avx512.h:127-134 for 16 lanes,
+// vector_avx2.h:130-136 for 8): repeatedly add the upper half of the live
+// lanes onto the lower half.  Lanes live in consecutive threads of a
+// warp (lane index = threadIdx % lanes); the result is valid in lane 0.
+// `__shfl_down_sync(v, s)` gives lane j the value of lane j+s.
+template <int LANES>
+__device__ __forceinline__ float lane_tree_sum(float v)
+{
+#pragma unroll
+	for (int s = LANES / 2; s >= 1; s /= 2) {
+		float o = __shfl_down_sync(0xffffffffu, v, s, LANES);
+		v = __fadd_rn(v, o);
+	}
+	return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+	for (int s = 16; s >= 1; s /= 2)
+		v += __shfl_xor_sync(0xffffffffu, v, s);
+	return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+	for (int s = 16; s >= 1; s /= 2)
+		v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+	return v;
+}
+
+// silu(g) * u exactly as nn.c:475-478 computes it: g / (1 + exp(-g)) * u,
+// each operation rounded once.
+__device__ __forceinline__ float swiglu(float g, float u)
+{
+	float den = __fadd_rn(1.0f, exp_rn(-g));
+	return __fmul_rn(__fdiv_rn(g, den), u);
+}
+
+}  // namespace moe

@@ -1,0 +1,56 @@
+// kernels.h — launchers shared between the kernel files and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+// router.cu ------------------------------------------------------------
+cudaError_t launch_router(const float *x, const float *w, const float *bias, int T, int d,
+			  int NE, int K, int lanes, int mode_exact, int renorm, float *logits,
+			  int32_t *ids, float *wts, float *probs, cudaStream_t st);
+cudaError_t launch_router_logits(const float *x, const float *w, int T, int d, int NE, int lanes,
+				 float *logits, cudaStream_t st);
+cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int32_t *counts,
+			    int32_t *offsets, int32_t *perm, int32_t *pos_of, int32_t *err,
+			    cudaStream_t st);
+
+// experts.cu -----------------------------------------------------------
+// Grouped expert GEMV over the expert segments given by counts/offsets.
+// For the segment of expert e (positions off..off+n-1 of perm order):
+//   in  row of position pos: in_perm  ? in[(perm[pos] / K)] : in[pos]
+//   out row of position pos: out_perm ? out[perm[pos]]      : out[pos]
+//   dual = 1: out[row][r] = swiglu(W1[e] row r . in, W2[e] row r . in)
+//   dual = 0: out[row][r] = W1[e] row r . in
+struct GemvArgs {
+	const void *const *w1;  // device array [NE] of device pointers
+	const void *const *w2;  // dual only
+	int qtype;
+	int rows, cols;         // weight matrix [rows, cols]
+	int NE, K;
+	int first_expert, n_local;  // experts computed here
+	const int32_t *counts, *offsets, *perm;
+	int in_perm, out_perm;
+	const float *in;        // [*, cols]
+	float *out;             // [*, rows]
+	int dual;
+	int tok;                // tokens per pass (set by the launcher)
+};
+cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st);
+
+// out[t, :] = sum_s Y[t*K + s, :] / (1 / w[t*K + s]) in slot order
+cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, float *out,
+			   cudaStream_t st);
+
+// ret[i] = ret[i] + add[i % n_add]  (bias of tensor_mma_transposed_2x2)
+cudaError_t launch_add_bias(float *ret, const float *add, int64_t total, int64_t n_add,
+			    cudaStream_t st);
+
+// synth.cu -------------------------------------------------------------
+cudaError_t launch_synth_gauss(float *dst, uint64_t stream_seed, uint64_t offset, int64_t n,
+			       float sd, cudaStream_t st);
+cudaError_t launch_quantize(const float *src, int64_t rows, int64_t cols, int qtype, void *dst,
+			    cudaStream_t st);
+
+}  // namespace moe

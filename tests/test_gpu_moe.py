@@ -1,0 +1,209 @@
+"""GPU parity of the whole MoE layer against the CPU oracle.
+
+Bars: expert ids and the per-expert permutation
+bit-exact, except where two router logits differ by less than 1e-6; the
+layer output within max-abs 2e-3 and rel-L2 1e-3 of the fp32 oracle.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3
+REL_L2 = 1e-3
+TIE = 1e-6
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+def assert_output_close(got, ref):
+    assert got.shape == ref.shape
+    assert np.isfinite(got).all()
+    err = float(np.abs(got - ref).max()) if got.size else 0.0
+    assert err <= MAX_ABS, f"max-abs {err}"
+    assert rel_l2(got, ref) <= REL_L2, f"rel-L2 {rel_l2(got, ref)}"
+
+
+def assert_routing(orc, x, layer, lanes, ids, w, ids_ref, w_ref):
+    """ids bit-exact except for experts whose router logit lies within 1e-6
+    of another expert's logit; weights of matching tokens within 2 ulp."""
+    bad = np.where((ids != ids_ref).any(axis=1))[0]
+    if bad.size:
+        logits = orc.router_logits(x[bad], layer["router_w"], lanes)
+        if layer.get("router_bias") is not None:
+            logits = logits + layer["router_bias"]
+        for r, t in enumerate(bad):
+            diff = set(ids[t].tolist()) ^ set(ids_ref[t].tolist())
+            l = logits[r]
+            for e in diff:
+                gaps = np.abs(l - l[e])
+                gaps[e] = np.inf
+                assert gaps.min() < TIE, f"token {t}: expert {e} differs without a near-tie"
+    good = np.setdiff1d(np.arange(ids.shape[0]), bad)
+    np.testing.assert_allclose(w[good], w_ref[good], rtol=2.5e-7, atol=0)
+    return bad.size
+
+
+def assert_dispatch(orc, ids, counts, offsets, perm, NE):
+    c, o, p = orc.dispatch(ids, NE)
+    np.testing.assert_array_equal(counts, c)
+    np.testing.assert_array_equal(offsets, o)
+    np.testing.assert_array_equal(perm, p)
+
+
+SMALL = dict(d=256, F=128, NE=16, K=4)
+
+
+@pytest.fixture(scope="module")
+def small_layers(orc):
+    out = {}
+    for qt in (orc.Q8_0, orc.Q4_0):
+        out[qt] = orc.make_layer(11, SMALL["d"], SMALL["F"], SMALL["NE"], SMALL["K"], qt)
+    return out
+
+
+def build(moe, L, flags=0):
+    return moe.Layer(L["d_model"], L["d_ff"], L["n_experts"], L["top_k"], L["qtype"],
+                     L["router_w"], L["gate"], L["up"], L["down"],
+                     router_bias=L.get("router_bias"), flags=flags)
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("T", [1, 2, 3, 17, 64])
+def test_small_layer(moe, orc, small_layers, qt, T):
+    L = small_layers[qt]
+    x = orc.make_tokens(100 + T, T, SMALL["d"])
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x)
+    lay = build(moe, L)
+    got = lay.forward(x)
+    ids, w, counts, offsets, perm = lay.routing(T)
+    assert_routing(orc, x, L, 16, ids, w, ids_ref, w_ref)
+    assert_dispatch(orc, ids, counts, offsets, perm, SMALL["NE"])
+    assert_output_close(got, ref)
+    lay.close()
+
+
+def test_top_k_seeding_quirk_duplicates_expert0(moe, orc, small_layers):
+    """nn.c:276-308 seeds every slot with element 0: with expert 0 the most
+    likely, all k slots are expert 0 (each weighted p0)."""
+    L = dict(small_layers[1])
+    bias = np.zeros(SMALL["NE"], np.float32)
+    bias[0] = 8.0
+    L["router_bias"] = bias
+    x = orc.make_tokens(5, 6, SMALL["d"])
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x)
+    assert (ids_ref == 0).all()
+    lay = build(moe, L)
+    got = lay.forward(x)
+    ids, w, counts, offsets, perm = lay.routing(6)
+    np.testing.assert_array_equal(ids, ids_ref)
+    assert counts[0] == 6 * SMALL["K"]
+    assert_dispatch(orc, ids, counts, offsets, perm, SMALL["NE"])
+    assert_output_close(got, ref)
+
+
+def test_partial_quirk_mixes_duplicates(moe, orc, small_layers):
+    """expert 0 ranked inside the top-k: slots below it become copies of 0."""
+    L = dict(small_layers[1])
+    bias = np.zeros(SMALL["NE"], np.float32)
+    bias[0] = 1.5
+    L["router_bias"] = bias
+    x = orc.make_tokens(6, 32, SMALL["d"])
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x)
+    dup = sum(int((r == 0).sum() > 1) for r in ids_ref)
+    assert dup > 0
+    lay = build(moe, L)
+    got = lay.forward(x)
+    ids, w, counts, offsets, perm = lay.routing(32)
+    assert_routing(orc, x, L, 16, ids, w, ids_ref, w_ref)
+    assert_output_close(got, ref)
+
+
+@pytest.mark.parametrize("flags,lanes,mode", [(1, 16, 1), (4, 8, 0), (5, 8, 1)])
+def test_modes_exact_topk_and_avx2_lanes(moe, orc, small_layers, flags, lanes, mode):
+    L = small_layers[1]
+    x = orc.make_tokens(9, 40, SMALL["d"])
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x, lanes=lanes, topk_mode=mode)
+    lay = build(moe, L)
+    got = lay.forward(x, flags=flags)
+    ids, w, *_ = lay.routing(40)
+    assert_routing(orc, x, L, lanes, ids, w, ids_ref, w_ref)
+    assert_output_close(got, ref)
+
+
+def test_zipf_bias(moe, orc):
+    L = orc.make_layer(4, 256, 128, 16, 4, orc.Q8_0, zipf=True)
+    x = orc.make_tokens(4, 48, 256)
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x)
+    lay = build(moe, L)
+    got = lay.forward(x)
+    ids, w, counts, offsets, perm = lay.routing(48)
+    assert_routing(orc, x, L, 16, ids, w, ids_ref, w_ref)
+    assert_dispatch(orc, ids, counts, offsets, perm, 16)
+    assert_output_close(got, ref)
+
+
+def test_mixtral_split_renorm_q4_0(moe, orc):
+    """llama.c:393-457: 8 experts top-2, renormalised, per-expert tensors."""
+    d, F, NE, K = 512, 384, 8, 2
+    L = orc.make_layer(3, d, F, NE, K, orc.Q4_0, renorm=True)
+    x = orc.make_tokens(3, 9, d)
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x)
+    got = moe.ffn_forward_split(x, L["router_w"], list(L["gate"]), list(L["up"]),
+                                list(L["down"]), orc.Q4_0, K, flags=moe.RENORM)
+    assert_output_close(got, ref)
+    lay = build(moe, L, flags=moe.RENORM)
+    got2 = lay.forward(x)
+    ids, w, *_ = lay.routing(9)
+    assert_routing(orc, x, L, 16, ids, w, ids_ref, w_ref)
+    np.testing.assert_array_equal(got, got2)
+
+
+def test_host_dropin_matches_device_layer(moe, orc, small_layers):
+    L = small_layers[1]
+    x = orc.make_tokens(12, 7, SMALL["d"])
+    lay = build(moe, L)
+    dev = lay.forward(x)
+    host = moe.ffn_forward(x, L["router_w"], L["gate"], L["up"], L["down"], orc.Q8_0,
+                           SMALL["K"])
+    np.testing.assert_array_equal(dev, host)
+    ref, *_ = orc.moe_ffn(L, x)
+    assert_output_close(host, ref)
+
+
+def test_deterministic(moe, orc, small_layers):
+    L = small_layers[1]
+    x = orc.make_tokens(13, 33, SMALL["d"])
+    lay = build(moe, L)
+    a = lay.forward(x)
+    b = lay.forward(x)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_empty_batch(moe, orc, small_layers):
+    L = small_layers[1]
+    lay = build(moe, L)
+    x = np.zeros((0, SMALL["d"]), np.float32)
+    assert lay.forward(x).shape == (0, SMALL["d"])
+
+
+# ---------------------------------------------------------------- config 0 shape
+@pytest.fixture(scope="module")
+def olmoe(orc):
+    """d 2048, 64 experts, top-8, d_ff 1024, Q8_0, seed 0."""
+    return orc.make_layer(0, 2048, 1024, 64, 8, orc.Q8_0)
+
+
+@pytest.mark.parametrize("T", [1, 4, 32])
+def test_config0_layer(moe, orc, olmoe, T):
+    x = orc.make_tokens(0, 32, 2048)[:T]
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(olmoe, x)
+    lay = build(moe, olmoe)
+    got = lay.forward(x)
+    ids, w, counts, offsets, perm = lay.routing(T)
+    assert_routing(orc, x, olmoe, 16, ids, w, ids_ref, w_ref)
+    assert_dispatch(orc, ids, counts, offsets, perm, 64)
+    assert_output_close(got, ref)
+    lay.close()
