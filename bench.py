@@ -146,7 +146,11 @@ def run_ours(args, rank, world, local_rank):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    stream = torch.cuda.current_stream().cuda_stream
+    # a dedicated stream: the handle of torch's default stream is 0, which the
+    # library reads as "use the library stream"
+    torch_stream = torch.cuda.Stream()
+    torch.cuda.set_stream(torch_stream)
+    stream = torch_stream.cuda_stream
     d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
     T = args.tokens
     NL = args.layers
@@ -179,10 +183,10 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record()
+    ev0.record(torch_stream)
     for i in range(args.steps):
         step(i, moe.PROFILE)
-    ev1.record()
+    ev1.record(torch_stream)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -205,7 +209,8 @@ def run_ours(args, rank, world, local_rank):
     tokens_per_s = world * T * args.steps / (ms_total / 1e3)
 
     # ---- e2e: reference-facing tensor_t call with host buffers (H2D + D2H inside)
-    e2e = run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist)
+    e2e = None if args.no_e2e else run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype,
+                                            rank, dist)
 
     # ---- roofline of the dominant kernel (gate/up + SwiGLU)
     hbm_peak, _, peak_kind = measured_peaks()
@@ -418,7 +423,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=32)
     ap.add_argument("--layers", type=int, default=8)
-    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -73,6 +73,8 @@ enum moe_status {
                              /* (llama.c:422-427); OLMoE does not            */
 #define MOE_FORCE_GEMV  0x10 /* always use the decode (GEMV) expert kernels  */
 #define MOE_FORCE_GEMM  0x20 /* always use the grouped tensor-core kernels   */
+#define MOE_SIMPLE      0x80 /* use the plain CUDA-core expert kernels (the   */
+                             /* cross-check path) instead of the MMA ones    */
 #define MOE_PROFILE     0x40 /* record CUDA events between the layer's stages */
                              /* (read back with moe_layer_stage_ms)          */
 
@@ -100,7 +102,11 @@ MOE_API const char *moe_version(void);
  * weights passed to a compute call are uploaded on first sight.
  * Replaces: nothing (the reference reads weights from the mmap'd GGUF,
  * gguf.c:490-530); this is the residency hook a caller adds after
- * gguf_tensor_3d (olmoe.c:180-182). */
+ * gguf_tensor_3d (olmoe.c:180-182).
+ * Lifetime rule: the device copy is trusted for as long as the host range
+ * stays registered, as for the read-only GGUF mapping the reference uses.
+ * A caller that frees or rewrites a registered host buffer must first call
+ * moe_unregister_weights (or moe_shutdown). */
 MOE_API int moe_register_weights(const moe_tensor_t *t);
 MOE_API int moe_unregister_weights(const moe_tensor_t *t);
 /* Bytes of weights resident on the current device. */
@@ -190,8 +196,9 @@ MOE_API int moe_layer_routing(moe_layer *layer, int32_t *ids, float *weights, in
 
 /* Device time of each stage, summed over the MOE_PROFILE forwards since
  * the last call, in ms, from CUDA events recorded on the launching stream:
- * [0] router (logits + softmax/top-k), [1] dispatch, [2] gate/up + SwiGLU,
- * [3] down, [4] combine; [5] (if n >= 6) the number of forwards summed.
+ * [0] router logits (and the fp16 split of the tokens), [1] softmax +
+ * top-k + dispatch, [2] gate/up + SwiGLU, [3] down, [4] combine; [5] (if
+ * n >= 6) the number of forwards summed.
  * Synchronises on the last event and resets the sums. */
 MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
 

@@ -18,8 +18,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
 
 F32, Q8_0, Q4_0 = 0, 1, 2
-TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE = (
-    0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40)
+TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE, SIMPLE = (
+    0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40, 0x80)
 
 ERRORS = {0: "MOE_OK", -1: "MOE_ERR_INVALID", -2: "MOE_ERR_UNSUPPORTED", -3: "MOE_ERR_CUDA",
           -4: "MOE_ERR_NOMEM", -5: "MOE_ERR_NOT_INIT", -6: "MOE_ERR_COMM", -7: "MOE_ERR_TIMEOUT"}
@@ -112,6 +112,14 @@ def init(device: int = 0):
 
 def shutdown():
     check(lib().moe_shutdown())
+
+
+def reset(device: int = 0):
+    """Drop every registered weight and cached layer (moe_shutdown), then
+    re-initialise.  Host-pointer-keyed registrations must not outlive the
+    host buffers they mirror."""
+    shutdown()
+    init(device)
 
 
 # ------------------------------------------------------------------ tensors

@@ -122,6 +122,14 @@ int resolve(const void *hp, size_t bytes, const void **dev)
 			return MOE_OK;
 		}
 	}
+	// a registration at the same start that is too short is replaced
+	auto same = g.regs.find(p);
+	if (same != g.regs.end()) {
+		CK(cudaDeviceSynchronize());
+		cudaFree(same->second.dev);
+		g.resident -= same->second.bytes;
+		g.regs.erase(same);
+	}
 	void *d = nullptr;
 	CK(cudaMalloc(&d, bytes));
 	cudaError_t e = cudaMemcpy(d, hp, bytes, cudaMemcpyHostToDevice);
@@ -180,9 +188,12 @@ struct moe_layer {
 	// moe_layer_stage_ms (stage boundaries on the launching stream)
 	std::vector<std::array<cudaEvent_t, 6>> prof;
 	size_t prof_used = 0;
+	bool mma_ok = false;  // tensor-core kernels usable (cols % 256, 16 B aligned)
 	// slices of scratch
 	float *logits, *wts, *h, *Y;
+	__half *x16, *h16;
 	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
+	int32_t *active, *n_active, *work;  // [NE], [1], [2]
 };
 
 namespace {
@@ -202,7 +213,9 @@ int layer_scratch(moe_layer *L, int64_t T)
 	size_t o_logits = take(cap * NE * 4), o_ids = take(cap * K * 4), o_wts = take(cap * K * 4);
 	size_t o_counts = take(NE * 4), o_offsets = take((NE + 1) * 4), o_perm = take(cap * K * 4);
 	size_t o_pos = take(cap * K * 4), o_err = take(4);
+	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8);
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
+	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)cap * K * 2 * F * 2);
 	if (L->scratch) {
 		CK(cudaStreamSynchronize(g.stream));
 		cudaFree(L->scratch);
@@ -220,8 +233,13 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->perm = (int32_t *)(b + o_perm);
 	L->pos_of = (int32_t *)(b + o_pos);
 	L->err = (int32_t *)(b + o_err);
+	L->active = (int32_t *)(b + o_active);
+	L->n_active = (int32_t *)(b + o_nact);
+	L->work = (int32_t *)(b + o_work);
 	L->h = (float *)(b + o_h);
 	L->Y = (float *)(b + o_Y);
+	L->x16 = (__half *)(b + o_x16);
+	L->h16 = (__half *)(b + o_h16);
 	L->capT = cap;
 	return MOE_OK;
 }
@@ -443,6 +461,11 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 				    (long long)e);
 	moe_layer *L = new moe_layer();
 	L->d = d;
+	L->mma_ok = moe::expert_mma_supported(d.qtype, (int)d.d_model) &&
+		    moe::expert_mma_supported(d.qtype, (int)d.d_ff);
+	for (int64_t e = first; e < first + nl; e++)
+		L->mma_ok = L->mma_ok && ((uintptr_t)d.gate[e] % 16 == 0) &&
+			    ((uintptr_t)d.up[e] % 16 == 0) && ((uintptr_t)d.down[e] % 16 == 0);
 	L->d.first_expert = first;
 	L->d.n_local = nl;
 	L->d.gate = L->d.up = L->d.down = nullptr;
@@ -512,53 +535,112 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		CK(cudaEventRecord(ev[0], st));
 	}
 
-	CK(moe::launch_router(x, d.router_w, d.router_bias, (int)T, D, NE, K, lanes,
-			      (flags & MOE_TOPK_EXACT) ? 1 : 0, (flags & MOE_RENORM) ? 1 : 0,
-			      L->logits, L->ids, L->wts, nullptr, st));
+	const bool simple = (flags & MOE_SIMPLE) || !L->mma_ok;
+	const int q4 = d.qtype == MOE_Q4_0;
+	// [0] router logits (+ the fp16 split of x the MMA kernels read)
+	if (moe::router_tiled_ok(D, NE)) {
+		CK(moe::launch_router_tiled(x, d.router_w, (int)T, D, NE, lanes, L->logits,
+					    simple ? nullptr : L->x16, q4, st));
+	} else {
+		CK(moe::launch_router_logits(x, d.router_w, (int)T, D, NE, lanes, L->logits, st));
+		if (!simple)
+			CK(moe::launch_split_f16(x, T, D, d.qtype, L->x16, st));
+	}
 	if (prof)
 		CK(cudaEventRecord(ev[1], st));
-	CK(cudaMemsetAsync(L->err, 0, sizeof(int32_t), st));
-	CK(moe::launch_dispatch(L->ids, (int)(T * K), NE, L->counts, L->offsets, L->perm,
-				L->pos_of, L->err, st));
+	// [1] softmax + top-k + dispatch
+	const int mode_exact = (flags & MOE_TOPK_EXACT) ? 1 : 0, renorm = (flags & MOE_RENORM) ? 1 : 0;
+	if (T <= 256 && moe::route_small_smem((int)T, NE, K) <= 160 * 1024) {
+		CK(moe::launch_route_small(L->logits, d.router_bias, (int)T, NE, K, lanes, mode_exact,
+					   renorm, (int)d.first_expert, (int)d.n_local, L->ids, L->wts,
+					   L->counts, L->offsets, L->perm, L->pos_of, L->active,
+					   L->n_active, L->err, L->work, st));
+	} else {
+		CK(moe::launch_router_topk(L->logits, d.router_bias, (int)T, NE, K, lanes, mode_exact,
+					   renorm, L->ids, L->wts, nullptr, st));
+		CK(moe::launch_dispatch(L->ids, (int)(T * K), NE, (int)d.first_expert,
+					(int)d.n_local, L->counts, L->offsets, L->perm, L->pos_of,
+					L->active, L->n_active, L->err, L->work, st));
+	}
 	if (d.n_local < d.n_experts)
 		CK(cudaMemsetAsync(L->Y, 0, (size_t)T * K * D * sizeof(float), st));
 
 	const void *const *dp = L->dptrs;
-	moe::GemvArgs gu{};
-	gu.w1 = dp;
-	gu.w2 = dp + NE;
-	gu.qtype = d.qtype;
-	gu.rows = F;
-	gu.cols = D;
-	gu.NE = NE;
-	gu.K = K;
-	gu.first_expert = (int)d.first_expert;
-	gu.n_local = (int)d.n_local;
-	gu.counts = L->counts;
-	gu.offsets = L->offsets;
-	gu.perm = L->perm;
-	gu.in_perm = 1;
-	gu.out_perm = 0;
-	gu.in = x;
-	gu.out = L->h;
-	gu.dual = 1;
 	if (prof)
 		CK(cudaEventRecord(ev[2], st));
-	CK(moe::launch_expert_gemv(gu, st));
-	if (prof)
-		CK(cudaEventRecord(ev[3], st));
-
-	moe::GemvArgs dn = gu;
-	dn.w1 = dp + 2 * NE;
-	dn.w2 = nullptr;
-	dn.rows = D;
-	dn.cols = F;
-	dn.in_perm = 0;
-	dn.out_perm = 1;
-	dn.in = L->h;
-	dn.out = L->Y;
-	dn.dual = 0;
-	CK(moe::launch_expert_gemv(dn, st));
+	if (simple) {
+		moe::GemvArgs gu{};
+		gu.w1 = dp;
+		gu.w2 = dp + NE;
+		gu.qtype = d.qtype;
+		gu.rows = F;
+		gu.cols = D;
+		gu.NE = NE;
+		gu.K = K;
+		gu.first_expert = (int)d.first_expert;
+		gu.n_local = (int)d.n_local;
+		gu.counts = L->counts;
+		gu.offsets = L->offsets;
+		gu.perm = L->perm;
+		gu.in_perm = 1;
+		gu.out_perm = 0;
+		gu.in = x;
+		gu.out = L->h;
+		gu.dual = 1;
+		CK(moe::launch_expert_gemv(gu, st));
+		if (prof)
+			CK(cudaEventRecord(ev[3], st));
+		moe::GemvArgs dn = gu;
+		dn.w1 = dp + 2 * NE;
+		dn.w2 = nullptr;
+		dn.rows = D;
+		dn.cols = F;
+		dn.in_perm = 0;
+		dn.out_perm = 1;
+		dn.in = L->h;
+		dn.out = L->Y;
+		dn.dual = 0;
+		CK(moe::launch_expert_gemv(dn, st));
+	} else {
+		moe::MmaArgs gu{};
+		gu.w1 = dp;
+		gu.w2 = dp + NE;
+		gu.qtype = d.qtype;
+		gu.rows = F;
+		gu.cols = D;
+		gu.NE = NE;
+		gu.K = K;
+		gu.first_expert = (int)d.first_expert;
+		gu.n_local = (int)d.n_local;
+		gu.counts = L->counts;
+		gu.offsets = L->offsets;
+		gu.perm = L->perm;
+		gu.in_perm = 1;
+		gu.out_perm = 0;
+		gu.in16 = L->x16;
+		gu.out16 = L->h16;
+		gu.dual = 1;
+		gu.err = L->err;
+		gu.active = L->active;
+		gu.n_active = L->n_active;
+		gu.work = L->work;
+		CK(moe::launch_expert_mma(gu, st));
+		if (prof)
+			CK(cudaEventRecord(ev[3], st));
+		moe::MmaArgs dn = gu;
+		dn.w1 = dp + 2 * NE;
+		dn.w2 = nullptr;
+		dn.rows = D;
+		dn.cols = F;
+		dn.in_perm = 0;
+		dn.out_perm = 1;
+		dn.in16 = L->h16;
+		dn.out16 = nullptr;
+		dn.out = L->Y;
+		dn.dual = 0;
+		dn.work = L->work + 1;
+		CK(moe::launch_expert_mma(dn, st));
+	}
 	if (prof)
 		CK(cudaEventRecord(ev[4], st));
 
@@ -594,14 +676,16 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 {
 	if (!L)
 		return fail(MOE_ERR_INVALID, "moe_layer_routing: null layer");
-	CK(cudaStreamSynchronize(g.stream));
+	CK(cudaDeviceSynchronize());  // the forward may have run on a caller stream
 	const int64_t T = L->lastT, K = L->d.top_k, NE = L->d.n_experts;
 	if (T == 0)
 		return MOE_OK;
 	int32_t err = 0;
 	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
-	if (err)
+	if (err == 1)
 		return fail(MOE_ERR_INVALID, "dispatch saw an expert id out of range");
+	if (err == 2)
+		return fail(MOE_ERR_TIMEOUT, "an expert kernel's bounded wait expired");
 	if (ids)
 		CK(cudaMemcpy(ids, L->ids, T * K * 4, cudaMemcpyDeviceToHost));
 	if (weights)
@@ -627,16 +711,56 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 	if (m == 0)
 		return MOE_OK;
 	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
-	// one "expert" holding all m rows of x: counts = {m}, offsets = {0, m}
+	// one "expert" holding all m rows of x: counts = {m}, offsets = {0, m}.
+	// The metadata and the fp16 split of x live in a per-thread device
+	// buffer, so calls from one thread must be ordered on one stream.
 	struct Meta {
 		const void *w;
-		int32_t counts[1], offsets[2];
+		int32_t counts[1], offsets[2], err[1], active[1], n_active[1], work[1];
 	};
 	static thread_local Meta *dmeta = nullptr;
+	static thread_local __half *x16 = nullptr;
+	static thread_local size_t x16_bytes = 0;
 	if (!dmeta)
 		CK(cudaMalloc(&dmeta, sizeof(Meta)));
-	Meta h{w, {(int32_t)m}, {0, (int32_t)m}};
+	Meta h{w, {(int32_t)m}, {0, (int32_t)m}, {0}, {0}, {1}, {0}};
 	CK(cudaMemcpyAsync(dmeta, &h, sizeof(Meta), cudaMemcpyHostToDevice, st));
+	const bool mma = moe::expert_mma_supported(qtype, (int)cols) && (uintptr_t)w % 16 == 0;
+	if (mma) {
+		const size_t need = (size_t)m * 2 * cols * sizeof(__half);
+		if (need > x16_bytes) {
+			CK(cudaStreamSynchronize(st));
+			if (x16)
+				cudaFree(x16);
+			x16 = nullptr;
+			x16_bytes = 0;
+			CK(cudaMalloc(&x16, need));
+			x16_bytes = need;
+		}
+		CK(moe::launch_split_f16(x, m, (int)cols, qtype, x16, st));
+		moe::MmaArgs a{};
+		a.w1 = reinterpret_cast<const void *const *>(&dmeta->w);
+		a.qtype = qtype;
+		a.rows = (int)rows;
+		a.cols = (int)cols;
+		a.NE = 1;
+		a.K = 1;
+		a.first_expert = 0;
+		a.n_local = 1;
+		a.counts = dmeta->counts;
+		a.offsets = dmeta->offsets;
+		a.perm = nullptr;
+		a.in_perm = a.out_perm = 0;
+		a.in16 = x16;
+		a.out = y;
+		a.dual = 0;
+		a.err = dmeta->err;
+		a.active = dmeta->active;
+		a.n_active = dmeta->n_active;
+		a.work = dmeta->work;
+		CK(moe::launch_expert_mma(a, st));
+		return MOE_OK;
+	}
 	moe::GemvArgs a{};
 	a.w1 = reinterpret_cast<const void *const *>(&dmeta->w);
 	a.qtype = qtype;

@@ -137,6 +137,28 @@ cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st)
 __global__ void combine_kernel(const float *__restrict__ Y, const float *__restrict__ w, int T,
 			       int K, int d, float *__restrict__ out)
 {
+	// one thread per 4 consecutive outputs of one token (d % 4 == 0)
+	const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+	const int d4 = d / 4;
+	if (i >= (int64_t)T * d4)
+		return;
+	const int t = (int)(i / d4);
+	const int j4 = (int)(i - (int64_t)t * d4);
+	float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+	for (int s = 0; s < K; s++) {
+		const float inv = __fdiv_rn(1.0f, w[t * K + s]);
+		const float4 y = __ldg(reinterpret_cast<const float4 *>(Y + ((int64_t)t * K + s) * d) + j4);
+		acc.x = __fadd_rn(__fdiv_rn(y.x, inv), acc.x);
+		acc.y = __fadd_rn(__fdiv_rn(y.y, inv), acc.y);
+		acc.z = __fadd_rn(__fdiv_rn(y.z, inv), acc.z);
+		acc.w = __fadd_rn(__fdiv_rn(y.w, inv), acc.w);
+	}
+	reinterpret_cast<float4 *>(out + (int64_t)t * d)[j4] = acc;
+}
+
+__global__ void combine_kernel_scalar(const float *__restrict__ Y, const float *__restrict__ w,
+				      int T, int K, int d, float *__restrict__ out)
+{
 	const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
 	if (i >= (int64_t)T * d)
 		return;
@@ -157,7 +179,13 @@ cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, 
 	const int64_t total = (int64_t)T * d;
 	if (total == 0)
 		return cudaSuccess;
-	combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(Y, w, T, K, d, out);
+	if (d % 4 == 0 && (uintptr_t)Y % 16 == 0 && (uintptr_t)out % 16 == 0) {
+		const int64_t n4 = total / 4;
+		combine_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(Y, w, T, K, d, out);
+	} else {
+		combine_kernel_scalar<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(Y, w, T, K, d,
+											 out);
+	}
 	return cudaGetLastError();
 }
 

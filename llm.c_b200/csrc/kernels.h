@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cuda_fp16.h>
 
 namespace moe {
 
@@ -12,9 +13,26 @@ cudaError_t launch_router(const float *x, const float *w, const float *bias, int
 			  int32_t *ids, float *wts, float *probs, cudaStream_t st);
 cudaError_t launch_router_logits(const float *x, const float *w, int T, int d, int NE, int lanes,
 				 float *logits, cudaStream_t st);
-cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int32_t *counts,
-			    int32_t *offsets, int32_t *perm, int32_t *pos_of, int32_t *err,
+// exact tiled router for d % 256 == 0 and NE % 16 == 0; also writes the
+// fp16 hi/lo split of x (x16 may be NULL; q4 = Q4_0 block permutation)
+bool router_tiled_ok(int d, int NE);
+cudaError_t launch_router_tiled(const float *x, const float *w, int T, int d, int NE, int lanes,
+				float *logits, __half *x16, int q4, cudaStream_t st);
+cudaError_t launch_router_topk(const float *logits, const float *bias, int T, int NE, int K,
+			       int lanes, int mode_exact, int renorm, int32_t *ids, float *wts,
+			       float *probs, cudaStream_t st);
+// dispatch also zeroes *err and work[0..1]
+cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int first, int nlocal,
+			    int32_t *counts, int32_t *offsets, int32_t *perm, int32_t *pos_of,
+			    int32_t *active, int32_t *n_active, int32_t *err, int32_t *work,
 			    cudaStream_t st);
+// top-k + dispatch in one CTA (needs route_small_smem(T, NE, K) <= ~200 KB)
+size_t route_small_smem(int T, int NE, int K);
+cudaError_t launch_route_small(const float *logits, const float *bias, int T, int NE, int K,
+			       int lanes, int mode_exact, int renorm, int first, int nlocal,
+			       int32_t *ids, float *wts, int32_t *counts, int32_t *offsets,
+			       int32_t *perm, int32_t *pos_of, int32_t *active, int32_t *n_active,
+			       int32_t *err, int32_t *work, cudaStream_t st);
 
 // experts.cu -----------------------------------------------------------
 // Grouped expert GEMV over the expert segments given by counts/offsets.
@@ -38,6 +56,32 @@ struct GemvArgs {
 	int tok;                // tokens per pass (set by the launcher)
 };
 cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st);
+
+// expert_mma.cu: tensor-core grouped expert GEMV (decode).  Same segment
+// semantics as GemvArgs; activations are fp16 hi/lo rows [row][2][cols]
+// (Q4_0: each 32-element block stored in the permuted order of q4_slot).
+struct MmaArgs {
+	const void *const *w1;
+	const void *const *w2;
+	int qtype;
+	int rows, cols;
+	int NE, K;
+	int first_expert, n_local;
+	const int32_t *counts, *offsets, *perm;
+	int in_perm, out_perm;
+	const __half *in16;     // [*, 2, cols]
+	float *out;             // single: [*, rows] fp32
+	__half *out16;          // dual:   [*, 2, rows] fp16 hi/lo
+	int dual;
+	int32_t *err;           // set to 2 when a bounded wait expires
+	const int32_t *active;  // [n_active] experts with work, ascending
+	const int32_t *n_active;
+	int32_t *work;          // item counter, zero at launch (dispatch zeroes it)
+};
+bool expert_mma_supported(int qtype, int cols);
+cudaError_t launch_expert_mma(const MmaArgs &a, cudaStream_t st);
+cudaError_t launch_split_f16(const float *x, int64_t rows, int cols, int qtype, __half *out,
+			     cudaStream_t st);
 
 // out[t, :] = sum_s Y[t*K + s, :] / (1 / w[t*K + s]) in slot order
 cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, float *out,

@@ -79,24 +79,165 @@ router_logits_kernel(const float *__restrict__ x, const float *__restrict__ w,
 }
 
 // ---------------------------------------------------------------------
-// softmax + top-k (+ optional renorm), one warp per token.
+// Tiled router logits (d % 256 == 0, NE % 16 == 0).  Same FMA chains as
+// router_logits_kernel, but each thread keeps four consecutive SIMD lanes
+// (one lane quad) for a TQ x EQ (token x expert) register tile, so every
+// float4 it reads from shared memory feeds 4*EQ (or 4*TQ) FMAs.  The CTA
+// tile is TT tokens x 16 experts; d is staged 256 columns at a time.
+// The lane tree (upper half onto lower half) becomes a shuffle with the
+// thread two (then one) quads away, then two in-register adds.
+// CTAs of the first expert tile also write the fp16 hi/lo split of x that
+// the expert kernels read (Q4_0: block-permuted, see q4_src).
 // ---------------------------------------------------------------------
-constexpr int kTopkWarps = 4;
+constexpr int kRChunk = 256;
+constexpr int kRET = 16;
 
-template <int LANES>
-__global__ void __launch_bounds__(32 * kTopkWarps)
-router_topk_kernel(const float *__restrict__ logits, const float *__restrict__ bias,
-		   int T, int NE, int K, int mode_exact, int renorm,
-		   int32_t *__restrict__ ids, float *__restrict__ wts, float *__restrict__ probs_out)
+__device__ __forceinline__ int q4_src_dev(int k)
 {
-	extern __shared__ float sm[];  // [kTopkWarps][NE] probs, then [kTopkWarps][2K]
-	const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-	const int t = blockIdx.x * kTopkWarps + warp;
-	if (t >= T)
-		return;  // whole warp leaves together
-	float *p = sm + warp * NE;
-	const float *lr = logits + (int64_t)t * NE;
+	const int base = k & ~31, c = (k & 31) >> 3, j = k & 7;
+	return base + 4 * c + 16 * ((j >> 1) & 1) + ((j >> 2) & 1) + 2 * (j & 1);
+}
 
+template <int LANES, int TQ, int EQ, int TT, int CH>
+__global__ void __launch_bounds__(256)
+router_tiled_kernel(const float *__restrict__ x, const float *__restrict__ w,
+		    float *__restrict__ logits, int T, int d, int NE,
+		    __half *__restrict__ x16, int q4)
+{
+	constexpr int LQ = LANES / 4;                 // lane quads per logit
+	constexpr int EG = kRET / EQ;                 // expert groups per CTA
+	constexpr int TG = TT / TQ;                   // token groups per CTA
+	static_assert(LQ * EG * TG == 256, "one thread per (lane quad, token grp, expert grp)");
+	constexpr int XV = TT * CH / 4 / 256;         // float4 per thread to stage x
+	constexpr int WV = kRET * CH / 4 / 256;       // float4 per thread to stage w
+	static_assert(XV >= 1 && WV >= 1, "tile too small for 256 threads");
+	extern __shared__ __align__(16) float rsm[];
+	float(*xs)[CH] = reinterpret_cast<float(*)[CH]>(rsm);             // [TT][CH]
+	float(*ws)[CH] = reinterpret_cast<float(*)[CH]>(rsm + TT * CH);   // [16][CH]
+
+	const int tid = threadIdx.x;
+	const int lq = tid % LQ, combo = tid / LQ;
+	const int tg = combo % TG, eg = combo / TG;
+	const int t0 = blockIdx.x * TT, e0 = blockIdx.y * kRET;
+	const bool write16 = x16 != nullptr && blockIdx.y == 0;
+
+	float acc[TQ][EQ][4];
+#pragma unroll
+	for (int a = 0; a < TQ; a++)
+#pragma unroll
+		for (int b = 0; b < EQ; b++)
+#pragma unroll
+			for (int j = 0; j < 4; j++)
+				acc[a][b][j] = 0.0f;
+
+	// register staging of the next chunk (global latency overlaps compute)
+	float4 xr[XV], wr[WV];
+	auto fetch = [&](int c0) {
+#pragma unroll
+		for (int v = 0; v < XV; v++) {
+			const int i = tid + v * 256, tt = i / (CH / 4), k4 = i % (CH / 4);
+			xr[v] = (t0 + tt < T) ? __ldg(reinterpret_cast<const float4 *>(
+							    x + (int64_t)(t0 + tt) * d + c0) + k4)
+					      : make_float4(0.f, 0.f, 0.f, 0.f);
+		}
+#pragma unroll
+		for (int v = 0; v < WV; v++) {
+			const int i = tid + v * 256, ee = i / (CH / 4), k4 = i % (CH / 4);
+			wr[v] = __ldg(reinterpret_cast<const float4 *>(w + (int64_t)(e0 + ee) * d + c0) + k4);
+		}
+	};
+	auto store = [&]() {
+#pragma unroll
+		for (int v = 0; v < XV; v++) {
+			const int i = tid + v * 256;
+			reinterpret_cast<float4 *>(xs[i / (CH / 4)])[i % (CH / 4)] = xr[v];
+		}
+#pragma unroll
+		for (int v = 0; v < WV; v++) {
+			const int i = tid + v * 256;
+			reinterpret_cast<float4 *>(ws[i / (CH / 4)])[i % (CH / 4)] = wr[v];
+		}
+	};
+
+	fetch(0);
+	store();
+	__syncthreads();
+	for (int c0 = 0; c0 < d; c0 += CH) {
+		const bool more = c0 + CH < d;
+		if (more)
+			fetch(c0 + CH);
+		if (write16) {
+			for (int i = tid; i < TT * CH; i += 256) {
+				const int tt = i / CH, k = i % CH;
+				if (t0 + tt >= T)
+					continue;
+				const float v = xs[tt][q4 ? q4_src_dev(k) : k];
+				const __half h = __float2half_rn(v);
+				__half *o = x16 + (int64_t)(t0 + tt) * 2 * d + c0 + k;
+				o[0] = h;
+				o[d] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+			}
+		}
+#pragma unroll 4
+		for (int s = 0; s < CH / LANES; s++) {
+			const int col = s * LANES + lq * 4;
+			float4 xv[TQ], wv[EQ];
+#pragma unroll
+			for (int a = 0; a < TQ; a++)
+				xv[a] = *reinterpret_cast<const float4 *>(&xs[tg * TQ + a][col]);
+#pragma unroll
+			for (int b = 0; b < EQ; b++)
+				wv[b] = *reinterpret_cast<const float4 *>(&ws[eg * EQ + b][col]);
+#pragma unroll
+			for (int a = 0; a < TQ; a++)
+#pragma unroll
+				for (int b = 0; b < EQ; b++) {
+					acc[a][b][0] = __fmaf_rn(xv[a].x, wv[b].x, acc[a][b][0]);
+					acc[a][b][1] = __fmaf_rn(xv[a].y, wv[b].y, acc[a][b][1]);
+					acc[a][b][2] = __fmaf_rn(xv[a].z, wv[b].z, acc[a][b][2]);
+					acc[a][b][3] = __fmaf_rn(xv[a].w, wv[b].w, acc[a][b][3]);
+				}
+		}
+		if (more) {
+			__syncthreads();  // everyone is done reading this chunk
+			store();
+			__syncthreads();
+		}
+	}
+	// lane tree: quads live in consecutive threads (lq = tid % LQ)
+#pragma unroll
+	for (int a = 0; a < TQ; a++)
+#pragma unroll
+		for (int b = 0; b < EQ; b++) {
+			float *v = acc[a][b];
+			if (LQ == 4) {
+				// lanes j += j+8  ==  quad lq += quad lq+2
+#pragma unroll
+				for (int j = 0; j < 4; j++)
+					v[j] = __fadd_rn(v[j], __shfl_down_sync(0xffffffffu, v[j], 2, 4));
+			}
+			// lanes j += j+4  ==  quad lq += quad lq+1
+#pragma unroll
+			for (int j = 0; j < 4; j++)
+				v[j] = __fadd_rn(v[j], __shfl_down_sync(0xffffffffu, v[j], 1, LQ));
+			const float s = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));
+			const int t = t0 + tg * TQ + a, e = e0 + eg * EQ + b;
+			if (lq == 0 && t < T)
+				logits[(int64_t)t * NE + e] = __fadd_rn(0.0f, s);
+		}
+}
+
+// ---------------------------------------------------------------------
+// softmax + top-k (+ optional renorm) of one token by one warp.
+// p: NE floats of shared scratch; sw/sid: K floats / ints of shared scratch.
+// ---------------------------------------------------------------------
+template <int LANES>
+__device__ void topk_token(const float *__restrict__ lr, const float *__restrict__ bias, int NE,
+			   int K, int mode_exact, int renorm, float *p, float *sw, int32_t *sid,
+			   int32_t *__restrict__ ids_out, float *__restrict__ w_out,
+			   float *__restrict__ probs_out, int32_t *ids_smem)
+{
+	const int lane = threadIdx.x % 32;
 	float mx = -INFINITY;
 	for (int e = lane; e < NE; e += 32) {
 		float v = lr[e];
@@ -129,18 +270,15 @@ router_topk_kernel(const float *__restrict__ logits, const float *__restrict__ b
 
 	if (probs_out)
 		for (int e = lane; e < NE; e += 32)
-			probs_out[(int64_t)t * NE + e] = p[e];
+			probs_out[e] = p[e];
 
-	// selections land in shared memory first so lane 0 can renormalise
-	float *sw = sm + kTopkWarps * NE + warp * 2 * K;
-	int32_t *sid = reinterpret_cast<int32_t *>(sw + K);
 	const float p0 = p[0];
 	for (int i = lane; i < NE; i += 32) {
 		const float v = p[i];
 		int rank = 0;
 		if (mode_exact) {
 			for (int j = 0; j < NE; j++) {
-				float o = p[j];
+				const float o = p[j];
 				rank += (o > v) || (o == v && j < i);
 			}
 			if (rank < K) {
@@ -159,7 +297,7 @@ router_topk_kernel(const float *__restrict__ logits, const float *__restrict__ b
 		} else {
 			rank = (p0 >= v) ? K : 0;
 			for (int j = 1; j < NE && rank < K; j++) {
-				float o = p[j];
+				const float o = p[j];
 				rank += (o > v) || (o == v && j < i);
 			}
 			if (rank < K) {
@@ -179,27 +317,52 @@ router_topk_kernel(const float *__restrict__ logits, const float *__restrict__ b
 	}
 	__syncwarp();
 	for (int q = lane; q < K; q += 32) {
-		ids[(int64_t)t * K + q] = sid[q];
-		wts[(int64_t)t * K + q] = sw[q];
+		ids_out[q] = sid[q];
+		w_out[q] = sw[q];
+		if (ids_smem)
+			ids_smem[q] = sid[q];
 	}
+	__syncwarp();
+}
+
+constexpr int kTopkWarps = 4;
+
+template <int LANES>
+__global__ void __launch_bounds__(32 * kTopkWarps)
+router_topk_kernel(const float *__restrict__ logits, const float *__restrict__ bias,
+		   int T, int NE, int K, int mode_exact, int renorm,
+		   int32_t *__restrict__ ids, float *__restrict__ wts, float *__restrict__ probs_out)
+{
+	extern __shared__ float sm[];  // [kTopkWarps][NE] probs, then [kTopkWarps][2K]
+	const int warp = threadIdx.x / 32;
+	const int t = blockIdx.x * kTopkWarps + warp;
+	if (t >= T)
+		return;  // whole warp leaves together
+	float *sw = sm + kTopkWarps * NE + warp * 2 * K;
+	topk_token<LANES>(logits + (int64_t)t * NE, bias, NE, K, mode_exact, renorm, sm + warp * NE,
+			  sw, reinterpret_cast<int32_t *>(sw + K), ids + (int64_t)t * K,
+			  wts + (int64_t)t * K, probs_out ? probs_out + (int64_t)t * NE : nullptr,
+			  nullptr);
 }
 
 // ---------------------------------------------------------------------
 // dispatch: counts[NE], offsets[NE+1], perm[T*K] (pairs p = t*K + slot
-// stably sorted by expert), pos_of[p] = position of pair p in perm.
+// stably sorted by expert), pos_of[p] = position of pair p in perm, and the
+// ascending list of experts in [first, first+nlocal) that received pairs.
 // One CTA of 1024 threads walks the pairs in chunks of 1024; within a
 // chunk a pair's rank among same-expert pairs comes from warp match masks
 // plus per-warp counts, so the order is stable and deterministic.
+// Also zeroes the error flag and the expert kernels' work counters.
+// smem: cnt[NE], run[NE], wcnt[32][NE]
 // ---------------------------------------------------------------------
 constexpr int kDispatchThreads = 1024;
 
-__global__ void __launch_bounds__(kDispatchThreads)
-dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE,
-		int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
-		int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
-		int32_t *__restrict__ err)
+__device__ void dispatch_body(const int32_t *ids, int npairs, int NE, int first, int nlocal,
+			      int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+			      int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
+			      int32_t *__restrict__ active, int32_t *__restrict__ n_active,
+			      int32_t *__restrict__ err, int32_t *ds)
 {
-	extern __shared__ int32_t ds[];
 	int32_t *cnt = ds;                // [NE]
 	int32_t *run = cnt + NE;          // [NE] running fill position
 	int32_t *wcnt = run + NE;         // [32 warps][NE]
@@ -209,7 +372,7 @@ dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE,
 		cnt[e] = 0;
 	__syncthreads();
 	for (int p = tid; p < npairs; p += blockDim.x) {
-		int e = ids[p];
+		const int e = ids[p];
 		if (e < 0 || e >= NE) {
 			atomicExch(err, 1);
 			continue;
@@ -218,14 +381,17 @@ dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE,
 	}
 	__syncthreads();
 	if (tid == 0) {
-		int acc = 0;
+		int acc = 0, na = 0;
 		for (int e = 0; e < NE; e++) {
 			offsets[e] = acc;
 			run[e] = acc;
 			counts[e] = cnt[e];
 			acc += cnt[e];
+			if (cnt[e] > 0 && e >= first && e < first + nlocal)
+				active[na++] = e;
 		}
 		offsets[NE] = acc;
+		*n_active = na;
 	}
 	__syncthreads();
 
@@ -246,7 +412,7 @@ dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE,
 			int before = 0;
 			for (int w = 0; w < warp; w++)
 				before += wcnt[w * NE + e];
-			int pos = run[e] + before + rank_w;
+			const int pos = run[e] + before + rank_w;
 			perm[pos] = p;
 			if (pos_of)
 				pos_of[p] = pos;
@@ -262,9 +428,95 @@ dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE,
 	}
 }
 
+__global__ void __launch_bounds__(kDispatchThreads)
+dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE, int first, int nlocal,
+		int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+		int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
+		int32_t *__restrict__ active, int32_t *__restrict__ n_active,
+		int32_t *__restrict__ err, int32_t *__restrict__ work)
+{
+	extern __shared__ int32_t ds[];
+	if (threadIdx.x == 0) {
+		*err = 0;
+		work[0] = work[1] = 0;
+	}
+	dispatch_body(ids, npairs, NE, first, nlocal, counts, offsets, perm, pos_of, active,
+		      n_active, err, ds);
+}
+
+// small batches: softmax/top-k of every token (warp w takes tokens w,
+// w+32, ...) and the dispatch in one CTA, ids kept in shared memory.
+// smem: probs [32][NE], sel [32][2K], ids [T*K], dispatch scratch
+template <int LANES>
+__global__ void __launch_bounds__(kDispatchThreads)
+route_small_kernel(const float *__restrict__ logits, const float *__restrict__ bias, int T,
+		   int NE, int K, int mode_exact, int renorm, int first, int nlocal,
+		   int32_t *__restrict__ ids, float *__restrict__ wts,
+		   int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+		   int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
+		   int32_t *__restrict__ active, int32_t *__restrict__ n_active,
+		   int32_t *__restrict__ err, int32_t *__restrict__ work)
+{
+	extern __shared__ float rs[];
+	const int warp = threadIdx.x / 32;
+	float *probs = rs;                                   // [32][NE]
+	float *sel = probs + 32 * NE;                        // [32][2K]
+	int32_t *ids_s = reinterpret_cast<int32_t *>(sel + 64 * K);  // [T*K]
+	int32_t *ds = ids_s + T * K;
+	if (threadIdx.x == 0) {
+		*err = 0;
+		work[0] = work[1] = 0;
+	}
+	for (int t = warp; t < T; t += 32) {
+		float *sw = sel + warp * 2 * K;
+		topk_token<LANES>(logits + (int64_t)t * NE, bias, NE, K, mode_exact, renorm,
+				  probs + warp * NE, sw, reinterpret_cast<int32_t *>(sw + K),
+				  ids + (int64_t)t * K, wts + (int64_t)t * K, nullptr, ids_s + t * K);
+	}
+	__syncthreads();
+	dispatch_body(ids_s, T * K, NE, first, nlocal, counts, offsets, perm, pos_of, active,
+		      n_active, err, ds);
+}
+
 // ---------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------
+template <int LANES, int TQ, int EQ, int TT, int CH>
+static cudaError_t run_tiled(const float *x, const float *w, float *logits, int T, int d, int NE,
+			     __half *x16, int q4, cudaStream_t st)
+{
+	const size_t smem = (size_t)(TT + kRET) * CH * sizeof(float);
+	auto fn = router_tiled_kernel<LANES, TQ, EQ, TT, CH>;
+	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+	if (e != cudaSuccess)
+		return e;
+	fn<<<dim3((T + TT - 1) / TT, NE / kRET), 256, smem, st>>>(x, w, logits, T, d, NE, x16, q4);
+	return cudaGetLastError();
+}
+
+cudaError_t launch_router_tiled(const float *x, const float *w, int T, int d, int NE, int lanes,
+				float *logits, __half *x16, int q4, cudaStream_t st)
+{
+	if (T == 0 || NE == 0)
+		return cudaSuccess;
+	// decode-sized batches: one logit (lane quad) per thread, 4-8 tokens per
+	// CTA so that many CTAs share the work; prefill: 4x4 register tiles
+	const bool big = T > 128;
+	if (lanes == 8) {
+		if (big)
+			return run_tiled<8, 2, 4, 64, 256>(x, w, logits, T, d, NE, x16, q4, st);
+		return run_tiled<8, 1, 1, 8, 256>(x, w, logits, T, d, NE, x16, q4, st);
+	}
+	if (big)
+		return run_tiled<16, 4, 4, 64, 256>(x, w, logits, T, d, NE, x16, q4, st);
+	return run_tiled<16, 1, 1, 4, 256>(x, w, logits, T, d, NE, x16, q4, st);
+}
+
+bool router_tiled_ok(int d, int NE)
+{
+	return d % kRChunk == 0 && NE % kRET == 0;
+}
+
 cudaError_t launch_router_logits(const float *x, const float *w, int T, int d, int NE, int lanes,
 				 float *logits, cudaStream_t st)
 {
@@ -289,15 +541,14 @@ cudaError_t launch_router_logits(const float *x, const float *w, int T, int d, i
 	return cudaGetLastError();
 }
 
-cudaError_t launch_router(const float *x, const float *w, const float *bias, int T, int d,
-			  int NE, int K, int lanes, int mode_exact, int renorm, float *logits,
-			  int32_t *ids, float *wts, float *probs, cudaStream_t st)
+cudaError_t launch_router_topk(const float *logits, const float *bias, int T, int NE, int K,
+			       int lanes, int mode_exact, int renorm, int32_t *ids, float *wts,
+			       float *probs, cudaStream_t st)
 {
-	cudaError_t e = launch_router_logits(x, w, T, d, NE, lanes, logits, st);
-	if (e != cudaSuccess || T == 0)
-		return e;
-	int blocks = (T + kTopkWarps - 1) / kTopkWarps;
-	size_t tsm = (size_t)kTopkWarps * (NE + 2 * K) * sizeof(float);
+	if (T == 0)
+		return cudaSuccess;
+	const int blocks = (T + kTopkWarps - 1) / kTopkWarps;
+	const size_t tsm = (size_t)kTopkWarps * (NE + 2 * K) * sizeof(float);
 	if (lanes == 8)
 		router_topk_kernel<8><<<blocks, 32 * kTopkWarps, tsm, st>>>(
 			logits, bias, T, NE, K, mode_exact, renorm, ids, wts, probs);
@@ -307,15 +558,56 @@ cudaError_t launch_router(const float *x, const float *w, const float *bias, int
 	return cudaGetLastError();
 }
 
-cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int32_t *counts,
-			    int32_t *offsets, int32_t *perm, int32_t *pos_of, int32_t *err,
+cudaError_t launch_router(const float *x, const float *w, const float *bias, int T, int d,
+			  int NE, int K, int lanes, int mode_exact, int renorm, float *logits,
+			  int32_t *ids, float *wts, float *probs, cudaStream_t st)
+{
+	cudaError_t e = launch_router_logits(x, w, T, d, NE, lanes, logits, st);
+	if (e != cudaSuccess)
+		return e;
+	return launch_router_topk(logits, bias, T, NE, K, lanes, mode_exact, renorm, ids, wts,
+				  probs, st);
+}
+
+static size_t dispatch_smem(int NE) { return (size_t)(2 * NE + 32 * NE) * sizeof(int32_t); }
+
+cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int first, int nlocal,
+			    int32_t *counts, int32_t *offsets, int32_t *perm, int32_t *pos_of,
+			    int32_t *active, int32_t *n_active, int32_t *err, int32_t *work,
 			    cudaStream_t st)
 {
-	size_t smem = (size_t)(2 * NE + 32 * NE) * sizeof(int32_t);
-	cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-			     (int)smem);
-	dispatch_kernel<<<1, kDispatchThreads, smem, st>>>(ids, npairs, NE, counts, offsets,
-							    perm, pos_of, err);
+	const size_t smem = dispatch_smem(NE);
+	cudaError_t e = cudaFuncSetAttribute(dispatch_kernel,
+					     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+	if (e != cudaSuccess)
+		return e;
+	dispatch_kernel<<<1, kDispatchThreads, smem, st>>>(ids, npairs, NE, first, nlocal, counts,
+							    offsets, perm, pos_of, active, n_active,
+							    err, work);
+	return cudaGetLastError();
+}
+
+size_t route_small_smem(int T, int NE, int K)
+{
+	return (size_t)(32 * NE + 64 * K) * sizeof(float) + (size_t)T * K * sizeof(int32_t) +
+	       dispatch_smem(NE);
+}
+
+cudaError_t launch_route_small(const float *logits, const float *bias, int T, int NE, int K,
+			       int lanes, int mode_exact, int renorm, int first, int nlocal,
+			       int32_t *ids, float *wts, int32_t *counts, int32_t *offsets,
+			       int32_t *perm, int32_t *pos_of, int32_t *active, int32_t *n_active,
+			       int32_t *err, int32_t *work, cudaStream_t st)
+{
+	const size_t smem = route_small_smem(T, NE, K);
+	auto fn = lanes == 8 ? route_small_kernel<8> : route_small_kernel<16>;
+	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+					     (int)smem);
+	if (e != cudaSuccess)
+		return e;
+	fn<<<1, kDispatchThreads, smem, st>>>(logits, bias, T, NE, K, mode_exact, renorm, first,
+					       nlocal, ids, wts, counts, offsets, perm, pos_of,
+					       active, n_active, err, work);
 	return cudaGetLastError();
 }
 

@@ -35,9 +35,17 @@ def orc():
 
 
 @pytest.fixture(scope="session")
-def moe():
+def moe_lib():
     """The CUDA library, initialised on device 0.  Fails loudly (no fallback)."""
     m = load_package()
     m.lib()
     m.init(0)
     return m
+
+
+@pytest.fixture
+def moe(moe_lib):
+    """Per test: the weight registry is keyed by host address, and numpy
+    reuses freed addresses, so every test starts from an empty registry."""
+    moe_lib.reset(0)
+    return moe_lib

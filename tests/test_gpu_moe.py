@@ -71,7 +71,7 @@ def build(moe, L, flags=0):
 
 
 @pytest.mark.parametrize("qt", [1, 2])
-@pytest.mark.parametrize("T", [1, 2, 3, 17, 64])
+@pytest.mark.parametrize("T", [1, 2, 3, 17, 64, 300])
 def test_small_layer(moe, orc, small_layers, qt, T):
     L = small_layers[qt]
     x = orc.make_tokens(100 + T, T, SMALL["d"])
@@ -82,6 +82,34 @@ def test_small_layer(moe, orc, small_layers, qt, T):
     assert_routing(orc, x, L, 16, ids, w, ids_ref, w_ref)
     assert_dispatch(orc, ids, counts, offsets, perm, SMALL["NE"])
     assert_output_close(got, ref)
+    lay.close()
+
+
+MID = dict(d=512, F=256, NE=16, K=4)
+
+
+@pytest.fixture(scope="module")
+def mid_layers(orc):
+    """shapes the tensor-core kernels take (2- and 1-block warp slices)"""
+    return {qt: orc.make_layer(21, MID["d"], MID["F"], MID["NE"], MID["K"], qt)
+            for qt in (orc.Q8_0, orc.Q4_0)}
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("T", [1, 5, 40, 130])
+def test_mid_layer_mma_and_simple(moe, orc, mid_layers, qt, T):
+    L = mid_layers[qt]
+    x = orc.make_tokens(200 + T, T, MID["d"])
+    ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x)
+    lay = build(moe, L)
+    got = lay.forward(x)
+    ids, w, counts, offsets, perm = lay.routing(T)
+    assert_routing(orc, x, L, 16, ids, w, ids_ref, w_ref)
+    assert_dispatch(orc, ids, counts, offsets, perm, MID["NE"])
+    assert_output_close(got, ref)
+    simple = lay.forward(x, flags=moe.SIMPLE)
+    assert_output_close(simple, ref)
+    assert rel_l2(got, simple) < 1e-5
     lay.close()
 
 
@@ -121,14 +149,15 @@ def test_partial_quirk_mixes_duplicates(moe, orc, small_layers):
     assert_output_close(got, ref)
 
 
+@pytest.mark.parametrize("T", [40, 333])
 @pytest.mark.parametrize("flags,lanes,mode", [(1, 16, 1), (4, 8, 0), (5, 8, 1)])
-def test_modes_exact_topk_and_avx2_lanes(moe, orc, small_layers, flags, lanes, mode):
+def test_modes_exact_topk_and_avx2_lanes(moe, orc, small_layers, flags, lanes, mode, T):
     L = small_layers[1]
-    x = orc.make_tokens(9, 40, SMALL["d"])
+    x = orc.make_tokens(9, T, SMALL["d"])
     ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x, lanes=lanes, topk_mode=mode)
     lay = build(moe, L)
     got = lay.forward(x, flags=flags)
-    ids, w, *_ = lay.routing(40)
+    ids, w, *_ = lay.routing(T)
     assert_routing(orc, x, L, lanes, ids, w, ids_ref, w_ref)
     assert_output_close(got, ref)
 
@@ -173,6 +202,20 @@ def test_host_dropin_matches_device_layer(moe, orc, small_layers):
     assert_output_close(host, ref)
 
 
+@pytest.mark.parametrize("qt", [1, 2])
+def test_simple_and_mma_paths_agree(moe, orc, small_layers, qt):
+    """the plain CUDA-core kernels (MOE_SIMPLE) cross-check the MMA kernels"""
+    L = small_layers[qt]
+    x = orc.make_tokens(14, 45, SMALL["d"])
+    lay = build(moe, L)
+    a = lay.forward(x)
+    b = lay.forward(x, flags=moe.SIMPLE)
+    ref, *_ = orc.moe_ffn(L, x)
+    assert_output_close(a, ref)
+    assert_output_close(b, ref)
+    assert rel_l2(a, b) < 1e-5
+
+
 def test_deterministic(moe, orc, small_layers):
     L = small_layers[1]
     x = orc.make_tokens(13, 33, SMALL["d"])
@@ -196,9 +239,9 @@ def olmoe(orc):
     return orc.make_layer(0, 2048, 1024, 64, 8, orc.Q8_0)
 
 
-@pytest.mark.parametrize("T", [1, 4, 32])
+@pytest.mark.parametrize("T", [1, 4, 32, 40])
 def test_config0_layer(moe, orc, olmoe, T):
-    x = orc.make_tokens(0, 32, 2048)[:T]
+    x = orc.make_tokens(0, 40, 2048)[:T]
     ref, ids_ref, w_ref, _ = orc.moe_ffn(olmoe, x)
     lay = build(moe, olmoe)
     got = lay.forward(x)
