@@ -524,6 +524,15 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 	const int lanes = (flags & MOE_LANES_AVX2) ? 8 : 16;
 	const bool prof = (flags & MOE_PROFILE) != 0;
 	cudaEvent_t *ev = nullptr;
+	// inside a stream capture an event record must be "external" to record a
+	// timestamp each time the graph runs
+	cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+	CK(cudaStreamIsCapturing(st, &cap));
+	auto record = [&](cudaEvent_t e) {
+		return cap == cudaStreamCaptureStatusActive
+			       ? cudaEventRecordWithFlags(e, st, cudaEventRecordExternal)
+			       : cudaEventRecord(e, st);
+	};
 	if (prof) {
 		if (L->prof_used == L->prof.size()) {
 			std::array<cudaEvent_t, 6> set{};
@@ -532,7 +541,7 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 			L->prof.push_back(set);
 		}
 		ev = L->prof[L->prof_used++].data();
-		CK(cudaEventRecord(ev[0], st));
+		CK(record(ev[0]));
 	}
 
 	const bool simple = (flags & MOE_SIMPLE) || !L->mma_ok;
@@ -547,7 +556,7 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 			CK(moe::launch_split_f16(x, T, D, d.qtype, L->x16, st));
 	}
 	if (prof)
-		CK(cudaEventRecord(ev[1], st));
+		CK(record(ev[1]));
 	// [1] softmax + top-k + dispatch
 	const int mode_exact = (flags & MOE_TOPK_EXACT) ? 1 : 0, renorm = (flags & MOE_RENORM) ? 1 : 0;
 	if (T <= 256 && moe::route_small_smem((int)T, NE, K) <= 160 * 1024) {
@@ -567,7 +576,7 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 
 	const void *const *dp = L->dptrs;
 	if (prof)
-		CK(cudaEventRecord(ev[2], st));
+		CK(record(ev[2]));
 	if (simple) {
 		moe::GemvArgs gu{};
 		gu.w1 = dp;
@@ -589,7 +598,7 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		gu.dual = 1;
 		CK(moe::launch_expert_gemv(gu, st));
 		if (prof)
-			CK(cudaEventRecord(ev[3], st));
+			CK(record(ev[3]));
 		moe::GemvArgs dn = gu;
 		dn.w1 = dp + 2 * NE;
 		dn.w2 = nullptr;
@@ -626,7 +635,7 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		gu.work = L->work;
 		CK(moe::launch_expert_mma(gu, st));
 		if (prof)
-			CK(cudaEventRecord(ev[3], st));
+			CK(record(ev[3]));
 		moe::MmaArgs dn = gu;
 		dn.w1 = dp + 2 * NE;
 		dn.w2 = nullptr;
@@ -642,11 +651,11 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		CK(moe::launch_expert_mma(dn, st));
 	}
 	if (prof)
-		CK(cudaEventRecord(ev[4], st));
+		CK(record(ev[4]));
 
 	CK(moe::launch_combine(L->Y, L->wts, (int)T, K, D, out, st));
 	if (prof)
-		CK(cudaEventRecord(ev[5], st));
+		CK(record(ev[5]));
 	return MOE_OK;
 }
 

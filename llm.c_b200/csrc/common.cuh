@@ -11,6 +11,49 @@
 
 namespace moe {
 
+// Raise a kernel's dynamic shared-memory limit once per process (the
+// attribute persists), remembering what was set per kernel.
+inline cudaError_t ensure_smem_ptr(const void *fn, size_t bytes)
+{
+	static const void *keys[128];
+	static size_t vals[128];
+	static int used = 0;
+	int i = 0;
+	for (; i < used; i++)
+		if (keys[i] == fn)
+			break;
+	if (i < used && bytes <= vals[i])
+		return cudaSuccess;
+	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+					     (int)bytes);
+	if (e != cudaSuccess)
+		return e;
+	if (i == used && used < 128)
+		keys[used++] = fn;
+	if (i < 128)
+		vals[i] = bytes;
+	return cudaSuccess;
+}
+
+template <typename F>
+inline cudaError_t ensure_smem(F *fn, size_t bytes)
+{
+	return ensure_smem_ptr(reinterpret_cast<const void *>(fn), bytes);
+}
+
+inline int sm_count()
+{
+	static int n = 0;
+	if (!n) {
+		int dev = 0;
+		cudaGetDevice(&dev);
+		cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+		if (n <= 0)
+			n = 148;
+	}
+	return n;
+}
+
 enum QType { kF32 = 0, kQ8_0 = 1, kQ4_0 = 2 };
 
 __host__ __device__ inline int64_t block_bytes(int qtype)

@@ -206,82 +206,129 @@ __host__ __device__ __forceinline__ int q4_src(int k)
 }
 
 // ---------------------------------------------------------------- kernel
-// One CTA = 1 producer warp + kMmaWarps (8) consumer warps.  A work item is
-// (active expert, 16-row tile): for DUAL, gate rows r0..r0+7 and the same
-// up rows (MMA rows 0-7 and 8-15, so gate and up of a (row, token) meet in
-// one thread for SwiGLU); for the single matrix, rows r0..r0+15.  Each CTA
-// takes a contiguous range of items, so consecutive items mostly share an
-// expert and its activations.
+// Warp-specialised CTA, one per SM: warps 0-7 do the math, warp 8 is the
+// TMA producer, warps 9-10 run the epilogue.
 //
-// A pipeline stage holds the tile's 16 weight rows over KC <= 2048 columns
-// as 16 contiguous row copies (2176 B for a Q8_0 row of 2048): long runs
-// of consecutive bytes, which HBM serves far better than short pieces of
-// many rows.  The consumer warps split the stage's K range: warp w owns
-// columns [w*KC/8, (w+1)*KC/8) and keeps the matching activation fragments
-// of the current 8 tokens in registers.  Partial sums are combined through
-// shared memory in warp order (deterministic), then warp 0 writes them.
-// The producer waits on a stage's "empty" barrier (8 consumer arrivals)
-// before refilling it and arms its "full" barrier with the byte count.
+// Work item = (active expert, 16-row tile): for DUAL, gate rows r0..r0+7
+// and the same up rows (MMA rows 0-7 and 8-15, so gate and up of a (row,
+// token) meet in one accumulator set for SwiGLU); for the single matrix,
+// rows r0..r0+15.  An item is processed in passes of 8 tokens.  Each CTA
+// takes a contiguous range of items balanced by cost (passes), which every
+// warp derives identically from the routing table, so consecutive items
+// mostly share an expert and its activations.
+//
+// Producer: per (item, pass, column chunk) one pipeline stage holding the
+// tile's 16 weight rows over KC <= 2048 columns as 16 contiguous row copies
+// (2176 B for a Q8_0 row of 2048) -- long runs of consecutive bytes, which
+// HBM serves far better than short pieces of many rows.
+// Math warps split the stage's K range (warp w owns columns w*KC/8 ..) and
+// keep the matching activation fragments of the pass's 8 tokens in
+// registers; at the end of a pass each writes its partial sums into one of
+// kRedBufs exchange buffers and moves on.
+// Epilogue warps (alternating passes) add the 8 partials in warp order
+// (deterministic), apply SwiGLU or the output permutation and store.
+// All waits are bounded; a warp whose wait expires records the error and
+// keeps walking its loops without waiting, so no warp is left blocked.
 constexpr int kTokTile = 8;          // tokens per pass (one MMA n-tile)
 constexpr int kMaxKC = 2048;         // columns per stage
+constexpr int kRedBufs = 4;          // partial-sum exchange buffers
+constexpr int kEpiWarps = 2;
 
 template <int QT>
 struct StageLayout {
 	static constexpr int BB = QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES;
 	static constexpr int RS = kMaxKC / QK * BB + 16;          // smem row stride (padded)
 	static constexpr int BYTES = 16 * RS;                    // one stage
-	static constexpr int RED = 2 * kMmaWarps * 32 * 16;      // partial sums, 2 buffers
-	static constexpr int TAB = 2 * 256 * 4;                  // active experts' (e|n), off
+	static constexpr int RED = kRedBufs * kMmaWarps * 32 * 16;
+	static constexpr int META = kRedBufs * 16;               // per buffer: r0, n, off, tg
+	static constexpr int TAB = 4 * 256 * 4;                  // (e|n), off, cost prefix [257]
 };
 
-__device__ __forceinline__ void consumer_sync()
+// cost-balanced contiguous item range of this CTA.  cost(item) = passes of
+// its expert; tab[512 + a] = cost of the items of active experts < a.
+__device__ __forceinline__ void item_range(const int32_t *tab, int n_active, int groups,
+					   int &i0, int &i1)
 {
-	asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
+	const int total = tab[512 + n_active];
+	const int64_t c0 = (int64_t)total * blockIdx.x / gridDim.x;
+	const int64_t c1 = (int64_t)total * (blockIdx.x + 1) / gridDim.x;
+	// first item whose cumulative cost start is >= c (items of expert a cost p_a each)
+	auto first_item = [&](int64_t c) {
+		int a = 0;
+		while (a < n_active && tab[512 + a + 1] <= c)
+			a++;
+		if (a == n_active)
+			return n_active * groups;
+		const int pa = (tab[a] >> 8) > 0 ? ((tab[a] >> 8) + kTokTile - 1) / kTokTile : 1;
+		const int64_t k = (c - tab[512 + a] + pa - 1) / pa;   // items of expert a before c
+		return a * groups + (int)(k < groups ? k : groups);
+	};
+	i0 = first_item(c0);
+	i1 = first_item(c1);
 }
 
 template <int QT, bool DUAL, int STAGES, int WB>
-__global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1)
+__global__ void __launch_bounds__((kMmaWarps + 1 + kEpiWarps) * 32, 1)
 expert_mma_kernel(MmaArgs a)
 {
-	// WB = blocks per consumer warp per stage (KC = 256*WB columns); the
+	// WB = blocks per math warp per stage (KC = 256*WB columns); the
 	// launcher guarantees cols % KC == 0
 	extern __shared__ __align__(128) uint8_t smem[];
 	using SL = StageLayout<QT>;
 	constexpr int BB = SL::BB, RS = SL::RS;
 	constexpr int ROWS = DUAL ? 8 : 16;  // matrix rows per item
+	constexpr int KC = WB * kMmaWarps * QK;
+	constexpr int PRODUCER = kMmaWarps, EPI0 = kMmaWarps + 1;
 
 	const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-	float4 *red = reinterpret_cast<float4 *>(smem + STAGES * SL::BYTES);     // [2][8][32]
-	int32_t *tab = reinterpret_cast<int32_t *>(smem + STAGES * SL::BYTES + SL::RED);
-	uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * SL::BYTES + SL::RED + SL::TAB);
+	uint8_t *p = smem + STAGES * SL::BYTES;
+	float4 *red = reinterpret_cast<float4 *>(p);                  // [kRedBufs][8][32]
+	int32_t *meta = reinterpret_cast<int32_t *>(p + SL::RED);     // [kRedBufs][4]
+	int32_t *tab = reinterpret_cast<int32_t *>(p + SL::RED + SL::META);
+	uint64_t *full = reinterpret_cast<uint64_t *>(p + SL::RED + SL::META + SL::TAB);
 	uint64_t *empty = full + STAGES;
+	uint64_t *rfull = empty + STAGES;
+	uint64_t *rempty = rfull + kRedBufs;
 	if (threadIdx.x < STAGES) {
 		mbar_init(&full[threadIdx.x], 1);
 		mbar_init(&empty[threadIdx.x], kMmaWarps);
 	}
+	if (threadIdx.x < kRedBufs) {
+		mbar_init(&rfull[threadIdx.x], kMmaWarps);
+		mbar_init(&rempty[threadIdx.x], 1);
+	}
 	// routing tables of the active experts, read once per CTA:
-	// tab[i] = expert | pair count << 8, tab[256+i] = its offset
+	// tab[i] = expert | pair count << 8, tab[256+i] = its offset,
+	// tab[512+i] = cost (passes) of all items of active experts < i
 	const int n_active = *a.n_active;
+	const int groups = (a.rows + ROWS - 1) / ROWS;
 	for (int i = threadIdx.x; i < n_active; i += blockDim.x) {
 		const int e = a.active[i];
 		tab[i] = e | (a.counts[e] << 8);
 		tab[256 + i] = a.offsets[e];
+	}
+	__syncthreads();
+	if (threadIdx.x == 0) {
+		int c = 0;
+		for (int i = 0; i < n_active; i++) {
+			tab[512 + i] = c;
+			c += groups * (((tab[i] >> 8) + kTokTile - 1) / kTokTile);
+		}
+		tab[512 + n_active] = c;
 	}
 	fence_mbar_init();
 	__syncthreads();
 
 	const int cols = a.cols;
 	const int64_t rb = (int64_t)(cols / QK) * BB;
-	constexpr int KC = WB * kMmaWarps * QK;    // columns per stage
 	const int nch = cols / KC;                 // column chunks per row
-	const int groups = (a.rows + ROWS - 1) / ROWS;
-	const int items = n_active * groups;
-	const int per = (items + gridDim.x - 1) / gridDim.x;
-	const int i0 = blockIdx.x * per, i1 = min(items, i0 + per);
+	int i0, i1;
+	item_range(tab, n_active, groups, i0, i1);
 
-	if (warp == kMmaWarps) {
+	if (warp == PRODUCER) {
 		// ------------------------------------------------ producer warp
 		uint32_t it = 0;
+		bool failed = false;
 		int ai = i0 / groups, r0 = (i0 % groups) * ROWS;
 		for (int item = i0; item < i1; item++, r0 += ROWS) {
 			if (r0 >= groups * ROWS) {
@@ -301,15 +348,14 @@ expert_mma_kernel(MmaArgs a)
 			for (int tg = 0; tg < n; tg += kTokTile) {
 				for (int ch = 0; ch < nch; ch++, it++) {
 					const int st = it % STAGES;
-					if (it >= STAGES) {
-						const bool ok = __all_sync(0xffffffffu,
-							mbar_wait(&empty[st], ((it / STAGES) - 1) & 1));
-						if (!ok) {
-							if (lane == 0)
-								atomicExch(a.err, 2);
-							return;
-						}
+					if (it >= STAGES && !failed &&
+					    !__all_sync(0xffffffffu, mbar_wait(&empty[st], ((it / STAGES) - 1) & 1))) {
+						failed = true;
+						if (lane == 0)
+							atomicExch(a.err, 2);
 					}
+					if (failed)
+						continue;
 					constexpr uint32_t cb = (uint32_t)(KC / QK * BB);  // bytes per row
 					if (lane == 0)
 						mbar_arrive_expect_tx(&full[st], 16 * cb);
@@ -325,17 +371,82 @@ expert_mma_kernel(MmaArgs a)
 		return;
 	}
 
-	// ---------------------------------------------------- consumer warps
-	// A consumer warp whose bounded wait expires records the error and keeps
-	// walking the item loop without waiting or computing, so that it still
-	// meets the other consumer warps at every named barrier (no hang).
+	if (warp >= EPI0) {
+		// ------------------------------------------------ epilogue warps
+		bool failed = false;
+		uint32_t pass = 0;
+		int ai = i0 / groups, r0 = (i0 % groups) * ROWS;
+		for (int item = i0; item < i1; item++, r0 += ROWS) {
+			if (r0 >= groups * ROWS) {
+				r0 = 0;
+				ai++;
+			}
+			const int n = tab[ai] >> 8, off = tab[256 + ai];
+			for (int tg = 0; tg < n; tg += kTokTile, pass++) {
+				if ((int)(pass % kEpiWarps) != warp - EPI0)
+					continue;
+				const int buf = pass % kRedBufs;
+				if (!failed &&
+				    !__all_sync(0xffffffffu, mbar_wait(&rfull[buf], (pass / kRedBufs) & 1))) {
+					failed = true;
+					if (lane == 0)
+						atomicExch(a.err, 2);
+				}
+				if (!failed) {
+					const float *rv = reinterpret_cast<const float *>(red + buf * kMmaWarps * 32);
+					// DUAL: 64 outputs (lane l of the MMA layout, token slot j),
+					// gate = value j and up = value 2+j of that lane; 2 per thread.
+					// Single: 128 outputs (lane l, value i); 4 per thread.
+#pragma unroll
+					for (int q = 0; q < (DUAL ? 2 : 4); q++) {
+						const int o = lane + 32 * q;
+						const int l = DUAL ? o >> 1 : o >> 2;
+						const int i = DUAL ? (o & 1) : (o & 3);
+						float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+						for (int w = 0; w < kMmaWarps; w++) {
+							s0 = __fadd_rn(s0, rv[(w * 32 + l) * 4 + i]);
+							if (DUAL)
+								s1 = __fadd_rn(s1, rv[(w * 32 + l) * 4 + 2 + i]);
+						}
+						const int gg = l >> 2, cc = l & 3;
+						const int t = tg + 2 * cc + (i & 1);
+						if (t >= n)
+							continue;
+						const int pos = off + t;
+						if (DUAL) {
+							const int r = r0 + gg;
+							if (r < a.rows) {
+								const float h = swiglu(s0, s1);
+								const __half hh = __float2half_rn(h);
+								const __half hl = __float2half_rn(__fsub_rn(h, __half2float(hh)));
+								__half *o16 = a.out16 + (int64_t)pos * 2 * a.rows;
+								const int slot_r = QT == kQ4_0 ? q4_slot(r) : r;
+								o16[slot_r] = hh;
+								o16[a.rows + slot_r] = hl;
+							}
+						} else {
+							const int r = r0 + gg + 8 * (i >> 1);
+							const int orow = a.out_perm ? a.perm[pos] : pos;
+							if (r < a.rows)
+								a.out[(int64_t)orow * a.rows + r] = s0;
+						}
+					}
+				}
+				__syncwarp();
+				if (lane == 0)
+					mbar_arrive(&rempty[buf]);
+			}
+		}
+		return;
+	}
+
+	// ---------------------------------------------------- math warps
 	const int g = lane >> 2, c = lane & 3;
 	bool failed = false;
 	uint4 xh[WB], xl[WB];
 	int x_e = -1, x_tg = -1, x_ch = -1;  // key of the fragments in registers
-	uint32_t it = 0;
-	int rbuf = 0;    // which half of red this pass writes
-	int epi = 0;     // pass counter: warps 2*(epi%4), +1 run the epilogue
+	uint32_t it = 0, pass = 0;
 	int ai = i0 / groups, r0 = (i0 % groups) * ROWS;
 	for (int item = i0; item < i1; item++, r0 += ROWS) {
 		if (r0 >= groups * ROWS) {
@@ -344,7 +455,7 @@ expert_mma_kernel(MmaArgs a)
 		}
 		const int e = tab[ai] & 255;
 		const int n = tab[ai] >> 8, off = tab[256 + ai];
-		for (int tg = 0; tg < n; tg += kTokTile) {
+		for (int tg = 0; tg < n; tg += kTokTile, pass++) {
 			float acc[4] = {0.f, 0.f, 0.f, 0.f};
 			for (int ch = 0; ch < nch; ch++, it++) {
 				const int kb0 = ch * (KC / QK) + warp * WB;  // first block (row-global)
@@ -371,11 +482,10 @@ expert_mma_kernel(MmaArgs a)
 					if (lane == 0)
 						atomicExch(a.err, 2);
 				}
-				const uint8_t *wt = smem + st * SL::BYTES + (warp * WB) * BB;
 				if (!failed) {
+					const uint8_t *wt = smem + st * SL::BYTES + (warp * WB) * BB;
 #pragma unroll
-				for (int b = 0; b < WB; b++) {
-					{
+					for (int b = 0; b < WB; b++) {
 						uint32_t A0[4], A1[4];
 						float d0, d1;
 						load_a<QT>(wt + g * RS + b * BB, wt + (g + 8) * RS + b * BB, c, A0,
@@ -391,62 +501,22 @@ expert_mma_kernel(MmaArgs a)
 						acc[3] = __fmaf_rn(d1, __fadd_rn(t0[3], t1[3]), acc[3]);
 					}
 				}
-				}
 				__syncwarp();
 				if (lane == 0)
 					mbar_arrive(&empty[st]);
 			}
-			// combine the 8 warps' partial sums in warp order, one output per
-			// consumer thread.  red has two halves used alternately, so one
-			// barrier per pass suffices: a half is rewritten two passes
-			// later, after every reader has passed the next barrier.
-			float4 *rb2 = red + rbuf * kMmaWarps * 32;
-			rbuf ^= 1;
-			rb2[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-			consumer_sync();
-			// the epilogue rotates over warp pairs (DUAL) or warp quads, so no
-			// warp carries it on every pass
-			const int ew = DUAL ? 2 : 4;
-			const int ebase = (epi % (kMmaWarps / ew)) * ew;
-			epi++;
-			const int tid = threadIdx.x - ebase * 32;
-			if (!failed && tid >= 0 && tid < (DUAL ? 64 : 128)) {
-				// DUAL: output (lane l, token slot j): gate = value j, up = value
-				// 2+j of lane l.  Single: value i of lane l.  Lane l = 4g + c
-				// holds rows g (+8) and tokens 2c, 2c+1 of the tile.
-				const int l = DUAL ? tid >> 1 : tid >> 2;
-				const int i = DUAL ? (tid & 1) : (tid & 3);
-				const float *rv = reinterpret_cast<const float *>(rb2);
-				float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-				for (int w = 0; w < kMmaWarps; w++) {
-					s0 = __fadd_rn(s0, rv[(w * 32 + l) * 4 + i]);
-					if (DUAL)
-						s1 = __fadd_rn(s1, rv[(w * 32 + l) * 4 + 2 + i]);
-				}
-				const int gg = l >> 2, cc = l & 3;
-				const int t = tg + 2 * cc + (i & 1);
-				if (t < n) {
-					const int pos = off + t;
-					if (DUAL) {
-						const int r = r0 + gg;
-						if (r < a.rows) {
-							const float h = swiglu(s0, s1);
-							const __half hh = __float2half_rn(h);
-							const __half hl = __float2half_rn(__fsub_rn(h, __half2float(hh)));
-							__half *o = a.out16 + (int64_t)pos * 2 * a.rows;
-							const int slot_r = QT == kQ4_0 ? q4_slot(r) : r;
-							o[slot_r] = hh;
-							o[a.rows + slot_r] = hl;
-						}
-					} else {
-						const int r = r0 + gg + 8 * (i >> 1);
-						const int orow = a.out_perm ? a.perm[pos] : pos;
-						if (r < a.rows)
-							a.out[(int64_t)orow * a.rows + r] = s0;
-					}
-				}
+			// hand the partial sums to the epilogue warps
+			const int buf = pass % kRedBufs;
+			if (pass >= kRedBufs && !failed &&
+			    !__all_sync(0xffffffffu, mbar_wait(&rempty[buf], ((pass / kRedBufs) - 1) & 1))) {
+				failed = true;
+				if (lane == 0)
+					atomicExch(a.err, 2);
 			}
+			red[(buf * kMmaWarps + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+			__syncwarp();
+			if (lane == 0)
+				mbar_arrive(&rfull[buf]);
 		}
 	}
 }
@@ -487,21 +557,24 @@ template <int QT, bool DUAL, int STAGES, int WB>
 static cudaError_t launch_t(const MmaArgs &a, cudaStream_t st)
 {
 	using SL = StageLayout<QT>;
-	const size_t smem = (size_t)STAGES * SL::BYTES + SL::RED + SL::TAB + 2 * STAGES * 8;
+	const size_t smem = (size_t)STAGES * SL::BYTES + SL::RED + SL::META + SL::TAB +
+			    (2 * STAGES + 2 * kRedBufs) * 8;
 	auto fn = expert_mma_kernel<QT, DUAL, STAGES, WB>;
-	constexpr int threads = (kMmaWarps + 1) * 32;
-	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					     (int)smem);
+	constexpr int threads = (kMmaWarps + 1 + kEpiWarps) * 32;
+	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
-	int dev = 0, sms = 148, per_sm = 1;
-	cudaGetDevice(&dev);
-	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-	e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
-	if (e != cudaSuccess)
-		return e;
-	if (per_sm < 1)
-		return cudaErrorInvalidConfiguration;
+	static int per_sm = 0;  // occupancy of this instantiation (fixed)
+	if (!per_sm) {
+		e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+		if (e != cudaSuccess)
+			return e;
+		if (per_sm < 1) {
+			per_sm = 0;
+			return cudaErrorInvalidConfiguration;
+		}
+	}
+	const int sms = sm_count();
 	int64_t grid = (int64_t)sms * per_sm;
 	const int rows_per_item = DUAL ? 8 : 16;
 	const int64_t max_items = (int64_t)a.n_local * ((a.rows + rows_per_item - 1) / rows_per_item);
@@ -545,11 +618,11 @@ cudaError_t launch_expert_mma(const MmaArgs &a, cudaStream_t st)
 		return cudaSuccess;
 	if (!expert_mma_supported(a.qtype, a.cols))
 		return cudaErrorInvalidValue;
-	// one CTA per SM: 8 consumer warps (2 per scheduler) keep up with HBM,
+	// one CTA per SM: 8 math warps (2 per scheduler) keep up with HBM,
 	// and the whole shared memory goes to a deep copy pipeline
 	if (a.qtype == kQ8_0)
-		return a.dual ? launch_wb<kQ8_0, true, 6>(a, st) : launch_wb<kQ8_0, false, 6>(a, st);
-	return a.dual ? launch_wb<kQ4_0, true, 10>(a, st) : launch_wb<kQ4_0, false, 10>(a, st);
+		return a.dual ? launch_wb<kQ8_0, true, 5>(a, st) : launch_wb<kQ8_0, false, 5>(a, st);
+	return a.dual ? launch_wb<kQ4_0, true, 9>(a, st) : launch_wb<kQ4_0, false, 9>(a, st);
 }
 
 }  // namespace moe

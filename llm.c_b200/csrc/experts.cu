@@ -122,8 +122,7 @@ cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st)
 		fn = a.dual ? expert_gemv_kernel<kQ8_0, true> : expert_gemv_kernel<kQ8_0, false>;
 	else
 		fn = a.dual ? expert_gemv_kernel<kQ4_0, true> : expert_gemv_kernel<kQ4_0, false>;
-	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					     (int)smem);
+	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
 	fn<<<grid, kGemvWarps * 32, smem, st>>>(b);

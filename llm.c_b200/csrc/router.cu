@@ -487,7 +487,7 @@ static cudaError_t run_tiled(const float *x, const float *w, float *logits, int 
 {
 	const size_t smem = (size_t)(TT + kRET) * CH * sizeof(float);
 	auto fn = router_tiled_kernel<LANES, TQ, EQ, TT, CH>;
-	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
 	fn<<<dim3((T + TT - 1) / TT, NE / kRET), 256, smem, st>>>(x, w, logits, T, d, NE, x16, q4);
@@ -526,14 +526,12 @@ cudaError_t launch_router_logits(const float *x, const float *w, int T, int d, i
 	size_t smem = (size_t)kRouterTT * d * sizeof(float);
 	cudaError_t e;
 	if (lanes == 8) {
-		e = cudaFuncSetAttribute(router_logits_kernel<8>,
-					 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+		e = ensure_smem(router_logits_kernel<8>, smem);
 		if (e != cudaSuccess)
 			return e;
 		router_logits_kernel<8><<<grid, 256, smem, st>>>(x, w, logits, T, d, NE);
 	} else {
-		e = cudaFuncSetAttribute(router_logits_kernel<16>,
-					 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+		e = ensure_smem(router_logits_kernel<16>, smem);
 		if (e != cudaSuccess)
 			return e;
 		router_logits_kernel<16><<<grid, 256, smem, st>>>(x, w, logits, T, d, NE);
@@ -577,8 +575,7 @@ cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int first, i
 			    cudaStream_t st)
 {
 	const size_t smem = dispatch_smem(NE);
-	cudaError_t e = cudaFuncSetAttribute(dispatch_kernel,
-					     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+	cudaError_t e = ensure_smem(dispatch_kernel, smem);
 	if (e != cudaSuccess)
 		return e;
 	dispatch_kernel<<<1, kDispatchThreads, smem, st>>>(ids, npairs, NE, first, nlocal, counts,
@@ -601,8 +598,7 @@ cudaError_t launch_route_small(const float *logits, const float *bias, int T, in
 {
 	const size_t smem = route_small_smem(T, NE, K);
 	auto fn = lanes == 8 ? route_small_kernel<8> : route_small_kernel<16>;
-	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					     (int)smem);
+	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
 	fn<<<1, kDispatchThreads, smem, st>>>(logits, bias, T, NE, K, mode_exact, renorm, first,
