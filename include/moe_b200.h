@@ -207,6 +207,21 @@ MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
 MOE_API int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols,
 		    const float *x, int64_t m, float *y, void *stream);
 
+/* No counterpart in the reference.  moe_gemv_device without any device
+ * allocation, for callers that cannot allocate at the point of the call: a
+ * decode loop being recorded into a CUDA graph, a real-time loop that must
+ * not take cudaMalloc's implicit synchronisation, or an engine whose device
+ * memory budget is handed out by someone else.  Inputs and outputs as for
+ * moe_gemv_device (device pointers); the scratch (launch metadata and the
+ * fp16 split of x) lives in one fixed 1 MiB device array inside the
+ * library, so m * cols must not exceed 262080 (MOE_ERR_INVALID otherwise).
+ * The array's device address is looked up on a device's first call: make
+ * that call before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU (other streams or threads) race.  NULL stream =
+ * the library stream. */
+MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t rows, int64_t cols,
+				    const float *x, int64_t m, float *y, void *stream);
+
 /* Synchronise the library stream. */
 MOE_API int moe_sync(void);
 

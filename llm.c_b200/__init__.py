@@ -72,6 +72,7 @@ SIGNATURES = {
     "moe_layer_routing": (_I, [_P, _P, _P, _P, _P, _P]),
     "moe_layer_stage_ms": (_I, [_P, C.POINTER(C.c_float), _I]),
     "moe_gemv_device": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
+    "moe_gemv_device_noalloc": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_sync": (_I, []),
     "moe_device_alloc": (_P, [_SZ]),
     "moe_device_free": (_I, [_P]),

@@ -174,6 +174,12 @@ int ensure_dev_io(size_t bytes)
 
 }  // namespace
 
+namespace moe {
+// used by noalloc.cu
+void set_last_error(const char *msg) { g_err = msg ? msg : ""; }
+cudaStream_t library_stream() { return g.init ? g.stream : nullptr; }
+}  // namespace moe
+
 // -------------------------------------------------------------------------
 // layer object
 // -------------------------------------------------------------------------
