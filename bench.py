@@ -234,7 +234,7 @@ def run_ours(args, rank, world, local_rank):
     gu_ms = stage[2] / max(nprof, 1)
     layer_bytes = float(np.mean(U)) * EXPERT_BYTES_Q8 + NE * d * 4 + 2 * T * d * 4
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None
-    roof = {"bound": "hbm", "kernel": "expert_gemv_kernel<Q8_0,dual> (gate/up + SwiGLU)",
+    roof = {"bound": "hbm", "kernel": "expert_mma_kernel<Q8_0, dual> (gate/up + SwiGLU)",
             "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
             "frac": achieved / hbm_peak if achieved else None, "traffic": None,
             "peak_source": peak_kind,
@@ -247,7 +247,11 @@ def run_ours(args, rank, world, local_rank):
     if os.path.exists(traffic):
         with open(traffic) as f:
             tj = json.load(f)
-        roof["traffic"] = tj.get("gate_up_bytes_per_launch")
+        # DRAM bytes of one captured launch, scaled by the routed experts
+        per_expert = tj.get("gate_up_dram_bytes_per_active_expert")
+        if per_expert and tj.get("kernel") == roof["kernel"]:
+            roof["traffic"] = per_expert * float(np.mean(U))
+            roof["traffic_source"] = "profiles/" + tj.get("source", "traffic.json")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
