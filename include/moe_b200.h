@@ -77,6 +77,8 @@ enum moe_status {
                              /* cross-check path) instead of the MMA ones    */
 #define MOE_PROFILE     0x40 /* record CUDA events between the layer's stages */
                              /* (read back with moe_layer_stage_ms)          */
+#define MOE_NO_FUSE     0x100 /* decode-sized batches: use the five-launch   */
+                             /* path instead of the fused layer kernel       */
 
 /* ------------------------------------------------------------------ */
 /* Library lifetime                                                     */
@@ -195,12 +197,23 @@ MOE_API int moe_layer_routing(moe_layer *layer, int32_t *ids, float *weights, in
 		      int32_t *offsets, int32_t *perm);
 
 /* Device time of each stage, summed over the MOE_PROFILE forwards since
- * the last call, in ms, from CUDA events recorded on the launching stream:
- * [0] router logits (and the fp16 split of the tokens), [1] softmax +
- * top-k + dispatch, [2] gate/up + SwiGLU, [3] down, [4] combine; [5] (if
- * n >= 6) the number of forwards summed.
- * Synchronises on the last event and resets the sums. */
+ * the last call, in ms: [0] router logits (and the fp16 split of the
+ * tokens), [1] softmax + top-k + dispatch, [2] gate/up + SwiGLU, [3] down,
+ * [4] combine; [5] (if n >= 6) the number of forwards summed.  Five-launch
+ * forwards are timed by CUDA events on the launching stream; the fused
+ * decode kernel records %globaltimer at its phase boundaries (latest CTA
+ * per boundary, grid barriers counted in the phase before them).
+ * Synchronises the device and resets the sums. */
 MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
+
+/* Diagnostics of the fused decode kernel: the raw %globaltimer stamps (ns)
+ * of the latest MOE_PROFILE fused forward not yet consumed by
+ * moe_layer_stage_ms, as [CTA][stamp] with 12 stamps per CTA: start, router
+ * end, barrier 1 exit, top-k done, barrier 1b exit, dispatch done, routing
+ * end, gate/up end, barrier 2 exit, down end, barrier 3 exit, end.  Returns the
+ * number of values written (CTAs x 12) or a negative moe_status.  Has no
+ * counterpart in the reference. */
+MOE_API int moe_layer_phase_stamps(moe_layer *layer, uint64_t *out, int n);
 
 /* y[m, rows] = x[m, cols] . W[rows, cols]^T with W in Q8_0/Q4_0 blocks on
  * the device (config-1 dense decode GEMV when m == 1).  Asynchronous. */

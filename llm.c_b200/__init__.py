@@ -20,6 +20,7 @@ LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
 F32, Q8_0, Q4_0 = 0, 1, 2
 TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE, SIMPLE = (
     0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40, 0x80)
+NO_FUSE = 0x100
 
 ERRORS = {0: "MOE_OK", -1: "MOE_ERR_INVALID", -2: "MOE_ERR_UNSUPPORTED", -3: "MOE_ERR_CUDA",
           -4: "MOE_ERR_NOMEM", -5: "MOE_ERR_NOT_INIT", -6: "MOE_ERR_COMM", -7: "MOE_ERR_TIMEOUT"}
@@ -71,6 +72,7 @@ SIGNATURES = {
     "moe_layer_forward": (_I, [_P, _P, _P, _I64, _I, _P]),
     "moe_layer_routing": (_I, [_P, _P, _P, _P, _P, _P]),
     "moe_layer_stage_ms": (_I, [_P, C.POINTER(C.c_float), _I]),
+    "moe_layer_phase_stamps": (_I, [_P, C.POINTER(C.c_uint64), _I]),
     "moe_gemv_device": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_gemv_device_noalloc": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_sync": (_I, []),
@@ -242,6 +244,16 @@ class Layer:
         ms = (C.c_float * 6)()
         check(lib().moe_layer_stage_ms(self.handle, ms, 6))
         return list(ms)[:5], int(ms[5])
+
+    PHASE_STAMPS = ("start", "router", "barrier1", "topk", "barrier1b", "dispatch", "routing",
+                    "gate_up", "barrier2", "down", "barrier3", "end")
+
+    def phase_stamps(self, n_ctas: int = 1024) -> np.ndarray:
+        """raw %globaltimer stamps [CTA, 12] (ns) of the latest profiled fused forward"""
+        buf = (C.c_uint64 * (n_ctas * len(self.PHASE_STAMPS)))()
+        n = lib().moe_layer_phase_stamps(self.handle, buf, len(buf))
+        check(n if n < 0 else 0)
+        return np.ctypeslib.as_array(buf)[:n].reshape(-1, len(self.PHASE_STAMPS)).copy()
 
     def routing(self, T: int):
         K, NE = self.top_k, self.n_experts

@@ -193,6 +193,7 @@ struct moe_layer {
 	// MOE_PROFILE: one set of 6 events per profiled forward since the last
 	// moe_layer_stage_ms (stage boundaries on the launching stream)
 	std::vector<std::array<cudaEvent_t, 6>> prof;
+	std::vector<int> prof_fused;  // per record: 1 = fused kernel (phase stamps)
 	size_t prof_used = 0;
 	bool mma_ok = false;  // tensor-core kernels usable (cols % 256, 16 B aligned)
 	// slices of scratch
@@ -200,9 +201,13 @@ struct moe_layer {
 	__half *x16, *h16;
 	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
 	int32_t *active, *n_active, *work;  // [NE], [1], [2]
+	unsigned long long *gbar;           // grid barrier arrivals of the fused kernel
+	uint64_t *stamps;                   // [kStampRecords][grid][stamps]
 };
 
 namespace {
+
+constexpr size_t kStampRecords = 64;  // profiled fused forwards kept per layer
 
 int layer_scratch(moe_layer *L, int64_t T)
 {
@@ -222,6 +227,8 @@ int layer_scratch(moe_layer *L, int64_t T)
 	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8);
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
 	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)cap * K * 2 * F * 2);
+	size_t o_gbar = take(8);
+	size_t o_stamps = take((size_t)kStampRecords * moe::sm_count() * moe::decode_stamps() * 8);
 	if (L->scratch) {
 		CK(cudaStreamSynchronize(g.stream));
 		cudaFree(L->scratch);
@@ -246,6 +253,10 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->Y = (float *)(b + o_Y);
 	L->x16 = (__half *)(b + o_x16);
 	L->h16 = (__half *)(b + o_h16);
+	L->gbar = (unsigned long long *)(b + o_gbar);
+	L->stamps = (uint64_t *)(b + o_stamps);
+	CK(cudaMemset(L->gbar, 0, 8));
+	CK(cudaDeviceSynchronize());  // ordered before launches on any stream
 	L->capT = cap;
 	return MOE_OK;
 }
@@ -539,19 +550,65 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 			       ? cudaEventRecordWithFlags(e, st, cudaEventRecordExternal)
 			       : cudaEventRecord(e, st);
 	};
+	const bool simple = (flags & MOE_SIMPLE) || !L->mma_ok;
+	const int q4 = d.qtype == MOE_Q4_0;
+	const int mode_exact = (flags & MOE_TOPK_EXACT) ? 1 : 0, renorm = (flags & MOE_RENORM) ? 1 : 0;
+
+	// decode-sized batch on one GPU: the whole layer in one fused kernel
+	if (!simple && !(flags & MOE_NO_FUSE) && d.n_local == d.n_experts &&
+	    moe::decode_supported(d.qtype, T, D, F, NE, K, (uintptr_t)x, (uintptr_t)d.router_w,
+				  (uintptr_t)out)) {
+		uint64_t *stamps = nullptr;
+		if (prof && L->prof_used < kStampRecords) {
+			stamps = L->stamps + L->prof_used * moe::sm_count() * moe::decode_stamps();
+			if (L->prof_fused.size() <= L->prof_used)
+				L->prof_fused.resize(L->prof_used + 1);
+			L->prof_fused[L->prof_used++] = 1;
+		}
+		moe::DecodeArgs a{};
+		a.x = x;
+		a.router_w = d.router_w;
+		a.router_bias = d.router_bias;
+		a.dptrs = L->dptrs;
+		a.T = (int)T;
+		a.D = D;
+		a.F = F;
+		a.NE = NE;
+		a.K = K;
+		a.mode_exact = mode_exact;
+		a.renorm = renorm;
+		a.logits = L->logits;
+		a.x16 = L->x16;
+		a.h16 = L->h16;
+		a.Y = L->Y;
+		a.out = out;
+		a.ids = L->ids;
+		a.wts = L->wts;
+		a.counts = L->counts;
+		a.offsets = L->offsets;
+		a.perm = L->perm;
+		a.active = L->active;
+		a.n_active = L->n_active;
+		a.err = L->err;
+		a.gbar = L->gbar;
+		a.stamps = stamps;
+		CK(moe::launch_decode_layer(a, d.qtype, lanes, st));
+		return MOE_OK;
+	}
+
 	if (prof) {
-		if (L->prof_used == L->prof.size()) {
+		while (L->prof.size() <= L->prof_used) {
 			std::array<cudaEvent_t, 6> set{};
 			for (auto &e : set)
 				CK(cudaEventCreate(&e));
 			L->prof.push_back(set);
 		}
+		if (L->prof_fused.size() <= L->prof_used)
+			L->prof_fused.resize(L->prof_used + 1);
+		L->prof_fused[L->prof_used] = 0;
 		ev = L->prof[L->prof_used++].data();
 		CK(record(ev[0]));
 	}
-
-	const bool simple = (flags & MOE_SIMPLE) || !L->mma_ok;
-	const int q4 = d.qtype == MOE_Q4_0;
 	// [0] router logits (+ the fp16 split of x the MMA kernels read)
 	if (moe::router_tiled_ok(D, NE)) {
 		CK(moe::launch_router_tiled(x, d.router_w, (int)T, D, NE, lanes, L->logits,
@@ -564,7 +621,6 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 	if (prof)
 		CK(record(ev[1]));
 	// [1] softmax + top-k + dispatch
-	const int mode_exact = (flags & MOE_TOPK_EXACT) ? 1 : 0, renorm = (flags & MOE_RENORM) ? 1 : 0;
 	if (T <= 256 && moe::route_small_smem((int)T, NE, K) <= 160 * 1024) {
 		CK(moe::launch_route_small(L->logits, d.router_bias, (int)T, NE, K, lanes, mode_exact,
 					   renorm, (int)d.first_expert, (int)d.n_local, L->ids, L->wts,
@@ -673,17 +729,55 @@ int moe_layer_stage_ms(moe_layer *L, float *ms, int n)
 		return fail(MOE_ERR_INVALID, "moe_layer_stage_ms: no MOE_PROFILE forward to report");
 	for (int i = 0; i < 5; i++)
 		ms[i] = 0.0f;
-	CK(cudaEventSynchronize(L->prof[L->prof_used - 1][5]));
-	for (size_t c = 0; c < L->prof_used; c++)
+	CK(cudaDeviceSynchronize());  // the forwards may have run on a caller stream
+	const int grid = moe::sm_count(), ns = moe::decode_stamps();
+	std::vector<uint64_t> st((size_t)grid * ns);
+	for (size_t c = 0; c < L->prof_used; c++) {
+		if (c < L->prof_fused.size() && L->prof_fused[c]) {
+			// phase boundaries: latest CTA per boundary, from the earliest start
+			CK(cudaMemcpy(st.data(), L->stamps + c * grid * ns, st.size() * 8,
+				      cudaMemcpyDeviceToHost));
+			int ends[5];
+			moe::decode_stage_ends(ends);
+			uint64_t bnd[6] = {UINT64_MAX, 0, 0, 0, 0, 0};
+			for (int b = 0; b < grid; b++) {
+				bnd[0] = std::min(bnd[0], st[(size_t)b * ns]);
+				for (int i = 0; i < 5; i++)
+					bnd[i + 1] = std::max(bnd[i + 1], st[(size_t)b * ns + ends[i]]);
+			}
+			for (int i = 0; i < 5; i++)
+				ms[i] += (float)((double)(bnd[i + 1] - bnd[i]) * 1e-6);
+			continue;
+		}
 		for (int i = 0; i < 5; i++) {
 			float t = 0.0f;
 			CK(cudaEventElapsedTime(&t, L->prof[c][i], L->prof[c][i + 1]));
 			ms[i] += t;
 		}
+	}
 	if (n >= 6)
 		ms[5] = (float)L->prof_used;
 	L->prof_used = 0;
 	return MOE_OK;
+}
+
+int moe_layer_phase_stamps(moe_layer *L, uint64_t *out, int n)
+{
+	if (!L || !out)
+		return fail(MOE_ERR_INVALID, "moe_layer_phase_stamps: null argument");
+	const int grid = moe::sm_count(), ns = moe::decode_stamps();
+	size_t rec = SIZE_MAX;
+	for (size_t c = 0; c < L->prof_used && c < L->prof_fused.size(); c++)
+		if (L->prof_fused[c])
+			rec = c;
+	if (rec == SIZE_MAX)
+		return fail(MOE_ERR_INVALID, "moe_layer_phase_stamps: no profiled fused forward");
+	if (n < grid * ns)
+		return fail(MOE_ERR_INVALID, "moe_layer_phase_stamps: need %d values", grid * ns);
+	CK(cudaDeviceSynchronize());
+	CK(cudaMemcpy(out, L->stamps + rec * grid * ns, (size_t)grid * ns * 8,
+		      cudaMemcpyDeviceToHost));
+	return grid * ns;
 }
 
 int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *counts,
@@ -697,10 +791,17 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 		return MOE_OK;
 	int32_t err = 0;
 	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
+	if (err == 2 || err == 3) {
+		// a barrier left half-passed must not poison the next forward
+		CK(cudaMemset(L->gbar, 0, 8));
+		CK(cudaDeviceSynchronize());
+	}
 	if (err == 1)
 		return fail(MOE_ERR_INVALID, "dispatch saw an expert id out of range");
 	if (err == 2)
 		return fail(MOE_ERR_TIMEOUT, "an expert kernel's bounded wait expired");
+	if (err == 3)
+		return fail(MOE_ERR_TIMEOUT, "the fused layer kernel's grid barrier expired");
 	if (ids)
 		CK(cudaMemcpy(ids, L->ids, T * K * 4, cudaMemcpyDeviceToHost));
 	if (weights)

@@ -1,0 +1,741 @@
+// expert_core.cuh — the warp-specialised grouped expert pipeline (decode),
+// shared by the stand-alone expert kernel (expert_mma.cu) and the fused
+// decode-layer kernel (decode.cu).
+//
+// Work: for every expert e with n_e routed (token, slot) pairs, stream the
+// expert's Q8_0/Q4_0 weight rows from HBM once and multiply them with the
+// n_e activation rows (fused SwiGLU for gate/up, plain for down).  This is
+// the memory-bound regime (n_e is ~1-32 at decode), so the pipeline is built
+// around moving bytes:
+//
+//  * One producer warp copies whole tile rows (16 rows x up to 2048 columns,
+//    2176 contiguous bytes per Q8_0 row) into a ring of shared-memory stages
+//    with cp.async.bulk, completing on per-stage mbarriers.  Long runs of
+//    consecutive bytes keep HBM at its copy bandwidth.
+//  * The int8 (or 4-bit) codes are turned into exact fp16 integers with a
+//    byte permute (q ^ 0x80 placed under the fp16 exponent of 1024, minus
+//    1152), so a weight byte costs about two instructions.
+//  * mma.sync m16n8k16 multiplies them with the activations split into two
+//    fp16 parts (x = hi + lo, both exact to ~2^-22 relative), accumulating
+//    one 32-element block in fp32; the block's fp16 scale d is applied to
+//    that partial sum in fp32.  The result is accurate to fp32 level, like
+//    the reference's dot_f32_quant (quant.c:103-155), which multiplies fp32
+//    activations by d*q.
+//  * K order inside a block is permuted (lane quad c owns bytes 8c..8c+7 of
+//    each Q8_0 block), identically for weights and activations, so every
+//    activation fragment is one 16-byte load.
+//  * Eight math warps split each stage's K range and hand fp32 partial sums
+//    to two epilogue warps through a 4-deep ring of exchange buffers; the
+//    epilogue adds them in warp order (deterministic), applies SwiGLU or the
+//    output permutation and stores.
+//
+// Every mbarrier wait is bounded: on expiry the waiting warp records an
+// error in a device flag (read by the host) and keeps walking its loops
+// without waiting, so no warp is left blocked and the kernel ends.
+#pragma once
+
+#include "common.cuh"
+
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+namespace moe {
+
+constexpr int kMmaWarps = 8;                 // math warps per CTA
+constexpr int kTokTile = 8;                  // tokens per pass (one MMA n-tile)
+constexpr int kMaxKC = 2048;                 // columns per stage
+constexpr int kRedBufs = 4;                  // partial-sum exchange buffers
+constexpr int kEpiWarps = 2;
+constexpr int kProducerWarp = kMmaWarps;
+constexpr int kEpiWarp0 = kMmaWarps + 1;
+constexpr int kCoreThreads = (kMmaWarps + 1 + kEpiWarps) * 32;
+constexpr int kMaxActive = 256;              // experts per layer (routing tables)
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bounded waits: 2 s
+
+// f(std::integral_constant<int, i>) for i = 0 .. N-1, unrolled at compile time
+template <int I, int N, typename F>
+__device__ __forceinline__ void static_for_impl(F &&f)
+{
+	if constexpr (I < N) {
+		f(std::integral_constant<int, I>{});
+		static_for_impl<I + 1, N>(f);
+	}
+}
+
+template <int N, typename F>
+__device__ __forceinline__ void static_for(F &&f)
+{
+	static_for_impl<0, N>(f);
+}
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_addr(const void *p)
+{
+	return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+	asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+		     : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init()
+{
+	asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async()
+{
+	asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+	asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+		     "r"(bytes)
+		     : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+	asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or ~100 us pass, so waiting warps do not steal issue slots
+// from the warps that are computing
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+	uint32_t ok;
+	asm volatile(
+		"{\n\t.reg .pred p;\n\t"
+		"mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n\t"
+		"selp.u32 %0, 1, 0, p;\n\t}"
+		: "=r"(ok)
+		: "r"(smem_addr(bar)), "r"(parity)
+		: "memory");
+	return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns()
+{
+	uint64_t t;
+	asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+	return t;
+}
+
+// bounded wait; false when kWaitLimitNs of wall time passed
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
+{
+	if (mbar_try_wait(bar, parity))
+		return true;
+	const uint64_t t0 = global_ns();
+	for (;;) {
+		if (mbar_try_wait(bar, parity))
+			return true;
+		if (global_ns() - t0 > kWaitLimitNs)
+			return false;
+	}
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+	asm volatile(
+		"cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+		::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+		: "memory");
+}
+
+// hint: bring [src, src + bytes) into L2 (no completion to wait for)
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes)
+{
+	asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+					  uint32_t b1)
+{
+	asm volatile(
+		"mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+		"{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+		: "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+		: "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// two int8 codes (low byte first) -> half2 of the exact integers
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w)
+{
+	const uint32_t biased = __byte_perm(w ^ 0x8080u, 0x64646464u, 0x4140);  // 1024 + q + 128
+	const __half2 h = __hsub2(*reinterpret_cast<const __half2 *>(&biased),
+				  __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
+	return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// nibbles (bits 0-3 and 16-19 of w) -> half2 of (nib - 8)
+__device__ __forceinline__ uint32_t u4x2_to_h2(uint32_t w)
+{
+	const uint32_t biased = (w & 0x000F000Fu) | 0x64006400u;  // 1024 + nib
+	const __half2 h = __hsub2(*reinterpret_cast<const __half2 *>(&biased),
+				  __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));
+	return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__device__ __forceinline__ uint16_t lds_u16(const uint8_t *p)
+{
+	return *reinterpret_cast<const uint16_t *>(p);
+}
+
+// A fragments (two k16 steps) of one 32-element block for rows g and g+8.
+// Q8_0 (34-byte block, codes at +2): lane quad c owns codes 8c..8c+7:
+//   step 0 = codes (8c,8c+1) | (8c+2,8c+3), step 1 = (8c+4,8c+5) | (8c+6,8c+7).
+// Q4_0 (18-byte block, byte j = code j low nibble, code j+16 high nibble):
+//   lane quad c owns bytes 4c..4c+3 and takes, per u32 of those bytes,
+//   pairs (b0,b2) low, (b0,b2) high, (b1,b3) low, (b1,b3) high nibbles.
+template <int QT>
+__device__ __forceinline__ void load_a(const uint8_t *rg, const uint8_t *rg8, int c,
+				       uint32_t (&a0)[4], uint32_t (&a1)[4], float &dg, float &dg8)
+{
+	dg = half_bits_to_float(lds_u16(rg));
+	dg8 = half_bits_to_float(lds_u16(rg8));
+	if (QT == kQ8_0) {
+		const uint8_t *pg = rg + 2 + 8 * c, *p8 = rg8 + 2 + 8 * c;
+		a0[0] = i8x2_to_h2(lds_u16(pg + 0));
+		a0[1] = i8x2_to_h2(lds_u16(p8 + 0));
+		a0[2] = i8x2_to_h2(lds_u16(pg + 2));
+		a0[3] = i8x2_to_h2(lds_u16(p8 + 2));
+		a1[0] = i8x2_to_h2(lds_u16(pg + 4));
+		a1[1] = i8x2_to_h2(lds_u16(p8 + 4));
+		a1[2] = i8x2_to_h2(lds_u16(pg + 6));
+		a1[3] = i8x2_to_h2(lds_u16(p8 + 6));
+	} else {
+		const uint8_t *pg = rg + 2 + 4 * c, *p8 = rg8 + 2 + 4 * c;
+		const uint32_t wg = (uint32_t)lds_u16(pg) | ((uint32_t)lds_u16(pg + 2) << 16);
+		const uint32_t w8 = (uint32_t)lds_u16(p8) | ((uint32_t)lds_u16(p8 + 2) << 16);
+		// wg bytes: b0 b1 b2 b3 -> (b0,b2) = bits 0-7 / 16-23, (b1,b3) = bits 8-15 / 24-31
+		a0[0] = u4x2_to_h2(wg);          // low nibbles of b0, b2
+		a0[1] = u4x2_to_h2(w8);
+		a0[2] = u4x2_to_h2(wg >> 4);     // high nibbles of b0, b2
+		a0[3] = u4x2_to_h2(w8 >> 4);
+		a1[0] = u4x2_to_h2(wg >> 8);     // low nibbles of b1, b3
+		a1[1] = u4x2_to_h2(w8 >> 8);
+		a1[2] = u4x2_to_h2(wg >> 12);    // high nibbles of b1, b3
+		a1[3] = u4x2_to_h2(w8 >> 12);
+	}
+}
+
+// Q4_0 activation order: slot k = 8c + j of a 32-element block holds element
+// [4c, 4c+2, 16+4c, 16+4c+2, 4c+1, 4c+3, 16+4c+1, 16+4c+3][j], matching the
+// nibble pairs load_a<Q4_0> builds.  q4_slot maps an element to its slot,
+// q4_src a slot to its element.
+__host__ __device__ __forceinline__ int q4_slot(int r)
+{
+	const int m = r & 31, h16 = m >> 4, mm = m & 15;
+	const int c = mm >> 2, odd = mm & 1, two = (mm >> 1) & 1;
+	return (r & ~31) | (8 * c + (two | (h16 << 1) | (odd << 2)));
+}
+
+__host__ __device__ __forceinline__ int q4_src(int k)
+{
+	const int base = k & ~31, c = (k & 31) >> 3, j = k & 7;
+	return base + 4 * c + 16 * ((j >> 1) & 1) + ((j >> 2) & 1) + 2 * (j & 1);
+}
+
+// ---------------------------------------------------------------- biased fragments
+// Used when a warp's blocks sit at known positions mod 4 in the stage row
+// (WB % 4 == 0), so every code byte is read with aligned 32/64-bit loads.
+// A code's fp16 value is code + BIAS (exact: 1152 + q for Q8_0 from
+// 0x6400 | (q ^ 0x80), 1024 + nib = (nib - 8) + 1032 for Q4_0), which saves
+// the per-pair subtraction; the MMA sum then carries BIAS * (sum of the
+// block's activations), which is removed in fp32 with that sum S.
+template <int QT>
+struct Bias {
+	static constexpr float value = QT == kQ8_0 ? 1152.0f : 1032.0f;
+};
+
+// the 8 code bytes of a Q8_0 block at position JM (mod 4) of its row,
+// p = block + 2 + 8c: rows are 8-byte aligned and blocks 34 bytes long, so
+// p is 2, 4, 6 or 0 (mod 8) for JM = 0, 1, 2, 3
+template <int JM>
+__device__ __forceinline__ void lds_q8_codes(const uint8_t *p, uint32_t &w0, uint32_t &w1)
+{
+	if (JM == 3) {
+		const uint2 v = *reinterpret_cast<const uint2 *>(p);
+		w0 = v.x;
+		w1 = v.y;
+	} else if (JM == 1) {
+		w0 = *reinterpret_cast<const uint32_t *>(p);
+		w1 = *reinterpret_cast<const uint32_t *>(p + 4);
+	} else if (JM == 0) {
+		const uint2 v = *reinterpret_cast<const uint2 *>(p - 2);
+		const uint32_t w2 = *reinterpret_cast<const uint32_t *>(p + 6);
+		w0 = __byte_perm(v.x, v.y, 0x5432);
+		w1 = __byte_perm(v.y, w2, 0x5432);
+	} else {
+		const uint32_t v0 = *reinterpret_cast<const uint32_t *>(p - 2);
+		const uint2 v = *reinterpret_cast<const uint2 *>(p + 2);
+		w0 = __byte_perm(v0, v.x, 0x5432);
+		w1 = __byte_perm(v.x, v.y, 0x5432);
+	}
+}
+
+// the 4 code bytes of a Q4_0 block at position JM (mod 2), p = block + 2 + 4c
+template <int JM>
+__device__ __forceinline__ uint32_t lds_q4_codes(const uint8_t *p)
+{
+	if (JM == 1)
+		return *reinterpret_cast<const uint32_t *>(p);
+	return __byte_perm(*reinterpret_cast<const uint32_t *>(p - 2),
+			   *reinterpret_cast<const uint32_t *>(p + 2), 0x5432);
+}
+
+// biased A fragments (same k slots as load_a) of block J for rows g, g+8
+template <int QT, int J>
+__device__ __forceinline__ void load_a_biased(const uint8_t *rg, const uint8_t *rg8, int c,
+					      uint32_t (&a0)[4], uint32_t (&a1)[4], float &dg,
+					      float &dg8)
+{
+	dg = half_bits_to_float(lds_u16(rg));
+	dg8 = half_bits_to_float(lds_u16(rg8));
+	if (QT == kQ8_0) {
+		constexpr uint32_t E = 0x64646464u;
+		uint32_t g0, g1, h0, h1;
+		lds_q8_codes<J % 4>(rg + 2 + 8 * c, g0, g1);
+		lds_q8_codes<J % 4>(rg8 + 2 + 8 * c, h0, h1);
+		g0 ^= 0x80808080u;
+		g1 ^= 0x80808080u;
+		h0 ^= 0x80808080u;
+		h1 ^= 0x80808080u;
+		a0[0] = __byte_perm(g0, E, 0x4140);  // codes 8c, 8c+1
+		a0[1] = __byte_perm(h0, E, 0x4140);
+		a0[2] = __byte_perm(g0, E, 0x4342);  // codes 8c+2, 8c+3
+		a0[3] = __byte_perm(h0, E, 0x4342);
+		a1[0] = __byte_perm(g1, E, 0x4140);  // codes 8c+4, 8c+5
+		a1[1] = __byte_perm(h1, E, 0x4140);
+		a1[2] = __byte_perm(g1, E, 0x4342);  // codes 8c+6, 8c+7
+		a1[3] = __byte_perm(h1, E, 0x4342);
+	} else {
+		const uint32_t wg = lds_q4_codes<J % 2>(rg + 2 + 4 * c);
+		const uint32_t w8 = lds_q4_codes<J % 2>(rg8 + 2 + 4 * c);
+		constexpr uint32_t M = 0x000F000Fu, E = 0x64006400u;
+		a0[0] = (wg & M) | E;          // low nibbles of b0, b2
+		a0[1] = (w8 & M) | E;
+		a0[2] = ((wg >> 4) & M) | E;   // high nibbles of b0, b2
+		a0[3] = ((w8 >> 4) & M) | E;
+		a1[0] = ((wg >> 8) & M) | E;   // low nibbles of b1, b3
+		a1[1] = ((w8 >> 8) & M) | E;
+		a1[2] = ((wg >> 12) & M) | E;  // high nibbles of b1, b3
+		a1[3] = ((w8 >> 12) & M) | E;
+	}
+}
+
+// ---------------------------------------------------------------- layout
+template <int QT>
+struct StageLayout {
+	static constexpr int BB = QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES;
+	static constexpr int RS = kMaxKC / QK * BB + 16;          // smem row stride (padded)
+	static constexpr int BYTES = 16 * RS;                    // one stage
+	static constexpr int RED = kRedBufs * kMmaWarps * 32 * 16;
+	static constexpr int SSUM = kMmaWarps * 8 * 8 * 4;  // per warp [8 blocks][8 tokens] f32
+};
+
+// One grouped matrix pass (gate/up with SwiGLU, or down).
+//
+// Work item = (active expert, 16-row tile): for DUAL, gate rows r0..r0+7
+// and the same up rows (MMA rows 0-7 and 8-15, so gate and up of a (row,
+// token) meet in one accumulator set for SwiGLU); for the single matrix,
+// rows r0..r0+15.  An item is processed in passes of 8 tokens.  Each CTA
+// takes a contiguous range of items balanced by cost (passes), which every
+// warp derives identically from the routing table.  Within the range, the
+// items of one expert (a segment) are walked token tile by token tile, so
+// the math warps load each tile's activations once per segment; the weights
+// of a second token tile come back from L2.
+//   in  row of position pos: in_perm  ? in16[perm[pos] / K] : in16[pos]
+//   out row of position pos: out_perm ? out[perm[pos]]      : out[pos]
+struct Phase {
+	const void *const *w1;   // device table [experts] of weight pointers
+	const void *const *w2;   // DUAL: the up matrices
+	int rows, cols, K;
+	const int32_t *en;       // [n_active] expert | pair count << 8
+	const int32_t *off;      // [n_active] first position of the expert
+	const int32_t *pre;      // [n_active + 1] cost prefix (passes x tiles)
+	int n_active;
+	const int32_t *perm;     // [pairs] pair of each position
+	int in_perm, out_perm;
+	const __half *in16;      // [*, 2, cols] fp16 hi/lo
+	__half *out16;           // DUAL: [*, 2, rows] fp16 hi/lo
+	float *out;              // single: [*, rows] fp32
+	int32_t *err;            // set to 2 when a bounded wait expires
+	const float *wdiv;       // single, optional: store y / (1 / wdiv[out row])
+};
+
+struct Bars {
+	uint64_t *full, *empty;      // [STAGES]
+	uint64_t *rfull, *rempty;    // [kRedBufs]
+};
+
+// per-thread pipeline position, carried across consecutive phases
+struct Pipe {
+	uint32_t it = 0;    // stage sequence number
+	uint32_t pass = 0;  // partial-sum exchange sequence number
+	bool failed = false;
+};
+
+__device__ __forceinline__ int passes_of(int en) { return ((en >> 8) + kTokTile - 1) / kTokTile; }
+
+// cost prefix of the active experts' items: pre[a] = cost of the items of
+// active experts < a, cost(item) = passes of its expert
+__device__ __forceinline__ void build_prefix(const int32_t *en, int n_active, int groups,
+					     int32_t *pre)
+{
+	int c = 0;
+	for (int i = 0; i < n_active; i++) {
+		pre[i] = c;
+		c += groups * passes_of(en[i]);
+	}
+	pre[n_active] = c;
+}
+
+// the same prefix computed by one whole warp (inclusive scan by shuffles)
+__device__ __forceinline__ void build_prefix_warp(const int32_t *en, int n_active, int groups,
+						  int32_t *pre)
+{
+	const int lane = threadIdx.x % 32;
+	int carry = 0;
+	for (int base = 0; base < n_active; base += 32) {
+		const int i = base + lane;
+		const int c = i < n_active ? groups * passes_of(en[i]) : 0;
+		int incl = c;
+#pragma unroll
+		for (int o = 1; o < 32; o <<= 1) {
+			const int u = __shfl_up_sync(0xffffffffu, incl, o);
+			if (lane >= o)
+				incl += u;
+		}
+		if (i < n_active)
+			pre[i] = carry + incl - c;
+		carry += __shfl_sync(0xffffffffu, incl, 31);
+	}
+	if (lane == 0)
+		pre[n_active] = carry;
+	__syncwarp();
+}
+
+// cost-balanced contiguous item range of this CTA
+__device__ __forceinline__ void item_range(const int32_t *en, const int32_t *pre, int n_active,
+					   int groups, int &i0, int &i1)
+{
+	const int total = pre[n_active];
+	const int64_t c0 = (int64_t)total * blockIdx.x / gridDim.x;
+	const int64_t c1 = (int64_t)total * (blockIdx.x + 1) / gridDim.x;
+	// first item whose cumulative cost start is >= c (items of expert a cost p_a each)
+	auto first_item = [&](int64_t c) {
+		int a = 0;
+		while (a < n_active && pre[a + 1] <= c)
+			a++;
+		if (a == n_active)
+			return n_active * groups;
+		const int pa = passes_of(en[a]) > 0 ? passes_of(en[a]) : 1;
+		const int64_t k = (c - pre[a] + pa - 1) / pa;   // items of expert a before c
+		return a * groups + (int)(k < groups ? k : groups);
+	};
+	i0 = first_item(c0);
+	i1 = first_item(c1);
+}
+
+// ---------------------------------------------------------------- producer
+template <int QT, bool DUAL, int STAGES, int WB>
+__device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, Pipe &p, int lane)
+{
+	using SL = StageLayout<QT>;
+	constexpr int BB = SL::BB, RS = SL::RS;
+	constexpr int ROWS = DUAL ? 8 : 16;
+	constexpr int KC = WB * kMmaWarps * QK;
+	constexpr uint32_t cb = (uint32_t)(KC / QK * BB);  // bytes per row and stage
+	const int groups = (ph.rows + ROWS - 1) / ROWS;
+	const int nch = ph.cols / KC;
+	const int64_t rb = (int64_t)(ph.cols / QK) * BB;
+	int i0, i1;
+	item_range(ph.en, ph.pre, ph.n_active, groups, i0, i1);
+	for (int seg = i0; seg < i1;) {
+		const int ai = seg / groups, seg_end = min(i1, (ai + 1) * groups);
+		const int e = ph.en[ai] & 255;
+		const int n = ph.en[ai] >> 8;
+		const uint8_t *base = static_cast<const uint8_t *>(
+			(DUAL && lane >= 8) ? ph.w2[e] : ph.w1[e]);
+		for (int tg = 0; tg < n; tg += kTokTile)
+		for (int item = seg; item < seg_end; item++) {
+			const int r0 = (item - ai * groups) * ROWS;
+			// lane l (< 16) copies tile row l
+			const int r = DUAL ? r0 + (lane & 7) : r0 + lane;
+			const uint8_t *src = base + (int64_t)min(r, ph.rows - 1) * rb;
+			for (int ch = 0; ch < nch; ch++, p.it++) {
+				const int st = p.it % STAGES;
+				if (p.it >= STAGES && !p.failed &&
+				    !__all_sync(0xffffffffu, mbar_wait(&b.empty[st], ((p.it / STAGES) - 1) & 1))) {
+					p.failed = true;
+					if (lane == 0)
+						atomicExch(ph.err, 2);
+				}
+				if (p.failed)
+					continue;
+				if (lane == 0)
+					mbar_arrive_expect_tx(&b.full[st], 16 * cb);
+				__syncwarp();
+				if (lane < 16) {
+					fence_proxy_async();
+					bulk_g2s(stages + st * SL::BYTES + lane * RS,
+						 src + (int64_t)ch * (KC / QK) * BB, cb, &b.full[st]);
+				}
+			}
+		}
+		seg = seg_end;
+	}
+}
+
+// ---------------------------------------------------------------- epilogue
+template <int QT, bool DUAL>
+__device__ void core_epilogue(const Phase &ph, const float4 *red, const Bars &b, Pipe &p, int epi,
+			      int lane)
+{
+	constexpr int ROWS = DUAL ? 8 : 16;
+	const int groups = (ph.rows + ROWS - 1) / ROWS;
+	int i0, i1;
+	item_range(ph.en, ph.pre, ph.n_active, groups, i0, i1);
+	for (int seg = i0; seg < i1;) {
+		const int ai = seg / groups, seg_end = min(i1, (ai + 1) * groups);
+		const int n = ph.en[ai] >> 8, off = ph.off[ai];
+		for (int tg = 0; tg < n; tg += kTokTile)
+		for (int item = seg; item < seg_end; item++, p.pass++) {
+			const int r0 = (item - ai * groups) * ROWS;
+			if ((int)(p.pass % kEpiWarps) != epi)
+				continue;
+			const int buf = p.pass % kRedBufs;
+			if (!p.failed &&
+			    !__all_sync(0xffffffffu, mbar_wait(&b.rfull[buf], (p.pass / kRedBufs) & 1))) {
+				p.failed = true;
+				if (lane == 0)
+					atomicExch(ph.err, 2);
+			}
+			if (!p.failed) {
+				const float *rv = reinterpret_cast<const float *>(red + buf * kMmaWarps * 32);
+				// DUAL: 64 outputs (lane l of the MMA layout, token slot j),
+				// gate = value j and up = value 2+j of that lane; 2 per thread.
+				// Single: 128 outputs (lane l, value i); 4 per thread.
+#pragma unroll
+				for (int q = 0; q < (DUAL ? 2 : 4); q++) {
+					const int o = lane + 32 * q;
+					const int l = DUAL ? o >> 1 : o >> 2;
+					const int i = DUAL ? (o & 1) : (o & 3);
+					float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+					for (int w = 0; w < kMmaWarps; w++) {
+						s0 = __fadd_rn(s0, rv[(w * 32 + l) * 4 + i]);
+						if (DUAL)
+							s1 = __fadd_rn(s1, rv[(w * 32 + l) * 4 + 2 + i]);
+					}
+					const int gg = l >> 2, cc = l & 3;
+					const int t = tg + 2 * cc + (i & 1);
+					if (t >= n)
+						continue;
+					const int pos = off + t;
+					if (DUAL) {
+						const int r = r0 + gg;
+						if (r < ph.rows) {
+							const float h = swiglu(s0, s1);
+							const __half hh = __float2half_rn(h);
+							const __half hl = __float2half_rn(__fsub_rn(h, __half2float(hh)));
+							__half *o16 = ph.out16 + (int64_t)pos * 2 * ph.rows;
+							const int slot_r = QT == kQ4_0 ? q4_slot(r) : r;
+							o16[slot_r] = hh;
+							o16[ph.rows + slot_r] = hl;
+						}
+					} else {
+						const int r = r0 + gg + 8 * (i >> 1);
+						const int orow = ph.out_perm ? ph.perm[pos] : pos;
+						// the combine's division (olmoe.c:397-404:
+						// y / (1 / w)), done here where y is produced
+						const float v = ph.wdiv ? __fdiv_rn(s0, __fdiv_rn(1.0f, ph.wdiv[orow])) : s0;
+						if (r < ph.rows)
+							ph.out[(int64_t)orow * ph.rows + r] = v;
+					}
+				}
+			}
+			__syncwarp();
+			if (lane == 0)
+				mbar_arrive(&b.rempty[buf]);
+		}
+		seg = seg_end;
+	}
+}
+
+// ---------------------------------------------------------------- math warps
+// COHERENT: the activations were written earlier in the same kernel by
+// other CTAs, so they are read through L2 (ld.global.cg), not the
+// read-only path.
+template <int QT, bool DUAL, int STAGES, int WB, bool COHERENT>
+__device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, float *ssum,
+			  const Bars &b, Pipe &p, int warp, int lane)
+{
+	constexpr bool FAST = WB % 4 == 0;  // biased fragments, aligned code loads
+	using SL = StageLayout<QT>;
+	constexpr int BB = SL::BB, RS = SL::RS;
+	constexpr int ROWS = DUAL ? 8 : 16;
+	constexpr int KC = WB * kMmaWarps * QK;
+	const int groups = (ph.rows + ROWS - 1) / ROWS;
+	const int cols = ph.cols;
+	const int nch = cols / KC;
+	const int g = lane >> 2, c = lane & 3;
+	uint4 xh[WB], xl[WB];
+	int x_e = -1, x_tg = -1, x_ch = -1;  // key of the fragments in registers
+	int i0, i1;
+	item_range(ph.en, ph.pre, ph.n_active, groups, i0, i1);
+	for (int seg = i0; seg < i1;) {
+		const int ai = seg / groups, seg_end = min(i1, (ai + 1) * groups);
+		const int e = ph.en[ai] & 255;
+		const int n = ph.en[ai] >> 8, off = ph.off[ai];
+		for (int tg = 0; tg < n; tg += kTokTile)
+		for (int item = seg; item < seg_end; item++, p.pass++) {
+			float acc[4] = {0.f, 0.f, 0.f, 0.f};
+			for (int ch = 0; ch < nch; ch++, p.it++) {
+				const int kb0 = ch * (KC / QK) + warp * WB;  // first block (row-global)
+				if (e != x_e || tg != x_tg || ch != x_ch) {
+					// token tg+g's activations for this warp's blocks; columns of
+					// tokens past n read the segment's first token (never stored)
+					const int t = tg + g < n ? tg + g : 0;
+					const int pos = off + t;
+					const int row = ph.in_perm ? ph.perm[pos] / ph.K : pos;
+					const __half *px = ph.in16 + (int64_t)row * 2 * cols + 8 * c;
+#pragma unroll
+					for (int bq = 0; bq < WB; bq++) {
+						const uint4 *ph_ = reinterpret_cast<const uint4 *>(px + (kb0 + bq) * QK);
+						const uint4 *pl_ =
+							reinterpret_cast<const uint4 *>(px + cols + (kb0 + bq) * QK);
+						xh[bq] = COHERENT ? __ldcg(ph_) : __ldg(ph_);
+						xl[bq] = COHERENT ? __ldcg(pl_) : __ldg(pl_);
+					}
+					x_e = e;
+					x_tg = tg;
+					x_ch = ch;
+					if (FAST) {
+						// S of each block for token g: this quad's 8 slots (hi + lo),
+						// then the 4 quads of the token (fixed order)
+						float *sw = ssum + warp * WB * 8;
+#pragma unroll
+						for (int bq = 0; bq < WB; bq++) {
+							const __half2 *hh = reinterpret_cast<const __half2 *>(&xh[bq]);
+							const __half2 *hl = reinterpret_cast<const __half2 *>(&xl[bq]);
+							float s = 0.0f;
+#pragma unroll
+							for (int i = 0; i < 4; i++) {
+								const float2 fh = __half22float2(hh[i]);
+								const float2 fl = __half22float2(hl[i]);
+								s = __fadd_rn(s, __fadd_rn(fh.x, fl.x));
+								s = __fadd_rn(s, __fadd_rn(fh.y, fl.y));
+							}
+							s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+							s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+							if (c == 0)
+								sw[bq * 8 + g] = s;
+						}
+						__syncwarp();
+					}
+				}
+				const int st = p.it % STAGES;
+				if (!p.failed &&
+				    !__all_sync(0xffffffffu, mbar_wait(&b.full[st], (p.it / STAGES) & 1))) {
+					p.failed = true;
+					if (lane == 0)
+						atomicExch(ph.err, 2);
+				}
+				if (!p.failed) {
+					const uint8_t *wt = stages + st * SL::BYTES + (warp * WB) * BB;
+					if constexpr (FAST) {
+						constexpr float BIAS = Bias<QT>::value;
+						const float *sw = ssum + warp * WB * 8 + 2 * c;
+						static_for<WB>([&](auto J) {
+							constexpr int bq = decltype(J)::value;
+							uint32_t A0[4], A1[4];
+							float d0, d1;
+							load_a_biased<QT, bq>(wt + g * RS + bq * BB, wt + (g + 8) * RS + bq * BB,
+									      c, A0, A1, d0, d1);
+							float t[4] = {0.f, 0.f, 0.f, 0.f};
+							mma_16816(t, A0, xh[bq].x, xh[bq].y);
+							mma_16816(t, A1, xh[bq].z, xh[bq].w);
+							mma_16816(t, A0, xl[bq].x, xl[bq].y);
+							mma_16816(t, A1, xl[bq].z, xl[bq].w);
+							const float2 S = *reinterpret_cast<const float2 *>(sw + bq * 8);
+							acc[0] = __fmaf_rn(d0, __fmaf_rn(-BIAS, S.x, t[0]), acc[0]);
+							acc[1] = __fmaf_rn(d0, __fmaf_rn(-BIAS, S.y, t[1]), acc[1]);
+							acc[2] = __fmaf_rn(d1, __fmaf_rn(-BIAS, S.x, t[2]), acc[2]);
+							acc[3] = __fmaf_rn(d1, __fmaf_rn(-BIAS, S.y, t[3]), acc[3]);
+						});
+					} else
+#pragma unroll
+					for (int bq = 0; bq < WB; bq++) {
+						uint32_t A0[4], A1[4];
+						float d0, d1;
+						load_a<QT>(wt + g * RS + bq * BB, wt + (g + 8) * RS + bq * BB, c, A0,
+							   A1, d0, d1);
+						float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+						mma_16816(t0, A0, xh[bq].x, xh[bq].y);
+						mma_16816(t1, A1, xh[bq].z, xh[bq].w);
+						mma_16816(t0, A0, xl[bq].x, xl[bq].y);
+						mma_16816(t1, A1, xl[bq].z, xl[bq].w);
+						acc[0] = __fmaf_rn(d0, __fadd_rn(t0[0], t1[0]), acc[0]);
+						acc[1] = __fmaf_rn(d0, __fadd_rn(t0[1], t1[1]), acc[1]);
+						acc[2] = __fmaf_rn(d1, __fadd_rn(t0[2], t1[2]), acc[2]);
+						acc[3] = __fmaf_rn(d1, __fadd_rn(t0[3], t1[3]), acc[3]);
+					}
+				}
+				__syncwarp();
+				if (lane == 0)
+					mbar_arrive(&b.empty[st]);
+			}
+			// hand the partial sums to the epilogue warps
+			const int buf = p.pass % kRedBufs;
+			if (p.pass >= kRedBufs && !p.failed &&
+			    !__all_sync(0xffffffffu, mbar_wait(&b.rempty[buf], ((p.pass / kRedBufs) - 1) & 1))) {
+				p.failed = true;
+				if (lane == 0)
+					atomicExch(ph.err, 2);
+			}
+			red[(buf * kMmaWarps + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+			__syncwarp();
+			if (lane == 0)
+				mbar_arrive(&b.rfull[buf]);
+		}
+		seg = seg_end;
+	}
+}
+
+// the mbarriers of one CTA: STAGES stage pairs and kRedBufs exchange pairs
+template <int STAGES>
+__device__ __forceinline__ Bars init_bars(uint64_t *base)
+{
+	Bars b{base, base + STAGES, base + 2 * STAGES, base + 2 * STAGES + kRedBufs};
+	if (threadIdx.x < STAGES) {
+		mbar_init(&b.full[threadIdx.x], 1);
+		mbar_init(&b.empty[threadIdx.x], kMmaWarps);
+	}
+	if (threadIdx.x < kRedBufs) {
+		mbar_init(&b.rfull[threadIdx.x], kMmaWarps);
+		mbar_init(&b.rempty[threadIdx.x], 1);
+	}
+	return b;
+}
+
+// blocks per math warp per stage: 8 (2048-column stages) when cols is a
+// multiple of 2048, else cols/256 if that is 1, 2 or 4 (one stage per row)
+__host__ __device__ inline int pick_wb(int cols)
+{
+	if (cols % 2048 == 0)
+		return 8;
+	if (cols == 1024 || cols == 512 || cols == 256)
+		return cols / 256;
+	return 0;
+}
+
+}  // namespace moe

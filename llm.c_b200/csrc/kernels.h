@@ -83,6 +83,33 @@ cudaError_t launch_expert_mma(const MmaArgs &a, cudaStream_t st);
 cudaError_t launch_split_f16(const float *x, int64_t rows, int cols, int qtype, __half *out,
 			     cudaStream_t st);
 
+// decode.cu: the whole layer of a decode-sized batch in one cooperative
+// kernel (router, routing, gate/up, down, combine).
+struct DecodeArgs {
+	const float *x;            // [T, D]
+	const float *router_w;     // [NE, D]
+	const float *router_bias;  // [NE] or NULL
+	const void *const *dptrs;  // device [3][NE]: gate, up, down weight pointers
+	int T, D, F, NE, K;
+	int mode_exact, renorm;
+	float *logits;             // [T, NE]
+	__half *x16;               // [T, 2, D]
+	__half *h16;               // [T*K, 2, F]
+	float *Y;                  // [T*K, D]
+	float *out;                // [T, D]
+	int32_t *ids;              // [T*K]
+	float *wts;                // [T*K]
+	int32_t *counts, *offsets, *perm, *active, *n_active;
+	int32_t *err;              // 0 ok, 2 bounded mbarrier wait expired, 3 grid barrier expired
+	unsigned long long *gbar;  // grid barrier arrivals, zero when allocated
+	uint64_t *stamps;          // NULL or [grid][decode_stamps()] phase times (ns)
+};
+bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr_t x,
+		      uintptr_t router_w, uintptr_t out);
+int decode_stamps();
+void decode_stage_ends(int *ends);
+cudaError_t launch_decode_layer(const DecodeArgs &a, int qtype, int lanes, cudaStream_t st);
+
 // out[t, :] = sum_s Y[t*K + s, :] / (1 / w[t*K + s]) in slot order
 cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, float *out,
 			   cudaStream_t st);

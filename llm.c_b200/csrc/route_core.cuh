@@ -1,0 +1,259 @@
+// route_core.cuh — per-token softmax + top-k and the stable expert dispatch,
+// shared by the routing kernels (router.cu) and the fused decode-layer
+// kernel (decode.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace moe {
+
+constexpr int kMaxTopkExperts = 256;  // experts per router (NE)
+
+// ---------------------------------------------------------------------
+// softmax + top-k (+ optional renorm) of one token by one warp, with the
+// token's NE probabilities held in registers (element lane + 32 j in v[j]).
+// sw/sid: K floats / ints of shared scratch (the selected slots).
+// ---------------------------------------------------------------------
+template <int LANES, int MAXJ>
+static __device__ __noinline__ void topk_token_j(const float *__restrict__ lr, const float *__restrict__ bias,
+				    int NE, int K, int mode_exact, int renorm, float *sw, int32_t *sid,
+				    int32_t *__restrict__ ids_out, float *__restrict__ w_out,
+				    float *__restrict__ probs_out, int32_t *ids_smem)
+{
+	static_assert(MAXJ * 32 <= kMaxTopkExperts, "register slots per lane");
+	constexpr unsigned FULL = 0xffffffffu;
+	const int lane = threadIdx.x % 32;
+	const int nj = (NE + 31) / 32;
+	float v[MAXJ];
+	float mx = -INFINITY;
+#pragma unroll
+	for (int j = 0; j < MAXJ; j++) {
+		const int e = lane + 32 * j;
+		v[j] = 0.0f;
+		if (j < nj && e < NE) {
+			float l = lr[e];
+			if (bias)
+				l = __fadd_rn(l, bias[e]);
+			v[j] = l;
+			mx = fmaxf(mx, l);
+		}
+	}
+	mx = warp_max(mx);
+#pragma unroll
+	for (int j = 0; j < MAXJ; j++)
+		if (j < nj && lane + 32 * j < NE)
+			v[j] = exp_rn(__fsub_rn(v[j], mx));
+
+	// nn.c:236-250: SIMD lane l (< LANES) sums elements l, l+LANES, l+2 LANES,
+	// ... of the vector part in order; the lanes meet in the halving tree;
+	// the scalar tail is added after it, in order
+	const int nv = NE - NE % LANES;
+	float s = 0.0f;
+#pragma unroll
+	for (int m = 0; m < MAXJ * 32 / LANES; m++) {
+		// element lane + LANES*m lives in lane lane + (LANES*m % 32), slot LANES*m / 32
+		const float o = __shfl_sync(FULL, v[(LANES * m) / 32], lane + (LANES * m) % 32);
+		if (m < nv / LANES)
+			s = __fadd_rn(s, o);
+	}
+	s = lane_tree_sum<LANES>(s);
+	for (int e = nv; e < NE; e++) {
+		float o = 0.0f;
+#pragma unroll
+		for (int j = 0; j < MAXJ; j++)
+			if (e / 32 == j)
+				o = __shfl_sync(FULL, v[j], e & 31);
+		s = __fadd_rn(s, o);  // lane 0's value is the reference's
+	}
+	s = __shfl_sync(FULL, s, 0);
+#pragma unroll
+	for (int j = 0; j < MAXJ; j++)
+		if (j < nj && lane + 32 * j < NE) {
+			v[j] = __fdiv_rn(v[j], s);
+			if (probs_out)
+				probs_out[lane + 32 * j] = v[j];
+		}
+
+	// rank of every element, all at once: element i's rank counts the
+	// elements ahead of it by (value desc, index asc).  Reference mode:
+	// nn.c:276-308 seeds all k slots with element 0, which equals ranking
+	// [p0 (k copies), p1, p2, ...] by (value desc, position asc): element
+	// i >= 1 starts behind the k copies when p0 >= p_i, and element 0 fills
+	// slots r0 .. k-1 where r0 = #{j >= 1 : p_j > p0}.  Slot = K-1-rank.
+	const float p0 = __shfl_sync(FULL, v[0], 0);
+	int rank[MAXJ];
+#pragma unroll
+	for (int j = 0; j < MAXJ; j++)
+		rank[j] = (!mode_exact && p0 >= v[j]) ? K : 0;
+	int r0 = 0;  // reference mode, element 0 (lane 0)
+	// Every shuffle is unconditional (a shuffle under a branch costs a
+	// reconvergence barrier); validity enters as predicates.
+#pragma unroll 8
+	for (int l = 0; l < 32; l++) {
+#pragma unroll
+		for (int jj = 0; jj < MAXJ; jj++) {
+			const float o = __shfl_sync(FULL, v[jj], l);
+			const int eo = l + 32 * jj;
+			const bool cand = eo < NE && (mode_exact || eo != 0);
+#pragma unroll
+			for (int j = 0; j < MAXJ; j++) {
+				const int e = lane + 32 * j;
+				rank[j] += cand && (o > v[j] || (o == v[j] && eo < e));
+			}
+			r0 += eo < NE && eo != 0 && o > p0;
+		}
+	}
+#pragma unroll
+	for (int j = 0; j < MAXJ; j++) {
+		const int e = lane + 32 * j;
+		if (j >= nj || e >= NE) {
+		} else if (!mode_exact && e == 0) {
+			for (int c = r0; c < K; c++) {
+				sid[K - 1 - c] = 0;
+				sw[K - 1 - c] = p0;
+			}
+		} else if (rank[j] < K) {
+			sid[K - 1 - rank[j]] = e;
+			sw[K - 1 - rank[j]] = v[j];
+		}
+	}
+	__syncwarp();
+	if (renorm && lane == 0) {
+		// llama.c:422-427: sequential sum in slot order, then divide
+		float sum = 0.0f;
+		for (int q = 0; q < K; q++)
+			sum = __fadd_rn(sum, sw[q]);
+		for (int q = 0; q < K; q++)
+			sw[q] = __fdiv_rn(sw[q], sum);
+	}
+	__syncwarp();
+	for (int q = lane; q < K; q += 32) {
+		ids_out[q] = sid[q];
+		w_out[q] = sw[q];
+		if (ids_smem)
+			ids_smem[q] = sid[q];
+	}
+	__syncwarp();
+}
+
+// NE <= 32 * MAXJ elements per token: the smallest register file that fits.
+// topk_token_j is kept out of line so that its register arrays stay in
+// registers inside large kernels as well.
+template <int LANES>
+static __device__ void topk_token(const float *__restrict__ lr, const float *__restrict__ bias,
+				  int NE, int K, int mode_exact, int renorm, float *sw, int32_t *sid,
+				  int32_t *__restrict__ ids_out, float *__restrict__ w_out,
+				  float *__restrict__ probs_out, int32_t *ids_smem)
+{
+	if (NE <= 64)
+		topk_token_j<LANES, 2>(lr, bias, NE, K, mode_exact, renorm, sw, sid, ids_out, w_out,
+				       probs_out, ids_smem);
+	else if (NE <= 128)
+		topk_token_j<LANES, 4>(lr, bias, NE, K, mode_exact, renorm, sw, sid, ids_out, w_out,
+				       probs_out, ids_smem);
+	else
+		topk_token_j<LANES, 8>(lr, bias, NE, K, mode_exact, renorm, sw, sid, ids_out, w_out,
+				       probs_out, ids_smem);
+}
+
+// ---------------------------------------------------------------------
+// dispatch: counts[NE], offsets[NE+1], perm[T*K] (pairs p = t*K + slot
+// stably sorted by expert), pos_of[p] = position of pair p in perm, and the
+// ascending list of experts in [first, first+nlocal) that received pairs.
+// One CTA walks the pairs in chunks of blockDim.x; within a chunk a
+// pair's rank among same-expert pairs comes from warp match masks plus
+// per-warp counts, so the order is stable and deterministic.  Every thread
+// of the CTA must call it (it synchronises the CTA).
+// smem: cnt[NE], run[NE], wcnt[warps][NE]; blockDim.x a multiple of 32
+// ---------------------------------------------------------------------
+static __device__ void dispatch_body(const int32_t *ids, int npairs, int NE, int first, int nlocal,
+			      int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+			      int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
+			      int32_t *__restrict__ active, int32_t *__restrict__ n_active,
+			      int32_t *__restrict__ err, int32_t *ds)
+{
+	int32_t *cnt = ds;                // [NE]
+	int32_t *run = cnt + NE;          // [NE] running fill position
+	int32_t *wcnt = run + NE;         // [warps][NE]
+	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+	const int nw = (int)blockDim.x / 32;  // warps of the CTA (at most 32)
+
+	for (int e = tid; e < NE; e += blockDim.x)
+		cnt[e] = 0;
+	__syncthreads();
+	for (int p = tid; p < npairs; p += blockDim.x) {
+		const int e = ids[p];
+		if (e < 0 || e >= NE) {
+			atomicExch(err, 1);
+			continue;
+		}
+		atomicAdd(&cnt[e], 1);
+	}
+	__syncthreads();
+	if (warp == 0) {
+		// exclusive scan of the counts and the list of active local experts,
+		// 32 experts at a time (shuffle scan, ballot compaction)
+		int acc = 0, na = 0;
+		for (int base = 0; base < NE; base += 32) {
+			const int e = base + lane;
+			const int c = e < NE ? cnt[e] : 0;
+			int incl = c;
+#pragma unroll
+			for (int o = 1; o < 32; o <<= 1) {
+				const int u = __shfl_up_sync(0xffffffffu, incl, o);
+				if (lane >= o)
+					incl += u;
+			}
+			const bool act = c > 0 && e >= first && e < first + nlocal;
+			const unsigned m = __ballot_sync(0xffffffffu, act);
+			if (e < NE) {
+				offsets[e] = acc + incl - c;
+				run[e] = acc + incl - c;
+				counts[e] = c;
+			}
+			if (act)
+				active[na + __popc(m & ((1u << lane) - 1u))] = e;
+			na += __popc(m);
+			acc += __shfl_sync(0xffffffffu, incl, 31);
+		}
+		if (lane == 0) {
+			offsets[NE] = acc;
+			*n_active = na;
+		}
+	}
+	__syncthreads();
+
+	for (int base = 0; base < npairs; base += blockDim.x) {
+		for (int i = tid; i < nw * NE; i += blockDim.x)
+			wcnt[i] = 0;
+		__syncthreads();
+		const int p = base + tid;
+		int e = (p < npairs) ? ids[p] : -1;
+		if (e >= NE)
+			e = -1;
+		const unsigned same = __match_any_sync(0xffffffffu, e);
+		const int rank_w = __popc(same & ((1u << lane) - 1u));
+		if (e >= 0 && rank_w == 0)
+			wcnt[warp * NE + e] = __popc(same);
+		__syncthreads();
+		if (e >= 0) {
+			int before = 0;
+			for (int w = 0; w < warp; w++)
+				before += wcnt[w * NE + e];
+			const int pos = run[e] + before + rank_w;
+			perm[pos] = p;
+			if (pos_of)
+				pos_of[p] = pos;
+		}
+		__syncthreads();
+		for (int e2 = tid; e2 < NE; e2 += blockDim.x) {
+			int add = 0;
+			for (int w = 0; w < nw; w++)
+				add += wcnt[w * NE + e2];
+			run[e2] += add;
+		}
+		__syncthreads();
+	}
+}
+
+}  // namespace moe

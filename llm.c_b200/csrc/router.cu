@@ -14,6 +14,7 @@
 //     k-1-rank.  Each element's rank is computed independently here.
 #include "common.cuh"
 #include "kernels.h"
+#include "route_core.cuh"
 
 namespace moe {
 
@@ -227,104 +228,6 @@ router_tiled_kernel(const float *__restrict__ x, const float *__restrict__ w,
 		}
 }
 
-// ---------------------------------------------------------------------
-// softmax + top-k (+ optional renorm) of one token by one warp.
-// p: NE floats of shared scratch; sw/sid: K floats / ints of shared scratch.
-// ---------------------------------------------------------------------
-template <int LANES>
-__device__ void topk_token(const float *__restrict__ lr, const float *__restrict__ bias, int NE,
-			   int K, int mode_exact, int renorm, float *p, float *sw, int32_t *sid,
-			   int32_t *__restrict__ ids_out, float *__restrict__ w_out,
-			   float *__restrict__ probs_out, int32_t *ids_smem)
-{
-	const int lane = threadIdx.x % 32;
-	float mx = -INFINITY;
-	for (int e = lane; e < NE; e += 32) {
-		float v = lr[e];
-		if (bias)
-			v = __fadd_rn(v, bias[e]);
-		p[e] = v;
-		mx = fmaxf(mx, v);
-	}
-	mx = warp_max(mx);
-	__syncwarp();
-	for (int e = lane; e < NE; e += 32)
-		p[e] = exp_rn(__fsub_rn(p[e], mx));
-	__syncwarp();
-
-	// lane-wise sums over the vector part (nn.c:236-246), then the tree,
-	// then the scalar tail (nn.c:247-250)
-	const int nv = NE - NE % LANES;
-	float s = 0.0f;
-	if (lane < LANES)
-		for (int e = lane; e < nv; e += LANES)
-			s = __fadd_rn(s, p[e]);
-	s = lane_tree_sum<LANES>(s);
-	if (lane == 0)
-		for (int e = nv; e < NE; e++)
-			s = __fadd_rn(s, p[e]);
-	s = __shfl_sync(0xffffffffu, s, 0);
-	for (int e = lane; e < NE; e += 32)
-		p[e] = __fdiv_rn(p[e], s);
-	__syncwarp();
-
-	if (probs_out)
-		for (int e = lane; e < NE; e += 32)
-			probs_out[e] = p[e];
-
-	const float p0 = p[0];
-	for (int i = lane; i < NE; i += 32) {
-		const float v = p[i];
-		int rank = 0;
-		if (mode_exact) {
-			for (int j = 0; j < NE; j++) {
-				const float o = p[j];
-				rank += (o > v) || (o == v && j < i);
-			}
-			if (rank < K) {
-				sid[K - 1 - rank] = i;
-				sw[K - 1 - rank] = v;
-			}
-		} else if (i == 0) {
-			// the k seeded copies of element 0
-			int r0 = 0;
-			for (int j = 1; j < NE; j++)
-				r0 += (p[j] > p0);
-			for (int c = 0; r0 + c < K; c++) {
-				sid[K - 1 - (r0 + c)] = 0;
-				sw[K - 1 - (r0 + c)] = p0;
-			}
-		} else {
-			rank = (p0 >= v) ? K : 0;
-			for (int j = 1; j < NE && rank < K; j++) {
-				const float o = p[j];
-				rank += (o > v) || (o == v && j < i);
-			}
-			if (rank < K) {
-				sid[K - 1 - rank] = i;
-				sw[K - 1 - rank] = v;
-			}
-		}
-	}
-	__syncwarp();
-	if (renorm && lane == 0) {
-		// llama.c:422-427: sequential sum in slot order, then divide
-		float sum = 0.0f;
-		for (int q = 0; q < K; q++)
-			sum = __fadd_rn(sum, sw[q]);
-		for (int q = 0; q < K; q++)
-			sw[q] = __fdiv_rn(sw[q], sum);
-	}
-	__syncwarp();
-	for (int q = lane; q < K; q += 32) {
-		ids_out[q] = sid[q];
-		w_out[q] = sw[q];
-		if (ids_smem)
-			ids_smem[q] = sid[q];
-	}
-	__syncwarp();
-}
-
 constexpr int kTopkWarps = 4;
 
 template <int LANES>
@@ -333,100 +236,19 @@ router_topk_kernel(const float *__restrict__ logits, const float *__restrict__ b
 		   int T, int NE, int K, int mode_exact, int renorm,
 		   int32_t *__restrict__ ids, float *__restrict__ wts, float *__restrict__ probs_out)
 {
-	extern __shared__ float sm[];  // [kTopkWarps][NE] probs, then [kTopkWarps][2K]
+	extern __shared__ float sm[];  // [kTopkWarps][2K] selected weights and ids
 	const int warp = threadIdx.x / 32;
 	const int t = blockIdx.x * kTopkWarps + warp;
 	if (t >= T)
 		return;  // whole warp leaves together
-	float *sw = sm + kTopkWarps * NE + warp * 2 * K;
-	topk_token<LANES>(logits + (int64_t)t * NE, bias, NE, K, mode_exact, renorm, sm + warp * NE,
+	float *sw = sm + warp * 2 * K;
+	topk_token<LANES>(logits + (int64_t)t * NE, bias, NE, K, mode_exact, renorm,
 			  sw, reinterpret_cast<int32_t *>(sw + K), ids + (int64_t)t * K,
 			  wts + (int64_t)t * K, probs_out ? probs_out + (int64_t)t * NE : nullptr,
 			  nullptr);
 }
 
-// ---------------------------------------------------------------------
-// dispatch: counts[NE], offsets[NE+1], perm[T*K] (pairs p = t*K + slot
-// stably sorted by expert), pos_of[p] = position of pair p in perm, and the
-// ascending list of experts in [first, first+nlocal) that received pairs.
-// One CTA of 1024 threads walks the pairs in chunks of 1024; within a
-// chunk a pair's rank among same-expert pairs comes from warp match masks
-// plus per-warp counts, so the order is stable and deterministic.
-// Also zeroes the error flag and the expert kernels' work counters.
-// smem: cnt[NE], run[NE], wcnt[32][NE]
-// ---------------------------------------------------------------------
 constexpr int kDispatchThreads = 1024;
-
-__device__ void dispatch_body(const int32_t *ids, int npairs, int NE, int first, int nlocal,
-			      int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
-			      int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
-			      int32_t *__restrict__ active, int32_t *__restrict__ n_active,
-			      int32_t *__restrict__ err, int32_t *ds)
-{
-	int32_t *cnt = ds;                // [NE]
-	int32_t *run = cnt + NE;          // [NE] running fill position
-	int32_t *wcnt = run + NE;         // [32 warps][NE]
-	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-
-	for (int e = tid; e < NE; e += blockDim.x)
-		cnt[e] = 0;
-	__syncthreads();
-	for (int p = tid; p < npairs; p += blockDim.x) {
-		const int e = ids[p];
-		if (e < 0 || e >= NE) {
-			atomicExch(err, 1);
-			continue;
-		}
-		atomicAdd(&cnt[e], 1);
-	}
-	__syncthreads();
-	if (tid == 0) {
-		int acc = 0, na = 0;
-		for (int e = 0; e < NE; e++) {
-			offsets[e] = acc;
-			run[e] = acc;
-			counts[e] = cnt[e];
-			acc += cnt[e];
-			if (cnt[e] > 0 && e >= first && e < first + nlocal)
-				active[na++] = e;
-		}
-		offsets[NE] = acc;
-		*n_active = na;
-	}
-	__syncthreads();
-
-	for (int base = 0; base < npairs; base += blockDim.x) {
-		for (int i = tid; i < 32 * NE; i += blockDim.x)
-			wcnt[i] = 0;
-		__syncthreads();
-		const int p = base + tid;
-		int e = (p < npairs) ? ids[p] : -1;
-		if (e >= NE)
-			e = -1;
-		const unsigned same = __match_any_sync(0xffffffffu, e);
-		const int rank_w = __popc(same & ((1u << lane) - 1u));
-		if (e >= 0 && rank_w == 0)
-			wcnt[warp * NE + e] = __popc(same);
-		__syncthreads();
-		if (e >= 0) {
-			int before = 0;
-			for (int w = 0; w < warp; w++)
-				before += wcnt[w * NE + e];
-			const int pos = run[e] + before + rank_w;
-			perm[pos] = p;
-			if (pos_of)
-				pos_of[p] = pos;
-		}
-		__syncthreads();
-		for (int e2 = tid; e2 < NE; e2 += blockDim.x) {
-			int add = 0;
-			for (int w = 0; w < 32; w++)
-				add += wcnt[w * NE + e2];
-			run[e2] += add;
-		}
-		__syncthreads();
-	}
-}
 
 __global__ void __launch_bounds__(kDispatchThreads)
 dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE, int first, int nlocal,
@@ -446,7 +268,7 @@ dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE, int first, 
 
 // small batches: softmax/top-k of every token (warp w takes tokens w,
 // w+32, ...) and the dispatch in one CTA, ids kept in shared memory.
-// smem: probs [32][NE], sel [32][2K], ids [T*K], dispatch scratch
+// smem: sel [32][2K], ids [T*K], dispatch scratch
 template <int LANES>
 __global__ void __launch_bounds__(kDispatchThreads)
 route_small_kernel(const float *__restrict__ logits, const float *__restrict__ bias, int T,
@@ -459,8 +281,7 @@ route_small_kernel(const float *__restrict__ logits, const float *__restrict__ b
 {
 	extern __shared__ float rs[];
 	const int warp = threadIdx.x / 32;
-	float *probs = rs;                                   // [32][NE]
-	float *sel = probs + 32 * NE;                        // [32][2K]
+	float *sel = rs;                                     // [32][2K]
 	int32_t *ids_s = reinterpret_cast<int32_t *>(sel + 64 * K);  // [T*K]
 	int32_t *ds = ids_s + T * K;
 	if (threadIdx.x == 0) {
@@ -470,7 +291,7 @@ route_small_kernel(const float *__restrict__ logits, const float *__restrict__ b
 	for (int t = warp; t < T; t += 32) {
 		float *sw = sel + warp * 2 * K;
 		topk_token<LANES>(logits + (int64_t)t * NE, bias, NE, K, mode_exact, renorm,
-				  probs + warp * NE, sw, reinterpret_cast<int32_t *>(sw + K),
+				  sw, reinterpret_cast<int32_t *>(sw + K),
 				  ids + (int64_t)t * K, wts + (int64_t)t * K, nullptr, ids_s + t * K);
 	}
 	__syncthreads();
@@ -546,7 +367,7 @@ cudaError_t launch_router_topk(const float *logits, const float *bias, int T, in
 	if (T == 0)
 		return cudaSuccess;
 	const int blocks = (T + kTopkWarps - 1) / kTopkWarps;
-	const size_t tsm = (size_t)kTopkWarps * (NE + 2 * K) * sizeof(float);
+	const size_t tsm = (size_t)kTopkWarps * 2 * K * sizeof(float);
 	if (lanes == 8)
 		router_topk_kernel<8><<<blocks, 32 * kTopkWarps, tsm, st>>>(
 			logits, bias, T, NE, K, mode_exact, renorm, ids, wts, probs);
@@ -586,7 +407,7 @@ cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int first, i
 
 size_t route_small_smem(int T, int NE, int K)
 {
-	return (size_t)(32 * NE + 64 * K) * sizeof(float) + (size_t)T * K * sizeof(int32_t) +
+	return (size_t)(64 * K) * sizeof(float) + (size_t)T * K * sizeof(int32_t) +
 	       dispatch_smem(NE);
 }
 

@@ -36,7 +36,11 @@ enum {
 	ORC_TOPK_EXACT = 1, /* true top-k by (value desc, index asc)          */
 };
 
-/* ---- synthetic input generator (shared spec) ---------- */
+/* ---- synthetic input generator (shared with synth.cu) ----------------
+ * stream = mix64(mix64(seed) ^ tag * 0xD1B54A32D192ED03); element i draws
+ * two splitmix64 counters and one Box-Muller normal.  Tags: router 1,
+ * gate 2, up 3, down 4, tokens 5, Zipf rank permutation 6, dense W 7,
+ * dense x 8. */
 uint64_t orc_mix64(uint64_t z);
 uint64_t orc_stream_seed(uint64_t seed, uint64_t tag);
 /* out[i] = sd * N(0,1) element (offset + i) of stream `stream` */

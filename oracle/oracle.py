@@ -203,7 +203,7 @@ def moe_ffn(layer: dict, x: np.ndarray, lanes=16, topk_mode=TOPK_REF):
 
 def make_layer(seed: int, d: int, F: int, NE: int, K: int, qtype: int = Q8_0,
                renorm: bool = False, zipf: bool = False, sd: float = 0.02) -> dict:
-    """Seeded synthetic MoE layer (generator spec: DESIGN.md)."""
+    """Seeded synthetic MoE layer (generator tags: router 1, gate 2, up 3, down 4)."""
     wr = gauss(seed, 1, NE * d, sd).reshape(NE, d)
     gate = quantize(qtype, gauss(seed, 2, NE * F * d, sd).reshape(NE, F, d))
     up = quantize(qtype, gauss(seed, 3, NE * F * d, sd).reshape(NE, F, d))

@@ -1,7 +1,8 @@
 """Writes tests/golden/*.npz: outputs of the REFERENCE (its own sources,
 compiled into oracle/_ref by oracle/Makefile) on seeded synthetic inputs.
 
-Run where /root/reference exists:  python tests/golden/make_golden.py
+Run where the reference sources are present (oracle/_ref built):
+    python tests/golden/make_golden.py
 Inputs are regenerated from their seeds by the shared generator in
 oracle/oracle.c; each fixture stores a digest of the generated weight bytes
 so a generator change is caught.  Cases:

@@ -2,8 +2,8 @@
 ran the reference's sources compiled into oracle/_ref on seeded inputs).
 
 CPU: the oracle restatement reproduces them bit for bit (so the oracle is
-pinned even where /root/reference is absent).  GPU: the library matches them
-within the BASELINE tolerance (ids bit-exact)."""
+pinned even where the reference sources are absent).  GPU: the library matches
+them within the north-star tolerance (ids bit-exact)."""
 import hashlib
 import os
 

@@ -1,5 +1,5 @@
 """The CPU oracle against the reference compiled from its own sources
-(oracle/_ref, built by oracle/Makefile when /root/reference is present).
+(oracle/_ref, built by oracle/Makefile when the reference sources are present).
 Bit-exact: both follow the reference's floating-point operation order.
 Skipped where the compiled reference is absent."""
 import numpy as np
