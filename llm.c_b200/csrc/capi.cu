@@ -227,7 +227,8 @@ int layer_scratch(moe_layer *L, int64_t T)
 	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8);
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
 	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)cap * K * 2 * F * 2);
-	size_t o_gbar = take(8);
+	const size_t gbar_bytes = moe::decode_barrier_bytes(moe::sm_count());
+	size_t o_gbar = take(gbar_bytes);
 	size_t o_stamps = take((size_t)kStampRecords * moe::sm_count() * moe::decode_stamps() * 8);
 	if (L->scratch) {
 		CK(cudaStreamSynchronize(g.stream));
@@ -255,7 +256,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->h16 = (__half *)(b + o_h16);
 	L->gbar = (unsigned long long *)(b + o_gbar);
 	L->stamps = (uint64_t *)(b + o_stamps);
-	CK(cudaMemset(L->gbar, 0, 8));
+	CK(cudaMemset(L->gbar, 0, gbar_bytes));
 	CK(cudaDeviceSynchronize());  // ordered before launches on any stream
 	L->capT = cap;
 	return MOE_OK;
@@ -793,7 +794,7 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
 	if (err == 2 || err == 3) {
 		// a barrier left half-passed must not poison the next forward
-		CK(cudaMemset(L->gbar, 0, 8));
+		CK(cudaMemset(L->gbar, 0, moe::decode_barrier_bytes(moe::sm_count())));
 		CK(cudaDeviceSynchronize());
 	}
 	if (err == 1)

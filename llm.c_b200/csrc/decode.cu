@@ -14,8 +14,7 @@
 //       barrier; then every CTA reads the selected (token, slot) pairs and
 //       computes their stable dispatch by expert into its own shared
 //       memory (redundant, but cheaper than another barrier); CTA 0 writes
-//       the dispatch to global memory for the host.  Meanwhile each CTA's
-//       producer warp asks L2 for its first gate/up weights.
+//       the dispatch to global memory for the host.
 //   P2  gate/up + SwiGLU over (active expert, 8-row) items — the expert
 //       pipeline of expert_core.cuh, writing h as fp16 hi/lo rows.
 //   --  grid barrier among the math and epilogue warps.  The producer warp
@@ -40,25 +39,29 @@
 
 namespace moe {
 
-// router tile of P0.  Threads 0-255 compute: warp w owns expert e0 + w of
-// the tile, lane = (token tk, lane quad lq); each thread keeps LANES/4
-// consecutive SIMD lanes of one (token, expert) logit.
+// router tile of P0: RT tokens x RE experts, whole 2048-column row chunks
+// staged by 16 bulk copies (one per row, issued by 16 lanes at once).
+// Warps 0-3 compute: for 16 SIMD lanes, warp w owns lane quad w and its
+// threads are (token, pair of experts); for 8 lanes, warp w owns lane quad
+// w & 1 and four experts, one per thread.  Each thread keeps its lanes' fp32
+// chains; the reference's halving tree over the lanes runs at the end, per
+// logit, from shared memory.
 template <int LANES>
 struct RTile {
 	static constexpr int LQ = LANES / 4;                 // lane quads per logit
-	static constexpr int RT = 32 / LQ;                   // tokens per tile: 8 or 16
+	static constexpr int RT = 8;                         // tokens per tile
 	static constexpr int RE = 8;                         // experts per tile
-	static constexpr int CH = 512;                       // columns per chunk
-	// row stride chosen so that the tokens of a quarter warp hit distinct banks
-	static constexpr int RS = CH * 4 + (LANES == 16 ? 64 : 32);
-	static constexpr int SLOT = (RT + RE) * RS;
-	// chunks in flight: all four of a 2048-column row for 16 lanes (one
-	// round trip per tile); three for the taller 8-lane tile
-	static constexpr int NSLOT = LANES == 16 ? 4 : 3;
+	static constexpr int EPT = LANES == 16 ? 2 : 1;      // experts per thread
+	static constexpr int CH = 2048;                      // columns per chunk
+	// 8 token rows of a warp read 8 distinct 16-byte bank groups
+	static constexpr int RS = CH * 4 + 16;
+	static constexpr int ROWS = RT + RE;
+	static constexpr int PART = ROWS * RS;               // lane partials start here
+	static constexpr int BYTES = PART + RT * RE * LANES * 4;
+	static constexpr int NSLOT = 1;
 };
 
 constexpr int kDecodeMaxT = 64;
-constexpr int kPrefetchItems = 8;  // gate/up items per CTA hinted into L2 at start
 constexpr int kDecodeMaxPairs = 1024;
 // %globaltimer stamps per CTA (thread 0): phase ends and barrier exits
 enum Stamp {
@@ -87,7 +90,7 @@ template <int QT, int STAGES>
 constexpr size_t decode_smem_bytes()
 {
 	return (size_t)STAGES * StageLayout<QT>::BYTES + StageLayout<QT>::RED +
-	       StageLayout<QT>::SSUM + DecodeSmem::END +
+	       StageLayout<QT>::SSUM + StageLayout<QT>::EPI + DecodeSmem::END +
 	       (2 * STAGES + 2 * kRedBufs + 4) * 8;  // + up to 4 router slot barriers
 }
 
@@ -99,19 +102,34 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
 	return v;
 }
 
-// Called by one thread per CTA after a CTA-level barrier.  *ctr counts the
-// arrivals since it was zeroed and is a multiple of gridDim.x between
-// barriers, so an arrival's ticket tells which barrier it belongs to and the
-// count that releases it: one atomic per CTA, then a bounded poll.
-__device__ bool grid_sync(unsigned long long *ctr, int32_t *err)
+__device__ __forceinline__ void st_relaxed_gpu(unsigned long long *p, unsigned long long v)
+{
+	asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Grid barrier state: bar[0] counts arrivals since the buffer was zeroed
+// (a multiple of gridDim.x between barriers), and CTA b polls its own flag
+// bar[kGridFlagStride * (b + 1)], on a cache line of its own, which holds
+// the number of barriers released so far.  An arrival's ticket tells which
+// barrier it belongs to; the last arriver of a barrier writes every flag.
+// Called by one thread per CTA after a CTA-level barrier; the poll is
+// bounded.
+constexpr int kGridFlagStride = 16;  // u64s: 128 bytes per flag
+
+__device__ bool grid_sync(unsigned long long *bar, int32_t *err)
 {
 	__threadfence();
 	const unsigned long long n = gridDim.x;
-	const unsigned long long ticket = atomicAdd(ctr, 1ull);
-	const unsigned long long target = (ticket / n + 1) * n;
-	if (ticket + 1 < target) {
+	const unsigned long long ticket = atomicAdd(bar, 1ull);
+	const unsigned long long epoch = ticket / n + 1;
+	unsigned long long *mine = bar + kGridFlagStride * (blockIdx.x + 1);
+	if (ticket + 1 == epoch * n) {
+		__threadfence();
+		for (unsigned b = 0; b < gridDim.x; b++)
+			st_relaxed_gpu(bar + kGridFlagStride * (b + 1), epoch);
+	} else {
 		const uint64_t t0 = global_ns();
-		while (ld_acquire_gpu(ctr) < target) {
+		while (ld_acquire_gpu(mine) < epoch) {
 			if (global_ns() - t0 > kWaitLimitNs) {
 				atomicExch(err, 3);
 				return false;
@@ -122,6 +140,8 @@ __device__ bool grid_sync(unsigned long long *ctr, int32_t *err)
 	__threadfence();
 	return true;
 }
+
+size_t decode_barrier_bytes(int ctas) { return (size_t)(ctas + 1) * kGridFlagStride * 8; }
 
 __device__ __forceinline__ void bar_math_epi()
 {
@@ -137,107 +157,94 @@ __device__ __forceinline__ void stamp(uint64_t *stamps, int k)
 
 // ---------------------------------------------------------------- P0 router
 template <int LANES>
-__device__ void router_tiles(const DecodeArgs &a, uint8_t *slots, uint64_t *rbar)
+__device__ void router_tiles(const DecodeArgs &a, uint8_t *buf, uint64_t *rbar)
 {
 	using R = RTile<LANES>;
-	const int tid = threadIdx.x;
+	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 	const int n_tt = (a.T + R::RT - 1) / R::RT, n_et = a.NE / R::RE;
 	const int nch = a.D / R::CH;
-	const int lq = tid % R::LQ, tk = (tid % 32) / R::LQ, ek = tid / 32;  // for tid < 256
-	uint32_t q = 0;  // chunks consumed by this CTA (slot use sequence)
+	// compute mapping (warps 0-3)
+	const int lq = LANES == 16 ? warp : (warp & 1);
+	const int tk = lane & 7;
+	const int e_first = LANES == 16 ? 2 * (lane >> 3) : 4 * (warp >> 1) + (lane >> 3);
+	float *part = reinterpret_cast<float *>(buf + R::PART);  // [RT][RE][LANES]
+	uint32_t q = 0;  // chunks through the buffer (barrier phase)
 	bool failed = false;
 	for (int u = blockIdx.x; u < n_tt * n_et; u += gridDim.x) {
 		const int t0 = (u / n_et) * R::RT, e0 = (u % n_et) * R::RE;
 		const int nt = min(R::RT, a.T - t0);
-		auto issue = [&](int c, uint32_t qq) {
-			const int s = qq % R::NSLOT;
-			uint8_t *base = slots + s * R::SLOT;
-			mbar_arrive_expect_tx(&rbar[s], (uint32_t)((nt + R::RE) * R::CH * 4));
-			for (int r = 0; r < nt; r++)
-				bulk_g2s(base + r * R::RS, a.x + (int64_t)(t0 + r) * a.D + c * R::CH,
-					 R::CH * 4, &rbar[s]);
-			for (int r = 0; r < R::RE; r++)
-				bulk_g2s(base + (R::RT + r) * R::RS,
-					 a.router_w + (int64_t)(e0 + r) * a.D + c * R::CH, R::CH * 4, &rbar[s]);
-		};
-		if (tid == 0 && !failed) {
-			fence_proxy_async();
-			for (int c = 0; c < min(nch, R::NSLOT); c++)
-				issue(c, q + c);
-		}
-		float acc[4] = {0.f, 0.f, 0.f, 0.f};
-		for (int c = 0; c < nch; c++) {
-			const uint32_t qq = q + c;
-			const int s = qq % R::NSLOT;
-			if (!failed && !mbar_wait(&rbar[s], (qq / R::NSLOT) & 1)) {
+		float acc[R::EPT][4];
+#pragma unroll
+		for (int k = 0; k < R::EPT; k++)
+#pragma unroll
+			for (int j = 0; j < 4; j++)
+				acc[k][j] = 0.0f;
+		for (int c = 0; c < nch; c++, q++) {
+			if (warp == 0 && !failed) {
+				// rows 0..RT-1: tokens (those past T are not copied); RT..: experts
+				if (lane == 0)
+					mbar_arrive_expect_tx(rbar, (uint32_t)((nt + R::RE) * R::CH * 4));
+				__syncwarp();
+				if (lane < R::ROWS && (lane >= R::RT || lane < nt)) {
+					const float *src = lane < R::RT
+								   ? a.x + (int64_t)(t0 + lane) * a.D
+								   : a.router_w + (int64_t)(e0 + lane - R::RT) * a.D;
+					fence_proxy_async();
+					bulk_g2s(buf + lane * R::RS, src + (int64_t)c * R::CH, R::CH * 4, rbar);
+				}
+			}
+			if (!failed && !mbar_wait(rbar, q & 1)) {
 				failed = true;
 				atomicExch(a.err, 2);
 			}
-			if (tid < 256 && !failed) {
-				const float *xs = reinterpret_cast<const float *>(slots + s * R::SLOT + tk * R::RS);
-				const float *ws =
-					reinterpret_cast<const float *>(slots + s * R::SLOT + (R::RT + ek) * R::RS);
-#pragma unroll 8
+			if (warp < 4 && !failed) {
+				const float *xs = reinterpret_cast<const float *>(buf + tk * R::RS);
+				const float *ws = reinterpret_cast<const float *>(buf + (R::RT + e_first) * R::RS);
+#pragma unroll 4
 				for (int st = 0; st < R::CH / LANES; st++) {
 					const int col = st * LANES + lq * 4;
 					const float4 xv = *reinterpret_cast<const float4 *>(xs + col);
-					const float4 wv = *reinterpret_cast<const float4 *>(ws + col);
-					acc[0] = __fmaf_rn(xv.x, wv.x, acc[0]);
-					acc[1] = __fmaf_rn(xv.y, wv.y, acc[1]);
-					acc[2] = __fmaf_rn(xv.z, wv.z, acc[2]);
-					acc[3] = __fmaf_rn(xv.w, wv.w, acc[3]);
+#pragma unroll
+					for (int k = 0; k < R::EPT; k++) {
+						const float4 wv = *reinterpret_cast<const float4 *>(
+							ws + k * (R::RS / 4) + col);
+						acc[k][0] = __fmaf_rn(xv.x, wv.x, acc[k][0]);
+						acc[k][1] = __fmaf_rn(xv.y, wv.y, acc[k][1]);
+						acc[k][2] = __fmaf_rn(xv.z, wv.z, acc[k][2]);
+						acc[k][3] = __fmaf_rn(xv.w, wv.w, acc[k][3]);
+					}
 				}
 			}
-			__syncthreads();  // the slot is free again
-			if (tid == 0 && !failed && c + R::NSLOT < nch) {
-				fence_proxy_async();
-				issue(c + R::NSLOT, qq + R::NSLOT);
-			}
+			__syncthreads();  // the buffer is free again
 		}
-		q += nch;
-		if (tid < 256) {
-			// lane tree of the reference (upper half onto lower half); quads
-			// live in consecutive threads
-			if (R::LQ == 4) {
+		// lane partials -> the reference's halving tree, one logit per thread
+		if (warp < 4)
+#pragma unroll
+			for (int k = 0; k < R::EPT; k++)
 #pragma unroll
 				for (int j = 0; j < 4; j++)
-					acc[j] = __fadd_rn(acc[j], __shfl_down_sync(0xffffffffu, acc[j], 2, 4));
-			}
+					part[(tk * R::RE + e_first + k) * LANES + lq * 4 + j] = acc[k][j];
+		__syncthreads();
+		if (tid < R::RT * R::RE) {
+			const int t = tid / R::RE, e = tid % R::RE;
+			float l[LANES];
 #pragma unroll
-			for (int j = 0; j < 4; j++)
-				acc[j] = __fadd_rn(acc[j], __shfl_down_sync(0xffffffffu, acc[j], 1, R::LQ));
-			const float sum = __fadd_rn(__fadd_rn(acc[0], acc[2]), __fadd_rn(acc[1], acc[3]));
-			if (lq == 0 && tk < nt)
-				a.logits[(int64_t)(t0 + tk) * a.NE + e0 + ek] = __fadd_rn(0.0f, sum);
+			for (int j = 0; j < LANES; j++)
+				l[j] = part[tid * LANES + j];
+#pragma unroll
+			for (int h = LANES / 2; h >= 1; h /= 2)
+#pragma unroll
+				for (int j = 0; j < h; j++)
+					l[j] = __fadd_rn(l[j], l[j + h]);
+			if (t < nt)
+				a.logits[(int64_t)(t0 + t) * a.NE + e0 + e] = __fadd_rn(0.0f, l[0]);
 		}
-	}
-}
-
-// Ask L2 for the head of the gate/up items this CTA will most likely stream
-// in P2 (the item range it would get if every expert had one pass of
-// tokens), so that HBM works during the latency-bound routing instead of
-// idling.  One warp; issued after the router's own loads are done, so that
-// it does not queue in front of them.
-template <int QT>
-__device__ void prefetch_gate_up(const DecodeArgs &a, int lane)
-{
-	constexpr int BB = StageLayout<QT>::BB;
-	const int groups = a.F / 8;
-	const int64_t total = (int64_t)a.NE * groups;
-	const int64_t i0 = total * blockIdx.x / gridDim.x;
-	const int64_t i1 = min(total * (blockIdx.x + 1) / gridDim.x, i0 + kPrefetchItems);
-	const uint32_t rb = (uint32_t)(a.D / QK * BB);
-	for (int64_t it = i0; it < i1; it++) {
-		const int e = (int)(it / groups), r = (int)(it % groups) * 8 + (lane & 7);
-		if (lane < 16) {
-			const uint8_t *w = static_cast<const uint8_t *>(a.dptrs[(lane < 8 ? 0 : a.NE) + e]);
-			bulk_prefetch_l2(w + (int64_t)r * rb, rb);
-		}
+		__syncthreads();
 	}
 }
 
 // ---------------------------------------------------------------- the kernel
-template <int QT, int LANES, int WB_GU, int WB_DN, int STAGES>
+template <int QT, int LANES, int WB_GU, int WB_DN, int MT_DN, int STAGES>
 __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs a)
 {
 	extern __shared__ __align__(128) uint8_t smem[];
@@ -246,7 +253,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	uint8_t *tail = smem + STAGES * SL::BYTES;
 	float4 *red = reinterpret_cast<float4 *>(tail);
 	float *ssum = reinterpret_cast<float *>(tail + SL::RED);
-	uint8_t *tb = tail + SL::RED + SL::SSUM;
+	float *stg = reinterpret_cast<float *>(tail + SL::RED + SL::SSUM);
+	uint8_t *tb = tail + SL::RED + SL::SSUM + SL::EPI;
 	int32_t *en = reinterpret_cast<int32_t *>(tb + DS::EN);
 	int32_t *off = reinterpret_cast<int32_t *>(tb + DS::OFF);
 	int32_t *pre_gu = reinterpret_cast<int32_t *>(tb + DS::PRE_GU);
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	int32_t *active_s = reinterpret_cast<int32_t *>(tb + DS::ACTIVE);
 	int32_t *nact_s = reinterpret_cast<int32_t *>(tb + DS::NACT);
 	uint64_t *bars = reinterpret_cast<uint64_t *>(tb + DS::BARS);
-	uint64_t *rbar = bars + 2 * STAGES + 2 * kRedBufs;  // [NSLOT] router slots
+	uint64_t *rbar = bars + 2 * STAGES + 2 * kRedBufs;  // router tile buffer
 
 	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 	const int T = a.T, D = a.D, F = a.F, NE = a.NE, K = a.K;
@@ -267,8 +275,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	if (blockIdx.x == 0 && tid == 0)
 		*a.err = 0;
 	const Bars b = init_bars<STAGES>(bars);
-	if (tid < RTile<LANES>::NSLOT)
-		mbar_init(&rbar[tid], 1);
+	if (tid == 0)
+		mbar_init(rbar, 1);
 	fence_mbar_init();
 	__syncthreads();
 
@@ -294,13 +302,10 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	stamp(a.stamps, kStB1);
 
 	// ------------------------------------------------ P1: routing
-	// softmax + top-k of token t by warp 0 of CTA t (t < T); the others
-	// start the L2 prefetch of their first gate/up items
+	// softmax + top-k of token t by warp 0 of CTA t (t < T)
 	{
 		float *lg = reinterpret_cast<float *>(smem);                 // [NE]
 		float *sel = lg + kMaxActive;                                // [2K]
-		if (warp == kProducerWarp)
-			prefetch_gate_up<QT>(a, lane);
 		for (int t = blockIdx.x; t < T; t += gridDim.x) {
 			if (warp == 0) {
 				for (int e = lane; e < NE; e += 32)
@@ -338,7 +343,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		if (warp == 0)
 			build_prefix_warp(en, n_active, (F + 7) / 8, pre_gu);
 		if (warp == 1)
-			build_prefix_warp(en, n_active, (D + 15) / 16, pre_dn);
+			build_prefix_warp(en, n_active, (D + 16 * MT_DN - 1) / (16 * MT_DN), pre_dn);
 		if (blockIdx.x == 0) {
 			// the routing, for the host (moe_layer_routing)
 			for (int i = tid; i < T * K; i += blockDim.x)
@@ -369,10 +374,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		Pipe pipe;
 		if (warp == kProducerWarp) {
 			core_producer<QT, true, STAGES, WB_GU>(gu, smem, b, pipe, lane);
-			core_producer<QT, false, STAGES, WB_DN>(dn, smem, b, pipe, lane);
+			core_producer<QT, false, STAGES, WB_DN, MT_DN>(dn, smem, b, pipe, lane);
 		} else {
 			if (warp >= kEpiWarp0)
-				core_epilogue<QT, true>(gu, red, b, pipe, warp - kEpiWarp0, lane);
+				core_epilogue<QT, true>(gu, red, stg + (warp - kEpiWarp0) * kEpiStage, b, pipe,
+							warp - kEpiWarp0, lane);
 			else
 				core_math<QT, true, STAGES, WB_GU, true>(gu, smem, red, ssum, b, pipe, warp, lane);
 			// every CTA's h rows must be written before any CTA reads them
@@ -383,9 +389,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			bar_math_epi();
 			stamp(a.stamps, kStB2);
 			if (warp >= kEpiWarp0)
-				core_epilogue<QT, false>(dn, red, b, pipe, warp - kEpiWarp0, lane);
+				core_epilogue<QT, false, MT_DN>(dn, red, stg + (warp - kEpiWarp0) * kEpiStage, b,
+								pipe, warp - kEpiWarp0, lane);
 			else
-				core_math<QT, false, STAGES, WB_DN, true>(dn, smem, red, ssum, b, pipe, warp, lane);
+				core_math<QT, false, STAGES, WB_DN, true, MT_DN>(dn, smem, red, ssum, b, pipe, warp,
+									  lane);
 		}
 	}
 	__syncthreads();
@@ -422,11 +430,10 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr_t x,
 		      uintptr_t router_w, uintptr_t out)
 {
-	const int wb_dn = pick_wb(F);
+	const Shape dn = pick_shape(F, false);
 	return (qtype == kQ8_0 || qtype == kQ4_0) && T >= 1 && T <= kDecodeMaxT &&
 	       T * K <= kDecodeMaxPairs && K >= 1 && K <= 32 && NE % 8 == 0 && NE <= kMaxActive &&
-	       D % 2048 == 0 && (wb_dn == 8 || wb_dn == 4) && x % 16 == 0 && router_w % 16 == 0 &&
-	       out % 16 == 0;
+	       D % 2048 == 0 && dn.wb == 8 && x % 16 == 0 && router_w % 16 == 0 && out % 16 == 0;
 }
 
 int decode_stamps() { return kStamps; }
@@ -440,15 +447,16 @@ void decode_stage_ends(int *ends)
 		ends[i] = e[i];
 }
 
-template <int QT, int LANES, int WB_DN>
+// MT_DN: m-tiles per down item (2 for d_ff = 1024, else 1)
+template <int QT, int LANES, int MT_DN>
 static cudaError_t launch_decode_t(const DecodeArgs &a, cudaStream_t st)
 {
 	constexpr int STAGES = QT == kQ8_0 ? 5 : 9;
 	constexpr size_t smem = decode_smem_bytes<QT, STAGES>();
 	static_assert(smem <= 227 * 1024, "fused decode kernel exceeds shared memory");
-	static_assert(RTile<LANES>::NSLOT * RTile<LANES>::SLOT <= STAGES * StageLayout<QT>::BYTES,
-		      "router slots fit in the stage ring");
-	auto fn = moe_decode_kernel<QT, LANES, 8, WB_DN, STAGES>;
+	static_assert(RTile<LANES>::BYTES <= STAGES * StageLayout<QT>::BYTES,
+		      "the router tile fits in the stage ring");
+	auto fn = moe_decode_kernel<QT, LANES, 8, 8, MT_DN, STAGES>;
 	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
@@ -467,16 +475,16 @@ static cudaError_t launch_decode_t(const DecodeArgs &a, cudaStream_t st)
 
 cudaError_t launch_decode_layer(const DecodeArgs &a, int qtype, int lanes, cudaStream_t st)
 {
-	const int wb_dn = pick_wb(a.F);
+	const bool mt2 = pick_shape(a.F, false).mt == 2;
 	const bool l16 = lanes != 8;
 	if (qtype == kQ8_0) {
-		if (wb_dn == 8)
-			return l16 ? launch_decode_t<kQ8_0, 16, 8>(a, st) : launch_decode_t<kQ8_0, 8, 8>(a, st);
-		return l16 ? launch_decode_t<kQ8_0, 16, 4>(a, st) : launch_decode_t<kQ8_0, 8, 4>(a, st);
+		if (mt2)
+			return l16 ? launch_decode_t<kQ8_0, 16, 2>(a, st) : launch_decode_t<kQ8_0, 8, 2>(a, st);
+		return l16 ? launch_decode_t<kQ8_0, 16, 1>(a, st) : launch_decode_t<kQ8_0, 8, 1>(a, st);
 	}
-	if (wb_dn == 8)
-		return l16 ? launch_decode_t<kQ4_0, 16, 8>(a, st) : launch_decode_t<kQ4_0, 8, 8>(a, st);
-	return l16 ? launch_decode_t<kQ4_0, 16, 4>(a, st) : launch_decode_t<kQ4_0, 8, 4>(a, st);
+	if (mt2)
+		return l16 ? launch_decode_t<kQ4_0, 16, 2>(a, st) : launch_decode_t<kQ4_0, 8, 2>(a, st);
+	return l16 ? launch_decode_t<kQ4_0, 16, 1>(a, st) : launch_decode_t<kQ4_0, 8, 1>(a, st);
 }
 
 }  // namespace moe

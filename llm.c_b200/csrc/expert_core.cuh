@@ -50,6 +50,7 @@ constexpr int kEpiWarps = 2;
 constexpr int kProducerWarp = kMmaWarps;
 constexpr int kEpiWarp0 = kMmaWarps + 1;
 constexpr int kCoreThreads = (kMmaWarps + 1 + kEpiWarps) * 32;
+constexpr int kEpiStage = 8 * 32;  // floats of staging per epilogue warp
 constexpr int kMaxActive = 256;              // experts per layer (routing tables)
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bounded waits: 2 s
@@ -147,12 +148,6 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 		"cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
 		::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
 		: "memory");
-}
-
-// hint: bring [src, src + bytes) into L2 (no completion to wait for)
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes)
-{
-	asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -339,6 +334,11 @@ struct StageLayout {
 	static constexpr int BYTES = 16 * RS;                    // one stage
 	static constexpr int RED = kRedBufs * kMmaWarps * 32 * 16;
 	static constexpr int SSUM = kMmaWarps * 8 * 8 * 4;  // per warp [8 blocks][8 tokens] f32
+	static constexpr int EPI = kEpiWarps * kEpiStage * 4;  // epilogue staging tiles
+	// two 1024-column rows share one row slot (items of two m-tiles): the
+	// second starts here (16-byte aligned for the copy, 8 for the loads)
+	static constexpr int HALF = 1024 / QK * BB + 16;
+	static_assert(HALF + 1024 / QK * BB <= RS && HALF % 16 == 0, "two half rows per slot");
 };
 
 // One grouped matrix pass (gate/up with SwiGLU, or down).
@@ -446,13 +446,15 @@ __device__ __forceinline__ void item_range(const int32_t *en, const int32_t *pre
 }
 
 // ---------------------------------------------------------------- producer
-template <int QT, bool DUAL, int STAGES, int WB>
+template <int QT, bool DUAL, int STAGES, int WB, int MT = 1>
 __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, Pipe &p, int lane)
 {
 	using SL = StageLayout<QT>;
 	constexpr int BB = SL::BB, RS = SL::RS;
-	constexpr int ROWS = DUAL ? 8 : 16;
-	constexpr int KC = WB * kMmaWarps * QK;
+	constexpr int ROWS = DUAL ? 8 : 16 * MT;
+	constexpr int COPY_ROWS = DUAL ? 16 : 16 * MT;  // weight rows per stage
+	constexpr int KC = WB * (kMmaWarps / MT) * QK;
+	static_assert(MT == 1 || (MT == 2 && !DUAL && KC == 1024), "two m-tiles: 1024-column rows");
 	constexpr uint32_t cb = (uint32_t)(KC / QK * BB);  // bytes per row and stage
 	const int groups = (ph.rows + ROWS - 1) / ROWS;
 	const int nch = ph.cols / KC;
@@ -468,7 +470,7 @@ __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, P
 		for (int tg = 0; tg < n; tg += kTokTile)
 		for (int item = seg; item < seg_end; item++) {
 			const int r0 = (item - ai * groups) * ROWS;
-			// lane l (< 16) copies tile row l
+			// lane l (< COPY_ROWS) copies tile row l
 			const int r = DUAL ? r0 + (lane & 7) : r0 + lane;
 			const uint8_t *src = base + (int64_t)min(r, ph.rows - 1) * rb;
 			for (int ch = 0; ch < nch; ch++, p.it++) {
@@ -482,12 +484,14 @@ __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, P
 				if (p.failed)
 					continue;
 				if (lane == 0)
-					mbar_arrive_expect_tx(&b.full[st], 16 * cb);
+					mbar_arrive_expect_tx(&b.full[st], COPY_ROWS * cb);
 				__syncwarp();
-				if (lane < 16) {
+				if (lane < COPY_ROWS) {
+					// m-tile 1 of a two-tile item goes to the second half of the slot
+					const int dst = MT == 2 ? (lane & 15) * RS + (lane >> 4) * SL::HALF : lane * RS;
 					fence_proxy_async();
-					bulk_g2s(stages + st * SL::BYTES + lane * RS,
-						 src + (int64_t)ch * (KC / QK) * BB, cb, &b.full[st]);
+					bulk_g2s(stages + st * SL::BYTES + dst, src + (int64_t)ch * (KC / QK) * BB, cb,
+						 &b.full[st]);
 				}
 			}
 		}
@@ -496,11 +500,14 @@ __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, P
 }
 
 // ---------------------------------------------------------------- epilogue
-template <int QT, bool DUAL>
-__device__ void core_epilogue(const Phase &ph, const float4 *red, const Bars &b, Pipe &p, int epi,
-			      int lane)
+// stg: this warp's staging tile (kEpiStage floats): the sums are written
+// there in MMA order and leave as contiguous 16-byte stores per token row.
+template <int QT, bool DUAL, int MT = 1>
+__device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, const Bars &b,
+			      Pipe &p, int epi, int lane)
 {
-	constexpr int ROWS = DUAL ? 8 : 16;
+	constexpr int ROWS = DUAL ? 8 : 16 * MT;
+	constexpr int KW = kMmaWarps / MT;  // warps (K slices) per m-tile
 	const int groups = (ph.rows + ROWS - 1) / ROWS;
 	int i0, i1;
 	item_range(ph.en, ph.pre, ph.n_active, groups, i0, i1);
@@ -523,43 +530,87 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, const Bars &b,
 				const float *rv = reinterpret_cast<const float *>(red + buf * kMmaWarps * 32);
 				// DUAL: 64 outputs (lane l of the MMA layout, token slot j),
 				// gate = value j and up = value 2+j of that lane; 2 per thread.
-				// Single: 128 outputs (lane l, value i); 4 per thread.
+				// Single: 128 outputs per m-tile (lane l, value i); 4 per thread
+				// and m-tile, the K-slice partials added in warp order.
 #pragma unroll
-				for (int q = 0; q < (DUAL ? 2 : 4); q++) {
+				for (int q = 0; q < (DUAL ? 2 : 4 * MT); q++) {
 					const int o = lane + 32 * q;
-					const int l = DUAL ? o >> 1 : o >> 2;
+					const int m = DUAL ? 0 : o >> 7;  // m-tile
+					const int l = DUAL ? o >> 1 : (o & 127) >> 2;
 					const int i = DUAL ? (o & 1) : (o & 3);
 					float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
-					for (int w = 0; w < kMmaWarps; w++) {
-						s0 = __fadd_rn(s0, rv[(w * 32 + l) * 4 + i]);
+					for (int w = 0; w < KW; w++) {
+						s0 = __fadd_rn(s0, rv[((m * KW + w) * 32 + l) * 4 + i]);
 						if (DUAL)
 							s1 = __fadd_rn(s1, rv[(w * 32 + l) * 4 + 2 + i]);
 					}
 					const int gg = l >> 2, cc = l & 3;
-					const int t = tg + 2 * cc + (i & 1);
-					if (t >= n)
-						continue;
-					const int pos = off + t;
+					const int tt = 2 * cc + (i & 1);  // token slot in the pass
+					const int t = tg + tt;
+					const int pos = off + (t < n ? t : 0);
 					if (DUAL) {
-						const int r = r0 + gg;
-						if (r < ph.rows) {
-							const float h = swiglu(s0, s1);
-							const __half hh = __float2half_rn(h);
-							const __half hl = __float2half_rn(__fsub_rn(h, __half2float(hh)));
+						// h = silu(gate) * up, stored as fp16 hi + lo
+						const float h = swiglu(s0, s1);
+						const __half hh = __float2half_rn(h);
+						const __half hl = __float2half_rn(__fsub_rn(h, __half2float(hh)));
+						if (QT == kQ8_0) {
+							__half *st16 = reinterpret_cast<__half *>(stg);
+							st16[tt * 16 + gg] = hh;       // [token][hi 8 | lo 8]
+							st16[tt * 16 + 8 + gg] = hl;
+						} else if (t < n && r0 + gg < ph.rows) {
+							const int r = r0 + gg;
 							__half *o16 = ph.out16 + (int64_t)pos * 2 * ph.rows;
-							const int slot_r = QT == kQ4_0 ? q4_slot(r) : r;
-							o16[slot_r] = hh;
-							o16[ph.rows + slot_r] = hl;
+							o16[q4_slot(r)] = hh;
+							o16[ph.rows + q4_slot(r)] = hl;
 						}
 					} else {
-						const int r = r0 + gg + 8 * (i >> 1);
+						// the combine's division (olmoe.c:397-404: y / (1 / w)),
+						// done here where y is produced
 						const int orow = ph.out_perm ? ph.perm[pos] : pos;
-						// the combine's division (olmoe.c:397-404:
-						// y / (1 / w)), done here where y is produced
-						const float v = ph.wdiv ? __fdiv_rn(s0, __fdiv_rn(1.0f, ph.wdiv[orow])) : s0;
-						if (r < ph.rows)
-							ph.out[(int64_t)orow * ph.rows + r] = v;
+						const float v =
+							ph.wdiv ? __fdiv_rn(s0, __fdiv_rn(1.0f, ph.wdiv[orow])) : s0;
+						stg[tt * ROWS + 16 * m + gg + 8 * (i >> 1)] = v;  // [token][row]
+					}
+				}
+				__syncwarp();
+				// rows of this item that exist, and whether 16-byte stores line up
+				const int nr = min(ROWS, ph.rows - r0);
+				if (DUAL && QT == kQ8_0) {
+					// 8 tokens x (8 hi, 8 lo) halves: lane -> (token, hi|lo)
+					if (lane < 16) {
+						const int tt = lane >> 1, t = tg + tt;
+						if (t < n) {
+							const __half *src = reinterpret_cast<const __half *>(stg) + lane * 8;
+							__half *o16 = ph.out16 + (int64_t)(off + t) * 2 * ph.rows +
+								      (lane & 1) * ph.rows + r0;
+							if (nr == 8 && ph.rows % 8 == 0)
+								*reinterpret_cast<uint4 *>(o16) =
+									*reinterpret_cast<const uint4 *>(src);
+							else
+								for (int r = 0; r < nr; r++)
+									o16[r] = src[r];
+						}
+					}
+				} else if (!DUAL) {
+					// 8 tokens x ROWS rows: lane -> (token, ROWS/4 consecutive rows)
+					constexpr int PER = ROWS / 4;
+					const int tt = lane >> 2, t = tg + tt;
+					if (t < n) {
+						const int pos = off + t;
+						const int orow = ph.out_perm ? ph.perm[pos] : pos;
+						const int rr = (lane & 3) * PER;
+						float *dst = ph.out + (int64_t)orow * ph.rows + r0 + rr;
+						const float *src = stg + tt * ROWS + rr;
+						if (nr == ROWS && ph.rows % 4 == 0) {
+#pragma unroll
+							for (int v = 0; v < PER; v += 4)
+								*reinterpret_cast<float4 *>(dst + v) =
+									*reinterpret_cast<const float4 *>(src + v);
+						} else {
+							for (int v = 0; v < PER && rr + v < nr; v++)
+								dst[v] = src[v];
+						}
 					}
 				}
 			}
@@ -575,15 +626,17 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, const Bars &b,
 // COHERENT: the activations were written earlier in the same kernel by
 // other CTAs, so they are read through L2 (ld.global.cg), not the
 // read-only path.
-template <int QT, bool DUAL, int STAGES, int WB, bool COHERENT>
+template <int QT, bool DUAL, int STAGES, int WB, bool COHERENT, int MT = 1>
 __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, float *ssum,
 			  const Bars &b, Pipe &p, int warp, int lane)
 {
 	constexpr bool FAST = WB % 4 == 0;  // biased fragments, aligned code loads
 	using SL = StageLayout<QT>;
 	constexpr int BB = SL::BB, RS = SL::RS;
-	constexpr int ROWS = DUAL ? 8 : 16;
-	constexpr int KC = WB * kMmaWarps * QK;
+	constexpr int ROWS = DUAL ? 8 : 16 * MT;
+	constexpr int KW = kMmaWarps / MT;  // K slices; warp = (m-tile, K slice)
+	constexpr int KC = WB * KW * QK;
+	const int mt = warp / KW, kq = warp % KW;
 	const int groups = (ph.rows + ROWS - 1) / ROWS;
 	const int cols = ph.cols;
 	const int nch = cols / KC;
@@ -600,7 +653,7 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, f
 		for (int item = seg; item < seg_end; item++, p.pass++) {
 			float acc[4] = {0.f, 0.f, 0.f, 0.f};
 			for (int ch = 0; ch < nch; ch++, p.it++) {
-				const int kb0 = ch * (KC / QK) + warp * WB;  // first block (row-global)
+				const int kb0 = ch * (KC / QK) + kq * WB;  // first block (row-global)
 				if (e != x_e || tg != x_tg || ch != x_ch) {
 					// token tg+g's activations for this warp's blocks; columns of
 					// tokens past n read the segment's first token (never stored)
@@ -651,7 +704,8 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, f
 						atomicExch(ph.err, 2);
 				}
 				if (!p.failed) {
-					const uint8_t *wt = stages + st * SL::BYTES + (warp * WB) * BB;
+					const uint8_t *wt =
+						stages + st * SL::BYTES + (kq * WB) * BB + (MT == 2 ? mt * SL::HALF : 0);
 					if constexpr (FAST) {
 						constexpr float BIAS = Bias<QT>::value;
 						const float *sw = ssum + warp * WB * 8 + 2 * c;
@@ -727,15 +781,24 @@ __device__ __forceinline__ Bars init_bars(uint64_t *base)
 	return b;
 }
 
-// blocks per math warp per stage: 8 (2048-column stages) when cols is a
-// multiple of 2048, else cols/256 if that is 1, 2 or 4 (one stage per row)
-__host__ __device__ inline int pick_wb(int cols)
+// Stage shape of a matrix pass: WB blocks per math warp, MT m-tiles per
+// item.  2048-column stages when cols is a multiple of 2048; a single
+// 1024-column matrix takes two m-tiles per item (32 rows, four K slices)
+// so that a stage still holds 16 slots of weights; else cols/256 blocks
+// per warp for 256/512/1024 columns.  {0, 0}: not supported.
+struct Shape {
+	int wb, mt;
+};
+
+__host__ __device__ inline Shape pick_shape(int cols, bool dual)
 {
 	if (cols % 2048 == 0)
-		return 8;
+		return {8, 1};
+	if (cols == 1024 && !dual)
+		return {8, 2};
 	if (cols == 1024 || cols == 512 || cols == 256)
-		return cols / 256;
-	return 0;
+		return {cols / 256, 1};
+	return {0, 0};
 }
 
 }  // namespace moe

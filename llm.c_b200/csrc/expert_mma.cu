@@ -7,24 +7,25 @@
 
 namespace moe {
 
-template <int QT, bool DUAL, int STAGES, int WB>
+template <int QT, bool DUAL, int STAGES, int WB, int MT>
 __global__ void __launch_bounds__(kCoreThreads, 1) expert_mma_kernel(MmaArgs a)
 {
-	// WB = blocks per math warp per stage (KC = 256*WB columns); the
-	// launcher guarantees cols % KC == 0
+	// WB = blocks per math warp per stage, MT = m-tiles per item (see
+	// pick_shape); the launcher guarantees cols % KC == 0
 	extern __shared__ __align__(128) uint8_t smem[];
 	using SL = StageLayout<QT>;
 	uint8_t *p = smem + STAGES * SL::BYTES;
 	float4 *red = reinterpret_cast<float4 *>(p);                   // [kRedBufs][8][32]
 	float *ssum = reinterpret_cast<float *>(p + SL::RED);           // activation block sums
-	int32_t *en = reinterpret_cast<int32_t *>(p + SL::RED + SL::SSUM);  // [256]
+	float *stg = reinterpret_cast<float *>(p + SL::RED + SL::SSUM); // epilogue staging
+	int32_t *en = reinterpret_cast<int32_t *>(p + SL::RED + SL::SSUM + SL::EPI);  // [256]
 	int32_t *off = en + kMaxActive;                                 // [256]
 	int32_t *pre = off + kMaxActive;                                // [257]
 	uint64_t *bars = reinterpret_cast<uint64_t *>(pre + kMaxActive + 4);
 	const Bars b = init_bars<STAGES>(bars);
 	// routing tables of the active experts, read once per CTA
 	const int n_active = *a.n_active;
-	constexpr int ROWS = DUAL ? 8 : 16;
+	constexpr int ROWS = DUAL ? 8 : 16 * MT;
 	const int groups = (a.rows + ROWS - 1) / ROWS;
 	for (int i = threadIdx.x; i < n_active; i += blockDim.x) {
 		const int e = a.active[i];
@@ -42,11 +43,12 @@ __global__ void __launch_bounds__(kCoreThreads, 1) expert_mma_kernel(MmaArgs a)
 	Pipe pipe;
 	const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 	if (warp == kProducerWarp)
-		core_producer<QT, DUAL, STAGES, WB>(ph, smem, b, pipe, lane);
+		core_producer<QT, DUAL, STAGES, WB, MT>(ph, smem, b, pipe, lane);
 	else if (warp >= kEpiWarp0)
-		core_epilogue<QT, DUAL>(ph, red, b, pipe, warp - kEpiWarp0, lane);
+		core_epilogue<QT, DUAL, MT>(ph, red, stg + (warp - kEpiWarp0) * kEpiStage, b, pipe,
+					    warp - kEpiWarp0, lane);
 	else
-		core_math<QT, DUAL, STAGES, WB, false>(ph, smem, red, ssum, b, pipe, warp, lane);
+		core_math<QT, DUAL, STAGES, WB, false, MT>(ph, smem, red, ssum, b, pipe, warp, lane);
 }
 
 // ---------------------------------------------------------------- x -> fp16 hi/lo
@@ -81,13 +83,14 @@ cudaError_t launch_split_f16(const float *x, int64_t rows, int cols, int qtype, 
 	return cudaGetLastError();
 }
 
-template <int QT, bool DUAL, int STAGES, int WB>
+template <int QT, bool DUAL, int STAGES, int WB, int MT>
 static cudaError_t launch_t(const MmaArgs &a, cudaStream_t st)
 {
 	using SL = StageLayout<QT>;
-	const size_t smem = (size_t)STAGES * SL::BYTES + SL::RED + SL::SSUM + (3 * kMaxActive + 4) * 4 +
+	const size_t smem = (size_t)STAGES * SL::BYTES + SL::RED + SL::SSUM + SL::EPI +
+			    (3 * kMaxActive + 4) * 4 +
 			    (2 * STAGES + 2 * kRedBufs) * 8;
-	auto fn = expert_mma_kernel<QT, DUAL, STAGES, WB>;
+	auto fn = expert_mma_kernel<QT, DUAL, STAGES, WB, MT>;
 	constexpr int threads = kCoreThreads;
 	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
@@ -104,7 +107,7 @@ static cudaError_t launch_t(const MmaArgs &a, cudaStream_t st)
 	}
 	const int sms = sm_count();
 	int64_t grid = (int64_t)sms * per_sm;
-	const int rows_per_item = DUAL ? 8 : 16;
+	const int rows_per_item = DUAL ? 8 : 16 * MT;
 	const int64_t max_items = (int64_t)a.n_local * ((a.rows + rows_per_item - 1) / rows_per_item);
 	if (grid > max_items)
 		grid = max_items;
@@ -114,17 +117,20 @@ static cudaError_t launch_t(const MmaArgs &a, cudaStream_t st)
 
 bool expert_mma_supported(int qtype, int cols)
 {
-	return (qtype == kQ8_0 || qtype == kQ4_0) && pick_wb(cols) > 0;
+	return (qtype == kQ8_0 || qtype == kQ4_0) && pick_shape(cols, true).wb > 0;
 }
 
 template <int QT, bool DUAL, int S>
 static cudaError_t launch_wb(const MmaArgs &a, cudaStream_t st)
 {
-	switch (pick_wb(a.cols)) {
-	case 8: return launch_t<QT, DUAL, S, 8>(a, st);
-	case 4: return launch_t<QT, DUAL, S, 4>(a, st);
-	case 2: return launch_t<QT, DUAL, S, 2>(a, st);
-	case 1: return launch_t<QT, DUAL, S, 1>(a, st);
+	const Shape sh = pick_shape(a.cols, DUAL);
+	if (!DUAL && sh.mt == 2)
+		return launch_t<QT, DUAL, S, 8, DUAL ? 1 : 2>(a, st);
+	switch (sh.wb) {
+	case 8: return launch_t<QT, DUAL, S, 8, 1>(a, st);
+	case 4: return launch_t<QT, DUAL, S, 4, 1>(a, st);
+	case 2: return launch_t<QT, DUAL, S, 2, 1>(a, st);
+	case 1: return launch_t<QT, DUAL, S, 1, 1>(a, st);
 	default: return cudaErrorInvalidValue;
 	}
 }

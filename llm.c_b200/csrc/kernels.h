@@ -101,12 +101,13 @@ struct DecodeArgs {
 	float *wts;                // [T*K]
 	int32_t *counts, *offsets, *perm, *active, *n_active;
 	int32_t *err;              // 0 ok, 2 bounded mbarrier wait expired, 3 grid barrier expired
-	unsigned long long *gbar;  // grid barrier arrivals, zero when allocated
+	unsigned long long *gbar;  // grid barrier state (decode_barrier_bytes), zero when allocated
 	uint64_t *stamps;          // NULL or [grid][decode_stamps()] phase times (ns)
 };
 bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr_t x,
 		      uintptr_t router_w, uintptr_t out);
 int decode_stamps();
+size_t decode_barrier_bytes(int ctas);
 void decode_stage_ends(int *ends);
 cudaError_t launch_decode_layer(const DecodeArgs &a, int qtype, int lanes, cudaStream_t st);
 

@@ -74,47 +74,112 @@ static __device__ __noinline__ void topk_token_j(const float *__restrict__ lr, c
 				probs_out[lane + 32 * j] = v[j];
 		}
 
-	// rank of every element, all at once: element i's rank counts the
-	// elements ahead of it by (value desc, index asc).  Reference mode:
-	// nn.c:276-308 seeds all k slots with element 0, which equals ranking
-	// [p0 (k copies), p1, p2, ...] by (value desc, position asc): element
-	// i >= 1 starts behind the k copies when p0 >= p_i, and element 0 fills
-	// slots r0 .. k-1 where r0 = #{j >= 1 : p_j > p0}.  Slot = K-1-rank.
+	// Reference mode: nn.c:276-308 seeds all k slots with element 0, which
+	// equals ranking [p0 (k copies), p1, p2, ...] by (value desc, position
+	// asc): the result is, in rank order, the elements ahead of element 0 in
+	// the (value desc, index asc) order (at most k of them), then copies of
+	// element 0 (weight p0).  Exact mode: the first k of that order.
+	// Slot of rank r = K-1-r.
 	const float p0 = __shfl_sync(FULL, v[0], 0);
-	int rank[MAXJ];
+	if constexpr (MAXJ == 2) {
+		// NE <= 64: bitonic sort of the 64 (value, index) keys, descending,
+		// positions lane and lane + 32 (padding sorts last)
+		float kv[2];
+		int ki[2];
 #pragma unroll
-	for (int j = 0; j < MAXJ; j++)
-		rank[j] = (!mode_exact && p0 >= v[j]) ? K : 0;
-	int r0 = 0;  // reference mode, element 0 (lane 0)
-	// Every shuffle is unconditional (a shuffle under a branch costs a
-	// reconvergence barrier); validity enters as predicates.
-#pragma unroll 8
-	for (int l = 0; l < 32; l++) {
-#pragma unroll
-		for (int jj = 0; jj < MAXJ; jj++) {
-			const float o = __shfl_sync(FULL, v[jj], l);
-			const int eo = l + 32 * jj;
-			const bool cand = eo < NE && (mode_exact || eo != 0);
-#pragma unroll
-			for (int j = 0; j < MAXJ; j++) {
-				const int e = lane + 32 * j;
-				rank[j] += cand && (o > v[j] || (o == v[j] && eo < e));
-			}
-			r0 += eo < NE && eo != 0 && o > p0;
+		for (int s = 0; s < 2; s++) {
+			ki[s] = lane + 32 * s;
+			kv[s] = ki[s] < NE ? v[s] : -1.0f;
 		}
-	}
+		auto first = [](float va, int ia, float vb, int ib) {  // a ahead of b
+			return va > vb || (va == vb && ia < ib);
+		};
+		// rolled loops: this code runs once per token and mostly with a cold
+		// instruction cache, so it is kept short
+#pragma unroll 1
+		for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll 1
+			for (int j = k >> 1; j > 0; j >>= 1) {
+				if (j == 32) {
+					// both positions of the pair live in this lane; the block
+					// (k = 64) is descending
+					if (!first(kv[0], ki[0], kv[1], ki[1])) {
+						const float tv = kv[0];
+						const int ti = ki[0];
+						kv[0] = kv[1];
+						ki[0] = ki[1];
+						kv[1] = tv;
+						ki[1] = ti;
+					}
+				} else {
 #pragma unroll
-	for (int j = 0; j < MAXJ; j++) {
-		const int e = lane + 32 * j;
-		if (j >= nj || e >= NE) {
-		} else if (!mode_exact && e == 0) {
-			for (int c = r0; c < K; c++) {
-				sid[K - 1 - c] = 0;
-				sw[K - 1 - c] = p0;
+					for (int s = 0; s < 2; s++) {
+						const int pos = lane + 32 * s;
+						const float ov = __shfl_xor_sync(FULL, kv[s], j);
+						const int oi = __shfl_xor_sync(FULL, ki[s], j);
+						const bool desc = (pos & k) == 0;     // block direction
+						const bool lower = (pos & j) == 0;    // lower position of the pair
+						const bool mine_first = first(kv[s], ki[s], ov, oi);
+						if (mine_first != (lower == desc)) {
+							kv[s] = ov;
+							ki[s] = oi;
+						}
+					}
+				}
 			}
-		} else if (rank[j] < K) {
-			sid[K - 1 - rank[j]] = e;
-			sw[K - 1 - rank[j]] = v[j];
+		}
+		// rank r sits in lane r (s = 0) for r < 32; element 0's rank q
+		const unsigned at0 = __ballot_sync(FULL, ki[0] == 0), at1 = __ballot_sync(FULL, ki[1] == 0);
+		const int q = at0 ? __ffs(at0) - 1 : 32 + __ffs(at1) - 1;
+#pragma unroll
+		for (int s = 0; s < 2; s++) {
+			const int rk = lane + 32 * s;  // rank held here
+			if (rk < K) {
+				const bool copy0 = !mode_exact && rk >= q;
+				sid[K - 1 - rk] = copy0 ? 0 : ki[s];
+				sw[K - 1 - rk] = copy0 ? p0 : kv[s];
+			}
+		}
+	} else {
+		// rank of every element, all at once: element i's rank counts the
+		// elements ahead of it by (value desc, index asc); in reference mode
+		// element i >= 1 starts behind the k copies when p0 >= p_i, and
+		// element 0 fills slots r0 .. k-1 where r0 = #{j >= 1 : p_j > p0}.
+		int rank[MAXJ];
+#pragma unroll
+		for (int j = 0; j < MAXJ; j++)
+			rank[j] = (!mode_exact && p0 >= v[j]) ? K : 0;
+		int r0 = 0;  // reference mode, element 0 (lane 0)
+		// Every shuffle is unconditional (a shuffle under a branch costs a
+		// reconvergence barrier); validity enters as predicates.
+#pragma unroll 8
+		for (int l = 0; l < 32; l++) {
+#pragma unroll
+			for (int jj = 0; jj < MAXJ; jj++) {
+				const float o = __shfl_sync(FULL, v[jj], l);
+				const int eo = l + 32 * jj;
+				const bool cand = eo < NE && (mode_exact || eo != 0);
+#pragma unroll
+				for (int j = 0; j < MAXJ; j++) {
+					const int e = lane + 32 * j;
+					rank[j] += cand && (o > v[j] || (o == v[j] && eo < e));
+				}
+				r0 += eo < NE && eo != 0 && o > p0;
+			}
+		}
+#pragma unroll
+		for (int j = 0; j < MAXJ; j++) {
+			const int e = lane + 32 * j;
+			if (j >= nj || e >= NE) {
+			} else if (!mode_exact && e == 0) {
+				for (int c = r0; c < K; c++) {
+					sid[K - 1 - c] = 0;
+					sw[K - 1 - c] = p0;
+				}
+			} else if (rank[j] < K) {
+				sid[K - 1 - rank[j]] = e;
+				sw[K - 1 - rank[j]] = v[j];
+			}
 		}
 	}
 	__syncwarp();

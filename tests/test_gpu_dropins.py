@@ -82,3 +82,17 @@ def test_invalid_arguments_fail_cleanly(moe, orc):
         moe.Layer(256, 128, 300, 4, 1, np.zeros((300, 256), np.float32),
                   np.zeros((300, 128, 272), np.uint8), np.zeros((300, 128, 272), np.uint8),
                   np.zeros((300, 256, 136), np.uint8))
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("rows,cols", [(100, 1024), (37, 2048), (8200, 1024)])
+@pytest.mark.parametrize("m", [1, 5])
+def test_gemv_partial_row_tiles(moe, orc, qt, rows, cols, m):
+    """row counts that end inside a 16- or 32-row tile: the last tile's
+    missing rows are neither computed into nor stored"""
+    w = orc.quantize(qt, orc.gauss(41, 7, rows * cols, 0.02).reshape(rows, cols))
+    x = orc.gauss(41, 8, m * cols, 1.0).reshape(m, cols)
+    ref = orc.gemm_q(x, w, qt, rows)
+    got = moe.gemv(w, qt, rows, cols, x)
+    assert got.shape == ref.shape
+    assert_output_close(got, ref)
