@@ -106,29 +106,35 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- ours
-def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream):
+def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=None):
     """NL device-resident layers generated on the GPU (generator tags: router
-    1, gate 2, up 3, down 4; layer l uses seed seed0 + l)."""
+    1, gate 2, up 3, down 4; layer l uses seed seed0 + l).  Expert parallelism:
+    only experts [first, first + n_local) are generated and held here, with
+    the same values as in the full layer."""
     import torch
+    n_local = NE if n_local is None else n_local
     rb_d = moe.row_bytes(qtype, d)
     rb_f = moe.row_bytes(qtype, F)
     layers, keep = [], []
-    tmp = torch.empty(NE * F * d, dtype=torch.float32, device="cuda")
+    tmp = torch.empty(n_local * F * d, dtype=torch.float32, device="cuda")
     for l in range(nl):
         seed = seed0 + l
         wr = torch.empty(NE * d, dtype=torch.float32, device="cuda")
         moe.check(moe.lib().moe_synth_gauss(wr.data_ptr(), seed, 1, 0, NE * d, 0.02, stream))
         mats = []
         for tag, rows, cols, rb in ((2, F, d, rb_d), (3, F, d, rb_d), (4, d, F, rb_f)):
-            q = torch.empty(NE * rows * rb, dtype=torch.uint8, device="cuda")
-            moe.check(moe.lib().moe_synth_gauss(tmp.data_ptr(), seed, tag, 0, NE * rows * cols,
-                                                0.02, stream))
-            moe.check(moe.lib().moe_quantize_device(tmp.data_ptr(), NE * rows, cols, qtype,
+            q = torch.empty(n_local * rows * rb, dtype=torch.uint8, device="cuda")
+            moe.check(moe.lib().moe_synth_gauss(tmp.data_ptr(), seed, tag, first * rows * cols,
+                                                n_local * rows * cols, 0.02, stream))
+            moe.check(moe.lib().moe_quantize_device(tmp.data_ptr(), n_local * rows, cols, qtype,
                                                     q.data_ptr(), stream))
             mats.append(q)
         torch.cuda.synchronize()
-        ptrs = [[m.data_ptr() + e * (m.numel() // NE) for e in range(NE)] for m in mats]
-        lay = moe.Layer(d, F, NE, K, qtype, wr.data_ptr(), ptrs[0], ptrs[1], ptrs[2])
+        ptrs = [[m.data_ptr() + (e - first) * rows_b if first <= e < first + n_local else 0
+                 for e in range(NE)]
+                for m, rows_b in zip(mats, (F * rb_d, F * rb_d, d * rb_f))]
+        lay = moe.Layer(d, F, NE, K, qtype, wr.data_ptr(), ptrs[0], ptrs[1], ptrs[2],
+                        first_expert=first, n_local=n_local)
         layers.append(lay)
         keep.append((wr, mats))
     del tmp
@@ -154,10 +160,21 @@ def run_ours(args, rank, world, local_rank):
     d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
     T = args.tokens
     NL = args.layers
-    layers, keep = build_layers(moe, NL, 0, d, F, NE, K, qtype, stream)
-    # tokens: config-0 input seed 0, tag 5 (rank r uses element offset r*T*d)
+    # N > 1: expert parallelism, rank r holds experts expert_range(r) of every
+    # layer; the tokens are the same on every rank (replicated, as after a
+    # replicated attention block) and every rank ends with the full output
+    first, n_local = moe.expert_range(rank, world, NE)
+    layers, keep = build_layers(moe, NL, 0, d, F, NE, K, qtype, stream, first, n_local)
+    if world > 1:
+        def gather(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+        for lay in layers:
+            moe.connect_expert_parallel(lay, rank, gather)
+    # tokens: config-0 input seed 0, tag 5
     x = torch.empty(T * d, dtype=torch.float32, device="cuda")
-    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 5, rank * T * d, T * d, 1.0, stream))
+    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 5, 0, T * d, 1.0, stream))
     out = torch.empty(T * d, dtype=torch.float32, device="cuda")
 
     def step(i, flags=0):
@@ -171,8 +188,8 @@ def run_ours(args, rank, world, local_rank):
     uniq = []
     for l in range(NL):
         step(l)
-        ids = layers[l].routing(T)[0]
-        uniq.append(len(np.unique(ids)))
+        ids = np.unique(layers[l].routing(T)[0])
+        uniq.append(int(((ids >= first) & (ids < first + n_local)).sum()))  # this rank's experts
     torch.cuda.synchronize()
 
     # The timed steps replay a CUDA graph of the NL rotated layer forwards
@@ -221,36 +238,44 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
     ms_step = ms_total / args.steps
-    tokens_per_s = world * T * args.steps / (ms_total / 1e3)
+    # every rank ends a step with the output of the same T tokens
+    tokens_per_s = T * args.steps / (ms_total / 1e3)
 
     # ---- e2e: reference-facing tensor_t call with host buffers (H2D + D2H inside)
-    e2e = None if args.no_e2e else run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype,
-                                            rank, dist)
+    if args.no_e2e:
+        e2e = None
+    elif world == 1:
+        e2e = run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist)
+    else:
+        e2e = run_e2e_ep(moe, args, layers, T, d, stream, dist)
 
-    # ---- roofline of the dominant kernel (gate/up + SwiGLU)
+    # ---- roofline of the dominant kernel: the fused decode-layer kernel, one
+    # launch per layer forward (router, routing, gate/up + SwiGLU, down, combine)
     hbm_peak, _, peak_kind = measured_peaks()
     U = np.array([uniq[i % NL] for i in range(args.steps)], float)
-    gu_bytes = float(np.mean(U)) * 2 * F * moe.row_bytes(qtype, d) + T * K * F * 4 + T * d * 4
-    gu_ms = stage[2] / max(nprof, 1)
     layer_bytes = float(np.mean(U)) * EXPERT_BYTES_Q8 + NE * d * 4 + 2 * T * d * 4
-    achieved = gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None
-    roof = {"bound": "hbm", "kernel": "expert_mma_kernel<Q8_0, dual> (gate/up + SwiGLU)",
+    stage_avg = stage / max(nprof, 1)
+    kernel_ms = float(stage_avg.sum())
+    achieved = layer_bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms > 0 else None
+    roof = {"bound": "hbm",
+            "kernel": "moe_decode_kernel<Q8_0, 16 lanes> (whole MoE layer, one launch)",
             "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
             "frac": achieved / hbm_peak if achieved else None, "traffic": None,
             "peak_source": peak_kind,
-            "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
-            "layer_achieved_gbs": layer_bytes / (ms_step / 1e3) / 1e9,
-            "layer_frac": layer_bytes / (ms_step / 1e3) / 1e9 / hbm_peak,
-            "stage_ms_avg": {n: float(v / max(nprof, 1)) for n, v in
-                             zip(["router", "dispatch", "gate_up", "down", "combine"], stage)}}
+            "algorithmic_bytes_per_launch": layer_bytes, "avg_launch_ms": kernel_ms,
+            "launch_time_source": "%globaltimer stamps of every CTA (earliest start to "
+                                  "latest end), averaged over the profiled replays",
+            "step_achieved_gbs": layer_bytes / (ms_step / 1e3) / 1e9,
+            "stage_ms_avg": {n: float(v) for n, v in
+                             zip(["router", "routing", "gate_up", "down", "combine"], stage_avg)}}
     traffic = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(traffic):
         with open(traffic) as f:
             tj = json.load(f)
         # DRAM bytes of one captured launch, scaled by the routed experts
-        per_expert = tj.get("gate_up_dram_bytes_per_active_expert")
+        per_expert, fixed = tj.get("bytes_per_active_expert"), tj.get("bytes_fixed", 0.0)
         if per_expert and tj.get("kernel") == roof["kernel"]:
-            roof["traffic"] = per_expert * float(np.mean(U))
+            roof["traffic"] = per_expert * float(np.mean(U)) + fixed
             roof["traffic_source"] = "profiles/" + tj.get("source", "traffic.json")
 
     cpu = None
@@ -261,28 +286,76 @@ def run_ours(args, rank, world, local_rank):
         "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d)" % T,
         "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x Q8_0 weights",
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32 activations x Q8_0 weights",
         "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) tokens)",
         "config": {"workload": "config0: OLMoE-1B-7B MoE FFN layer, d 2048, 64 experts top-8, "
                                "d_ff 1024 SwiGLU, Q8_0, T=%d tokens" % T,
-                   "tokens_per_rank": T, "layers_rotated": NL,
+                   "tokens_per_step": T, "layers_rotated": NL,
                    "l2": f"{NL} distinct layers rotated; each step streams "
                          f"{np.mean(U) * EXPERT_BYTES_Q8 / 1e6:.0f} MB of experts > 126 MB L2",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                   "parallelism": (f"expert-parallel x{world}: {n_local} experts per GPU, the "
+                                   "(token, slot) rows exchanged over NVLink inside the fused "
+                                   "kernel, every GPU combines the full output")
+                                  if world > 1 else "single GPU"},
         "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
-        "gpu_launches": 5 * args.steps,  # router, top-k+dispatch, gate/up, down, combine
+        "gpu_launches": args.steps,  # one fused decode-layer kernel per forward
         "host_enqueue_ms": host_ms,
         "timing": "CUDA events on the launching stream around CUDA-graph replays "
                   f"({NL} layer forwards per graph)",
         "distinct_experts_per_step": float(np.mean(U)),
     }
+    if world > 1:
+        got = [None] * world
+        dist.all_gather_object(got, (float(np.mean(uniq)), kernel_ms))
+        line["per_rank_active_experts"] = [g[0] for g in got]
+        line["per_rank_kernel_ms"] = [g[1] for g in got]
     if rank == 0:
         print(json.dumps(line), flush=True)
+    # no rank frees its exchange buffers while another may still write to them
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     for lay in layers:
         lay.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_e2e_ep(moe, args, layers, T, d, stream, dist):
+    """Expert-parallel e2e: per step, this rank's tokens come from pinned host
+    memory and its output goes back to pinned host memory around the layer
+    call (moe_layer_forward); wall clock per rank, max over ranks."""
+    import torch
+    nl = len(layers)
+    xin = torch.randn(T * d, dtype=torch.float32, generator=torch.Generator().manual_seed(0))
+    xin = xin.pin_memory()
+    xout = torch.empty(T * d, dtype=torch.float32).pin_memory()
+    xd = torch.empty(T * d, dtype=torch.float32, device="cuda")
+    od = torch.empty(T * d, dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def call(i):
+        xd.copy_(xin, non_blocking=True)
+        layers[i % nl].forward_device(xd.data_ptr(), od.data_ptr(), T, 0, s.cuda_stream)
+        xout.copy_(od, non_blocking=True)
+        s.synchronize()
+
+    for i in range(max(args.warmup, 2)):
+        call(i)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        call(i)
+    sec = time.perf_counter() - t0
+    t = torch.tensor([sec], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sec = float(t.item())
+    return {"value": T * args.steps / sec, "unit": "tokens/s",
+            "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
+            "api": "moe_layer_forward (expert-parallel; pinned host -> device copy of the "
+                   "tokens and device -> pinned host copy of the output inside the step)",
+            "timer": "host wall clock per rank, max over ranks"}
 
 
 def run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist):

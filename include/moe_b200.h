@@ -206,6 +206,24 @@ MOE_API int moe_layer_routing(moe_layer *layer, int32_t *ids, float *weights, in
  * Synchronises the device and resets the sums. */
 MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
 
+/* Expert parallelism over NVLink (no counterpart in the reference, which
+ * runs on one host).  A layer created with n_local < n_experts owns an
+ * exchange buffer; once every rank has passed its buffer's handle to the
+ * others, decode-sized forwards (T <= 64) run the fused kernel on every
+ * rank: the router and top-k run for all tokens on every rank (x must be
+ * the same everywhere), each rank computes the (token, slot) rows of its
+ * own experts and writes them into every rank's buffer as they are
+ * produced, and every rank combines all rows in slot order -- so each
+ * rank's output is the full layer output, identical on all ranks and to a
+ * single GPU's.  Every rank must run the same sequence of forwards of the
+ * layer.  Larger batches (or a layer whose peers are not set) return the
+ * partial output of the local experts, for the caller to sum.
+ * moe_layer_ipc_handle writes this rank's 64-byte cudaIpcMemHandle_t;
+ * moe_layer_set_peers takes all ranks' handles ([world][64] bytes, in rank
+ * order), 2 <= world <= 8, once. */
+MOE_API int moe_layer_ipc_handle(moe_layer *layer, void *handle);
+MOE_API int moe_layer_set_peers(moe_layer *layer, int rank, int world, const void *handles);
+
 /* Diagnostics of the fused decode kernel: the raw %globaltimer stamps (ns)
  * of the latest MOE_PROFILE fused forward not yet consumed by
  * moe_layer_stage_ms, as [CTA][stamp] with 12 stamps per CTA: start, router

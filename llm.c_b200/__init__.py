@@ -73,6 +73,8 @@ SIGNATURES = {
     "moe_layer_routing": (_I, [_P, _P, _P, _P, _P, _P]),
     "moe_layer_stage_ms": (_I, [_P, C.POINTER(C.c_float), _I]),
     "moe_layer_phase_stamps": (_I, [_P, C.POINTER(C.c_uint64), _I]),
+    "moe_layer_ipc_handle": (_I, [_P, _P]),
+    "moe_layer_set_peers": (_I, [_P, _I, _I, _P]),
     "moe_gemv_device": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_gemv_device_noalloc": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_sync": (_I, []),
@@ -186,6 +188,23 @@ class DeviceBuffer:
             pass
 
 
+# ------------------------------------------------------------------ expert parallelism
+def expert_range(rank: int, world: int, n_experts: int):
+    """(first_expert, n_local) of `rank`: contiguous, balanced ranges that
+    cover every expert once"""
+    if world < 1 or not 0 <= rank < world or n_experts < world:
+        raise ValueError(f"rank {rank} of {world} over {n_experts} experts")
+    first = rank * n_experts // world
+    return first, (rank + 1) * n_experts // world - first
+
+
+def connect_expert_parallel(layer: "Layer", rank: int, all_gather) -> None:
+    """exchange the layer's buffer handles between the ranks and connect them;
+    `all_gather(obj) -> list` gathers one picklable object from every rank
+    in rank order (e.g. torch.distributed.all_gather_object)"""
+    layer.set_peers(rank, all_gather(layer.ipc_handle()))
+
+
 # ------------------------------------------------------------------ layer
 class Layer:
     """Device-resident MoE layer (moe_layer_create).  `gate`/`up` are uint8
@@ -254,6 +273,19 @@ class Layer:
         n = lib().moe_layer_phase_stamps(self.handle, buf, len(buf))
         check(n if n < 0 else 0)
         return np.ctypeslib.as_array(buf)[:n].reshape(-1, len(self.PHASE_STAMPS)).copy()
+
+    def ipc_handle(self) -> bytes:
+        """this rank's 64-byte handle of the layer's exchange buffer (expert
+        parallelism; the layer must own only some experts)"""
+        buf = (C.c_char * 64)()
+        check(lib().moe_layer_ipc_handle(self.handle, buf))
+        return bytes(buf)
+
+    def set_peers(self, rank: int, handles) -> None:
+        """connect the ranks: `handles` are every rank's ipc_handle(), in rank order"""
+        blob = b"".join(handles)
+        buf = (C.c_char * len(blob)).from_buffer_copy(blob)
+        check(lib().moe_layer_set_peers(self.handle, rank, len(handles), buf))
 
     def routing(self, T: int):
         K, NE = self.top_k, self.n_experts

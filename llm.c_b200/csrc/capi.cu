@@ -203,6 +203,14 @@ struct moe_layer {
 	int32_t *active, *n_active, *work;  // [NE], [1], [2]
 	unsigned long long *gbar;           // grid barrier arrivals of the fused kernel
 	uint64_t *stamps;                   // [kStampRecords][grid][stamps]
+	// expert parallelism (n_local < n_experts): exchange buffer of this rank
+	// (two halves of y_half floats + counters), peers once connected
+	char *xbuf = nullptr;
+	int64_t y_half = 0;
+	int ep_rank = 0, ep_world = 1;
+	std::vector<void *> opened;         // peer buffers opened by IPC
+	float **d_ybuf = nullptr;           // device [world]
+	unsigned long long **d_inbound = nullptr;
 };
 
 namespace {
@@ -497,8 +505,19 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 	if (e == cudaSuccess)
 		e = cudaMemcpy(L->dptrs, host.data(), host.size() * sizeof(void *),
 			       cudaMemcpyHostToDevice);
+	if (e == cudaSuccess && nl < d.n_experts) {
+		// rows of every (token, slot) pair of a decode batch, twice
+		L->y_half = (int64_t)moe::decode_max_t() * d.top_k * d.d_model;
+		const size_t xb = moe::ep_exchange_bytes(L->y_half);
+		e = cudaMalloc(&L->xbuf, xb);
+		if (e == cudaSuccess)
+			e = cudaMemset(L->xbuf, 0, xb);
+		if (e == cudaSuccess)
+			e = cudaDeviceSynchronize();
+	}
 	if (e != cudaSuccess) {
 		cudaFree(L->dptrs);
+		cudaFree(L->xbuf);
 		delete L;
 		return cuda_fail(e, "moe_layer_create");
 	}
@@ -514,6 +533,11 @@ int moe_layer_destroy(moe_layer *L)
 		cudaStreamSynchronize(g.stream);
 	cudaFree(L->dptrs);
 	cudaFree(L->scratch);
+	for (void *p : L->opened)
+		cudaIpcCloseMemHandle(p);
+	cudaFree(L->d_ybuf);
+	cudaFree(L->d_inbound);
+	cudaFree(L->xbuf);
 	for (auto &set : L->prof)
 		for (auto ev : set)
 			cudaEventDestroy(ev);
@@ -556,7 +580,8 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 	const int mode_exact = (flags & MOE_TOPK_EXACT) ? 1 : 0, renorm = (flags & MOE_RENORM) ? 1 : 0;
 
 	// decode-sized batch on one GPU: the whole layer in one fused kernel
-	if (!simple && !(flags & MOE_NO_FUSE) && d.n_local == d.n_experts &&
+	const bool ep_ready = L->ep_world > 1 && L->d_ybuf;
+	if (!simple && !(flags & MOE_NO_FUSE) && (d.n_local == d.n_experts || ep_ready) &&
 	    moe::decode_supported(d.qtype, T, D, F, NE, K, (uintptr_t)x, (uintptr_t)d.router_w,
 				  (uintptr_t)out)) {
 		uint64_t *stamps = nullptr;
@@ -593,6 +618,16 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		a.err = L->err;
 		a.gbar = L->gbar;
 		a.stamps = stamps;
+		a.first_expert = (int)d.first_expert;
+		a.n_local = (int)d.n_local;
+		a.rank = L->ep_rank;
+		a.world = ep_ready ? L->ep_world : 1;
+		a.ybuf = L->d_ybuf;
+		a.ybuf_half = L->y_half;
+		a.inbound = L->d_inbound;
+		a.launches = ep_ready ? reinterpret_cast<unsigned long long *>(
+						L->xbuf + 2 * L->y_half * 4 + moe::kMaxEpRanks * moe::kEpFlagStride * 8)
+				      : nullptr;
 		CK(moe::launch_decode_layer(a, d.qtype, lanes, st));
 		return MOE_OK;
 	}
@@ -762,6 +797,59 @@ int moe_layer_stage_ms(moe_layer *L, float *ms, int n)
 	return MOE_OK;
 }
 
+int moe_layer_ipc_handle(moe_layer *L, void *handle)
+{
+	if (!L || !handle)
+		return fail(MOE_ERR_INVALID, "moe_layer_ipc_handle: null argument");
+	if (!L->xbuf)
+		return fail(MOE_ERR_INVALID, "moe_layer_ipc_handle: the layer computes every expert "
+			    "(no exchange buffer)");
+	cudaIpcMemHandle_t h;
+	CK(cudaIpcGetMemHandle(&h, L->xbuf));
+	memcpy(handle, &h, sizeof(h));
+	return MOE_OK;
+}
+
+int moe_layer_set_peers(moe_layer *L, int rank, int world, const void *handles)
+{
+	if (!L || !handles)
+		return fail(MOE_ERR_INVALID, "moe_layer_set_peers: null argument");
+	if (!L->xbuf)
+		return fail(MOE_ERR_INVALID, "moe_layer_set_peers: the layer computes every expert");
+	if (world < 2 || world > moe::kMaxEpRanks || rank < 0 || rank >= world)
+		return fail(MOE_ERR_INVALID, "moe_layer_set_peers: rank %d of %d (2..%d ranks)", rank,
+			    world, moe::kMaxEpRanks);
+	if (L->d_ybuf)
+		return fail(MOE_ERR_INVALID, "moe_layer_set_peers: peers already set");
+	std::vector<float *> yb(world);
+	std::vector<unsigned long long *> inb(world);
+	const auto *hs = static_cast<const cudaIpcMemHandle_t *>(handles);
+	for (int r = 0; r < world; r++) {
+		void *base = L->xbuf;
+		if (r != rank) {
+			cudaError_t e = cudaIpcOpenMemHandle(&base, hs[r], cudaIpcMemLazyEnablePeerAccess);
+			if (e != cudaSuccess) {
+				for (void *p : L->opened)
+					cudaIpcCloseMemHandle(p);
+				L->opened.clear();
+				return cuda_fail(e, "moe_layer_set_peers: cudaIpcOpenMemHandle");
+			}
+			L->opened.push_back(base);
+		}
+		yb[r] = static_cast<float *>(base);
+		inb[r] = reinterpret_cast<unsigned long long *>(static_cast<char *>(base) +
+								 2 * L->y_half * 4);
+	}
+	CK(cudaMalloc(&L->d_ybuf, world * sizeof(float *)));
+	CK(cudaMalloc(&L->d_inbound, world * sizeof(unsigned long long *)));
+	CK(cudaMemcpy(L->d_ybuf, yb.data(), world * sizeof(float *), cudaMemcpyHostToDevice));
+	CK(cudaMemcpy(L->d_inbound, inb.data(), world * sizeof(unsigned long long *),
+		      cudaMemcpyHostToDevice));
+	L->ep_rank = rank;
+	L->ep_world = world;
+	return MOE_OK;
+}
+
 int moe_layer_phase_stamps(moe_layer *L, uint64_t *out, int n)
 {
 	if (!L || !out)
@@ -792,7 +880,7 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 		return MOE_OK;
 	int32_t err = 0;
 	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
-	if (err == 2 || err == 3) {
+	if (err == 2 || err == 3 || err == 4) {
 		// a barrier left half-passed must not poison the next forward
 		CK(cudaMemset(L->gbar, 0, moe::decode_barrier_bytes(moe::sm_count())));
 		CK(cudaDeviceSynchronize());
@@ -803,6 +891,9 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 		return fail(MOE_ERR_TIMEOUT, "an expert kernel's bounded wait expired");
 	if (err == 3)
 		return fail(MOE_ERR_TIMEOUT, "the fused layer kernel's grid barrier expired");
+	if (err == 4)
+		return fail(MOE_ERR_TIMEOUT, "the expert-parallel exchange wait expired (a rank "
+			    "missing or behind)");
 	if (ids)
 		CK(cudaMemcpy(ids, L->ids, T * K * 4, cudaMemcpyDeviceToHost));
 	if (weights)

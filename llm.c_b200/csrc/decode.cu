@@ -91,7 +91,7 @@ constexpr size_t decode_smem_bytes()
 {
 	return (size_t)STAGES * StageLayout<QT>::BYTES + StageLayout<QT>::RED +
 	       StageLayout<QT>::SSUM + StageLayout<QT>::EPI + DecodeSmem::END +
-	       (2 * STAGES + 2 * kRedBufs + 4) * 8;  // + up to 4 router slot barriers
+	       (2 * STAGES + 2 * kRedBufs + 1 + kMaxEpRanks) * 8;  // + router barrier, peer table
 }
 
 // ---------------------------------------------------------------- grid barrier
@@ -105,6 +105,18 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
 __device__ __forceinline__ void st_relaxed_gpu(unsigned long long *p, unsigned long long v)
 {
 	asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p)
+{
+	unsigned long long v;
+	asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+	return v;
+}
+
+__device__ __forceinline__ void red_add_release_sys(unsigned long long *p, unsigned long long v)
+{
+	asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // Grid barrier state: bar[0] counts arrivals since the buffer was zeroed
@@ -277,10 +289,39 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	const Bars b = init_bars<STAGES>(bars);
 	if (tid == 0)
 		mbar_init(rbar, 1);
+	// expert parallelism: this launch's number (the same on every rank, as
+	// every rank runs the same launches) and, by its parity, the half of
+	// each exchange buffer it writes -- a rank one launch ahead writes the
+	// other half, so it never overwrites rows that are still being combined
+	const bool ep = a.world > 1;
+	const unsigned long long epoch = ep ? *reinterpret_cast<volatile unsigned long long *>(a.launches) + 1 : 0;
+	const int64_t half_off = (int64_t)(epoch & 1) * a.ybuf_half;
+	float *Y = ep ? a.ybuf[a.rank] + half_off : a.Y;
+	float **ypeers = reinterpret_cast<float **>(rbar + 1);  // [world - 1] (smem)
+	if (ep && tid < a.world && tid != a.rank)
+		ypeers[tid - (tid > a.rank)] = a.ybuf[tid] + half_off;
 	fence_mbar_init();
 	__syncthreads();
 
 	// ------------------------------------------------ P0: logits + x split
+	// The top-k of token t runs after barrier 1 on CTA (units + t) % grid,
+	// normally a CTA without router work.  Such a CTA first runs the top-k
+	// once on dummy logits, so that its code is in the SM's instruction cache
+	// (it is otherwise fetched cold, from memory, when the result is needed).
+	const int units = ((T + RTile<LANES>::RT - 1) / RTile<LANES>::RT) * (NE / RTile<LANES>::RE);
+	const int topk_first = units % (int)gridDim.x;  // CTA of token 0
+	const int my_token0 = ((int)blockIdx.x - topk_first + (int)gridDim.x) % (int)gridDim.x;
+	if ((int)blockIdx.x >= units && my_token0 < T && warp == 0) {
+		float *lg = reinterpret_cast<float *>(smem);
+		float *sel = lg + kMaxActive;
+		int32_t *dummy = reinterpret_cast<int32_t *>(sel + 2 * K);
+		for (int e = lane; e < NE; e += 32)
+			lg[e] = 0.0f;
+		__syncwarp();
+		topk_token<LANES>(lg, nullptr, NE, K, a.mode_exact, a.renorm, sel,
+				  reinterpret_cast<int32_t *>(sel + K), dummy, reinterpret_cast<float *>(dummy + K),
+				  nullptr, nullptr);
+	}
 	router_tiles<LANES>(a, smem, rbar);
 	{
 		const int64_t total = (int64_t)T * D;
@@ -302,11 +343,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	stamp(a.stamps, kStB1);
 
 	// ------------------------------------------------ P1: routing
-	// softmax + top-k of token t by warp 0 of CTA t (t < T)
+	// softmax + top-k of token t by warp 0 of CTA (units + t) % grid
 	{
 		float *lg = reinterpret_cast<float *>(smem);                 // [NE]
 		float *sel = lg + kMaxActive;                                // [2K]
-		for (int t = blockIdx.x; t < T; t += gridDim.x) {
+		for (int t = my_token0; t < T; t += gridDim.x) {
 			if (warp == 0) {
 				for (int e = lane; e < NE; e += 32)
 					lg[e] = __ldcg(a.logits + (int64_t)t * NE + e);
@@ -329,8 +370,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			wts_s[i] = __ldcg(a.wts + i);
 		}
 		__syncthreads();
-		dispatch_body(ids_s, T * K, NE, 0, NE, counts_s, offsets_s, perm_s, nullptr, active_s,
-			      nact_s, a.err, ds);
+		dispatch_body(ids_s, T * K, NE, a.first_expert, a.n_local, counts_s, offsets_s, perm_s,
+			      nullptr, active_s, nact_s, a.err, ds);
 		__syncthreads();
 		stamp(a.stamps, kStDispatch);
 		const int n_active = *nact_s;
@@ -367,10 +408,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	{
 		const int n_active = *nact_s;
 		const Phase gu{a.dptrs, a.dptrs + NE, F, D, K, en, off, pre_gu, n_active, perm_s, 1, 0,
-			       a.x16, a.h16, nullptr, a.err, nullptr};
-		// down stores z = y / (1 / w) per (token, slot) row; P4 only adds
+			       a.x16, a.h16, nullptr, a.err, nullptr, nullptr, 0};
+		// down stores z = y / (1 / w) per (token, slot) row, also into the
+		// other ranks' exchange buffers; P4 only adds
 		const Phase dn{a.dptrs + 2 * NE, nullptr, D, F, K, en, off, pre_dn, n_active, perm_s, 0, 1,
-			       a.h16, nullptr, a.Y, a.err, wts_s};
+			       a.h16, nullptr, Y, a.err, wts_s, ypeers, ep ? a.world - 1 : 0};
 		Pipe pipe;
 		if (warp == kProducerWarp) {
 			core_producer<QT, true, STAGES, WB_GU>(gu, smem, b, pipe, lane);
@@ -396,11 +438,37 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 									  lane);
 		}
 	}
-	__syncthreads();
-	stamp(a.stamps, kStP3);
-	if (tid == 0)
-		grid_sync(a.gbar, a.err);
-	__syncthreads();
+	if (!ep) {
+		__syncthreads();
+		stamp(a.stamps, kStP3);
+		if (tid == 0)
+			grid_sync(a.gbar, a.err);
+		__syncthreads();
+	} else {
+		// every CTA of every rank announces that its rows are out: the rows
+		// it stored (here and over NVLink) are made visible system-wide,
+		// then one arrival per CTA on each rank's counter for this rank;
+		// each rank waits until every rank's CTAs have arrived
+		__threadfence_system();
+		__syncthreads();
+		stamp(a.stamps, kStP3);
+		if (tid == 0)
+			for (int r = 0; r < a.world; r++)
+				red_add_release_sys(a.inbound[r] + kEpFlagStride * a.rank, 1ull);
+		if (tid < a.world) {
+			const unsigned long long *cnt = a.inbound[a.rank] + kEpFlagStride * tid;
+			const unsigned long long want = epoch * gridDim.x;
+			const uint64_t t0 = global_ns();
+			while (ld_acquire_sys(cnt) < want) {
+				if (global_ns() - t0 > kWaitLimitNs) {
+					atomicExch(a.err, 4);
+					break;
+				}
+				__nanosleep(64);
+			}
+		}
+		__syncthreads();
+	}
 	stamp(a.stamps, kStB3);
 
 	// ------------------------------------------------ P4: combine
@@ -414,7 +482,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 			for (int s = 0; s < K; s++) {
 				const float4 z = __ldcg(reinterpret_cast<const float4 *>(
-							       a.Y + ((int64_t)t * K + s) * D) + j4);
+							       Y + ((int64_t)t * K + s) * D) + j4);
 				acc.x = __fadd_rn(z.x, acc.x);
 				acc.y = __fadd_rn(z.y, acc.y);
 				acc.z = __fadd_rn(z.z, acc.z);
@@ -424,6 +492,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		}
 	}
 	stamp(a.stamps, kStEnd);
+	if (ep && blockIdx.x == 0 && tid == 0)
+		*a.launches = epoch;  // every CTA read it before arriving above
 }
 
 // ---------------------------------------------------------------- launch
@@ -437,6 +507,8 @@ bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr
 }
 
 int decode_stamps() { return kStamps; }
+
+int decode_max_t() { return kDecodeMaxT; }
 
 // stamp index ending each of the five reported stages (router, routing,
 // gate/up, down, combine); stage 0 starts at the earliest kStStart

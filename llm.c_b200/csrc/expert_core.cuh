@@ -369,6 +369,8 @@ struct Phase {
 	float *out;              // single: [*, rows] fp32
 	int32_t *err;            // set to 2 when a bounded wait expires
 	const float *wdiv;       // single, optional: store y / (1 / wdiv[out row])
+	float *const *peers;     // single, optional: the same rows also go to these
+	int npeers;              // buffers (other GPUs' memory, expert parallelism)
 };
 
 struct Bars {
@@ -607,9 +609,21 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 							for (int v = 0; v < PER; v += 4)
 								*reinterpret_cast<float4 *>(dst + v) =
 									*reinterpret_cast<const float4 *>(src + v);
+							// expert parallelism: every GPU gets the row, written
+							// over NVLink while the next tiles are computed
+							for (int q = 0; q < ph.npeers; q++) {
+								float *pd = ph.peers[q] + (int64_t)orow * ph.rows + r0 + rr;
+#pragma unroll
+								for (int v = 0; v < PER; v += 4)
+									*reinterpret_cast<float4 *>(pd + v) =
+										*reinterpret_cast<const float4 *>(src + v);
+							}
 						} else {
-							for (int v = 0; v < PER && rr + v < nr; v++)
+							for (int v = 0; v < PER && rr + v < nr; v++) {
 								dst[v] = src[v];
+								for (int q = 0; q < ph.npeers; q++)
+									ph.peers[q][(int64_t)orow * ph.rows + r0 + rr + v] = src[v];
+							}
 						}
 					}
 				}

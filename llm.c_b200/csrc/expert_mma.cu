@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) expert_mma_kernel(MmaArgs a)
 	__syncthreads();
 
 	Phase ph{a.w1, a.w2, a.rows, a.cols, a.K, en, off, pre, n_active, a.perm, a.in_perm,
-		 a.out_perm, a.in16, a.out16, a.out, a.err, nullptr};
+		 a.out_perm, a.in16, a.out16, a.out, a.err, nullptr, nullptr, 0};
 	Pipe pipe;
 	const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 	if (warp == kProducerWarp)

@@ -103,10 +103,29 @@ struct DecodeArgs {
 	int32_t *err;              // 0 ok, 2 bounded mbarrier wait expired, 3 grid barrier expired
 	unsigned long long *gbar;  // grid barrier state (decode_barrier_bytes), zero when allocated
 	uint64_t *stamps;          // NULL or [grid][decode_stamps()] phase times (ns)
+	// expert parallelism (world > 1): this GPU computes experts
+	// [first_expert, first_expert + n_local) and writes each of their
+	// (token, slot) rows into every rank's exchange buffer; then every rank
+	// combines all rows in slot order.
+	int first_expert, n_local;
+	int rank, world;
+	float *const *ybuf;        // device [world]: exchange buffers (two halves each)
+	int64_t ybuf_half;         // floats from one half to the other
+	unsigned long long *const *inbound;  // device [world]: rank r's arrival counters
+	unsigned long long *launches;        // this rank's count of expert-parallel launches
 };
+constexpr int kMaxEpRanks = 8;
+constexpr int kEpFlagStride = 16;  // u64s (128 bytes) per counter
+// exchange buffer of one rank: two Y halves of y_half floats, then
+// kMaxEpRanks arrival counters and the launch counter
+inline size_t ep_exchange_bytes(int64_t y_half)
+{
+	return (size_t)(2 * y_half) * 4 + (size_t)(kMaxEpRanks + 1) * kEpFlagStride * 8;
+}
 bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr_t x,
 		      uintptr_t router_w, uintptr_t out);
 int decode_stamps();
+int decode_max_t();
 size_t decode_barrier_bytes(int ctas);
 void decode_stage_ends(int *ends);
 cudaError_t launch_decode_layer(const DecodeArgs &a, int qtype, int lanes, cudaStream_t st);

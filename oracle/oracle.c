@@ -551,6 +551,61 @@ void orc_gemm_q(const float *a, size_t m, size_t k, const void *b, int type,
 /* ------------------------------------------------------------------ */
 
 /* olmoe.c:343-407 (renorm = 0) and llama.c:393-457 (renorm = 1) */
+/* The per-(token, slot) terms y / (1 / w) of the combine (olmoe.c:397-404)
+ * for the slots whose expert lies in [first, first + nlocal): z[t*K + s]
+ * rows; the other rows are left as they are.  Adding the rows of a token in
+ * slot order, starting from 0, gives orc_moe_ffn's output bit for bit —
+ * the expert-parallel decomposition of the layer (each rank computes the
+ * rows of its experts, the rows are exchanged, every rank combines). */
+void orc_moe_slot_terms(const orc_moe_layer *L, const float *x, size_t T, size_t first,
+			size_t nlocal, float *z, int32_t *ids_out, float *w_out)
+{
+	size_t d = L->d_model, NE = L->n_experts, K = L->top_k, F = L->d_ff;
+	float *logits = malloc(T * NE * sizeof(float));
+	float *hidden = malloc(F * sizeof(float));
+	float *y = malloc(d * sizeof(float));
+	int32_t ids[64];
+	float w[64];
+
+	orc_router_logits(x, T, d, L->router_w, NE, L->lanes, logits);
+	if (L->router_bias)
+		for (size_t t = 0; t < T; t++)
+			for (size_t e = 0; e < NE; e++)
+				logits[t * NE + e] = logits[t * NE + e] + L->router_bias[e];
+	for (size_t t = 0; t < T; t++) {
+		float *p = logits + t * NE;
+		orc_softmax_1d(p, NE, L->lanes);
+		orc_top_k(p, NE, ids, w, K, L->topk_mode);
+		if (L->renorm) {
+			float sum = 0.0f;
+			for (size_t s = 0; s < K; s++)
+				sum = sum + w[s];
+			for (size_t s = 0; s < K; s++)
+				w[s] = w[s] / sum;
+		}
+		for (size_t s = 0; s < K; s++) {
+			size_t e = (size_t)ids[s];
+			if (e < first || e >= first + nlocal)
+				continue;
+			const uint8_t *g = (const uint8_t *)L->gate + e * L->gate_stride;
+			const uint8_t *u = (const uint8_t *)L->up + e * L->up_stride;
+			const uint8_t *dn = (const uint8_t *)L->down + e * L->down_stride;
+			orc_fused_ffn_silu(x + t * d, d, F, L->qtype, g, u, dn, L->lanes, hidden, y);
+			float inv = 1.0f / w[s];
+			float *zr = z + (t * K + s) * d;
+			for (size_t j = 0; j < d; j++)
+				zr[j] = y[j] / inv;
+		}
+		if (ids_out)
+			memcpy(ids_out + t * K, ids, K * sizeof(int32_t));
+		if (w_out)
+			memcpy(w_out + t * K, w, K * sizeof(float));
+	}
+	free(logits);
+	free(hidden);
+	free(y);
+}
+
 void orc_moe_ffn(const orc_moe_layer *L, const float *x, size_t T, float *out,
 		 int32_t *ids_out, float *w_out, float *probs_out)
 {

@@ -109,6 +109,11 @@ typedef struct {
 /* out[T,d]; optional ids/weights[T,k] (after renorm), logits/probs[T,NE] */
 void orc_moe_ffn(const orc_moe_layer *L, const float *x, size_t T, float *out,
 		 int32_t *ids, float *weights, float *probs);
+/* z[t*K + s] = y / (1 / w) for the slots whose expert is in [first, first +
+ * nlocal) (other rows untouched); their sum over s, in slot order, is
+ * orc_moe_ffn's output (the expert-parallel decomposition) */
+void orc_moe_slot_terms(const orc_moe_layer *L, const float *x, size_t T, size_t first,
+			size_t nlocal, float *z, int32_t *ids_out, float *w_out);
 
 #ifdef __cplusplus
 }

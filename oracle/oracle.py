@@ -68,6 +68,7 @@ def lib():
         L.orc_fused_ffn_silu.argtypes = [P, sz, sz, C.c_int, P, P, P, C.c_int, P, P]
         L.orc_gemm_q.argtypes = [P, sz, sz, P, C.c_int, sz, C.c_int, P]
         L.orc_moe_ffn.argtypes = [C.POINTER(MoeLayer), P, sz, P, P, P, P]
+        L.orc_moe_slot_terms.argtypes = [C.POINTER(MoeLayer), P, sz, sz, sz, P, P, P]
         _lib = L
     return _lib
 
@@ -199,6 +200,39 @@ def moe_ffn(layer: dict, x: np.ndarray, lanes=16, topk_mode=TOPK_REF):
     lib().orc_moe_ffn(C.byref(L), _p(x), T, _p(out), _p(ids), _p(w), _p(probs))
     del keep
     return out, ids, w, probs
+
+
+def moe_slot_terms(layer: dict, x: np.ndarray, first: int, nlocal: int, lanes=16,
+                   topk_mode=TOPK_REF):
+    """z [T*K, d]: the combine terms y / (1 / w) of the (token, slot) pairs whose
+    expert is in [first, first + nlocal), zero rows elsewhere; summing a token's
+    rows in slot order from 0 gives moe_ffn's output bit for bit."""
+    x = np.ascontiguousarray(x, np.float32)
+    T, d = x.shape
+    gate, up, down = (np.ascontiguousarray(layer[k]) for k in ("gate", "up", "down"))
+    NE = gate.shape[0]
+    F = layer["d_ff"]
+    K = layer["top_k"]
+    rb = layer.get("router_bias")
+    keep = [x, gate, up, down, layer["router_w"], rb]
+    L = MoeLayer(d, F, NE, K, layer["qtype"], int(layer.get("renorm", 0)), topk_mode, lanes,
+                 _p(layer["router_w"]), _p(rb), _p(gate), _p(up), _p(down),
+                 gate[0].nbytes, up[0].nbytes, down[0].nbytes)
+    z = np.zeros((T * K, d), np.float32)
+    ids = np.empty((T, K), np.int32)
+    w = np.empty((T, K), np.float32)
+    lib().orc_moe_slot_terms(C.byref(L), _p(x), T, first, nlocal, _p(z), _p(ids), _p(w))
+    del keep
+    return z, ids, w
+
+
+def combine_slot_terms(z: np.ndarray, T: int, K: int) -> np.ndarray:
+    """out[t] = sum over slots s (in order, from 0) of z[t*K + s]"""
+    z = z.reshape(T, K, -1)
+    out = np.zeros((T, z.shape[2]), np.float32)
+    for s in range(K):
+        out = out + z[:, s]
+    return out
 
 
 def make_layer(seed: int, d: int, F: int, NE: int, K: int, qtype: int = Q8_0,

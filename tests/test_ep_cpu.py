@@ -1,0 +1,76 @@
+"""Expert parallelism on the CPU: the decomposition the fused kernel uses
+across GPUs, run by gloo ranks with the oracle.
+
+Each rank computes the combine terms y / (1 / w) of the (token, slot) pairs
+whose expert it owns (expert_range), the ranks exchange their rows (here an
+all-gather, on the GPUs direct NVLink stores), and every rank adds each
+token's rows in slot order.  The result must equal the single-process
+oracle bit for bit on every rank.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import load_package
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, case, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as orc
+        moe = load_package()
+        d, F, NE, K, qt, T, seed, renorm = case
+        L = orc.make_layer(seed, d, F, NE, K, qt, renorm=renorm, zipf=not renorm)
+        x = orc.make_tokens(seed, T, d)
+        first, nl = moe.expert_range(rank, world, NE)
+        z, ids, w = orc.moe_slot_terms(L, x, first, nl)
+        # rows of experts owned elsewhere are zero here; exactly one rank owns each row
+        rows = torch.from_numpy(z)
+        gathered = [torch.empty_like(rows) for _ in range(world)]
+        dist.all_gather(gathered, rows)
+        owner = np.array([[moe.expert_range(r, world, NE)[0] <= e < sum(moe.expert_range(r, world, NE))
+                           for r in range(world)] for e in ids.reshape(-1)])
+        assert (owner.sum(axis=1) == 1).all()
+        full = np.stack([g.numpy() for g in gathered])[owner.argmax(axis=1), np.arange(T * K)]
+        out = orc.combine_slot_terms(full, T, K)
+        ref, *_ = orc.moe_ffn(L, x)
+        results[rank] = bool(np.array_equal(out, ref))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("case", [
+    (256, 128, 16, 4, 1, 9, 4, False),   # Q8_0, Zipf-skewed router
+    (512, 256, 8, 2, 2, 5, 3, True),     # Q4_0, Mixtral-style renormalised top-2
+])
+def test_expert_parallel_decomposition_is_exact(world, case):
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    mp.start_processes(_rank_main, args=(world, free_port(), case, results), nprocs=world,
+                       join=True, start_method="spawn")
+    assert dict(results) == {r: True for r in range(world)}
+
+
+@pytest.mark.parametrize("world,ne", [(2, 64), (3, 64), (8, 64), (8, 8), (7, 16)])
+def test_expert_range_covers_every_expert_once(world, ne):
+    moe = load_package()
+    seen = []
+    for r in range(world):
+        first, nl = moe.expert_range(r, world, ne)
+        assert nl >= ne // world
+        seen += list(range(first, first + nl))
+    assert seen == list(range(ne))
