@@ -71,8 +71,12 @@ enum moe_status {
                              /* default follows the AVX-512 build (16 lanes) */
 #define MOE_RENORM      0x08 /* Mixtral: renormalise the top-k weights       */
                              /* (llama.c:422-427); OLMoE does not            */
-#define MOE_FORCE_GEMV  0x10 /* always use the decode (GEMV) expert kernels  */
-#define MOE_FORCE_GEMM  0x20 /* always use the grouped tensor-core kernels   */
+#define MOE_FORCE_GEMV  0x10 /* never use the prefill GEMM (T > 64): the    */
+                             /* decode expert kernels for every batch size   */
+#define MOE_FORCE_GEMM  0x20 /* use the prefill tcgen05 GEMM for any T (it  */
+                             /* is the default above 64 tokens; fp16-rounded */
+                             /* weights and activations: layer output about  */
+                             /* 5e-4 rel-L2 from fp32)                       */
 #define MOE_SIMPLE      0x80 /* use the plain CUDA-core expert kernels (the   */
                              /* cross-check path) instead of the MMA ones    */
 #define MOE_PROFILE     0x40 /* record CUDA events between the layer's stages */

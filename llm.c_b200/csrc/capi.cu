@@ -196,9 +196,11 @@ struct moe_layer {
 	std::vector<int> prof_fused;  // per record: 1 = fused kernel (phase stamps)
 	size_t prof_used = 0;
 	bool mma_ok = false;  // tensor-core kernels usable (cols % 256, 16 B aligned)
+	bool gemm_ok = false; // prefill GEMM usable (weight tensor maps built)
+	void *wmaps = nullptr;  // device [3][NE] weight tensor maps: gate, up, down
 	// slices of scratch
 	float *logits, *wts, *h, *Y;
-	__half *x16, *h16;
+	__half *x16, *h16, *x16p;  // tokens hi/lo (token order), h hi/lo, tokens hi/lo (pair order)
 	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
 	int32_t *active, *n_active, *work;  // [NE], [1], [2]
 	unsigned long long *gbar;           // grid barrier arrivals of the fused kernel
@@ -235,6 +237,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8);
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
 	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)cap * K * 2 * F * 2);
+	size_t o_x16p = take((size_t)cap * K * 2 * D * 2);
 	const size_t gbar_bytes = moe::decode_barrier_bytes(moe::sm_count());
 	size_t o_gbar = take(gbar_bytes);
 	size_t o_stamps = take((size_t)kStampRecords * moe::sm_count() * moe::decode_stamps() * 8);
@@ -261,6 +264,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->h = (float *)(b + o_h);
 	L->Y = (float *)(b + o_Y);
 	L->x16 = (__half *)(b + o_x16);
+	L->x16p = (__half *)(b + o_x16p);
 	L->h16 = (__half *)(b + o_h16);
 	L->gbar = (unsigned long long *)(b + o_gbar);
 	L->stamps = (uint64_t *)(b + o_stamps);
@@ -505,6 +509,25 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 	if (e == cudaSuccess)
 		e = cudaMemcpy(L->dptrs, host.data(), host.size() * sizeof(void *),
 			       cudaMemcpyHostToDevice);
+	const int qt = (int)d.qtype, D = (int)d.d_model, F = (int)d.d_ff;
+	L->gemm_ok = L->mma_ok && moe::expert_gemm_supported(qt, F, D, 1) &&
+		     moe::expert_gemm_supported(qt, D, F, 0);
+	if (e == cudaSuccess && L->gemm_ok) {
+		// tensor maps of every local expert matrix for the prefill GEMM
+		const size_t mb = moe::weight_map_bytes();
+		std::vector<uint8_t> maps(3 * d.n_experts * mb, 0);
+		for (int64_t x = first; x < first + nl && L->gemm_ok; x++)
+			L->gemm_ok = moe::encode_weight_map(&maps[x * mb], host[x], qt, F, D) &&
+				     moe::encode_weight_map(&maps[(d.n_experts + x) * mb],
+							    host[d.n_experts + x], qt, F, D) &&
+				     moe::encode_weight_map(&maps[(2 * d.n_experts + x) * mb],
+							    host[2 * d.n_experts + x], qt, D, F);
+		if (L->gemm_ok) {
+			e = cudaMalloc(&L->wmaps, maps.size());
+			if (e == cudaSuccess)
+				e = cudaMemcpy(L->wmaps, maps.data(), maps.size(), cudaMemcpyHostToDevice);
+		}
+	}
 	if (e == cudaSuccess && nl < d.n_experts) {
 		// rows of every (token, slot) pair of a decode batch, twice
 		L->y_half = (int64_t)moe::decode_max_t() * d.top_k * d.d_model;
@@ -517,6 +540,7 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 	}
 	if (e != cudaSuccess) {
 		cudaFree(L->dptrs);
+		cudaFree(L->wmaps);
 		cudaFree(L->xbuf);
 		delete L;
 		return cuda_fail(e, "moe_layer_create");
@@ -532,6 +556,7 @@ int moe_layer_destroy(moe_layer *L)
 	if (g.init)
 		cudaStreamSynchronize(g.stream);
 	cudaFree(L->dptrs);
+	cudaFree(L->wmaps);
 	cudaFree(L->scratch);
 	for (void *p : L->opened)
 		cudaIpcCloseMemHandle(p);
@@ -581,7 +606,7 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 
 	// decode-sized batch on one GPU: the whole layer in one fused kernel
 	const bool ep_ready = L->ep_world > 1 && L->d_ybuf;
-	if (!simple && !(flags & MOE_NO_FUSE) && (d.n_local == d.n_experts || ep_ready) &&
+	if (!simple && !(flags & (MOE_NO_FUSE | MOE_FORCE_GEMM)) && (d.n_local == d.n_experts || ep_ready) &&
 	    moe::decode_supported(d.qtype, T, D, F, NE, K, (uintptr_t)x, (uintptr_t)d.router_w,
 				  (uintptr_t)out)) {
 		uint64_t *stamps = nullptr;
@@ -645,13 +670,17 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		ev = L->prof[L->prof_used++].data();
 		CK(record(ev[0]));
 	}
+	// prefill-sized batches: grouped GEMMs on tcgen05 (the tokens are gathered
+	// into pair order after the dispatch instead of split in token order)
+	const bool gemm = !simple && L->gemm_ok && !(flags & MOE_FORCE_GEMV) &&
+			  (T > moe::decode_max_t() || (flags & MOE_FORCE_GEMM)) && (uintptr_t)x % 16 == 0;
 	// [0] router logits (+ the fp16 split of x the MMA kernels read)
 	if (moe::router_tiled_ok(D, NE)) {
 		CK(moe::launch_router_tiled(x, d.router_w, (int)T, D, NE, lanes, L->logits,
-					    simple ? nullptr : L->x16, q4, st));
+					    (simple || gemm) ? nullptr : L->x16, q4, st));
 	} else {
 		CK(moe::launch_router_logits(x, d.router_w, (int)T, D, NE, lanes, L->logits, st));
-		if (!simple)
+		if (!simple && !gemm)
 			CK(moe::launch_split_f16(x, T, D, d.qtype, L->x16, st));
 	}
 	if (prof)
@@ -675,7 +704,42 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 	const void *const *dp = L->dptrs;
 	if (prof)
 		CK(record(ev[2]));
-	if (simple) {
+	if (gemm) {
+		const int64_t pairs = T * K;
+		CK(moe::launch_gather_split(x, L->perm, pairs, D, K, L->x16p, st));
+		const size_t mb = moe::weight_map_bytes();
+		moe::GemmArgs gu{};
+		gu.maps1 = L->wmaps;
+		gu.maps2 = (const uint8_t *)L->wmaps + NE * mb;
+		gu.qtype = d.qtype;
+		gu.rows = F;
+		gu.cols = D;
+		gu.n_local = (int)d.n_local;
+		gu.counts = L->counts;
+		gu.offsets = L->offsets;
+		gu.perm = L->perm;
+		gu.active = L->active;
+		gu.n_active = L->n_active;
+		gu.out_perm = 0;
+		gu.in16 = L->x16p;
+		gu.out16 = L->h16;
+		gu.dual = 1;
+		gu.err = L->err;
+		CK(moe::launch_expert_gemm(gu, pairs, st));
+		if (prof)
+			CK(record(ev[3]));
+		moe::GemmArgs dn = gu;
+		dn.maps1 = (const uint8_t *)L->wmaps + 2 * NE * mb;
+		dn.maps2 = nullptr;
+		dn.rows = D;
+		dn.cols = F;
+		dn.out_perm = 1;
+		dn.in16 = L->h16;
+		dn.out16 = nullptr;
+		dn.out = L->Y;
+		dn.dual = 0;
+		CK(moe::launch_expert_gemm(dn, pairs, st));
+	} else if (simple) {
 		moe::GemvArgs gu{};
 		gu.w1 = dp;
 		gu.w2 = dp + NE;

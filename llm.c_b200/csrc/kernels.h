@@ -130,6 +130,36 @@ size_t decode_barrier_bytes(int ctas);
 void decode_stage_ends(int *ends);
 cudaError_t launch_decode_layer(const DecodeArgs &a, int qtype, int lanes, cudaStream_t st);
 
+// expert_gemm.cu: prefill-sized grouped GEMM on tcgen05 (see the file).
+// Segment semantics as MmaArgs; activations are fp16 hi/lo rows in pair
+// order, natural column order: in16 [in_rows][2][cols].  maps1/maps2 are device
+// arrays of per-expert weight tensor maps (encode_weight_map), indexed by
+// the global expert id.
+struct GemmArgs {
+	const void *maps1;       // W1 (gate, or down) tensor maps [NE]
+	const void *maps2;       // dual: W2 (up) tensor maps [NE]
+	int qtype;
+	int rows, cols;          // weight matrix; rows % 128 (dual) / 256, cols % 256
+	int n_local;
+	const int32_t *counts, *offsets, *perm;
+	const int32_t *active, *n_active;
+	int out_perm;
+	const __half *in16;
+	__half *out16;           // dual: [pairs][2][rows] swiglu as fp16 hi/lo
+	float *out;              // single: [pairs][rows]
+	int dual;
+	int32_t *err;
+};
+bool expert_gemm_supported(int qtype, int rows, int cols, int dual);
+// one weight matrix (rows x cols, GGUF blocks, 16-byte aligned) as the tensor
+// map the GEMM reads raw chunks through; map points at weight_map_bytes()
+bool encode_weight_map(void *map, const void *w, int qtype, int rows, int cols);
+size_t weight_map_bytes();
+cudaError_t launch_expert_gemm(const GemmArgs &a, int64_t in_rows, cudaStream_t st);
+// out[pos] = fp16 hi/lo of x[perm[pos] / K] (pair order, natural columns)
+cudaError_t launch_gather_split(const float *x, const int32_t *perm, int64_t pairs, int cols,
+				int K, __half *out, cudaStream_t st);
+
 // out[t, :] = sum_s Y[t*K + s, :] / (1 / w[t*K + s]) in slot order
 cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, float *out,
 			   cudaStream_t st);

@@ -109,7 +109,10 @@ def test_mid_layer_mma_and_simple(moe, orc, mid_layers, qt, T):
     assert_output_close(got, ref)
     simple = lay.forward(x, flags=moe.SIMPLE)
     assert_output_close(simple, ref)
-    assert rel_l2(got, simple) < 1e-5
+    # up to 64 tokens both paths are fp32-accurate; above, the prefill GEMM
+    # rounds the weights to fp16 (checked against the oracle above)
+    if T <= 64:
+        assert rel_l2(got, simple) < 1e-5
     lay.close()
 
 
