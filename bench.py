@@ -11,11 +11,14 @@ rotated so that every step streams 428 MB of experts that are not in the
 126 MB L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload config0|config1] [--tokens T]
+                  [--tokens T] [--layers NL] [--prefill-tokens P]
 
-Prints one JSON line (rank 0).  Under torchrun each rank runs its own
-replica of the layer on its own tokens (weak scaling); the time is the max
-over ranks.
+Prints one JSON line (rank 0).  Under torchrun the layer is expert-parallel:
+rank r holds experts expert_range(r) of every layer, every rank gets the
+same T tokens and ends with the full output (strong scaling); the time is
+the max over ranks.  On one GPU the line also carries a "prefill" object:
+the same layers on P tokens (default 2048), which runs the tcgen05 grouped
+GEMM, with its tensor roofline.
 """
 from __future__ import annotations
 
@@ -268,8 +271,11 @@ def run_ours(args, rank, world, local_rank):
             "step_achieved_gbs": layer_bytes / (ms_step / 1e3) / 1e9,
             "stage_ms_avg": {n: float(v) for n, v in
                              zip(["router", "routing", "gate_up", "down", "combine"], stage_avg)}}
+    if T > DECODE_MAX_T:
+        roof = dict(gemm_roofline(stage_avg, T, d, F, K),
+                    stage_ms_avg=roof["stage_ms_avg"], step_ms=ms_step)
     traffic = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(traffic):
+    if T <= DECODE_MAX_T and os.path.exists(traffic):
         with open(traffic) as f:
             tj = json.load(f)
         # DRAM bytes of one captured launch, scaled by the routed experts
@@ -277,6 +283,10 @@ def run_ours(args, rank, world, local_rank):
         if per_expert and tj.get("kernel") == roof["kernel"]:
             roof["traffic"] = per_expert * float(np.mean(U)) + fixed
             roof["traffic_source"] = "profiles/" + tj.get("source", "traffic.json")
+
+    prefill = None
+    if world == 1 and args.prefill_tokens > 0:
+        prefill = run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -298,11 +308,15 @@ def run_ours(args, rank, world, local_rank):
                                    "kernel, every GPU combines the full output")
                                   if world > 1 else "single GPU"},
         "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
-        "gpu_launches": args.steps,  # one fused decode-layer kernel per forward
+        # one fused decode-layer kernel per forward; above 64 tokens: router,
+        # top-k + dispatch (one launch up to 256 tokens, two above), gather,
+        # two GEMMs and the combine
+        "gpu_launches": args.steps * (1 if T <= DECODE_MAX_T else 6 if T <= 256 else 7),
         "host_enqueue_ms": host_ms,
         "timing": "CUDA events on the launching stream around CUDA-graph replays "
                   f"({NL} layer forwards per graph)",
         "distinct_experts_per_step": float(np.mean(U)),
+        "prefill": prefill,
     }
     if world > 1:
         got = [None] * world
@@ -320,6 +334,77 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+DECODE_MAX_T = 64   # batches above this take the prefill GEMM path
+
+
+def gemm_roofline(stage, P, d, F, K):
+    """tensor roofline of the prefill grouped GEMM from the stage times"""
+    flops = 2.0 * P * K * 3 * d * F                  # useful: gate, up, down
+    gemm_ms = float(stage[2] + stage[3])
+    _, tc_peak, peak_kind = measured_peaks()
+    useful = flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    return {
+        "bound": "tensor",
+        "kernel": "expert_gemm_kernel<Q8_0> gate/up (dual) + down: tcgen05 kind::f16, "
+                  "M 128 pairs x N 256 weight rows, three fp16 hi/lo products",
+        "achieved": useful, "unit": "TFLOP/s",
+        "achieved_executed": 3 * useful if useful else None,
+        "peak": tc_peak, "peak_source": peak_kind + " bf16 dense (burst); fp16 runs at the "
+                                          "same tensor rate",
+        "frac": useful / tc_peak if useful else None,
+        "frac_executed": 3 * useful / tc_peak if useful else None,
+        "algorithmic_flops_per_step": flops, "avg_launch_ms": gemm_ms,
+        "traffic": None,
+        "note": "each product is x_hi w_hi + x_lo w_hi + x_hi w_lo, so the tensor cores "
+                "execute 3x the algorithmic FLOPs (the precision bar needs ~22-bit "
+                "operands); the gate_up stage includes the fp16 hi/lo gather of the tokens",
+        "launch_time_source": "CUDA events between the layer's stages, one profiled "
+                              "forward per layer"}
+
+
+def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream):
+    """Prefill leg: P tokens per layer forward (the grouped tcgen05 GEMM
+    path), rotated over the same layers; device time with CUDA events, the
+    stages from one profiled forward per layer."""
+    import torch
+    P = args.prefill_tokens
+    NL = len(layers)
+    x = torch.empty(P * d, dtype=torch.float32, device="cuda")
+    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 6, 0, P * d, 1.0, stream))
+    out = torch.empty(P * d, dtype=torch.float32, device="cuda")
+
+    def fwd(i, flags=0):
+        layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), P, flags, stream)
+
+    for i in range(max(3, NL)):
+        fwd(i)
+    torch.cuda.synchronize()
+    steps = max(NL, args.prefill_steps)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(torch_stream)
+    for i in range(steps):
+        fwd(i)
+    ev1.record(torch_stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    stage = np.zeros(5)
+    for l in range(NL):
+        fwd(l, moe.PROFILE)
+    torch.cuda.synchronize()
+    for lay in layers:
+        s, c = lay.stage_ms()
+        stage += np.array(s)
+    stage /= NL
+    return {
+        "tokens": P, "value": P / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+        "steps": steps,
+        "stage_ms_avg": {n: float(v) for n, v in
+                         zip(["router", "routing", "gate_up", "down", "combine"], stage)},
+        "roofline": gemm_roofline(stage, P, d, F, K),
+    }
 
 
 def run_e2e_ep(moe, args, layers, T, d, stream, dist):
@@ -419,7 +504,7 @@ def run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist):
     moe.lib().moe_host_free(xout_p)
     return {"value": world * T * args.steps / sec, "unit": "tokens/s",
             "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
-            "api": "moe_ffn_forward (tensor_t drop-in, pageable->device copies inside)",
+            "api": "moe_ffn_forward (tensor_t drop-in; tokens and output in pinned host buffers from moe_host_alloc, host<->device copies inside the call)",
             "timer": "host wall clock around synchronous calls"}
 
 
@@ -518,6 +603,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=32)
     ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--prefill-tokens", type=int, default=2048,
+                    help="tokens of the one-GPU prefill leg (0: skip)")
+    ap.add_argument("--prefill-steps", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()

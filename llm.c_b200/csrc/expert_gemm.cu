@@ -193,14 +193,6 @@ struct ItemWalk {
 	}
 };
 
-// raw 8 codes of a Q8_0 block at p (2-byte aligned) as two little-endian words
-__device__ __forceinline__ void ld_codes8(const uint8_t *p, uint32_t &w0, uint32_t &w1)
-{
-	const uint16_t *h = reinterpret_cast<const uint16_t *>(p);
-	w0 = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
-	w1 = (uint32_t)h[2] | ((uint32_t)h[3] << 16);
-}
-
 // two int8 codes (low byte first) -> half2 of the exact integers
 __device__ __forceinline__ __half2 codes_to_h2(uint32_t w)
 {
@@ -240,11 +232,28 @@ __device__ __forceinline__ void convert_slice(const uint8_t *raw, int pad, uint8
 	const int coff = QT == kQ8_0 ? 2 + 8 * c : 2 + 8 * (c & 1);
 	const int o0 = r0 * 64 + ((c ^ ((r0 >> 1) & 3)) << 4);  // same phase for every unit
 	uint32_t dq[U], w0[U], w1[U];
+	// the 8 code bytes (at pad + 2 + 8c into the row, rows 16-byte aligned)
+	// are 4-byte aligned when pad = 2 mod 4; otherwise (the same for every
+	// thread of the slice) three aligned words are read and shifted by 16 bits
+	if (pad & 2) {
 #pragma unroll
-	for (int k = 0; k < U; k++) {
-		const uint8_t *b = b0 + k * RSTEP * GL::WIN;
-		dq[k] = *reinterpret_cast<const uint16_t *>(b);
-		ld_codes8(b + coff, w0[k], w1[k]);
+		for (int k = 0; k < U; k++) {
+			const uint8_t *b = b0 + k * RSTEP * GL::WIN;
+			dq[k] = *reinterpret_cast<const uint16_t *>(b);
+			const uint32_t *p = reinterpret_cast<const uint32_t *>(b + coff);
+			w0[k] = p[0];
+			w1[k] = p[1];
+		}
+	} else {
+#pragma unroll
+		for (int k = 0; k < U; k++) {
+			const uint8_t *b = b0 + k * RSTEP * GL::WIN;
+			dq[k] = *reinterpret_cast<const uint16_t *>(b);
+			const uint32_t *p = reinterpret_cast<const uint32_t *>(b + coff - 2);
+			const uint32_t a0 = p[0], a1 = p[1], a2 = p[2];
+			w0[k] = __funnelshift_r(a0, a1, 16);
+			w1[k] = __funnelshift_r(a1, a2, 16);
+		}
 	}
 	const int sh = (QT == kQ4_0 && (c & 2)) ? 4 : 0;
 #pragma unroll
