@@ -175,6 +175,8 @@ def run_ours(args, rank, world, local_rank):
             return got
         for lay in layers:
             moe.connect_expert_parallel(lay, rank, gather)
+        # batches above 64 tokens sum the ranks' partial outputs (NCCL)
+        moe.init_expert_parallel_comm(rank, world, gather)
     # tokens: config-0 input seed 0, tag 5
     x = torch.empty(T * d, dtype=torch.float32, device="cuda")
     moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 5, 0, T * d, 1.0, stream))
@@ -188,11 +190,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     # routing of the layers (distinct experts touched = algorithmic bytes)
-    uniq = []
+    uniq, pairs_local = [], []
     for l in range(NL):
         step(l)
-        ids = np.unique(layers[l].routing(T)[0])
+        ids_all = layers[l].routing(T)[0]
+        ids = np.unique(ids_all)
         uniq.append(int(((ids >= first) & (ids < first + n_local)).sum()))  # this rank's experts
+        pairs_local.append(int(((ids_all >= first) & (ids_all < first + n_local)).sum()))
     torch.cuda.synchronize()
 
     # The timed steps replay a CUDA graph of the NL rotated layer forwards
@@ -272,7 +276,7 @@ def run_ours(args, rank, world, local_rank):
             "stage_ms_avg": {n: float(v) for n, v in
                              zip(["router", "routing", "gate_up", "down", "combine"], stage_avg)}}
     if T > DECODE_MAX_T:
-        roof = dict(gemm_roofline(stage_avg, T, d, F, K),
+        roof = dict(gemm_roofline(stage_avg, float(np.mean(pairs_local)), d, F),
                     stage_ms_avg=roof["stage_ms_avg"], step_ms=ms_step)
     traffic = os.path.join(ROOT, "profiles", "traffic.json")
     if T <= DECODE_MAX_T and os.path.exists(traffic):
@@ -285,8 +289,8 @@ def run_ours(args, rank, world, local_rank):
             roof["traffic_source"] = "profiles/" + tj.get("source", "traffic.json")
 
     prefill = None
-    if world == 1 and args.prefill_tokens > 0:
-        prefill = run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream)
+    if args.prefill_tokens > 0:
+        prefill = run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream, dist)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -339,9 +343,10 @@ def run_ours(args, rank, world, local_rank):
 DECODE_MAX_T = 64   # batches above this take the prefill GEMM path
 
 
-def gemm_roofline(stage, P, d, F, K):
-    """tensor roofline of the prefill grouped GEMM from the stage times"""
-    flops = 2.0 * P * K * 3 * d * F                  # useful: gate, up, down
+def gemm_roofline(stage, pairs, d, F):
+    """tensor roofline of the prefill grouped GEMM from the stage times;
+    pairs = (token, slot) pairs routed to this rank's experts"""
+    flops = 2.0 * pairs * 3 * d * F                  # useful: gate, up, down
     gemm_ms = float(stage[2] + stage[3])
     _, tc_peak, peak_kind = measured_peaks()
     useful = flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
@@ -364,10 +369,13 @@ def gemm_roofline(stage, P, d, F, K):
                               "forward per layer"}
 
 
-def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream):
+def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream, dist=None):
     """Prefill leg: P tokens per layer forward (the grouped tcgen05 GEMM
-    path), rotated over the same layers; device time with CUDA events, the
-    stages from one profiled forward per layer."""
+    path), rotated over the same layers; device time with CUDA events (max
+    over ranks), the stages from one profiled forward per layer.  Expert
+    parallel (N > 1): every rank runs its experts' GEMMs on the same P
+    tokens and the partial outputs are summed by the library's NCCL
+    all-reduce inside the step."""
     import torch
     P = args.prefill_tokens
     NL = len(layers)
@@ -382,6 +390,9 @@ def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream):
         fwd(i)
     torch.cuda.synchronize()
     steps = max(NL, args.prefill_steps)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(torch_stream)
@@ -390,9 +401,17 @@ def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream):
     ev1.record(torch_stream)
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     stage = np.zeros(5)
+    pairs = []
     for l in range(NL):
         fwd(l, moe.PROFILE)
+        ids = layers[l].routing(P)[0]
+        first = layers[l].first_expert
+        pairs.append(int(((ids >= first) & (ids < first + layers[l].n_local)).sum()))
     torch.cuda.synchronize()
     for lay in layers:
         s, c = lay.stage_ms()
@@ -403,7 +422,11 @@ def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream):
         "steps": steps,
         "stage_ms_avg": {n: float(v) for n, v in
                          zip(["router", "routing", "gate_up", "down", "combine"], stage)},
-        "roofline": gemm_roofline(stage, P, d, F, K),
+        "roofline": gemm_roofline(stage, float(np.mean(pairs)), d, F),
+        "parallelism": "single GPU" if not dist else
+                       f"expert-parallel x{dist.get_world_size()}: GEMMs of the local experts, "
+                       "partial outputs summed by an NCCL all-reduce in the step (stages and "
+                       "roofline of rank 0)",
     }
 
 

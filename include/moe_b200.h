@@ -220,13 +220,26 @@ MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
  * produced, and every rank combines all rows in slot order -- so each
  * rank's output is the full layer output, identical on all ranks and to a
  * single GPU's.  Every rank must run the same sequence of forwards of the
- * layer.  Larger batches (or a layer whose peers are not set) return the
- * partial output of the local experts, for the caller to sum.
+ * layer.  Larger batches (and layers whose peers are not set) run the
+ * router and top-k for all tokens and the grouped GEMMs for the local
+ * experts; once moe_ep_init has been called, the ranks' partial outputs
+ * (each the slot-order combine of its own experts' rows) are summed by an
+ * NCCL all-reduce on the forward's stream, so every rank again ends with
+ * the full output (identical on all ranks, within fp32 rounding of one
+ * GPU's); without it the partial output is returned for the caller to sum.
  * moe_layer_ipc_handle writes this rank's 64-byte cudaIpcMemHandle_t;
  * moe_layer_set_peers takes all ranks' handles ([world][64] bytes, in rank
  * order), 2 <= world <= 8, once. */
 MOE_API int moe_layer_ipc_handle(moe_layer *layer, void *handle);
 MOE_API int moe_layer_set_peers(moe_layer *layer, int rank, int world, const void *handles);
+/* The library's NCCL communicator for expert-parallel batches above 64
+ * tokens (libnccl.so.2 is loaded at run time).  Rank 0 calls
+ * moe_ep_unique_id (128 bytes) and shares the bytes out of band; then every
+ * rank calls moe_ep_init(rank, world, id) once, after moe_init.
+ * moe_ep_finalize (also run by moe_shutdown) destroys it. */
+MOE_API int moe_ep_unique_id(void *id);
+MOE_API int moe_ep_init(int rank, int world, const void *id);
+MOE_API int moe_ep_finalize(void);
 
 /* Diagnostics of the fused decode kernel: the raw %globaltimer stamps (ns)
  * of the latest MOE_PROFILE fused forward not yet consumed by

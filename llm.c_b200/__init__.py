@@ -75,6 +75,9 @@ SIGNATURES = {
     "moe_layer_phase_stamps": (_I, [_P, C.POINTER(C.c_uint64), _I]),
     "moe_layer_ipc_handle": (_I, [_P, _P]),
     "moe_layer_set_peers": (_I, [_P, _I, _I, _P]),
+    "moe_ep_unique_id": (_I, [_P]),
+    "moe_ep_init": (_I, [_I, _I, _P]),
+    "moe_ep_finalize": (_I, []),
     "moe_gemv_device": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_gemv_device_noalloc": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P]),
     "moe_sync": (_I, []),
@@ -205,6 +208,17 @@ def connect_expert_parallel(layer: "Layer", rank: int, all_gather) -> None:
     layer.set_peers(rank, all_gather(layer.ipc_handle()))
 
 
+def init_expert_parallel_comm(rank: int, world: int, all_gather) -> None:
+    """create the library's NCCL communicator (moe_ep_init), once per process;
+    rank 0's unique id travels through `all_gather` (as above)"""
+    uid = (C.c_char * 128)()
+    if rank == 0:
+        check(lib().moe_ep_unique_id(uid))
+    ids = all_gather(bytes(uid) if rank == 0 else None)
+    buf = (C.c_char * 128).from_buffer_copy(ids[0])
+    check(lib().moe_ep_init(rank, world, buf))
+
+
 # ------------------------------------------------------------------ layer
 class Layer:
     """Device-resident MoE layer (moe_layer_create).  `gate`/`up` are uint8
@@ -215,6 +229,8 @@ class Layer:
                  router_bias=None, flags=0, first_expert=0, n_local=0):
         self.bufs = []
         self.d_model, self.d_ff, self.n_experts, self.top_k = d_model, d_ff, n_experts, top_k
+        self.first_expert = first_expert
+        self.n_local = n_local if n_local else n_experts - first_expert
 
         def dev(a):
             if isinstance(a, int):

@@ -9,6 +9,9 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
@@ -72,6 +75,51 @@ struct Ctx {
 };
 
 Ctx g;
+
+// NCCL, loaded at run time (no link dependency): the expert-parallel
+// communicator of larger batches.  dlopen by soname reuses a libnccl.so.2
+// the process has already loaded (e.g. by a framework).
+struct Nccl {
+	void *lib = nullptr;
+	ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+	ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+	ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+				   ncclComm_t, cudaStream_t) = nullptr;
+	ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+	const char *(*error_string)(ncclResult_t) = nullptr;
+	ncclComm_t comm = nullptr;
+	int rank = 0, world = 1;
+};
+
+Nccl nccl;
+
+int nccl_load()
+{
+	if (nccl.lib)
+		return MOE_OK;
+	void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+	if (!h)
+		h = dlopen("libnccl.so.2", RTLD_NOW);
+	if (!h)
+		return fail(MOE_ERR_COMM, "libnccl.so.2 not found: %s", dlerror());
+	nccl.get_unique_id = (decltype(nccl.get_unique_id))dlsym(h, "ncclGetUniqueId");
+	nccl.comm_init_rank = (decltype(nccl.comm_init_rank))dlsym(h, "ncclCommInitRank");
+	nccl.all_reduce = (decltype(nccl.all_reduce))dlsym(h, "ncclAllReduce");
+	nccl.comm_destroy = (decltype(nccl.comm_destroy))dlsym(h, "ncclCommDestroy");
+	nccl.error_string = (decltype(nccl.error_string))dlsym(h, "ncclGetErrorString");
+	if (!nccl.get_unique_id || !nccl.comm_init_rank || !nccl.all_reduce || !nccl.comm_destroy ||
+	    !nccl.error_string)
+		return fail(MOE_ERR_COMM, "libnccl.so.2 lacks an entry point");
+	nccl.lib = h;
+	return MOE_OK;
+}
+
+#define CK_NCCL(call)                                                              \
+	do {                                                                       \
+		ncclResult_t r_ = (call);                                          \
+		if (r_ != ncclSuccess)                                             \
+			return fail(MOE_ERR_COMM, "%s: %s", #call, nccl.error_string(r_)); \
+	} while (0)
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -302,6 +350,7 @@ int moe_shutdown(void)
 	if (!g.init)
 		return MOE_OK;
 	cudaStreamSynchronize(g.stream);
+	moe_ep_finalize();
 	for (auto &kv : g.layers)
 		moe_layer_destroy(kv.second);
 	g.layers.clear();
@@ -319,6 +368,51 @@ int moe_shutdown(void)
 	g.stream = nullptr;
 	g.init = false;
 	g.device = -1;
+	return MOE_OK;
+}
+
+int moe_ep_unique_id(void *id)
+{
+	if (!id)
+		return fail(MOE_ERR_INVALID, "moe_ep_unique_id: null argument");
+	if (int rc = nccl_load())
+		return rc;
+	ncclUniqueId u;
+	CK_NCCL(nccl.get_unique_id(&u));
+	memcpy(id, &u, sizeof(u));
+	return MOE_OK;
+}
+
+int moe_ep_init(int rank, int world, const void *id)
+{
+	if (!id || world < 1 || rank < 0 || rank >= world)
+		return fail(MOE_ERR_INVALID, "moe_ep_init: rank %d of %d", rank, world);
+	if (int rc = ensure_init())
+		return rc;
+	if (int rc = nccl_load())
+		return rc;
+	if (nccl.comm)
+		return fail(MOE_ERR_INVALID, "moe_ep_init: already initialised");
+	ncclUniqueId u;
+	memcpy(&u, id, sizeof(u));
+	CK_NCCL(nccl.comm_init_rank(&nccl.comm, world, u, rank));
+	nccl.rank = rank;
+	nccl.world = world;
+	return MOE_OK;
+}
+
+int moe_ep_finalize(void)
+{
+	if (!nccl.comm)
+		return MOE_OK;
+	if (g.init)
+		cudaStreamSynchronize(g.stream);
+	const ncclResult_t r = nccl.comm_destroy(nccl.comm);
+	nccl.comm = nullptr;
+	nccl.rank = 0;
+	nccl.world = 1;
+	if (r != ncclSuccess)
+		return fail(MOE_ERR_COMM, "ncclCommDestroy: %s", nccl.error_string(r));
 	return MOE_OK;
 }
 
@@ -816,6 +910,10 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		CK(record(ev[4]));
 
 	CK(moe::launch_combine(L->Y, L->wts, (int)T, K, D, out, st));
+	// expert parallelism outside the fused kernel: every rank holds the
+	// combine of its own experts' rows; their sum is the layer output
+	if (d.n_local < d.n_experts && nccl.comm)
+		CK_NCCL(nccl.all_reduce(out, out, (size_t)T * D, ncclFloat32, ncclSum, nccl.comm, st));
 	if (prof)
 		CK(record(ev[5]));
 	return MOE_OK;

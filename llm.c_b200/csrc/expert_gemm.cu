@@ -127,7 +127,7 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar)
 		     : "memory");
 }
 
-// 2-D tiled TMA load (no multicast); map is a kernel parameter or a tensor
+// 2-D tiled TMA load into this CTA's shared memory; map is a kernel parameter or a tensor
 // map in global memory
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, int y, uint64_t *bar)
 {

@@ -1,11 +1,13 @@
-"""Expert parallelism on the CPU: the decomposition the fused kernel uses
-across GPUs, run by gloo ranks with the oracle.
+"""Expert parallelism on the CPU: the decompositions the GPU path uses across
+GPUs, run by gloo ranks with the oracle.
 
 Each rank computes the combine terms y / (1 / w) of the (token, slot) pairs
 whose expert it owns (expert_range), the ranks exchange their rows (here an
 all-gather, on the GPUs direct NVLink stores), and every rank adds each
 token's rows in slot order.  The result must equal the single-process
-oracle bit for bit on every rank.
+oracle bit for bit on every rank.  Batches above 64 tokens instead sum
+the ranks' partial outputs (an all-reduce): identical on every rank and
+within fp32 reassociation of the oracle.
 """
 import os
 import socket
@@ -63,6 +65,42 @@ def test_expert_parallel_decomposition_is_exact(world, case):
     mp.start_processes(_rank_main, args=(world, free_port(), case, results), nprocs=world,
                        join=True, start_method="spawn")
     assert dict(results) == {r: True for r in range(world)}
+
+
+def _rank_partial(rank, world, port, case, results):
+    """larger batches: each rank's partial output (slot-order combine of its
+    own experts' rows), summed across the ranks as the NCCL all-reduce does"""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as orc
+        moe = load_package()
+        d, F, NE, K, qt, T, seed, renorm = case
+        L = orc.make_layer(seed, d, F, NE, K, qt, renorm=renorm, zipf=not renorm)
+        x = orc.make_tokens(seed, T, d)
+        first, nl = moe.expert_range(rank, world, NE)
+        z, ids, w = orc.moe_slot_terms(L, x, first, nl)
+        part = torch.from_numpy(orc.combine_slot_terms(z, T, K))
+        dist.all_reduce(part)
+        ref, *_ = orc.moe_ffn(L, x)
+        results[rank] = (part.numpy().tobytes(), float(np.abs(part.numpy() - ref).max()),
+                         float(np.abs(ref).max()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_partial_sums_match_oracle(world):
+    case = (256, 128, 16, 4, 1, 70, 5, False)
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    mp.start_processes(_rank_partial, args=(world, free_port(), case, results), nprocs=world,
+                       join=True, start_method="spawn")
+    res = dict(results)
+    assert len({res[r][0] for r in range(world)}) == 1      # identical on every rank
+    err, scale = res[0][1], res[0][2]
+    assert err <= 1e-6 * max(scale, 1.0)                     # fp32 reassociation only
 
 
 @pytest.mark.parametrize("world,ne", [(2, 64), (3, 64), (8, 64), (8, 8), (7, 16)])
