@@ -24,7 +24,8 @@
 //       (token, slot) pair.
 //   --  grid barrier
 //   P4  combine: out[t] = sum_s y[t,s] / (1/w[t,s]) in slot order
-//       (olmoe.c:397-404); the divisions happen in P3's epilogue, P4 adds
+//       (olmoe.c:397-404); spread over every CTA, the divisions cost
+//       little here, while in P3's epilogue they held back the down rows
 //       the quotients in slot order, spread over every thread of the grid.
 //
 // Replacing five launches (and their drain / ramp-up) by one also keeps the
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		int32_t *ds = reinterpret_cast<int32_t *>(smem);
 		for (int i = tid; i < T * K; i += blockDim.x) {
 			ids_s[i] = __ldcg(a.ids + i);
-			wts_s[i] = __ldcg(a.wts + i);
+			wts_s[i] = __fdiv_rn(1.0f, __ldcg(a.wts + i));  // 1 / w, the combine's divisor
 		}
 		__syncthreads();
 		dispatch_body(ids_s, T * K, NE, a.first_expert, a.n_local, counts_s, offsets_s, perm_s,
@@ -409,10 +410,10 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		const int n_active = *nact_s;
 		const Phase gu{a.dptrs, a.dptrs + NE, F, D, K, en, off, pre_gu, n_active, perm_s, 1, 0,
 			       a.x16, a.h16, nullptr, a.err, nullptr, nullptr, 0};
-		// down stores z = y / (1 / w) per (token, slot) row, also into the
-		// other ranks' exchange buffers; P4 only adds
+		// down stores y per (token, slot) row, also into the other ranks'
+		// exchange buffers; P4 divides by 1 / w and adds
 		const Phase dn{a.dptrs + 2 * NE, nullptr, D, F, K, en, off, pre_dn, n_active, perm_s, 0, 1,
-			       a.h16, nullptr, Y, a.err, wts_s, ypeers, ep ? a.world - 1 : 0};
+			       a.h16, nullptr, Y, a.err, nullptr, ypeers, ep ? a.world - 1 : 0};
 		Pipe pipe;
 		if (warp == kProducerWarp) {
 			core_producer<QT, true, STAGES, WB_GU>(gu, smem, b, pipe, lane);
@@ -472,23 +473,27 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	stamp(a.stamps, kStB3);
 
 	// ------------------------------------------------ P4: combine
+	// one output element per thread; the rows of 8 slots are loaded before
+	// their divisions, so the L2 round trips overlap
 	{
-		const int d4 = D / 4;
-		const int64_t total = (int64_t)T * d4;
+		const int64_t total = (int64_t)T * D;
 		for (int64_t i = (int64_t)blockIdx.x * blockDim.x + tid; i < total;
 		     i += (int64_t)gridDim.x * blockDim.x) {
-			const int t = (int)(i / d4);
-			const int j4 = (int)(i - (int64_t)t * d4);
-			float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-			for (int s = 0; s < K; s++) {
-				const float4 z = __ldcg(reinterpret_cast<const float4 *>(
-							       Y + ((int64_t)t * K + s) * D) + j4);
-				acc.x = __fadd_rn(z.x, acc.x);
-				acc.y = __fadd_rn(z.y, acc.y);
-				acc.z = __fadd_rn(z.z, acc.z);
-				acc.w = __fadd_rn(z.w, acc.w);
+			const int t = (int)(i / D);
+			const int j = (int)(i - (int64_t)t * D);
+			const float *yt = Y + (int64_t)t * K * D + j;
+			float acc = 0.0f;
+			for (int s0 = 0; s0 < K; s0 += 8) {
+				float y[8];
+#pragma unroll
+				for (int u = 0; u < 8; u++)
+					y[u] = s0 + u < K ? __ldcg(yt + (int64_t)(s0 + u) * D) : 0.0f;
+#pragma unroll
+				for (int u = 0; u < 8; u++)
+					if (s0 + u < K)
+						acc = __fadd_rn(__fdiv_rn(y[u], wts_s[t * K + s0 + u]), acc);
 			}
-			reinterpret_cast<float4 *>(a.out + (int64_t)t * D)[j4] = acc;
+			a.out[(int64_t)t * D + j] = acc;
 		}
 	}
 	stamp(a.stamps, kStEnd);

@@ -335,9 +335,10 @@ struct StageLayout {
 	static constexpr int RED = kRedBufs * kMmaWarps * 32 * 16;
 	static constexpr int SSUM = kMmaWarps * 8 * 8 * 4;  // per warp [8 blocks][8 tokens] f32
 	static constexpr int EPI = kEpiWarps * kEpiStage * 4;  // epilogue staging tiles
-	// two 1024-column rows share one row slot (items of two m-tiles): the
-	// second starts here (16-byte aligned for the copy, 8 for the loads)
-	static constexpr int HALF = 1024 / QK * BB + 16;
+	// two 1024-column rows share one row slot (items of two m-tiles): rows
+	// 2j and 2j + 1 of the item, adjacent as in HBM, so one copy of 2 rows
+	// fills the slot; the second starts here (16-byte aligned)
+	static constexpr int HALF = 1024 / QK * BB;
 	static_assert(HALF + 1024 / QK * BB <= RS && HALF % 16 == 0, "two half rows per slot");
 };
 
@@ -472,8 +473,12 @@ __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, P
 		for (int tg = 0; tg < n; tg += kTokTile)
 		for (int item = seg; item < seg_end; item++) {
 			const int r0 = (item - ai * groups) * ROWS;
-			// lane l (< COPY_ROWS) copies tile row l
-			const int r = DUAL ? r0 + (lane & 7) : r0 + lane;
+			// lane l (< COPY_ROWS) copies tile row l; two m-tiles: m-tile m's
+			// row j is item row 2j + m, and lane j < 16 copies rows 2j, 2j + 1
+			// with one request when both exist (copy requests, not bytes,
+			// bound the rate of 1 KB rows)
+			const bool pair = MT == 2 && r0 + 2 * (lane & 15) + 1 < ph.rows;
+			const int r = DUAL ? r0 + (lane & 7) : MT == 2 ? r0 + 2 * (lane & 15) + (lane >> 4) : r0 + lane;
 			const uint8_t *src = base + (int64_t)min(r, ph.rows - 1) * rb;
 			for (int ch = 0; ch < nch; ch++, p.it++) {
 				const int st = p.it % STAGES;
@@ -488,9 +493,15 @@ __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, P
 				if (lane == 0)
 					mbar_arrive_expect_tx(&b.full[st], COPY_ROWS * cb);
 				__syncwarp();
-				if (lane < COPY_ROWS) {
-					// m-tile 1 of a two-tile item goes to the second half of the slot
-					const int dst = MT == 2 ? (lane & 15) * RS + (lane >> 4) * SL::HALF : lane * RS;
+				// m-tile 1 of a two-tile item goes to the second half of the slot
+				const int dst = MT == 2 ? (lane & 15) * RS + (lane >> 4) * SL::HALF : lane * RS;
+				if (MT == 2 && pair) {
+					if (lane < 16) {
+						fence_proxy_async();
+						bulk_g2s(stages + st * SL::BYTES + dst, src + (int64_t)ch * (KC / QK) * BB,
+							 2 * cb, &b.full[st]);
+					}
+				} else if (lane < COPY_ROWS) {
 					fence_proxy_async();
 					bulk_g2s(stages + st * SL::BYTES + dst, src + (int64_t)ch * (KC / QK) * BB, cb,
 						 &b.full[st]);
@@ -572,7 +583,8 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 						const int orow = ph.out_perm ? ph.perm[pos] : pos;
 						const float v =
 							ph.wdiv ? __fdiv_rn(s0, __fdiv_rn(1.0f, ph.wdiv[orow])) : s0;
-						stg[tt * ROWS + 16 * m + gg + 8 * (i >> 1)] = v;  // [token][row]
+						// [token][item row]; m-tile m's row j is item row 2j + m
+						stg[tt * ROWS + (MT == 2 ? 2 * (gg + 8 * (i >> 1)) + m : gg + 8 * (i >> 1))] = v;
 					}
 				}
 				__syncwarp();
