@@ -109,7 +109,8 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- ours
-def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=None):
+def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=None,
+                 router_bias=None):
     """NL device-resident layers generated on the GPU (generator tags: router
     1, gate 2, up 3, down 4; layer l uses seed seed0 + l).  Expert parallelism:
     only experts [first, first + n_local) are generated and held here, with
@@ -137,7 +138,7 @@ def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=No
                  for e in range(NE)]
                 for m, rows_b in zip(mats, (F * rb_d, F * rb_d, d * rb_f))]
         lay = moe.Layer(d, F, NE, K, qtype, wr.data_ptr(), ptrs[0], ptrs[1], ptrs[2],
-                        first_expert=first, n_local=n_local)
+                        router_bias=router_bias, first_expert=first, n_local=n_local)
         layers.append(lay)
         keep.append((wr, mats))
     del tmp
@@ -430,6 +431,124 @@ def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream, dist=None)
     }
 
 
+def zipf_router_bias(n, s=1.1, seed=4):
+    """per-expert router offsets -s * ln(rank), ranks 1..n in a seeded
+    random order (config 4's Zipf-skewed expert load)"""
+    ranks = np.random.default_rng(seed).permutation(n) + 1
+    return (-s * np.log(ranks.astype(np.float64))).astype(np.float32)
+
+
+def run_sweep(args, rank, world, local_rank):
+    """Config 4: the config-0 layer with a Zipf(1.1)-biased router over a
+    sweep of token counts, expert-parallel over the N ranks (64/N experts
+    each).  One JSON line with one entry per T."""
+    import torch
+    torch.cuda.set_device(local_rank)
+    moe = load_package()
+    moe.init(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    torch_stream = torch.cuda.Stream()
+    torch.cuda.set_stream(torch_stream)
+    stream = torch_stream.cuda_stream
+    d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
+    NL = 2
+    first, n_local = moe.expert_range(rank, world, NE)
+    layers, keep = build_layers(moe, NL, 40, d, F, NE, K, qtype, stream, first, n_local,
+                                router_bias=zipf_router_bias(NE))
+    if world > 1:
+        def gather(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+        for lay in layers:
+            moe.connect_expert_parallel(lay, rank, gather)
+        moe.init_expert_parallel_comm(rank, world, gather)
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    rows = []
+    for T in [int(t) for t in args.sweep.split(",")]:
+        x = torch.empty(T * d, dtype=torch.float32, device="cuda")
+        moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 4, 5, 0, T * d, 1.0, stream))
+        out = torch.empty(T * d, dtype=torch.float32, device="cuda")
+
+        def fwd(i, flags=0):
+            layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), T, flags, stream)
+
+        for i in range(max(3, NL)):
+            fwd(i)
+        torch.cuda.synchronize()
+        ids = [None] * NL
+        for l in range(NL):
+            fwd(l)
+            ids[l] = layers[l].routing(T)[0]
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch_stream, capture_error_mode="relaxed"):
+            for l in range(NL):
+                fwd(l)
+        graph.replay()
+        torch.cuda.synchronize()
+        reps = max(2, min(64, int(2e5 / max(T, 64)) // NL))
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(torch_stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(torch_stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * NL)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        local = [((a >= first) & (a < first + n_local)) for a in ids]
+        uniq = float(np.mean([len(np.unique(a[m])) for a, m in zip(ids, local)]))
+        pairs = float(np.mean([m.sum() for m in local]))
+        counts = np.bincount(ids[0].reshape(-1), minlength=NE)
+        row = {"tokens": T, "value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+               "steps": reps * NL, "rank0_experts": uniq, "rank0_pairs": pairs,
+               "max_pairs_per_expert": int(counts.max()),
+               "path": "fused decode kernel" if T <= DECODE_MAX_T else "grouped tcgen05 GEMM"}
+        if T <= DECODE_MAX_T:
+            row["rank0_achieved_gbs"] = (uniq * EXPERT_BYTES_Q8 + NE * d * 4 + 2 * T * d * 4) / (ms / 1e3) / 1e9
+            row["rank0_frac_of_hbm"] = row["rank0_achieved_gbs"] / hbm_peak
+        else:
+            fl = 2.0 * pairs * 3 * d * F
+            row["rank0_tflops_algorithmic"] = fl / (ms / 1e3) / 1e12
+            row["rank0_frac_of_tensor_peak"] = row["rank0_tflops_algorithmic"] / tc_peak
+        rows.append(row)
+        graph = None
+        del x, out
+        torch.cuda.synchronize()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MoE-layer tokens/s over a token sweep (config 4: config-0 layer, "
+                      "Zipf(1.1)-biased router)",
+            "n_gpus": world, "unit": "tokens/s", "higher_is_better": True,
+            "scaling": "strong", "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) "
+                                         "tokens, Zipf(1.1) router offsets)",
+            "timing": "CUDA events around CUDA-graph replays of 2 rotated layers, max over ranks; "
+                      "whole step (the layer forward) per T",
+            "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": tc_peak, "source": peak_kind},
+            "parallelism": f"expert-parallel x{world}" if world > 1 else "single GPU",
+            "sweep": rows}), flush=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    for lay in layers:
+        lay.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_e2e_ep(moe, args, layers, T, d, stream, dist):
     """Expert-parallel e2e: per step, this rank's tokens come from pinned host
     memory and its output goes back to pinned host memory around the layer
@@ -629,6 +748,8 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="tokens of the one-GPU prefill leg (0: skip)")
     ap.add_argument("--prefill-steps", type=int, default=16)
+    ap.add_argument("--sweep", default="",
+                    help="comma-separated token counts: run config 4 (Zipf router) instead")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()
@@ -638,6 +759,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.sweep:
+        run_sweep(args, rank, world, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 
