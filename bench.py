@@ -110,7 +110,7 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- ours
 def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=None,
-                 router_bias=None):
+                 router_bias=None, flags=0):
     """NL device-resident layers generated on the GPU (generator tags: router
     1, gate 2, up 3, down 4; layer l uses seed seed0 + l).  Expert parallelism:
     only experts [first, first + n_local) are generated and held here, with
@@ -138,7 +138,8 @@ def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=No
                  for e in range(NE)]
                 for m, rows_b in zip(mats, (F * rb_d, F * rb_d, d * rb_f))]
         lay = moe.Layer(d, F, NE, K, qtype, wr.data_ptr(), ptrs[0], ptrs[1], ptrs[2],
-                        router_bias=router_bias, first_expert=first, n_local=n_local)
+                        router_bias=router_bias, flags=flags, first_expert=first,
+                        n_local=n_local)
         layers.append(lay)
         keep.append((wr, mats))
     del tmp
@@ -441,7 +442,9 @@ def zipf_router_bias(n, s=1.1, seed=4):
 def run_sweep(args, rank, world, local_rank):
     """Config 4: the config-0 layer with a Zipf(1.1)-biased router over a
     sweep of token counts, expert-parallel over the N ranks (64/N experts
-    each).  One JSON line with one entry per T."""
+    each).  --sweep-shape mixtral: the config-3 layer instead (d 4096, d_ff
+    14336, 8 experts top-2 renormalised, Q4_0, no router offsets; at 8 GPUs
+    one expert per GPU).  One JSON line with one entry per T."""
     import torch
     torch.cuda.set_device(local_rank)
     moe = load_package()
@@ -455,11 +458,18 @@ def run_sweep(args, rank, world, local_rank):
     torch_stream = torch.cuda.Stream()
     torch.cuda.set_stream(torch_stream)
     stream = torch_stream.cuda_stream
-    d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
+    mixtral = args.sweep_shape == "mixtral"
+    if mixtral:
+        d, F, NE, K, qtype = 4096, 14336, 8, 2, moe.Q4_0
+    else:
+        d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
+    expert_bytes = 3 * F * d // 32 * (18 if qtype == moe.Q4_0 else 34)
     NL = 2
     first, n_local = moe.expert_range(rank, world, NE)
-    layers, keep = build_layers(moe, NL, 40, d, F, NE, K, qtype, stream, first, n_local,
-                                router_bias=zipf_router_bias(NE))
+    layers, keep = build_layers(moe, NL, 3 if mixtral else 40, d, F, NE, K, qtype, stream,
+                                first, n_local,
+                                router_bias=None if mixtral else zipf_router_bias(NE),
+                                flags=moe.RENORM if mixtral else 0)
     if world > 1:
         def gather(obj):
             got = [None] * world
@@ -517,23 +527,31 @@ def run_sweep(args, rank, world, local_rank):
                "max_pairs_per_expert": int(counts.max()),
                "path": "fused decode kernel" if T <= DECODE_MAX_T else "grouped tcgen05 GEMM"}
         if T <= DECODE_MAX_T:
-            row["rank0_achieved_gbs"] = (uniq * EXPERT_BYTES_Q8 + NE * d * 4 + 2 * T * d * 4) / (ms / 1e3) / 1e9
+            row["rank0_achieved_gbs"] = (uniq * expert_bytes + NE * d * 4 + 2 * T * d * 4) / (ms / 1e3) / 1e9
             row["rank0_frac_of_hbm"] = row["rank0_achieved_gbs"] / hbm_peak
         else:
             fl = 2.0 * pairs * 3 * d * F
             row["rank0_tflops_algorithmic"] = fl / (ms / 1e3) / 1e12
             row["rank0_frac_of_tensor_peak"] = row["rank0_tflops_algorithmic"] / tc_peak
+        if dist:
+            got = [None] * world
+            dist.all_gather_object(got, (uniq, pairs))
+            row["per_rank_experts"] = [g[0] for g in got]
+            row["per_rank_pairs"] = [g[1] for g in got]
         rows.append(row)
         graph = None
         del x, out
         torch.cuda.synchronize()
     if rank == 0:
         print(json.dumps({
-            "metric": "MoE-layer tokens/s over a token sweep (config 4: config-0 layer, "
-                      "Zipf(1.1)-biased router)",
+            "metric": ("MoE-layer tokens/s over a token sweep (config-3 layer: Mixtral-8x7B "
+                       "shape, Q4_0, top-2 renormalised)") if mixtral else
+                      ("MoE-layer tokens/s over a token sweep (config 4: config-0 layer, "
+                       "Zipf(1.1)-biased router)"),
             "n_gpus": world, "unit": "tokens/s", "higher_is_better": True,
-            "scaling": "strong", "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) "
-                                         "tokens, Zipf(1.1) router offsets)",
+            "scaling": "strong",
+            "data": "synthetic (seeded N(0,0.02) weights -> %s, N(0,1) tokens%s)" % (
+                "Q4_0" if mixtral else "Q8_0", "" if mixtral else ", Zipf(1.1) router offsets"),
             "timing": "CUDA events around CUDA-graph replays of 2 rotated layers, max over ranks; "
                       "whole step (the layer forward) per T",
             "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": tc_peak, "source": peak_kind},
@@ -750,6 +768,7 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=16)
     ap.add_argument("--sweep", default="",
                     help="comma-separated token counts: run config 4 (Zipf router) instead")
+    ap.add_argument("--sweep-shape", choices=["olmoe", "mixtral"], default="olmoe")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     args = ap.parse_args()

@@ -248,7 +248,18 @@ __host__ __device__ __forceinline__ int q4_src(int k)
 template <int QT>
 struct Bias {
 	static constexpr float value = QT == kQ8_0 ? 1152.0f : 1032.0f;
+	static constexpr unsigned short half = QT == kQ8_0 ? 0x6480 : 0x6408;  // fp16 of value
 };
+
+// biased fp16 pair (BIAS + c0, BIAS + c1) -> the exact codes (c0, c1): the
+// subtraction is exact (both are integers below 2048)
+template <int QT>
+__device__ __forceinline__ uint32_t unbias2(uint32_t a)
+{
+	const __half2 b = __halves2half2(__ushort_as_half(Bias<QT>::half), __ushort_as_half(Bias<QT>::half));
+	const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&a), b);
+	return *reinterpret_cast<const uint32_t *>(&r);
+}
 
 // the 8 code bytes of a Q8_0 block at position JM (mod 4) of its row,
 // p = block + 2 + 8c: rows are 8-byte aligned and blocks 34 bytes long, so
@@ -698,29 +709,6 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, f
 					x_e = e;
 					x_tg = tg;
 					x_ch = ch;
-					if (FAST) {
-						// S of each block for token g: this quad's 8 slots (hi + lo),
-						// then the 4 quads of the token (fixed order)
-						float *sw = ssum + warp * WB * 8;
-#pragma unroll
-						for (int bq = 0; bq < WB; bq++) {
-							const __half2 *hh = reinterpret_cast<const __half2 *>(&xh[bq]);
-							const __half2 *hl = reinterpret_cast<const __half2 *>(&xl[bq]);
-							float s = 0.0f;
-#pragma unroll
-							for (int i = 0; i < 4; i++) {
-								const float2 fh = __half22float2(hh[i]);
-								const float2 fl = __half22float2(hl[i]);
-								s = __fadd_rn(s, __fadd_rn(fh.x, fl.x));
-								s = __fadd_rn(s, __fadd_rn(fh.y, fl.y));
-							}
-							s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
-							s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
-							if (c == 0)
-								sw[bq * 8 + g] = s;
-						}
-						__syncwarp();
-					}
 				}
 				const int st = p.it % STAGES;
 				if (!p.failed &&
@@ -733,24 +721,28 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, f
 					const uint8_t *wt =
 						stages + st * SL::BYTES + (kq * WB) * BB + (MT == 2 ? mt * SL::HALF : 0);
 					if constexpr (FAST) {
-						constexpr float BIAS = Bias<QT>::value;
-						const float *sw = ssum + warp * WB * 8 + 2 * c;
 						static_for<WB>([&](auto J) {
 							constexpr int bq = decltype(J)::value;
 							uint32_t A0[4], A1[4];
 							float d0, d1;
 							load_a_biased<QT, bq>(wt + g * RS + bq * BB, wt + (g + 8) * RS + bq * BB,
 									      c, A0, A1, d0, d1);
+							// exact codes: the products and the block sums stay
+							// small, so fp32 keeps them to ~1e-7
+#pragma unroll
+							for (int j = 0; j < 4; j++) {
+								A0[j] = unbias2<QT>(A0[j]);
+								A1[j] = unbias2<QT>(A1[j]);
+							}
 							float t[4] = {0.f, 0.f, 0.f, 0.f};
 							mma_16816(t, A0, xh[bq].x, xh[bq].y);
 							mma_16816(t, A1, xh[bq].z, xh[bq].w);
 							mma_16816(t, A0, xl[bq].x, xl[bq].y);
 							mma_16816(t, A1, xl[bq].z, xl[bq].w);
-							const float2 S = *reinterpret_cast<const float2 *>(sw + bq * 8);
-							acc[0] = __fmaf_rn(d0, __fmaf_rn(-BIAS, S.x, t[0]), acc[0]);
-							acc[1] = __fmaf_rn(d0, __fmaf_rn(-BIAS, S.y, t[1]), acc[1]);
-							acc[2] = __fmaf_rn(d1, __fmaf_rn(-BIAS, S.x, t[2]), acc[2]);
-							acc[3] = __fmaf_rn(d1, __fmaf_rn(-BIAS, S.y, t[3]), acc[3]);
+							acc[0] = __fmaf_rn(d0, t[0], acc[0]);
+							acc[1] = __fmaf_rn(d0, t[1], acc[1]);
+							acc[2] = __fmaf_rn(d1, t[2], acc[2]);
+							acc[3] = __fmaf_rn(d1, t[3], acc[3]);
 						});
 					} else
 #pragma unroll
