@@ -91,7 +91,7 @@ template <int QT, int STAGES>
 constexpr size_t decode_smem_bytes()
 {
 	return (size_t)STAGES * StageLayout<QT>::BYTES + StageLayout<QT>::RED +
-	       StageLayout<QT>::SSUM + StageLayout<QT>::EPI + DecodeSmem::END +
+	       StageLayout<QT>::EPI + DecodeSmem::END +
 	       (2 * STAGES + 2 * kRedBufs + 1 + kMaxEpRanks) * 8;  // + router barrier, peer table
 }
 
@@ -254,9 +254,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	using DS = DecodeSmem;
 	uint8_t *tail = smem + STAGES * SL::BYTES;
 	float4 *red = reinterpret_cast<float4 *>(tail);
-	float *ssum = reinterpret_cast<float *>(tail + SL::RED);
-	float *stg = reinterpret_cast<float *>(tail + SL::RED + SL::SSUM);
-	uint8_t *tb = tail + SL::RED + SL::SSUM + SL::EPI;
+	float *stg = reinterpret_cast<float *>(tail + SL::RED);
+	uint8_t *tb = tail + SL::RED + SL::EPI;
 	int32_t *en = reinterpret_cast<int32_t *>(tb + DS::EN);
 	int32_t *off = reinterpret_cast<int32_t *>(tb + DS::OFF);
 	int32_t *pre_gu = reinterpret_cast<int32_t *>(tb + DS::PRE_GU);
@@ -412,7 +411,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				core_epilogue<QT, true>(gu, red, stg + (warp - kEpiWarp0) * kEpiStage, b, pipe,
 							warp - kEpiWarp0, lane);
 			else
-				core_math<QT, true, STAGES, WB_GU, true>(gu, smem, red, ssum, b, pipe, warp, lane);
+				core_math<QT, true, STAGES, WB_GU, true>(gu, smem, red, b, pipe, warp, lane);
 			// every CTA's h rows must be written before any CTA reads them
 			bar_math_epi();
 			stamp(a.stamps, kStP2);
@@ -424,7 +423,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				core_epilogue<QT, false, MT_DN>(dn, red, stg + (warp - kEpiWarp0) * kEpiStage, b,
 								pipe, warp - kEpiWarp0, lane);
 			else
-				core_math<QT, false, STAGES, WB_DN, true, MT_DN>(dn, smem, red, ssum, b, pipe, warp,
+				core_math<QT, false, STAGES, WB_DN, true, MT_DN>(dn, smem, red, b, pipe, warp,
 									  lane);
 		}
 	}

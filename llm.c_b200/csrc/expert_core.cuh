@@ -241,14 +241,14 @@ __host__ __device__ __forceinline__ int q4_src(int k)
 // ---------------------------------------------------------------- biased fragments
 // Used when a warp's blocks sit at known positions mod 4 in the stage row
 // (WB % 4 == 0), so every code byte is read with aligned 32/64-bit loads.
-// A code's fp16 value is code + BIAS (exact: 1152 + q for Q8_0 from
-// 0x6400 | (q ^ 0x80), 1024 + nib = (nib - 8) + 1032 for Q4_0), which saves
-// the per-pair subtraction; the MMA sum then carries BIAS * (sum of the
-// block's activations), which is removed in fp32 with that sum S.
+// The loads build fp16 values code + BIAS with bit operations only (exact:
+// 1152 + q for Q8_0 from 0x6400 | (q ^ 0x80), 1024 + nib = (nib - 8) + 1032
+// for Q4_0); unbias2 then subtracts BIAS exactly, one instruction per pair.
+// (Feeding the biased values to the MMA and removing BIAS * (block sum of
+// the activations) afterwards is cheaper but cancels ~10 bits in fp32.)
 template <int QT>
 struct Bias {
-	static constexpr float value = QT == kQ8_0 ? 1152.0f : 1032.0f;
-	static constexpr unsigned short half = QT == kQ8_0 ? 0x6480 : 0x6408;  // fp16 of value
+	static constexpr unsigned short half = QT == kQ8_0 ? 0x6480 : 0x6408;  // fp16 1152 / 1032
 };
 
 // biased fp16 pair (BIAS + c0, BIAS + c1) -> the exact codes (c0, c1): the
@@ -344,7 +344,6 @@ struct StageLayout {
 	static constexpr int RS = kMaxKC / QK * BB + 16;          // smem row stride (padded)
 	static constexpr int BYTES = 16 * RS;                    // one stage
 	static constexpr int RED = kRedBufs * kMmaWarps * 32 * 16;
-	static constexpr int SSUM = kMmaWarps * 8 * 8 * 4;  // per warp [8 blocks][8 tokens] f32
 	static constexpr int EPI = kEpiWarps * kEpiStage * 4;  // epilogue staging tiles
 	// two 1024-column rows share one row slot (items of two m-tiles): rows
 	// 2j and 2j + 1 of the item, adjacent as in HBM, so one copy of 2 rows
@@ -664,7 +663,7 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 // other CTAs, so they are read through L2 (ld.global.cg), not the
 // read-only path.
 template <int QT, bool DUAL, int STAGES, int WB, bool COHERENT, int MT = 1>
-__device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red, float *ssum,
+__device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 			  const Bars &b, Pipe &p, int warp, int lane)
 {
 	constexpr bool FAST = WB % 4 == 0;  // biased fragments, aligned code loads

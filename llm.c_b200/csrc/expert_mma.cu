@@ -16,9 +16,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) expert_mma_kernel(MmaArgs a)
 	using SL = StageLayout<QT>;
 	uint8_t *p = smem + STAGES * SL::BYTES;
 	float4 *red = reinterpret_cast<float4 *>(p);                   // [kRedBufs][8][32]
-	float *ssum = reinterpret_cast<float *>(p + SL::RED);           // activation block sums
-	float *stg = reinterpret_cast<float *>(p + SL::RED + SL::SSUM); // epilogue staging
-	int32_t *en = reinterpret_cast<int32_t *>(p + SL::RED + SL::SSUM + SL::EPI);  // [256]
+	float *stg = reinterpret_cast<float *>(p + SL::RED);            // epilogue staging
+	int32_t *en = reinterpret_cast<int32_t *>(p + SL::RED + SL::EPI);  // [256]
 	int32_t *off = en + kMaxActive;                                 // [256]
 	int32_t *pre = off + kMaxActive;                                // [257]
 	uint64_t *bars = reinterpret_cast<uint64_t *>(pre + kMaxActive + 4);
@@ -48,7 +47,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) expert_mma_kernel(MmaArgs a)
 		core_epilogue<QT, DUAL, MT>(ph, red, stg + (warp - kEpiWarp0) * kEpiStage, b, pipe,
 					    warp - kEpiWarp0, lane);
 	else
-		core_math<QT, DUAL, STAGES, WB, false, MT>(ph, smem, red, ssum, b, pipe, warp, lane);
+		core_math<QT, DUAL, STAGES, WB, false, MT>(ph, smem, red, b, pipe, warp, lane);
 }
 
 // ---------------------------------------------------------------- x -> fp16 hi/lo
@@ -87,7 +86,7 @@ template <int QT, bool DUAL, int STAGES, int WB, int MT>
 static cudaError_t launch_t(const MmaArgs &a, cudaStream_t st)
 {
 	using SL = StageLayout<QT>;
-	const size_t smem = (size_t)STAGES * SL::BYTES + SL::RED + SL::SSUM + SL::EPI +
+	const size_t smem = (size_t)STAGES * SL::BYTES + SL::RED + SL::EPI +
 			    (3 * kMaxActive + 4) * 4 +
 			    (2 * STAGES + 2 * kRedBufs) * 8;
 	auto fn = expert_mma_kernel<QT, DUAL, STAGES, WB, MT>;
