@@ -44,6 +44,12 @@ namespace moe {
 
 constexpr int kMmaWarps = 8;                 // math warps per CTA
 constexpr int kTokTile = 8;                  // tokens per pass (one MMA n-tile)
+// An expert with more than 8 tokens streams its rows once per token tile:
+// the items of a CTA's segment are walked in chunks of this many, tile by
+// tile, so that the rows of the second and later tiles (the chunk's ~560 KB,
+// ~80 MB over the grid) are still in L2.  Activations are reloaded once per
+// chunk and tile instead of once per segment and tile.
+constexpr int kChunkItems = 16;
 constexpr int kMaxKC = 2048;                 // columns per stage
 constexpr int kRedBufs = 4;                  // partial-sum exchange buffers
 constexpr int kEpiWarps = 2;
@@ -480,8 +486,9 @@ __device__ void core_producer(const Phase &ph, uint8_t *stages, const Bars &b, P
 		const int n = ph.en[ai] >> 8;
 		const uint8_t *base = static_cast<const uint8_t *>(
 			(DUAL && lane >= 8) ? ph.w2[e] : ph.w1[e]);
+		for (int c0 = seg; c0 < seg_end; c0 += kChunkItems)
 		for (int tg = 0; tg < n; tg += kTokTile)
-		for (int item = seg; item < seg_end; item++) {
+		for (int item = c0; item < min(seg_end, c0 + kChunkItems); item++) {
 			const int r0 = (item - ai * groups) * ROWS;
 			// lane l (< COPY_ROWS) copies tile row l; two m-tiles: m-tile m's
 			// row j is item row 2j + m, and lane j < 16 copies rows 2j, 2j + 1
@@ -537,8 +544,9 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 	for (int seg = i0; seg < i1;) {
 		const int ai = seg / groups, seg_end = min(i1, (ai + 1) * groups);
 		const int n = ph.en[ai] >> 8, off = ph.off[ai];
+		for (int c0 = seg; c0 < seg_end; c0 += kChunkItems)
 		for (int tg = 0; tg < n; tg += kTokTile)
-		for (int item = seg; item < seg_end; item++, p.pass++) {
+		for (int item = c0; item < min(seg_end, c0 + kChunkItems); item++, p.pass++) {
 			const int r0 = (item - ai * groups) * ROWS;
 			if ((int)(p.pass % kEpiWarps) != epi)
 				continue;
@@ -685,8 +693,9 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 		const int ai = seg / groups, seg_end = min(i1, (ai + 1) * groups);
 		const int e = ph.en[ai] & 255;
 		const int n = ph.en[ai] >> 8, off = ph.off[ai];
+		for (int c0 = seg; c0 < seg_end; c0 += kChunkItems)
 		for (int tg = 0; tg < n; tg += kTokTile)
-		for (int item = seg; item < seg_end; item++, p.pass++) {
+		for (int item = c0; item < min(seg_end, c0 + kChunkItems); item++, p.pass++) {
 			float acc[4] = {0.f, 0.f, 0.f, 0.f};
 			for (int ch = 0; ch < nch; ch++, p.it++) {
 				const int kb0 = ch * (KC / QK) + kq * WB;  // first block (row-global)
