@@ -257,9 +257,9 @@ MOE_API int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols
 
 /* No counterpart in the reference.  moe_gemv_device without any device
  * allocation, for callers that cannot allocate at the point of the call: a
- * decode loop being recorded into a CUDA graph, a real-time loop that must
- * not take cudaMalloc's implicit synchronisation, or an engine whose device
- * memory budget is handed out by someone else.  Inputs and outputs as for
+ * real-time decode loop that must not take cudaMalloc's implicit
+ * synchronisation, or an engine whose device memory budget is fixed and
+ * handed out by someone else.  Inputs and outputs as for
  * moe_gemv_device (device pointers); the scratch (launch metadata and the
  * fp16 split of x) lives in one fixed 1 MiB device array inside the
  * library, so m * cols must not exceed 262080 (MOE_ERR_INVALID otherwise).

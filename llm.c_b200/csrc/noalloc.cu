@@ -2,12 +2,12 @@
 // its scratch in a fixed device array, so that a call allocates nothing.
 //
 // Who needs it: callers that cannot call cudaMalloc (or any allocator) at
-// the point of the call -- a decode loop being recorded into a CUDA graph
-// (allocation is not a stream operation and breaks a capture), a real-time
-// loop that must never pay cudaMalloc's implicit device synchronisation, or
-// a host engine embedded in a process whose device memory budget is fixed
-// and handed out by someone else.  They pass inputs and outputs; the
-// scratch lives in g_noalloc_scratch below.
+// the point of the call -- a real-time decode loop that must never pay
+// cudaMalloc's implicit device synchronisation, or a host engine embedded in
+// a process whose device memory budget is fixed and handed out by someone
+// else, so that a library allocating behind its back breaks the budget.
+// They pass inputs and outputs; the scratch lives in g_noalloc_scratch
+// below, which every GPU that loads the library holds until exit.
 //
 // Scratch layout (kNoallocBytes = 1 MiB):
 //   [0, 256)     launch metadata: expert pointer table, counts, offsets,
@@ -39,7 +39,7 @@ constexpr size_t kNoallocBytes = 1u << 20;
 constexpr size_t kNoallocMeta = 256;
 constexpr int kMaxDevices = 64;
 
-__device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocBytes];
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocBytes];
 
 struct NoallocMeta {
 	const void *w;          // expert pointer table of one "expert"

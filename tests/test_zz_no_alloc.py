@@ -2,11 +2,11 @@
 other test module).
 
 This entry point is for callers that cannot allocate device memory where they
-call the GEMV: a decode loop being recorded into a CUDA graph, a real-time
-loop that must not take cudaMalloc's implicit synchronisation, or an engine
-whose device memory budget is handed out by someone else.  Its scratch lives
-in a fixed 1 MiB device array inside the library, so it must give the same
-results as the allocating moe_gemv_device, call after call.
+call the GEMV: a real-time decode loop that must not take cudaMalloc's
+implicit synchronisation, or an engine whose device memory budget is fixed and
+handed out by someone else.  Its scratch lives in a fixed 1 MiB device array
+inside the library (the previous call's contents stay in it), so it must give
+the same results as the allocating moe_gemv_device, call after call.
 """
 import numpy as np
 import pytest
