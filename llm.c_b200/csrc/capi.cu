@@ -1081,6 +1081,11 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 	if (m == 0)
 		return MOE_OK;
 	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+	// one activation row (decode): the memory-bound GEMV, no scratch
+	if (m == 1 && moe::gemv1_supported(qtype, rows, cols, (uintptr_t)w, (uintptr_t)x, (uintptr_t)y)) {
+		CK(moe::launch_gemv1(w, qtype, rows, cols, x, y, st));
+		return MOE_OK;
+	}
 	// one "expert" holding all m rows of x: counts = {m}, offsets = {0, m}.
 	// The metadata and the fp16 split of x live in a per-thread device
 	// buffer, so calls from one thread must be ordered on one stream.

@@ -57,6 +57,12 @@ struct GemvArgs {
 };
 cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st);
 
+// gemv.cu: y[rows] = W[rows, cols] . x[cols] for one activation row (see the
+// file); needs cols % 64 == 0 and 4-byte aligned W (16-byte aligned x)
+bool gemv1_supported(int qtype, int64_t rows, int64_t cols, uintptr_t w, uintptr_t x, uintptr_t y);
+cudaError_t launch_gemv1(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
+			 float *y, cudaStream_t st);
+
 // expert_mma.cu: tensor-core grouped expert GEMV (decode).  Same segment
 // semantics as GemvArgs; activations are fp16 hi/lo rows [row][2][cols]
 // (Q4_0: each 32-element block stored in the permuted order of q4_slot).

@@ -96,3 +96,17 @@ def test_gemv_partial_row_tiles(moe, orc, qt, rows, cols, m):
     got = moe.gemv(w, qt, rows, cols, x)
     assert got.shape == ref.shape
     assert_output_close(got, ref)
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(1, 3, 64), (2, 5, 64), (1, 7, 192), (2, 1, 4160),
+                                          (1, 33, 96), (2, 2, 128)])
+def test_gemv_single_row(moe, orc, qt, rows, cols):
+    """one activation row: the warp-per-row GEMV (rows of an even number of
+    blocks; 96 columns = 3 blocks takes the general path) is fp32-accurate"""
+    w = orc.quantize(qt, orc.gauss(43, 7, rows * cols, 0.02).reshape(rows, cols))
+    x = orc.gauss(43, 8, cols, 1.0)
+    ref = orc.gemm_q(x[None], w, qt, rows)
+    got = moe.gemv(w, qt, rows, cols, x)
+    assert got.shape == ref.shape
+    assert float(np.abs(got - ref).max()) <= 1e-5
+    assert rel_l2(got, ref) <= 1e-5
