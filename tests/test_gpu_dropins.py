@@ -110,3 +110,42 @@ def test_gemv_single_row(moe, orc, qt, rows, cols):
     assert got.shape == ref.shape
     assert float(np.abs(got - ref).max()) <= 1e-5
     assert rel_l2(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(2, 37, 256), (1, 50, 512), (2, 16, 4096),
+                                          (1, 100, 2304), (2, 33, 14336), (1, 17, 14336),
+                                          (2, 2048, 4096), (1, 9, 16384), (2, 5, 16640)])
+def test_gemv_single_row_large(moe, orc, qt, rows, cols):
+    """one activation row at model sizes: rows of 256 to 16640 columns (one
+    to four load rounds per lane, the 14336-column down projection among
+    them), more rows than the grid has warps (2048), fp32-accurate"""
+    w = orc.quantize(qt, orc.gauss(47, 7, rows * cols, 0.02).reshape(rows, cols))
+    x = orc.gauss(47, 8, cols, 1.0)
+    ref = orc.gemm_q(x[None], w, qt, rows)
+    got = moe.gemv(w, qt, rows, cols, x)
+    assert got.shape == ref.shape
+    assert float(np.abs(got - ref).max()) <= 1e-5
+    assert rel_l2(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_gemv_single_row_unaligned_weights(moe, orc, qt):
+    """weights 4 bytes past a 16-byte boundary (the kernel needs 4-byte
+    alignment only: its loads are aligned 32-bit words)"""
+    rows, cols = 40, 512
+    w = orc.quantize(qt, orc.gauss(49, 7, rows * cols, 0.02).reshape(rows, cols))
+    x = orc.gauss(49, 8, cols, 1.0)
+    ref = orc.gemm_q(x[None], w, qt, rows)
+    bw = moe.DeviceBuffer(w.nbytes + 16)
+    bx = moe.DeviceBuffer.from_numpy(x)
+    by = moe.DeviceBuffer(rows * 4)
+    try:
+        moe.check(moe.lib().moe_memcpy_h2d(bw.ptr + 4, np.ascontiguousarray(w).ctypes.data, w.nbytes))
+        moe.gemv_device(bw.ptr + 4, qt, rows, cols, bx.ptr, 1, by.ptr)
+        moe.check(moe.lib().moe_sync())
+        got = by.to_numpy(np.float32, (1, rows))
+    finally:
+        for b in (bw, bx, by):
+            b.free()
+    assert float(np.abs(got - ref).max()) <= 1e-5
+    assert rel_l2(got, ref) <= 1e-5
