@@ -72,9 +72,31 @@ struct Ctx {
 	void *dev_io = nullptr;
 	size_t dev_io_bytes = 0;
 	std::map<std::vector<uintptr_t>, moe_layer *> layers;
+	// moe_ffn_forward's repeat calls: (router, gate, up, down host bases,
+	// qtype, experts, d_ff, d_model, top-k) -> the layer in `layers`
+	std::map<std::array<uintptr_t, 9>, moe_layer *> ffn_fast;
 };
 
 Ctx g;
+
+// Destroy the cached layers whose key points into [host, host + bytes) (their
+// device weights are about to be freed); the repeat-call map only refers to
+// cached layers, so it is emptied.
+void drop_layers_in(uintptr_t host, size_t bytes)
+{
+	g.ffn_fast.clear();
+	for (auto lt = g.layers.begin(); lt != g.layers.end();) {
+		bool hit = false;
+		for (uintptr_t k : lt->first)
+			hit |= k >= host && k < host + bytes;
+		if (hit) {
+			moe_layer_destroy(lt->second);
+			lt = g.layers.erase(lt);
+		} else {
+			++lt;
+		}
+	}
+}
 
 // NCCL, loaded at run time (no link dependency): the expert-parallel
 // communicator of larger batches.  dlopen by soname reuses a libnccl.so.2
@@ -174,6 +196,7 @@ int resolve(const void *hp, size_t bytes, const void **dev)
 	auto same = g.regs.find(p);
 	if (same != g.regs.end()) {
 		CK(cudaDeviceSynchronize());
+		drop_layers_in(same->second.host, same->second.bytes);
 		cudaFree(same->second.dev);
 		g.resident -= same->second.bytes;
 		g.regs.erase(same);
@@ -354,6 +377,7 @@ int moe_shutdown(void)
 	for (auto &kv : g.layers)
 		moe_layer_destroy(kv.second);
 	g.layers.clear();
+	g.ffn_fast.clear();
 	for (auto &kv : g.regs)
 		cudaFree(kv.second.dev);
 	g.regs.clear();
@@ -449,18 +473,7 @@ int moe_unregister_weights(const moe_tensor_t *t)
 	if (it == g.regs.end())
 		return fail(MOE_ERR_INVALID, "moe_unregister_weights: tensor not registered");
 	CK(cudaStreamSynchronize(g.stream));
-	// drop cached layers that point into this range
-	for (auto lt = g.layers.begin(); lt != g.layers.end();) {
-		bool hit = false;
-		for (uintptr_t k : lt->first)
-			hit |= k >= it->second.host && k < it->second.host + it->second.bytes;
-		if (hit) {
-			moe_layer_destroy(lt->second);
-			lt = g.layers.erase(lt);
-		} else {
-			++lt;
-		}
-	}
+	drop_layers_in(it->second.host, it->second.bytes);
 	cudaFree(it->second.dev);
 	g.resident -= it->second.bytes;
 	g.regs.erase(it);
@@ -1321,10 +1334,10 @@ int moe_fused_ffn_silu(const moe_tensor_t *in, moe_tensor_t *out, moe_tensor_t *
 // ---------------------------------------------------------------- layer drop-ins
 namespace {
 
-int forward_common(const moe_tensor_t *input, moe_tensor_t *output, const moe_tensor_t *gate_inp,
-		   int qtype, int64_t NE, int64_t F, const std::vector<const void *> &hg,
-		   const std::vector<const void *> &hu, const std::vector<const void *> &hd,
-		   size_t gbytes, size_t dbytes, size_t topk, int flags)
+// the tensors of a drop-in forward against the experts' shape: input
+// [T, Dw] fp32, router [NE, Dw] fp32, output room for T x Dw (host IO)
+int check_io(const moe_tensor_t *input, const moe_tensor_t *output, const moe_tensor_t *gate_inp,
+	     int64_t NE, int64_t Dw, int flags)
 {
 	if (!input || !output || !gate_inp)
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: null tensor");
@@ -1332,12 +1345,45 @@ int forward_common(const moe_tensor_t *input, moe_tensor_t *output, const moe_te
 	    gate_inp->ndim != 2)
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: input/router must be 2-D fp32");
 	const int64_t T = (int64_t)input->dim[0], D = (int64_t)input->dim[1];
+	if (D != Dw)
+		return fail(MOE_ERR_INVALID, "moe_ffn_forward: input rows of %lld, experts take %lld",
+			    (long long)D, (long long)Dw);
 	if ((int64_t)gate_inp->dim[0] != NE || (int64_t)gate_inp->dim[1] != D)
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: router is [%llu,%llu], want [%lld,%lld]",
 			    (unsigned long long)gate_inp->dim[0], (unsigned long long)gate_inp->dim[1],
 			    (long long)NE, (long long)D);
 	if (output->maxcap < (uint64_t)(T * D) && !(flags & MOE_DEVICE_IO))
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: output too small");
+	return MOE_OK;
+}
+
+// the forward of a cached layer: device pointers as given (MOE_DEVICE_IO),
+// else the tokens copied in from the host and the output copied back
+int forward_io(moe_layer *L, const moe_tensor_t *input, moe_tensor_t *output, int flags)
+{
+	const int64_t T = (int64_t)input->dim[0], D = (int64_t)input->dim[1];
+	if (flags & MOE_DEVICE_IO)
+		return moe_layer_forward(L, input->data, output->data, T, flags, nullptr);
+	const size_t xb = align_up(T * D * 4, 256);
+	if (int rc = ensure_dev_io(2 * xb))
+		return rc;
+	float *dx = (float *)g.dev_io, *dy = (float *)((char *)g.dev_io + xb);
+	CK(cudaMemcpyAsync(dx, input->data, T * D * 4, cudaMemcpyHostToDevice, g.stream));
+	if (int rc = moe_layer_forward(L, dx, dy, T, flags, nullptr))
+		return rc;
+	CK(cudaMemcpyAsync(output->data, dy, T * D * 4, cudaMemcpyDeviceToHost, g.stream));
+	CK(cudaStreamSynchronize(g.stream));
+	return MOE_OK;
+}
+
+int forward_common(const moe_tensor_t *input, moe_tensor_t *output, const moe_tensor_t *gate_inp,
+		   int qtype, int64_t NE, int64_t F, int64_t Dw, const std::vector<const void *> &hg,
+		   const std::vector<const void *> &hu, const std::vector<const void *> &hd,
+		   size_t gbytes, size_t dbytes, size_t topk, int flags, moe_layer **used)
+{
+	if (int rc = check_io(input, output, gate_inp, NE, Dw, flags))
+		return rc;
+	const int64_t D = Dw;
 	if (int rc = ensure_init())
 		return rc;
 	// resolve device weights (upload on first sight)
@@ -1381,18 +1427,9 @@ int forward_common(const moe_tensor_t *input, moe_tensor_t *output, const moe_te
 			return rc;
 		g.layers[key] = L;
 	}
-	if (flags & MOE_DEVICE_IO)
-		return moe_layer_forward(L, input->data, output->data, T, flags, nullptr);
-	const size_t xb = align_up(T * D * 4, 256);
-	if (int rc = ensure_dev_io(2 * xb))
-		return rc;
-	float *dx = (float *)g.dev_io, *dy = (float *)((char *)g.dev_io + xb);
-	CK(cudaMemcpyAsync(dx, input->data, T * D * 4, cudaMemcpyHostToDevice, g.stream));
-	if (int rc = moe_layer_forward(L, dx, dy, T, flags, nullptr))
-		return rc;
-	CK(cudaMemcpyAsync(output->data, dy, T * D * 4, cudaMemcpyDeviceToHost, g.stream));
-	CK(cudaStreamSynchronize(g.stream));
-	return MOE_OK;
+	if (used)
+		*used = L;
+	return forward_io(L, input, output, flags);
 }
 
 }  // namespace
@@ -1418,6 +1455,20 @@ int moe_ffn_forward(const moe_tensor_t *input, moe_tensor_t *output, const moe_t
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: expert shapes disagree");
 	if (qt != MOE_Q8_0 && qt != MOE_Q4_0)
 		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward: expert dtype %d", qt);
+	// repeat call with the same tensors: the cached layer, without
+	// resolving every expert's view again (~200 lookups and a 198-entry key)
+	const std::array<uintptr_t, 9> fk{(uintptr_t)(gate_inp ? gate_inp->data : nullptr),
+					 (uintptr_t)gate_exps->qdata, (uintptr_t)up_exps->qdata,
+					 (uintptr_t)down_exps->qdata, (uintptr_t)qt, (uintptr_t)NE,
+					 (uintptr_t)F, (uintptr_t)D, (uintptr_t)topk};
+	if (g.init) {
+		auto ft = g.ffn_fast.find(fk);
+		if (ft != g.ffn_fast.end()) {
+			if (int rc = check_io(input, output, gate_inp, NE, D, flags))
+				return rc;
+			return forward_io(ft->second, input, output, flags);
+		}
+	}
 	// tensor_at_q (olmoe.c:20-60): expert e starts e*rows*(cols/32)*bsz bytes in
 	const size_t gb = (size_t)(F * qrow_bytes(qt, D)), db = (size_t)(D * qrow_bytes(qt, F));
 	if (int rc = ensure_init())
@@ -1436,7 +1487,12 @@ int moe_ffn_forward(const moe_tensor_t *input, moe_tensor_t *output, const moe_t
 		hu[e] = (const char *)up_exps->qdata + e * gb;
 		hd[e] = (const char *)down_exps->qdata + e * db;
 	}
-	return forward_common(input, output, gate_inp, qt, NE, F, hg, hu, hd, gb, db, topk, flags);
+	moe_layer *L = nullptr;
+	const int rc = forward_common(input, output, gate_inp, qt, NE, F, D, hg, hu, hd, gb, db, topk,
+				      flags, &L);
+	if (L)
+		g.ffn_fast[fk] = L;
+	return rc;
 }
 
 int moe_ffn_forward_split(const moe_tensor_t *input, moe_tensor_t *output,
@@ -1462,8 +1518,8 @@ int moe_ffn_forward_split(const moe_tensor_t *input, moe_tensor_t *output,
 		hd[e] = c->qdata;
 	}
 	const size_t gb = (size_t)(F * qrow_bytes(qt, D)), db = (size_t)(D * qrow_bytes(qt, F));
-	return forward_common(input, output, gate_inp, qt, (int64_t)n_experts, F, hg, hu, hd, gb,
-			      db, topk, flags);
+	return forward_common(input, output, gate_inp, qt, (int64_t)n_experts, F, D, hg, hu, hd, gb,
+			      db, topk, flags, nullptr);
 }
 
 }  // extern "C"

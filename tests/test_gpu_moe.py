@@ -205,6 +205,36 @@ def test_host_dropin_matches_device_layer(moe, orc, small_layers):
     assert_output_close(host, ref)
 
 
+def test_host_dropin_repeat_and_reregister(moe, orc):
+    """moe_ffn_forward called again with the same tensors reuses its cached
+    layer (same output); after moe_unregister_weights and new contents at the
+    same host addresses, the next call uploads and uses the new weights; a
+    token width that differs from the experts' is refused"""
+    import ctypes as C
+    d, F, NE, K = SMALL["d"], SMALL["F"], SMALL["NE"], SMALL["K"]
+    L1 = orc.make_layer(21, d, F, NE, K, orc.Q8_0)
+    L2 = orc.make_layer(22, d, F, NE, K, orc.Q8_0)
+    router = np.array(L1["router_w"], np.float32, copy=True)
+    gate, up, down = (np.array(L1[k], copy=True) for k in ("gate", "up", "down"))
+    x = orc.make_tokens(10, 23, d)
+    a = moe.ffn_forward(x, router, gate, up, down, orc.Q8_0, K)
+    b = moe.ffn_forward(x, router, gate, up, down, orc.Q8_0, K)
+    np.testing.assert_array_equal(a, b)
+    assert_output_close(a, orc.moe_ffn(L1, x)[0])
+    views = [moe.tensor(router), moe.tensor(gate, orc.Q8_0, (NE, F, d)),
+             moe.tensor(up, orc.Q8_0, (NE, F, d)), moe.tensor(down, orc.Q8_0, (NE, d, F))]
+    for t in views:
+        moe.check(moe.lib().moe_unregister_weights(C.byref(t)))
+    router[...] = L2["router_w"]
+    gate[...], up[...], down[...] = L2["gate"], L2["up"], L2["down"]
+    c = moe.ffn_forward(x, router, gate, up, down, orc.Q8_0, K)
+    assert_output_close(c, orc.moe_ffn(L2, x)[0])
+    with pytest.raises(moe.MoeError):
+        moe.ffn_forward(np.zeros((2, 2 * d), np.float32), router, gate, up, down, orc.Q8_0, K)
+    for t in views:
+        moe.check(moe.lib().moe_unregister_weights(C.byref(t)))
+
+
 @pytest.mark.parametrize("qt", [1, 2])
 def test_simple_and_mma_paths_agree(moe, orc, small_layers, qt):
     """the plain CUDA-core kernels (MOE_SIMPLE) cross-check the MMA kernels"""
