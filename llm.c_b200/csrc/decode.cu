@@ -410,6 +410,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			if (warp >= kEpiWarp0)
 				core_epilogue<QT, true>(gu, red, stg + (warp - kEpiWarp0) * kEpiStage, b, pipe,
 							warp - kEpiWarp0, lane);
+			else if (D > WB_GU * kMmaWarps * QK)  // rows of several stages
+				core_math<QT, true, STAGES, WB_GU, true, 1, true>(gu, smem, red, b, pipe, warp, lane);
 			else
 				core_math<QT, true, STAGES, WB_GU, true>(gu, smem, red, b, pipe, warp, lane);
 			// every CTA's h rows must be written before any CTA reads them
@@ -422,6 +424,9 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			if (warp >= kEpiWarp0)
 				core_epilogue<QT, false, MT_DN>(dn, red, stg + (warp - kEpiWarp0) * kEpiStage, b,
 								pipe, warp - kEpiWarp0, lane);
+			else if (F > WB_DN * (kMmaWarps / MT_DN) * QK)
+				core_math<QT, false, STAGES, WB_DN, true, MT_DN, true>(dn, smem, red, b, pipe,
+										warp, lane);
 			else
 				core_math<QT, false, STAGES, WB_DN, true, MT_DN>(dn, smem, red, b, pipe, warp,
 									  lane);

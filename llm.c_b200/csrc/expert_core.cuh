@@ -669,8 +669,12 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 // ---------------------------------------------------------------- math warps
 // COHERENT: the activations were written earlier in the same kernel by
 // other CTAs, so they are read through L2 (ld.global.cg), not the
-// read-only path.
-template <int QT, bool DUAL, int STAGES, int WB, bool COHERENT, int MT = 1>
+// read-only path.  PF: rows span several stages; as each block's activation
+// fragments are used up, the same token tile's fragments of the next column
+// chunk are loaded into them, so the next stage does not start with a round
+// trip to L2 (a wrong guess, at a tile or segment change, is caught by the
+// key check and reloaded).
+template <int QT, bool DUAL, int STAGES, int WB, bool COHERENT, int MT = 1, bool PF = false>
 __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 			  const Bars &b, Pipe &p, int warp, int lane)
 {
@@ -687,6 +691,7 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 	const int g = lane >> 2, c = lane & 3;
 	uint4 xh[WB], xl[WB];
 	int x_e = -1, x_tg = -1, x_ch = -1;  // key of the fragments in registers
+	const __half *x_px = nullptr;        // their token row (hi part, lane quad c)
 	int i0, i1;
 	item_range(ph.en, ph.pre, ph.n_active, groups, i0, i1);
 	for (int seg = i0; seg < i1;) {
@@ -706,6 +711,7 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 					const int pos = off + t;
 					const int row = ph.in_perm ? ph.perm[pos] / ph.K : pos;
 					const __half *px = ph.in16 + (int64_t)row * 2 * cols + 8 * c;
+					x_px = px;
 #pragma unroll
 					for (int bq = 0; bq < WB; bq++) {
 						const uint4 *ph_ = reinterpret_cast<const uint4 *>(px + (kb0 + bq) * QK);
@@ -728,6 +734,9 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 				if (!p.failed) {
 					const uint8_t *wt =
 						stages + st * SL::BYTES + (kq * WB) * BB + (MT == 2 ? mt * SL::HALF : 0);
+					const bool pf = PF && nch > 1;
+					const int ch_n = ch + 1 < nch ? ch + 1 : 0;
+					const __half *pf_src = x_px + (ch_n * (KC / QK) + kq * WB) * QK;
 					if constexpr (FAST) {
 						static_for<WB>([&](auto J) {
 							constexpr int bq = decltype(J)::value;
@@ -751,7 +760,15 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 							acc[1] = __fmaf_rn(d0, t[1], acc[1]);
 							acc[2] = __fmaf_rn(d1, t[2], acc[2]);
 							acc[3] = __fmaf_rn(d1, t[3], acc[3]);
+							if (pf) {
+								const uint4 *ph_ = reinterpret_cast<const uint4 *>(pf_src + bq * QK);
+								const uint4 *pl_ = reinterpret_cast<const uint4 *>(pf_src + cols + bq * QK);
+								xh[bq] = COHERENT ? __ldcg(ph_) : __ldg(ph_);
+								xl[bq] = COHERENT ? __ldcg(pl_) : __ldg(pl_);
+							}
 						});
+						if (pf)
+							x_ch = ch_n;
 					} else
 #pragma unroll
 					for (int bq = 0; bq < WB; bq++) {
