@@ -4,21 +4,24 @@ tokens/s and achieved HBM TB/s).
 
 Default workload = BASELINE config 0: one OLMoE-1B-7B-shaped MoE FFN layer
 (d_model 2048, 64 experts, top-8 without renormalisation, d_ff 1024 SwiGLU,
-Q8_0 experts, fp32 router) on T = 32 tokens.  A step is one layer forward
-over the T tokens.  Weights are synthetic (seeded N(0, 0.02) through the
-shared generator, quantized to Q8_0 on the device); NL distinct layers are
-rotated so that every step streams 428 MB of experts that are not in the
-126 MB L2.
+Q8_0 experts, fp32 router) on T = 32 tokens per GPU.  A step is one layer
+forward.  Weights are synthetic (seeded N(0, 0.02) through the shared
+generator, quantized to Q8_0 on the device); NL distinct layers are rotated
+so that every step streams experts that are not in the 126 MB L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--tokens T] [--layers NL] [--prefill-tokens P]
+                  [--tokens T] [--layers NL] [--prefill-tokens P] [--no-sweeps] ...
 
-Prints one JSON line (rank 0).  Under torchrun the layer is expert-parallel:
-rank r holds experts expert_range(r) of every layer, every rank gets the
-same T tokens and ends with the full output (strong scaling); the time is
-the max over ranks.  On one GPU the line also carries a "prefill" object:
-the same layers on P tokens (default 2048), which runs the tcgen05 grouped
-GEMM, with its tensor roofline.
+Prints one JSON line (rank 0).  Under torchrun the layer is expert-parallel
+and token-sharded: rank r holds experts expert_range(r) of every layer and
+its own T tokens (rows [r*T, r*T+T) of one global batch), so the work per GPU
+is fixed as N grows (weak scaling); the time is the max over ranks and the
+value counts every rank's tokens.  The line also carries: the replicated-token
+variant at N > 1 (every rank the same tokens, strong scaling), the prefill leg
+(P tokens per GPU, the tcgen05 grouped GEMM, NCCL all-to-all at N > 1), the
+config-1 GEMV, the config-3 (Mixtral-shaped) and config-4 (Zipf-skewed) token
+sweeps, the reference CPU baseline on identical bytes, and a parity block
+(the measured layer's output against the reference or the oracle).
 """
 from __future__ import annotations
 
@@ -108,7 +111,8 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-# --------------------------------------------------------------------------- ours
+
+
 def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=None,
                  router_bias=None, flags=0):
     """NL device-resident layers generated on the GPU (generator tags: router
@@ -146,7 +150,11 @@ def build_layers(moe, nl, seed0, d, F, NE, K, qtype, stream, first=0, n_local=No
     return layers, keep
 
 
-def run_ours(args, rank, world, local_rank):
+# --------------------------------------------------------------------------- ours
+DECODE_MAX_T = 64   # batches above this take the prefill GEMM path
+
+
+def init_rank(world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
     moe = load_package()
@@ -161,62 +169,53 @@ def run_ours(args, rank, world, local_rank):
     # library reads as "use the library stream"
     torch_stream = torch.cuda.Stream()
     torch.cuda.set_stream(torch_stream)
-    stream = torch_stream.cuda_stream
-    d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
-    T = args.tokens
-    NL = args.layers
-    # N > 1: expert parallelism, rank r holds experts expert_range(r) of every
-    # layer; the tokens are the same on every rank (replicated, as after a
-    # replicated attention block) and every rank ends with the full output
-    first, n_local = moe.expert_range(rank, world, NE)
-    layers, keep = build_layers(moe, NL, 0, d, F, NE, K, qtype, stream, first, n_local)
-    if world > 1:
-        def gather(obj):
-            got = [None] * world
-            dist.all_gather_object(got, obj)
-            return got
-        for lay in layers:
-            moe.connect_expert_parallel(lay, rank, gather)
-        # batches above 64 tokens sum the ranks' partial outputs (NCCL)
-        moe.init_expert_parallel_comm(rank, world, gather)
-    # tokens: config-0 input seed 0, tag 5
-    x = torch.empty(T * d, dtype=torch.float32, device="cuda")
-    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 5, 0, T * d, 1.0, stream))
-    out = torch.empty(T * d, dtype=torch.float32, device="cuda")
+    return torch, moe, dist, torch_stream
 
-    def step(i, flags=0):
-        layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), T, flags, stream)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
+def gather_fn(dist, world):
+    def gather(obj):
+        got = [None] * world
+        dist.all_gather_object(got, obj)
+        return got
+    return gather
 
-    # routing of the layers (distinct experts touched = algorithmic bytes)
-    uniq, pairs_local = [], []
-    for l in range(NL):
-        step(l)
-        ids_all = layers[l].routing(T)[0]
-        ids = np.unique(ids_all)
-        uniq.append(int(((ids >= first) & (ids < first + n_local)).sum()))  # this rank's experts
-        pairs_local.append(int(((ids_all >= first) & (ids_all < first + n_local)).sum()))
-    torch.cuda.synchronize()
 
-    # The timed steps replay a CUDA graph of the NL rotated layer forwards
-    # (one graph launch per NL steps), so host launch overhead is out of the
-    # device timing.  Each captured forward records per-stage timestamps
-    # (external event records) that reflect the last replay.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=torch_stream, capture_error_mode="relaxed"):
+def max_over_ranks(dist, v):
+    if not dist:
+        return v
+    import torch
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def synth_tokens(moe, torch, n_tok, d, seed, tag, first_tok, stream):
+    """rows [first_tok, first_tok + n_tok) of the token stream (seed, tag)"""
+    x = torch.empty(n_tok * d, dtype=torch.float32, device="cuda")
+    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), seed, tag, first_tok * d, n_tok * d, 1.0,
+                                        stream))
+    return x
+
+
+def time_graph_steps(torch, dist, torch_stream, step, NL, K, profile_flag):
+    """Exactly K layer forwards (step(i, flags)) from CUDA graphs: a graph of
+    NL rotated forwards replayed K // NL times plus a graph of the first
+    K % NL forwards; CUDA events on the launching stream, max over ranks.
+    Returns (ms for the K steps, the NL-forward graph, host enqueue ms)."""
+    g_full = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_full, stream=torch_stream, capture_error_mode="relaxed"):
         for l in range(NL):
-            step(l, moe.PROFILE)
-    graph.replay()
+            step(l, profile_flag)
+    g_full.replay()
+    rem = K % NL
+    g_rem = None
+    if rem:
+        g_rem = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_rem, stream=torch_stream, capture_error_mode="relaxed"):
+            for l in range(rem):
+                step(l, 0)
+        g_rem.replay()
     torch.cuda.synchronize()
-    reps = max(1, args.steps // NL)
-    args.steps = reps * NL
-
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    time.sleep(0.3)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -224,15 +223,83 @@ def run_ours(args, rank, world, local_rank):
     ev1 = torch.cuda.Event(enable_timing=True)
     h0 = time.perf_counter()
     ev0.record(torch_stream)
-    for _ in range(reps):
-        graph.replay()
+    for _ in range(K // NL):
+        g_full.replay()
+    if g_rem is not None:
+        g_rem.replay()
     ev1.record(torch_stream)
     host_ms = (time.perf_counter() - h0) * 1e3
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1))
+    return ms, g_full, host_ms
+
+
+def time_graph_long(torch, dist, torch_stream, g_full, NL, ms_per_step, min_ms=200.0):
+    """the same graph replayed for at least min_ms (a steadier figure beside
+    the exact-K one)"""
+    reps = max(1, int(min_ms / max(ms_per_step * NL, 1e-3)) + 1)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(torch_stream)
+    for _ in range(reps):
+        g_full.replay()
+    ev1.record(torch_stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1))
+    return {"steps": reps * NL, "ms_per_step": ms / (reps * NL), "timed_ms": ms}
+
+
+def run_ours(args, rank, world, local_rank):
+    torch, moe, dist, torch_stream = init_rank(world, local_rank)
+    stream = torch_stream.cuda_stream
+    d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
+    T, NL = args.tokens, args.layers
+    first, n_local = moe.expert_range(rank, world, NE)
+    layers, keep = build_layers(moe, NL, 0, d, F, NE, K, qtype, stream, first, n_local)
+    if world > 1:
+        gather = gather_fn(dist, world)
+        for lay in layers:
+            moe.connect_expert_parallel(lay, rank, gather)
+        moe.init_expert_parallel_comm(rank, world, gather)
+    # N > 1: token-sharded expert parallelism.  Rank r holds experts
+    # expert_range(r) of every layer and its own T tokens, rows [r*T, r*T+T)
+    # of one global batch (as data-parallel attention feeds an
+    # expert-parallel FFN); tokens go to the experts' ranks and rows back.
+    shard = moe.EP_SHARDED if world > 1 else 0
+    x = synth_tokens(moe, torch, T, d, 0, 5, rank * T, stream)   # config-0 tokens: seed 0, tag 5
+    out = torch.empty(T * d, dtype=torch.float32, device="cuda")
+
+    def step(i, flags=0):
+        layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), T, shard | flags, stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # routing of each layer: this rank's experts that received pairs (their
+    # bytes are the algorithmic bytes) and its pairs
+    uniq, pairs_local = [], []
+    for l in range(NL):
+        step(l)
+        counts = layers[l].routing(T, world)[2]
+        loc = counts[first:first + n_local]
+        uniq.append(int((loc > 0).sum()))
+        pairs_local.append(int(loc.sum()))
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    ms_total, g_full, host_ms = time_graph_steps(torch, dist, torch_stream, step, NL, args.steps,
+                                                 moe.PROFILE)
+    ms_step = ms_total / args.steps
+    long_run = time_graph_long(torch, dist, torch_stream, g_full, NL, ms_step)
     clk = clocks.stop()
-    ms_total = ev0.elapsed_time(ev1)
     stage = np.zeros(5)
     nprof = 0
     for lay in layers:
@@ -242,21 +309,9 @@ def run_ours(args, rank, world, local_rank):
             nprof += c
         except moe.MoeError:
             pass
-    if dist:
-        t = torch.tensor([ms_total], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
-    ms_step = ms_total / args.steps
-    # every rank ends a step with the output of the same T tokens
-    tokens_per_s = T * args.steps / (ms_total / 1e3)
-
-    # ---- e2e: reference-facing tensor_t call with host buffers (H2D + D2H inside)
-    if args.no_e2e:
-        e2e = None
-    elif world == 1:
-        e2e = run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist)
-    else:
-        e2e = run_e2e_ep(moe, args, layers, T, d, stream, dist)
+    status = [lay.status() for lay in layers]
+    del g_full
+    tokens_per_s = world * T * args.steps / (ms_total / 1e3)
 
     # ---- roofline of the dominant kernel: the fused decode-layer kernel, one
     # launch per layer forward (router, routing, gate/up + SwiGLU, down, combine)
@@ -266,22 +321,24 @@ def run_ours(args, rank, world, local_rank):
     stage_avg = stage / max(nprof, 1)
     kernel_ms = float(stage_avg.sum())
     achieved = layer_bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms > 0 else None
+    stage_names = ["router", "routing", "gate_up", "down", "combine"]
     roof = {"bound": "hbm",
             "kernel": "moe_decode_kernel<Q8_0, 16 lanes> (whole MoE layer, one launch)",
             "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
             "frac": achieved / hbm_peak if achieved else None, "traffic": None,
-            "peak_source": peak_kind,
+            "peak_source": peak_kind + " (burst copy bandwidth)",
             "algorithmic_bytes_per_launch": layer_bytes, "avg_launch_ms": kernel_ms,
+            "bytes_basis": "this rank's routed experts x 6,684,672 B + router 524,288 B + "
+                           "its tokens in and out",
             "launch_time_source": "%globaltimer stamps of every CTA (earliest start to "
                                   "latest end), averaged over the profiled replays",
             "step_achieved_gbs": layer_bytes / (ms_step / 1e3) / 1e9,
-            "stage_ms_avg": {n: float(v) for n, v in
-                             zip(["router", "routing", "gate_up", "down", "combine"], stage_avg)}}
+            "stage_ms_avg": {n: float(v) for n, v in zip(stage_names, stage_avg)}}
     if T > DECODE_MAX_T:
         roof = dict(gemm_roofline(stage_avg, float(np.mean(pairs_local)), d, F),
                     stage_ms_avg=roof["stage_ms_avg"], step_ms=ms_step)
     traffic = os.path.join(ROOT, "profiles", "traffic.json")
-    if T <= DECODE_MAX_T and os.path.exists(traffic):
+    if T <= DECODE_MAX_T and world == 1 and os.path.exists(traffic):
         with open(traffic) as f:
             tj = json.load(f)
         # DRAM bytes of one captured launch, scaled by the routed experts
@@ -290,52 +347,129 @@ def run_ours(args, rank, world, local_rank):
             roof["traffic"] = per_expert * float(np.mean(U)) + fixed
             roof["traffic_source"] = "profiles/" + tj.get("source", "traffic.json")
 
+    # ---- parity of the measured layer: layer 0 on this rank's tokens again,
+    # checked on rank 0 (N = 1: against the reference itself, in cpu_baseline)
+    layers[0].forward_device(x.data_ptr(), out.data_ptr(), T, shard, stream)
+    torch.cuda.synchronize()
+    out0 = out.view(T, d).cpu().numpy().copy()
+    ids0 = layers[0].routing(T, world)[0]
+    x_host = x.view(T, d).cpu().numpy().copy()
+
+    # ---- replicated tokens (N > 1): every rank the same T tokens and the full
+    # output (strong scaling of the same kernel), for comparison
+    replicated = None
+    if world > 1 and not args.no_replicated:
+        xr = synth_tokens(moe, torch, T, d, 0, 5, 0, stream)
+
+        def step_rep(i, flags=0):
+            layers[i % NL].forward_device(xr.data_ptr(), out.data_ptr(), T, flags, stream)
+
+        for i in range(max(3, NL)):
+            step_rep(i)
+        torch.cuda.synchronize()
+        ms_rep, g_rep, _ = time_graph_steps(torch, dist, torch_stream, step_rep, NL, 4 * NL,
+                                            moe.PROFILE)
+        del g_rep
+        st_rep = np.zeros(5)
+        n_rep = 0
+        for lay in layers:
+            s, c = lay.stage_ms()
+            st_rep += np.array(s)
+            n_rep += c
+        replicated = {"value": T * 4 * NL / (ms_rep / 1e3), "unit": "tokens/s",
+                      "ms_per_step": ms_rep / (4 * NL), "steps": 4 * NL,
+                      "scaling": "strong",
+                      "stage_ms_avg": {n: float(v) for n, v in
+                                       zip(stage_names, st_rep / max(n_rep, 1))},
+                      "how": "every rank the same T tokens; each (token, slot) row of a rank's "
+                             "experts written into every rank's exchange buffer; every rank "
+                             "combines the full output"}
+
+    # ---- e2e: the reference-facing call with host buffers (H2D + D2H inside)
+    if args.no_e2e:
+        e2e = None
+    elif world == 1:
+        e2e = run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist)
+    else:
+        e2e = run_e2e_ep(moe, args, layers, x_host, T, d, stream, dist)
+
     prefill = None
     if args.prefill_tokens > 0:
-        prefill = run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream, dist)
+        prefill = run_prefill(moe, torch, args, layers, rank, world, d, F, NE, K, stream,
+                              torch_stream, dist)
 
     gemv1 = None
     if world == 1 and not args.no_gemv:
         gemv1 = run_config1_gemv(moe, stream, torch_stream)
 
-    cpu = None
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(moe, keep[0], x, T, d, F, NE, K, qtype)
+        cpu, parity = cpu_baseline(keep[0], x_host, out0, ids0, T, d, F, NE, K, qtype)
+    elif rank == 0 and not args.no_parity:
+        parity = oracle_parity(x_host, out0, ids0, d, F, NE, K, args.parity_tokens)
+
+    sweeps = {}
+    if not args.no_sweeps:
+        # free all but layer 0 first (no rank may still write into them)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        for lay in layers[1:]:
+            lay.close()
+        del layers[1:], keep[1:]
+        torch.cuda.empty_cache()
+        sweeps["config4"] = sweep_leg(moe, torch, dist, rank, world, torch_stream, "olmoe",
+                                      [int(t) for t in args.sweep4.split(",") if t])
+        sweeps["config3"] = sweep_leg(moe, torch, dist, rank, world, torch_stream, "mixtral",
+                                      [int(t) for t in args.sweep3.split(",") if t],
+                                      cpu_tokens=0 if (world > 1 or args.no_cpu) else 2)
 
     line = {
-        "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d)" % T,
+        "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d%s)" % (
+            T, " per GPU" if world > 1 else ""),
         "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32 activations x Q8_0 weights",
+        "scaling": "weak" if world > 1 else "strong", "vs_baseline": None,
+        "dtype": "fp32 activations x Q8_0 weights",
         "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) tokens)",
         "config": {"workload": "config0: OLMoE-1B-7B MoE FFN layer, d 2048, 64 experts top-8, "
-                               "d_ff 1024 SwiGLU, Q8_0, T=%d tokens" % T,
-                   "tokens_per_step": T, "layers_rotated": NL,
+                               "d_ff 1024 SwiGLU, Q8_0, T=%d tokens per GPU" % T,
+                   "tokens_per_step": world * T, "tokens_per_gpu": T, "layers_rotated": NL,
                    "l2": f"{NL} distinct layers rotated; each step streams "
-                         f"{np.mean(U) * EXPERT_BYTES_Q8 / 1e6:.0f} MB of experts > 126 MB L2",
-                   "parallelism": (f"expert-parallel x{world}: {n_local} experts per GPU, the "
-                                   "(token, slot) rows exchanged over NVLink inside the fused "
-                                   "kernel, every GPU combines the full output")
+                         f"{np.mean(U) * EXPERT_BYTES_Q8 / 1e6:.0f} MB of experts per GPU "
+                         f"(> 126 MB L2 over the rotation)",
+                   "parallelism": (f"expert-parallel x{world}, token-sharded: {n_local} experts "
+                                   f"and {T} tokens per GPU; tokens and top-k ids to every rank "
+                                   "and each (token, slot) row back to its token's rank over "
+                                   "NVLink inside the fused kernel")
                                   if world > 1 else "single GPU"},
-        "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+        "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "parity": parity, "clocks": clk,
         # one fused decode-layer kernel per forward; above 64 tokens: router,
         # top-k + dispatch (one launch up to 256 tokens, two above), gather,
         # two GEMMs and the combine
         "gpu_launches": args.steps * (1 if T <= DECODE_MAX_T else 6 if T <= 256 else 7),
         "host_enqueue_ms": host_ms,
-        "timing": "CUDA events on the launching stream around CUDA-graph replays "
-                  f"({NL} layer forwards per graph)",
+        "timing": "CUDA events on the launching stream around CUDA-graph replays: exactly "
+                  f"{args.steps} layer forwards ({NL} rotated layers per graph, plus a graph "
+                  "of the remainder), max over ranks",
+        "long_timing": long_run,
+        "device_status": "ok" if not any(status) else status,
         "distinct_experts_per_step": float(np.mean(U)),
+        "replicated_tokens": replicated,
         "prefill": prefill,
         "config1_gemv": gemv1,
+        "sweeps": sweeps,
     }
     if world > 1:
-        got = [None] * world
-        dist.all_gather_object(got, (float(np.mean(uniq)), kernel_ms))
+        got = gather_fn(dist, world)((float(np.mean(uniq)), float(np.mean(pairs_local)),
+                                      kernel_ms, [float(v) for v in stage_avg]))
         line["per_rank_active_experts"] = [g[0] for g in got]
-        line["per_rank_kernel_ms"] = [g[1] for g in got]
+        line["per_rank_pairs"] = [g[1] for g in got]
+        line["per_rank_kernel_ms"] = [g[2] for g in got]
+        line["per_rank_stage_ms"] = [dict(zip(stage_names, g[3])) for g in got]
     if rank == 0:
         print(json.dumps(line), flush=True)
+    bad = parity is not None and not parity.get("pass", True)
     # no rank frees its exchange buffers while another may still write to them
     torch.cuda.synchronize()
     if dist:
@@ -345,9 +479,197 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+    if bad:
+        print("PARITY FAILED: " + json.dumps(parity), file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
-DECODE_MAX_T = 64   # batches above this take the prefill GEMM path
+def parity_block(got, ref, ids, ids_ref, against, n_tok):
+    err = float(np.abs(got - ref).max())
+    rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+    ids_equal = bool(np.array_equal(ids, ids_ref))
+    return {"against": against, "tokens": n_tok, "max_abs": err, "rel_l2": rel,
+            "ids_equal": ids_equal, "tolerance": {"max_abs": 2e-3, "rel_l2": 1e-3},
+            "pass": err <= 2e-3 and rel <= 1e-3 and ids_equal}
+
+
+def oracle_parity(x_host, out0, ids0, d, F, NE, K, n_tok):
+    """rank 0's first tokens of layer 0 (seed 0) against the CPU oracle on
+    the same layer, generated on the host by the same seeded generator"""
+    from oracle import oracle as orc
+    n = min(n_tok, x_host.shape[0])
+    L = orc.make_layer(0, d, F, NE, K, orc.Q8_0)
+    ref, ids_ref, _, _ = orc.moe_ffn(L, x_host[:n])
+    return parity_block(out0[:n], ref, ids0[:n], ids_ref, "oracle (CPU restatement of the "
+                        "reference) on the same seeded layer and tokens", n)
+
+
+def run_prefill(moe, torch, args, layers, rank, world, d, F, NE, K, stream, torch_stream, dist):
+    """Prefill leg: P tokens per GPU per layer forward (the grouped tcgen05
+    GEMM path), rotated over the same layers, CUDA events (max over ranks).
+    N > 1: token-sharded, the token rows and result rows routed with NCCL
+    point-to-point transfers around each rank's GEMMs (not capturable: the
+    transfer sizes are read on the host), so eager launches."""
+    P = args.prefill_tokens
+    NL = len(layers)
+    shard = moe.EP_SHARDED if world > 1 else 0
+    x = synth_tokens(moe, torch, P, d, 0, 6, rank * P, stream)
+    out = torch.empty(P * d, dtype=torch.float32, device="cuda")
+
+    def fwd(i, flags=0):
+        layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), P, shard | flags, stream)
+
+    for i in range(max(3, NL)):
+        fwd(i)
+    torch.cuda.synchronize()
+    steps = max(NL, args.prefill_steps)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(torch_stream)
+    for i in range(steps):
+        fwd(i)
+    ev1.record(torch_stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1)) / steps
+    stage = np.zeros(5)
+    pairs = []
+    for l in range(NL):
+        fwd(l, moe.PROFILE)
+        counts = layers[l].routing(P, world)[2]
+        first = layers[l].first_expert
+        pairs.append(int(counts[first:first + layers[l].n_local].sum()))
+    torch.cuda.synchronize()
+    for lay in layers:
+        s, c = lay.stage_ms()
+        stage += np.array(s)
+    stage /= NL
+    res = {
+        "tokens_per_gpu": P, "value": world * P / (ms / 1e3), "unit": "tokens/s",
+        "ms_per_step": ms, "steps": steps,
+        "stage_ms_avg": {n: float(v) for n, v in
+                         zip(["router", "routing", "gate_up", "down", "combine"], stage)},
+        "parallelism": "single GPU" if world == 1 else
+                       f"expert-parallel x{world}, token-sharded: NCCL all-to-all of the token "
+                       "rows and of the result rows around each rank's grouped GEMMs "
+                       "(stages of rank 0: routing includes the count exchange, gate_up the "
+                       "dispatch transfers, combine the return transfers)",
+    }
+    if world == 1:
+        res["roofline"] = gemm_roofline(stage, float(np.mean(pairs)), d, F)
+    return res
+
+
+def zipf_router_bias(n, s=1.1, seed=4):
+    """per-expert router offsets -s * ln(rank), ranks 1..n in a seeded
+    random order (config 4's Zipf-skewed expert load)"""
+    ranks = np.random.default_rng(seed).permutation(n) + 1
+    return (-s * np.log(ranks.astype(np.float64))).astype(np.float32)
+
+
+def sweep_leg(moe, torch, dist, rank, world, torch_stream, shape, token_counts, cpu_tokens=0,
+              NL=2):
+    """Config 4 (shape "olmoe": the config-0 layer with a Zipf(1.1)-biased
+    router) or the config-3 layer (shape "mixtral": d 4096, d_ff 14336, 8
+    experts top-2 renormalised, Q4_0; one expert per GPU at 8 GPUs) over a
+    list of per-GPU token counts, token-sharded over the N ranks.  Decode
+    sizes are timed from CUDA graphs, larger ones eagerly."""
+    stream = torch_stream.cuda_stream
+    mixtral = shape == "mixtral"
+    if mixtral:
+        d, F, NE, K, qtype = 4096, 14336, 8, 2, moe.Q4_0
+    else:
+        d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
+    expert_bytes = 3 * F * d // 32 * (18 if qtype == moe.Q4_0 else 34)
+    first, n_local = moe.expert_range(rank, world, NE)
+    layers, keep = build_layers(moe, NL, 3 if mixtral else 40, d, F, NE, K, qtype, stream,
+                                first, n_local,
+                                router_bias=None if mixtral else zipf_router_bias(NE),
+                                flags=moe.RENORM if mixtral else 0)
+    if world > 1:
+        gather = gather_fn(dist, world)
+        for lay in layers:
+            moe.connect_expert_parallel(lay, rank, gather)
+    shard = moe.EP_SHARDED if world > 1 else 0
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    rows = []
+    for T in token_counts:
+        x = synth_tokens(moe, torch, T, d, 4, 5, rank * T, stream)
+        out = torch.empty(T * d, dtype=torch.float32, device="cuda")
+
+        def fwd(i, flags=0):
+            layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), T, shard | flags, stream)
+
+        for i in range(max(3, NL)):
+            fwd(i)
+        torch.cuda.synchronize()
+        counts = []
+        for l in range(NL):
+            fwd(l)
+            counts.append(layers[l].routing(T, world)[2])
+        torch.cuda.synchronize()
+        fused = T <= DECODE_MAX_T and world * T * K <= 2048
+        reps = max(2, min(32, int(1e5 / max(T, 64)) // NL))
+        if fused or world == 1:
+            ms, g, _ = time_graph_steps(torch, dist, torch_stream, fwd, NL, reps * NL, 0)
+            del g
+        else:
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(torch_stream)
+            for i in range(reps * NL):
+                fwd(i)
+            e1.record(torch_stream)
+            torch.cuda.synchronize()
+            ms = max_over_ranks(dist, e0.elapsed_time(e1))
+        ms /= reps * NL
+        loc = [c[first:first + n_local] for c in counts]
+        uniq = float(np.mean([(c > 0).sum() for c in loc]))
+        pairs = float(np.mean([c.sum() for c in loc]))
+        row = {"tokens_per_gpu": T, "value": world * T / (ms / 1e3), "unit": "tokens/s",
+               "ms_per_step": ms, "steps": reps * NL, "rank0_experts": uniq,
+               "rank0_pairs": pairs, "max_pairs_per_expert": int(counts[0].max()),
+               "path": "fused decode kernel" if T <= DECODE_MAX_T else "grouped tcgen05 GEMM"}
+        if T <= DECODE_MAX_T:
+            row["rank0_achieved_gbs"] = (uniq * expert_bytes + NE * d * 4 + 2 * T * d * 4) / (ms / 1e3) / 1e9
+            row["rank0_frac_of_hbm"] = row["rank0_achieved_gbs"] / hbm_peak
+        elif world == 1:
+            fl = 2.0 * pairs * 3 * d * F
+            row["rank0_tflops_algorithmic"] = fl / (ms / 1e3) / 1e12
+            row["rank0_frac_of_tensor_peak"] = row["rank0_tflops_algorithmic"] / tc_peak
+        else:
+            row["rank0_pairs_note"] = "pairs of rank 0's own tokens routed to its experts"
+            row["path"] = "NCCL all-to-all around the grouped tcgen05 GEMM"
+        if dist:
+            got = gather_fn(dist, world)((uniq, pairs))
+            row["per_rank_experts"] = [g[0] for g in got]
+            row["per_rank_pairs"] = [g[1] for g in got]
+        rows.append(row)
+        del x, out
+        torch.cuda.synchronize()
+    cpu = None
+    if cpu_tokens and rank == 0:
+        cpu = cpu_reference_sample(keep[0], d, F, NE, K, qtype, cpu_tokens, renorm=mixtral)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    for lay in layers:
+        lay.close()
+    del keep
+    torch.cuda.empty_cache()
+    return {
+        "workload": ("config3: Mixtral-8x7B MoE layer, d 4096, 8 experts top-2 renormalised, "
+                     "d_ff 14336, Q4_0") if mixtral else
+                    ("config4: config-0 layer with a Zipf(1.1)-biased router"),
+        "scaling": "weak (tokens per GPU fixed)" if world > 1 else "single GPU",
+        "timing": "CUDA events, max over ranks; graphs for decode sizes, eager above",
+        "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": tc_peak, "source": peak_kind},
+        "rows": rows, "cpu_reference": cpu}
 
 
 def gemm_roofline(stage, pairs, d, F):
@@ -374,202 +696,6 @@ def gemm_roofline(stage, pairs, d, F):
                 "operands); the gate_up stage includes the fp16 hi/lo gather of the tokens",
         "launch_time_source": "CUDA events between the layer's stages, one profiled "
                               "forward per layer"}
-
-
-def run_prefill(moe, args, layers, d, F, NE, K, stream, torch_stream, dist=None):
-    """Prefill leg: P tokens per layer forward (the grouped tcgen05 GEMM
-    path), rotated over the same layers; device time with CUDA events (max
-    over ranks), the stages from one profiled forward per layer.  Expert
-    parallel (N > 1): every rank runs its experts' GEMMs on the same P
-    tokens and the partial outputs are summed by the library's NCCL
-    all-reduce inside the step."""
-    import torch
-    P = args.prefill_tokens
-    NL = len(layers)
-    x = torch.empty(P * d, dtype=torch.float32, device="cuda")
-    moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 0, 6, 0, P * d, 1.0, stream))
-    out = torch.empty(P * d, dtype=torch.float32, device="cuda")
-
-    def fwd(i, flags=0):
-        layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), P, flags, stream)
-
-    for i in range(max(3, NL)):
-        fwd(i)
-    torch.cuda.synchronize()
-    steps = max(NL, args.prefill_steps)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(torch_stream)
-    for i in range(steps):
-        fwd(i)
-    ev1.record(torch_stream)
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1) / steps
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    stage = np.zeros(5)
-    pairs = []
-    for l in range(NL):
-        fwd(l, moe.PROFILE)
-        ids = layers[l].routing(P)[0]
-        first = layers[l].first_expert
-        pairs.append(int(((ids >= first) & (ids < first + layers[l].n_local)).sum()))
-    torch.cuda.synchronize()
-    for lay in layers:
-        s, c = lay.stage_ms()
-        stage += np.array(s)
-    stage /= NL
-    return {
-        "tokens": P, "value": P / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-        "steps": steps,
-        "stage_ms_avg": {n: float(v) for n, v in
-                         zip(["router", "routing", "gate_up", "down", "combine"], stage)},
-        "roofline": gemm_roofline(stage, float(np.mean(pairs)), d, F),
-        "parallelism": "single GPU" if not dist else
-                       f"expert-parallel x{dist.get_world_size()}: GEMMs of the local experts, "
-                       "partial outputs summed by an NCCL all-reduce in the step (stages and "
-                       "roofline of rank 0)",
-    }
-
-
-def zipf_router_bias(n, s=1.1, seed=4):
-    """per-expert router offsets -s * ln(rank), ranks 1..n in a seeded
-    random order (config 4's Zipf-skewed expert load)"""
-    ranks = np.random.default_rng(seed).permutation(n) + 1
-    return (-s * np.log(ranks.astype(np.float64))).astype(np.float32)
-
-
-def run_sweep(args, rank, world, local_rank):
-    """Config 4: the config-0 layer with a Zipf(1.1)-biased router over a
-    sweep of token counts, expert-parallel over the N ranks (64/N experts
-    each).  --sweep-shape mixtral: the config-3 layer instead (d 4096, d_ff
-    14336, 8 experts top-2 renormalised, Q4_0, no router offsets; at 8 GPUs
-    one expert per GPU).  One JSON line with one entry per T."""
-    import torch
-    torch.cuda.set_device(local_rank)
-    moe = load_package()
-    moe.init(local_rank)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
-    torch_stream = torch.cuda.Stream()
-    torch.cuda.set_stream(torch_stream)
-    stream = torch_stream.cuda_stream
-    mixtral = args.sweep_shape == "mixtral"
-    if mixtral:
-        d, F, NE, K, qtype = 4096, 14336, 8, 2, moe.Q4_0
-    else:
-        d, F, NE, K, qtype = 2048, 1024, 64, 8, moe.Q8_0
-    expert_bytes = 3 * F * d // 32 * (18 if qtype == moe.Q4_0 else 34)
-    NL = 2
-    first, n_local = moe.expert_range(rank, world, NE)
-    layers, keep = build_layers(moe, NL, 3 if mixtral else 40, d, F, NE, K, qtype, stream,
-                                first, n_local,
-                                router_bias=None if mixtral else zipf_router_bias(NE),
-                                flags=moe.RENORM if mixtral else 0)
-    if world > 1:
-        def gather(obj):
-            got = [None] * world
-            dist.all_gather_object(got, obj)
-            return got
-        for lay in layers:
-            moe.connect_expert_parallel(lay, rank, gather)
-        moe.init_expert_parallel_comm(rank, world, gather)
-    hbm_peak, tc_peak, peak_kind = measured_peaks()
-    rows = []
-    for T in [int(t) for t in args.sweep.split(",")]:
-        x = torch.empty(T * d, dtype=torch.float32, device="cuda")
-        moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 4, 5, 0, T * d, 1.0, stream))
-        out = torch.empty(T * d, dtype=torch.float32, device="cuda")
-
-        def fwd(i, flags=0):
-            layers[i % NL].forward_device(x.data_ptr(), out.data_ptr(), T, flags, stream)
-
-        for i in range(max(3, NL)):
-            fwd(i)
-        torch.cuda.synchronize()
-        ids = [None] * NL
-        for l in range(NL):
-            fwd(l)
-            ids[l] = layers[l].routing(T)[0]
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=torch_stream, capture_error_mode="relaxed"):
-            for l in range(NL):
-                fwd(l)
-        graph.replay()
-        torch.cuda.synchronize()
-        reps = max(2, min(64, int(2e5 / max(T, 64)) // NL))
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(torch_stream)
-        for _ in range(reps):
-            graph.replay()
-        e1.record(torch_stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / (reps * NL)
-        if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        local = [((a >= first) & (a < first + n_local)) for a in ids]
-        uniq = float(np.mean([len(np.unique(a[m])) for a, m in zip(ids, local)]))
-        pairs = float(np.mean([m.sum() for m in local]))
-        counts = np.bincount(ids[0].reshape(-1), minlength=NE)
-        row = {"tokens": T, "value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-               "steps": reps * NL, "rank0_experts": uniq, "rank0_pairs": pairs,
-               "max_pairs_per_expert": int(counts.max()),
-               "path": "fused decode kernel" if T <= DECODE_MAX_T else "grouped tcgen05 GEMM"}
-        if T <= DECODE_MAX_T:
-            row["rank0_achieved_gbs"] = (uniq * expert_bytes + NE * d * 4 + 2 * T * d * 4) / (ms / 1e3) / 1e9
-            row["rank0_frac_of_hbm"] = row["rank0_achieved_gbs"] / hbm_peak
-        else:
-            fl = 2.0 * pairs * 3 * d * F
-            row["rank0_tflops_algorithmic"] = fl / (ms / 1e3) / 1e12
-            row["rank0_frac_of_tensor_peak"] = row["rank0_tflops_algorithmic"] / tc_peak
-        if dist:
-            got = [None] * world
-            dist.all_gather_object(got, (uniq, pairs))
-            row["per_rank_experts"] = [g[0] for g in got]
-            row["per_rank_pairs"] = [g[1] for g in got]
-        rows.append(row)
-        graph = None
-        del x, out
-        torch.cuda.synchronize()
-    if rank == 0:
-        print(json.dumps({
-            "metric": ("MoE-layer tokens/s over a token sweep (config-3 layer: Mixtral-8x7B "
-                       "shape, Q4_0, top-2 renormalised)") if mixtral else
-                      ("MoE-layer tokens/s over a token sweep (config 4: config-0 layer, "
-                       "Zipf(1.1)-biased router)"),
-            "n_gpus": world, "unit": "tokens/s", "higher_is_better": True,
-            "scaling": "strong",
-            "data": "synthetic (seeded N(0,0.02) weights -> %s, N(0,1) tokens%s)" % (
-                "Q4_0" if mixtral else "Q8_0", "" if mixtral else ", Zipf(1.1) router offsets"),
-            "timing": "CUDA events around CUDA-graph replays of 2 rotated layers, max over ranks; "
-                      "whole step (the layer forward) per T",
-            "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": tc_peak, "source": peak_kind},
-            "parallelism": f"expert-parallel x{world}" if world > 1 else "single GPU",
-            "sweep": rows}), flush=True)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    for lay in layers:
-        lay.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
 
 
 def run_config1_gemv(moe, stream, torch_stream, copies=8, reps=48):
@@ -643,42 +769,6 @@ def run_config1_gemv(moe, stream, torch_stream, copies=8, reps=48):
             "timing": f"CUDA events around {reps * copies} back-to-back eager calls over {copies} "
                       "distinct weight matrices (264 MB > L2), enqueued behind a spin kernel; "
                       "_graph: the same calls replayed from a CUDA graph"}
-
-
-def run_e2e_ep(moe, args, layers, T, d, stream, dist):
-    """Expert-parallel e2e: per step, this rank's tokens come from pinned host
-    memory and its output goes back to pinned host memory around the layer
-    call (moe_layer_forward); wall clock per rank, max over ranks."""
-    import torch
-    nl = len(layers)
-    xin = torch.randn(T * d, dtype=torch.float32, generator=torch.Generator().manual_seed(0))
-    xin = xin.pin_memory()
-    xout = torch.empty(T * d, dtype=torch.float32).pin_memory()
-    xd = torch.empty(T * d, dtype=torch.float32, device="cuda")
-    od = torch.empty(T * d, dtype=torch.float32, device="cuda")
-    s = torch.cuda.current_stream()
-
-    def call(i):
-        xd.copy_(xin, non_blocking=True)
-        layers[i % nl].forward_device(xd.data_ptr(), od.data_ptr(), T, 0, s.cuda_stream)
-        xout.copy_(od, non_blocking=True)
-        s.synchronize()
-
-    for i in range(max(args.warmup, 2)):
-        call(i)
-    dist.barrier()
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        call(i)
-    sec = time.perf_counter() - t0
-    t = torch.tensor([sec], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    sec = float(t.item())
-    return {"value": T * args.steps / sec, "unit": "tokens/s",
-            "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
-            "api": "moe_layer_forward (expert-parallel; pinned host -> device copy of the "
-                   "tokens and device -> pinned host copy of the output inside the step)",
-            "timer": "host wall clock per rank, max over ranks"}
 
 
 def run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist):
@@ -774,32 +864,108 @@ def ref_variant():
     return "avx512" if " avx512f" in flags else "avx2"
 
 
-def cpu_baseline(moe, layer0, x_dev, T, d, F, NE, K, qtype, sample_tokens=8, reps=3):
+def run_e2e_ep(moe, args, layers, x_host, T, d, stream, dist):
+    """Expert-parallel e2e (token-sharded): per step, this rank's tokens come
+    from pinned host memory and its output goes back to pinned host memory
+    around the layer call (moe_layer_forward); host wall clock per rank, max
+    over ranks; value = every rank's tokens."""
+    import torch
+    nl = len(layers)
+    world = dist.get_world_size()
+    xin = torch.from_numpy(x_host.reshape(-1).copy()).pin_memory()
+    xout = torch.empty(T * d, dtype=torch.float32).pin_memory()
+    xd = torch.empty(T * d, dtype=torch.float32, device="cuda")
+    od = torch.empty(T * d, dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def call(i):
+        xd.copy_(xin, non_blocking=True)
+        layers[i % nl].forward_device(xd.data_ptr(), od.data_ptr(), T, moe.EP_SHARDED,
+                                      s.cuda_stream)
+        xout.copy_(od, non_blocking=True)
+        s.synchronize()
+
+    for i in range(max(args.warmup, 2)):
+        call(i)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        call(i)
+    sec = max_over_ranks(dist, time.perf_counter() - t0)
+    return {"value": world * T * args.steps / sec, "unit": "tokens/s",
+            "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
+            "api": "moe_layer_forward with MOE_EP_SHARDED (pinned host -> device copy of this "
+                   "rank's tokens and device -> pinned host copy of their output inside the "
+                   "step; bytes per GPU)",
+            "timer": "host wall clock per rank, max over ranks"}
+
+
+def cpu_baseline(layer0, x_host, out0, ids0, T, d, F, NE, K, qtype, reps=3):
     """The reference's own CPU path (oracle/_ref, compiled from its sources)
-    on the SAME bytes as the GPU run, on a bounded sample of tokens."""
+    on the SAME bytes and tokens as the GPU run: the AVX-512 build (what the
+    reference's own Makefile selects on this host, -march=native) and the
+    AVX2 build, median of `reps` calls after a warm-up.  Its output is the
+    parity check of the measured layer: the GPU output of the same layer on
+    the same tokens must be within the tolerance, with the same expert ids."""
+    from oracle import oracle as orc
+    wr, mats = layer0
+    arrays = dict(x=x_host, router_w=wr.view(NE, d).cpu().numpy(), gate=mats[0].cpu().numpy(),
+                  up=mats[1].cpu().numpy(), down=mats[2].cpu().numpy(), qtype=qtype, d_ff=F,
+                  top_k=K, renorm=0)
+    res, parity = {}, None
+    for variant in ("avx512", "avx2"):
+        if not orc.ref_available(variant) or (variant == "avx512" and ref_variant() != "avx512"):
+            continue
+        r = orc.ref_call("bench", variant, reps=reps, **arrays)
+        sec = float(np.median(r["seconds"]))
+        res[variant] = {"value": T / sec, "seconds_per_call": sec}
+        if parity is None:
+            parity = parity_block(out0, r["out"], ids0, r["ids"],
+                                  f"the reference itself (oracle/_ref libref_{variant}.so) on "
+                                  "identical bytes and tokens", T)
+    if not res:
+        return ({"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                 "sample": "oracle/_ref not built"}, None)
+    main = "avx512" if "avx512" in res else "avx2"
+    return ({"value": res[main]["value"], "unit": "tokens/s", "cores": 1, "kind": "reference",
+             "variant": main, "builds": res, "host_physical_cores": physical_cores(),
+             "sample": f"all {T} config-0 tokens of layer 0 through ref_moe_ffn (reference "
+                       "sources, -march=x86-64-v4 / -v3), median of "
+                       f"{reps} calls after 1 warm-up, identical bytes to the GPU run; the "
+                       "reference runs these expert GEMVs on one thread (below its 16 MFLOP "
+                       "threading threshold, thread_pool.c:25,178-185) while its pool spins on "
+                       "every physical core"}, parity)
+
+
+def cpu_reference_sample(layer0, d, F, NE, K, qtype, n_tok, renorm, reps=2):
+    """the reference on a few tokens of a layer whose expert GEMVs are above
+    its threading threshold (config 3: 117 MFLOP per GEMV), so its thread
+    pool runs on every physical core"""
     from oracle import oracle as orc
     variant = ref_variant()
     if not orc.ref_available(variant):
-        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
-                "sample": f"oracle/_ref/libref_{variant}.so not built"}
+        return None
     wr, mats = layer0
-    xs = x_dev.view(T, d)[:sample_tokens].cpu().numpy()
-    r = orc.ref_call("bench", variant, x=xs, router_w=wr.view(NE, d).cpu().numpy(),
+    import torch
+    x = torch.randn(n_tok, d, generator=torch.Generator().manual_seed(3)).numpy()
+    r = orc.ref_call("bench", variant, reps=reps, x=x, router_w=wr.view(NE, d).cpu().numpy(),
                      gate=mats[0].cpu().numpy(), up=mats[1].cpu().numpy(),
-                     down=mats[2].cpu().numpy(), qtype=qtype, d_ff=F, top_k=K, renorm=0,
-                     reps=reps)
+                     down=mats[2].cpu().numpy(), qtype=qtype, d_ff=F, top_k=K,
+                     renorm=int(renorm), timeout=1200)
     sec = float(np.median(r["seconds"]))
-    return {"value": sample_tokens / sec, "unit": "tokens/s", "cores": 1, "kind": "reference",
-            "variant": variant, "host_physical_cores": physical_cores(),
-            "sample": f"{sample_tokens} of the {T} config-0 tokens through ref_moe_ffn "
-                      f"(reference sources, -march=x86-64-{'v4' if variant == 'avx512' else 'v3'}), "
-                      f"median of {reps} calls after 1 warm-up, identical bytes to the GPU run; "
-                      "the reference runs these expert GEMVs on one thread (below its 16 MFLOP "
-                      "threading threshold) while its pool spins on every physical core"}
+    return {"value": n_tok / sec, "unit": "tokens/s", "cores": physical_cores(),
+            "kind": "reference", "variant": variant,
+            "sample": f"{n_tok} tokens through ref_moe_ffn on the config-3 layer, median of "
+                      f"{reps} calls after 1 warm-up; above the 16 MFLOP threshold the "
+                      "reference splits each GEMV over its thread pool (one thread per "
+                      "physical core)"}
 
 
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
+    """The reference's own CPU path (oracle/_ref: its sources compiled as its
+    Makefile does, -march=native selects AVX-512 on this host) on the same
+    config, metric and unit as our arm: config 0, all T tokens per step."""
     if rank != 0:
         return
     from oracle import oracle as orc
@@ -811,23 +977,33 @@ def run_reference(args, rank, world):
     d, F, NE, K = 2048, 1024, 64, 8
     L = orc.make_layer(0, d, F, NE, K, orc.Q8_0)
     x = orc.make_tokens(0, args.tokens, d)
-    S = min(8, args.tokens)
-    r = orc.ref_call("bench", variant, timeout=3600, x=x[:S], router_w=L["router_w"],
+    r = orc.ref_call("bench", variant, timeout=3600, x=x, router_w=L["router_w"],
                      gate=L["gate"], up=L["up"], down=L["down"], qtype=orc.Q8_0, d_ff=F,
                      top_k=K, renorm=0, reps=args.steps + args.warmup)
     secs = np.array(r["seconds"])[args.warmup:]
     tot = float(secs.sum())
-    val = S * len(secs) / tot
+    val = args.tokens * len(secs) / tot
+    avx2 = None
+    if variant == "avx512" and orc.ref_available("avx2"):
+        r2 = orc.ref_call("bench", "avx2", timeout=3600, x=x, router_w=L["router_w"],
+                          gate=L["gate"], up=L["up"], down=L["down"], qtype=orc.Q8_0, d_ff=F,
+                          top_k=K, renorm=0, reps=3)
+        avx2 = {"value": args.tokens / float(np.median(r2["seconds"])), "unit": "tokens/s",
+                "sample": "median of 3 calls after 1 warm-up"}
     cpu = {"value": val, "unit": "tokens/s", "cores": 1, "kind": "reference",
            "variant": variant, "host_physical_cores": physical_cores(),
-           "sample": f"{S} of the {args.tokens} config-0 tokens per step through ref_moe_ffn"}
+           "sample": f"all {args.tokens} config-0 tokens per step through ref_moe_ffn "
+                     "(single-threaded by the reference's 16 MFLOP threshold)",
+           "avx2_build": avx2}
     print(json.dumps({
         "impl": "reference", "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d)" % args.tokens,
         "value": val, "unit": "tokens/s", "n_gpus": world, "steps": len(secs),
         "warmup": args.warmup, "ms_per_step": tot / len(secs) * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x Q8_0 weights",
         "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, N(0,1) tokens)",
-        "config": {"workload": "config0: OLMoE-1B-7B MoE FFN layer on the reference CPU path"},
+        "config": {"workload": "config0: OLMoE-1B-7B MoE FFN layer, d 2048, 64 experts top-8, "
+                               "d_ff 1024 SwiGLU, Q8_0, T=%d tokens" % args.tokens,
+                   "tokens_per_step": args.tokens},
         "cpu_baseline": cpu,
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0}}), flush=True)
@@ -839,26 +1015,32 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=32)
+    ap.add_argument("--tokens", type=int, default=32, help="tokens per GPU per step")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--prefill-tokens", type=int, default=2048,
-                    help="tokens of the one-GPU prefill leg (0: skip)")
+                    help="tokens per GPU of the prefill leg (0: skip)")
     ap.add_argument("--prefill-steps", type=int, default=16)
-    ap.add_argument("--sweep", default="",
-                    help="comma-separated token counts: run config 4 (Zipf router) instead")
-    ap.add_argument("--sweep-shape", choices=["olmoe", "mixtral"], default="olmoe")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sweep4", default="1,8,64,512,4096",
+                    help="per-GPU token counts of the config-4 leg")
+    ap.add_argument("--sweep3", default="1,32,512",
+                    help="per-GPU token counts of the config-3 leg")
+    ap.add_argument("--parity-tokens", type=int, default=8,
+                    help="tokens of rank 0 checked against the oracle at N > 1")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the config-1 GEMV leg")
+    ap.add_argument("--no-sweeps", action="store_true", help="skip the config-3/4 legs")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check at N > 1")
+    ap.add_argument("--no-replicated", action="store_true",
+                    help="skip the replicated-token leg at N > 1")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    args.steps = max(args.steps, 1)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
-    elif args.sweep:
-        run_sweep(args, rank, world, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 

@@ -83,6 +83,10 @@ enum moe_status {
                              /* (read back with moe_layer_stage_ms)          */
 #define MOE_NO_FUSE     0x100 /* decode-sized batches: use the five-launch   */
                              /* path instead of the fused layer kernel       */
+#define MOE_EP_SHARDED  0x200 /* expert-parallel layers: x holds this rank's */
+                             /* own tokens and out receives their outputs    */
+                             /* (tokens travel to the experts' ranks and the */
+                             /* rows back); see moe_layer_set_peers          */
 
 /* ------------------------------------------------------------------ */
 /* Library lifetime                                                     */
@@ -191,9 +195,20 @@ typedef struct moe_layer_desc {
 MOE_API int moe_layer_create(moe_layer **out, const moe_layer_desc *desc);
 MOE_API int moe_layer_destroy(moe_layer *layer);
 /* out[T,d] = MoE(x[T,d]); x/out device fp32; stream = cudaStream_t or
- * NULL for the library stream.  Asynchronous. */
+ * NULL for the library stream.  Asynchronous: a failure inside the kernels
+ * (an expired bounded wait, an expert id out of range) is recorded in the
+ * layer's device error word, which stays set until moe_layer_status or
+ * moe_layer_routing reads it. */
 MOE_API int moe_layer_forward(moe_layer *layer, const float *x, float *out, int64_t T,
 		      int flags, void *stream);
+/* Waits for the device, then reads and clears the layer's error word:
+ * MOE_OK, MOE_ERR_TIMEOUT (a bounded wait expired: a grid barrier, a
+ * pipeline wait, or the expert-parallel exchange -- a rank missing or
+ * behind) or MOE_ERR_INVALID (an expert id out of range; ranks that passed
+ * different T to a token-sharded forward).  The output of the forward
+ * that set it is not valid.  No counterpart in the reference, which
+ * asserts (quant.c:571-574). */
+MOE_API int moe_layer_status(moe_layer *layer);
 /* Routing of the last forward, copied to HOST buffers (any may be NULL):
  * ids/weights [T,k] in top-k output order, counts [NE], offsets [NE+1],
  * perm [T*k] (pair p = t*k + slot, stably sorted by expert). */
@@ -232,6 +247,26 @@ MOE_API int moe_layer_stage_ms(moe_layer *layer, float *ms, int n);
  * order), 2 <= world <= 8, once. */
 MOE_API int moe_layer_ipc_handle(moe_layer *layer, void *handle);
 MOE_API int moe_layer_set_peers(moe_layer *layer, int rank, int world, const void *handles);
+/* Token-sharded expert parallelism (forward flag MOE_EP_SHARDED): every rank
+ * passes its OWN T tokens (the same T on every rank) and receives their
+ * outputs, as in data-parallel attention feeding expert-parallel FFNs.
+ * Decode-sized forwards (T <= 64 and world*T*top_k <= 2048) run the fused
+ * kernel: each rank writes its tokens (fp16 hi/lo) and top-k ids into every
+ * rank's exchange buffer over NVLink, each rank's experts process the pairs
+ * of all ranks' tokens, and each finished (token, slot) row goes straight to
+ * the exchange buffer of the rank that owns the token, which combines its
+ * tokens in slot order -- bit-identical to one GPU on the concatenated
+ * batch.  Larger forwards (once moe_ep_init has been called) route the
+ * token rows to the experts' ranks and the rows back with NCCL
+ * point-to-point transfers (an all-to-all), with the grouped GEMMs between.
+ * Every rank must run the same sequence of forwards with the same flags. */
+/* Limit (ms) of the cross-rank waits of the fused kernel (default 2000). */
+MOE_API int moe_layer_set_wait_ms(moe_layer *layer, int ms);
+/* After an expired exchange wait: clear this rank's exchange counters and
+ * error word.  Every rank calls it between two host-side barriers (so no
+ * rank's next forward starts before every rank has reset) before the next
+ * forward. */
+MOE_API int moe_layer_ep_reset(moe_layer *layer);
 /* The library's NCCL communicator for expert-parallel batches above 64
  * tokens (libnccl.so.2 is loaded at run time).  Rank 0 calls
  * moe_ep_unique_id (128 bytes) and shares the bytes out of band; then every
@@ -266,11 +301,16 @@ MOE_API int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols
  * The array's device address is looked up on a device's first call: make
  * that call before any stream capture.  All calls share the array: calls
  * that overlap on the GPU (other streams or threads) race.  NULL stream =
- * the library stream. */
+ * the library stream (the first such call initialises the library on the
+ * current device: a stream, no memory).  The call is asynchronous; a
+ * bounded wait that expires inside it sets a sticky flag in the array,
+ * which moe_sync reports as MOE_ERR_TIMEOUT (a caller on its own stream
+ * synchronises that stream first). */
 MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t rows, int64_t cols,
 				    const float *x, int64_t m, float *y, void *stream);
 
-/* Synchronise the library stream. */
+/* Synchronise the library stream.  Returns MOE_ERR_TIMEOUT (once) if a
+ * moe_gemv_device_noalloc call on this device recorded an expired wait. */
 MOE_API int moe_sync(void);
 
 /* ------------------------------------------------------------------ */

@@ -21,6 +21,7 @@ F32, Q8_0, Q4_0 = 0, 1, 2
 TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE, SIMPLE = (
     0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40, 0x80)
 NO_FUSE = 0x100
+EP_SHARDED = 0x200
 
 ERRORS = {0: "MOE_OK", -1: "MOE_ERR_INVALID", -2: "MOE_ERR_UNSUPPORTED", -3: "MOE_ERR_CUDA",
           -4: "MOE_ERR_NOMEM", -5: "MOE_ERR_NOT_INIT", -6: "MOE_ERR_COMM", -7: "MOE_ERR_TIMEOUT"}
@@ -71,6 +72,9 @@ SIGNATURES = {
     "moe_layer_destroy": (_I, [_P]),
     "moe_layer_forward": (_I, [_P, _P, _P, _I64, _I, _P]),
     "moe_layer_routing": (_I, [_P, _P, _P, _P, _P, _P]),
+    "moe_layer_status": (_I, [_P]),
+    "moe_layer_set_wait_ms": (_I, [_P, _I]),
+    "moe_layer_ep_reset": (_I, [_P]),
     "moe_layer_stage_ms": (_I, [_P, C.POINTER(C.c_float), _I]),
     "moe_layer_phase_stamps": (_I, [_P, C.POINTER(C.c_uint64), _I]),
     "moe_layer_ipc_handle": (_I, [_P, _P]),
@@ -270,7 +274,7 @@ class Layer:
         bx = DeviceBuffer.from_numpy(x)
         bo = DeviceBuffer(x.nbytes)
         self.forward_device(bx.ptr, bo.ptr, T, flags)
-        check(lib().moe_sync())
+        check(lib().moe_layer_status(self.handle))   # waits; raises on a device-side failure
         self.last_T = T
         return bo.to_numpy(np.float32, x.shape)
 
@@ -303,13 +307,26 @@ class Layer:
         buf = (C.c_char * len(blob)).from_buffer_copy(blob)
         check(lib().moe_layer_set_peers(self.handle, rank, len(handles), buf))
 
-    def routing(self, T: int):
+    def status(self) -> int:
+        """moe_layer_status: waits for the device and returns (and clears) the
+        layer's error status as a code (0 = ok); does not raise"""
+        return lib().moe_layer_status(self.handle)
+
+    def set_wait_ms(self, ms: int) -> None:
+        check(lib().moe_layer_set_wait_ms(self.handle, ms))
+
+    def ep_reset(self) -> None:
+        check(lib().moe_layer_ep_reset(self.handle))
+
+    def routing(self, T: int, world: int = 1):
+        """routing of the last forward; `world` > 1 after a token-sharded
+        forward, whose dispatch covers every rank's T tokens"""
         K, NE = self.top_k, self.n_experts
         ids = np.empty((T, K), np.int32)
         w = np.empty((T, K), np.float32)
         counts = np.empty(NE, np.int32)
         offsets = np.empty(NE + 1, np.int32)
-        perm = np.empty(T * K, np.int32)
+        perm = np.empty(world * T * K, np.int32)
         check(lib().moe_layer_routing(self.handle, ids.ctypes.data, w.ctypes.data,
                                       counts.ctypes.data, offsets.ctypes.data, perm.ctypes.data))
         return ids, w, counts, offsets, perm

@@ -71,6 +71,7 @@ struct Ctx {
 	size_t pin_bytes = 0;
 	void *dev_io = nullptr;
 	size_t dev_io_bytes = 0;
+	int32_t *err_pin = nullptr;  // pinned word: a layer's error word read with the output
 	std::map<std::vector<uintptr_t>, moe_layer *> layers;
 	// moe_ffn_forward's repeat calls: (router, gate, up, down host bases,
 	// qtype, experts, d_ff, d_model, top-k) -> the layer in `layers`
@@ -107,6 +108,13 @@ struct Nccl {
 	ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
 	ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
 				   ncclComm_t, cudaStream_t) = nullptr;
+	ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+				   cudaStream_t) = nullptr;
+	ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t,
+			     cudaStream_t) = nullptr;
+	ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+	ncclResult_t (*group_start)() = nullptr;
+	ncclResult_t (*group_end)() = nullptr;
 	ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
 	const char *(*error_string)(ncclResult_t) = nullptr;
 	ncclComm_t comm = nullptr;
@@ -129,8 +137,14 @@ int nccl_load()
 	nccl.all_reduce = (decltype(nccl.all_reduce))dlsym(h, "ncclAllReduce");
 	nccl.comm_destroy = (decltype(nccl.comm_destroy))dlsym(h, "ncclCommDestroy");
 	nccl.error_string = (decltype(nccl.error_string))dlsym(h, "ncclGetErrorString");
+	nccl.all_gather = (decltype(nccl.all_gather))dlsym(h, "ncclAllGather");
+	nccl.send = (decltype(nccl.send))dlsym(h, "ncclSend");
+	nccl.recv = (decltype(nccl.recv))dlsym(h, "ncclRecv");
+	nccl.group_start = (decltype(nccl.group_start))dlsym(h, "ncclGroupStart");
+	nccl.group_end = (decltype(nccl.group_end))dlsym(h, "ncclGroupEnd");
 	if (!nccl.get_unique_id || !nccl.comm_init_rank || !nccl.all_reduce || !nccl.comm_destroy ||
-	    !nccl.error_string)
+	    !nccl.error_string || !nccl.all_gather || !nccl.send || !nccl.recv ||
+	    !nccl.group_start || !nccl.group_end)
 		return fail(MOE_ERR_COMM, "libnccl.so.2 lacks an entry point");
 	nccl.lib = h;
 	return MOE_OK;
@@ -171,11 +185,15 @@ const void *tensor_host_ptr(const moe_tensor_t *t)
 	return t->type == MOE_F32 ? (const void *)t->data : t->qdata;
 }
 
+// initialise on the current device (device 0 in a fresh process) if needed
 int ensure_init()
 {
 	if (g.init)
 		return MOE_OK;
-	return moe_init(0) == MOE_OK ? MOE_OK : MOE_ERR_NOT_INIT;
+	int dev = 0;
+	if (cudaGetDevice(&dev) != cudaSuccess)
+		dev = 0;
+	return moe_init(dev) == MOE_OK ? MOE_OK : MOE_ERR_NOT_INIT;
 }
 
 // device address for host range [p, p+bytes): a registered range that
@@ -230,6 +248,8 @@ int ensure_pinned(size_t bytes)
 
 int ensure_dev_io(size_t bytes)
 {
+	if (!g.err_pin)
+		CK(cudaHostAlloc(&g.err_pin, 64, cudaHostAllocDefault));
 	if (g.dev_io_bytes >= bytes)
 		return MOE_OK;
 	CK(cudaStreamSynchronize(g.stream));
@@ -248,7 +268,19 @@ int ensure_dev_io(size_t bytes)
 namespace moe {
 // used by noalloc.cu
 void set_last_error(const char *msg) { g_err = msg ? msg : ""; }
+int ensure_library()
+{
+	if (int rc = ensure_init())
+		return rc;
+	int dev = -1;
+	cudaGetDevice(&dev);
+	if (dev != g.device)
+		return fail(MOE_ERR_INVALID, "the library stream belongs to device %d, the current "
+			    "device is %d: pass a stream", g.device, dev);
+	return MOE_OK;
+}
 cudaStream_t library_stream() { return g.init ? g.stream : nullptr; }
+int noalloc_take_error();  // noalloc.cu
 }  // namespace moe
 
 // -------------------------------------------------------------------------
@@ -261,6 +293,7 @@ struct moe_layer {
 	size_t scratch_bytes = 0;
 	int64_t capT = -1;
 	int64_t lastT = 0;
+	int64_t last_pairs = 0;  // entries of perm written by the last forward
 	// MOE_PROFILE: one set of 6 events per profiled forward since the last
 	// moe_layer_stage_ms (stage boundaries on the launching stream)
 	std::vector<std::array<cudaEvent_t, 6>> prof;
@@ -277,13 +310,27 @@ struct moe_layer {
 	unsigned long long *gbar;           // grid barrier arrivals of the fused kernel
 	uint64_t *stamps;                   // [kStampRecords][grid][stamps]
 	// expert parallelism (n_local < n_experts): exchange buffer of this rank
-	// (two halves of y_half floats + counters), peers once connected
+	// (moe::ep_layout: two Y halves, counters, gathered ids and tokens),
+	// peers once connected
 	char *xbuf = nullptr;
 	int64_t y_half = 0;
+	moe::EpLayout xl{};
 	int ep_rank = 0, ep_world = 1;
+	uint64_t ep_wait_ns = 0;            // 0: the kernel's default limit
 	std::vector<void *> opened;         // peer buffers opened by IPC
 	float **d_ybuf = nullptr;           // device [world]
-	unsigned long long **d_inbound = nullptr;
+	unsigned long long **d_inbound = nullptr, **d_routed = nullptr;
+	__half **d_xg = nullptr;
+	int32_t **d_idg = nullptr;
+	// token-sharded forwards above the fused kernel's sizes (NCCL all-to-all)
+	struct A2A {
+		void *buf = nullptr;     // received tokens, their h and their rows
+		size_t bytes = 0;
+		int32_t *meta = nullptr; // device: every rank's counts, local counts,
+		                         // offsets, active list, n_active
+		int32_t *host = nullptr; // pinned mirror of meta
+		size_t meta_ints = 0;
+	} a2a;
 };
 
 namespace {
@@ -303,11 +350,13 @@ int layer_scratch(moe_layer *L, int64_t T)
 		return o;
 	};
 	size_t o_logits = take(cap * NE * 4), o_ids = take(cap * K * 4), o_wts = take(cap * K * 4);
-	size_t o_counts = take(NE * 4), o_offsets = take((NE + 1) * 4), o_perm = take(cap * K * 4);
+	// token-sharded expert parallelism dispatches every rank's pairs
+	const int64_t pcap = std::max<int64_t>(cap * K, L->xbuf ? moe::kDecodeMaxPairsAll : 0);
+	size_t o_counts = take(NE * 4), o_offsets = take((NE + 1) * 4), o_perm = take(pcap * 4);
 	size_t o_pos = take(cap * K * 4), o_err = take(4);
 	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8);
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
-	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)cap * K * 2 * F * 2);
+	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)pcap * 2 * F * 2);
 	size_t o_x16p = take((size_t)cap * K * 2 * D * 2);
 	const size_t gbar_bytes = moe::decode_barrier_bytes(moe::sm_count());
 	size_t o_gbar = take(gbar_bytes);
@@ -342,6 +391,238 @@ int layer_scratch(moe_layer *L, int64_t T)
 	CK(cudaMemset(L->gbar, 0, gbar_bytes));
 	CK(cudaDeviceSynchronize());  // ordered before launches on any stream
 	L->capT = cap;
+	return MOE_OK;
+}
+
+// the status of a layer's device error word `err` (already read, with the
+// device idle); clears the word, and after an expired wait the grid-barrier
+// counter, so that the next forward starts clean
+int take_error(moe_layer *L, int32_t err)
+{
+	if (err == 0)
+		return MOE_OK;
+	CK(cudaMemset(L->err, 0, 4));
+	if (err == 2 || err == 3 || err == 4)
+		CK(cudaMemset(L->gbar, 0, moe::decode_barrier_bytes(moe::sm_count())));
+	CK(cudaDeviceSynchronize());
+	switch (err) {
+	case 1:
+		return fail(MOE_ERR_INVALID, "dispatch saw an expert id out of range");
+	case 2:
+		return fail(MOE_ERR_TIMEOUT, "an expert kernel's bounded wait expired");
+	case 3:
+		return fail(MOE_ERR_TIMEOUT, "the fused layer kernel's grid barrier expired");
+	case 4:
+		return fail(MOE_ERR_TIMEOUT, "the expert-parallel exchange wait expired (a rank "
+			    "missing or behind; every rank calls moe_layer_ep_reset before going on)");
+	case 5:
+		return fail(MOE_ERR_INVALID, "token-sharded forward: the ranks passed different T");
+	default:
+		return fail(MOE_ERR_CUDA, "layer error word %d", (int)err);
+	}
+}
+
+// Token-sharded expert parallelism above the fused kernel's sizes: this
+// rank routes its own T tokens over all experts; each pair's token row
+// (fp16 hi/lo) travels to the rank that owns the pair's expert, every rank
+// runs the grouped GEMMs over the pairs it received (grouped by expert), the
+// rows travel back, and each rank combines its own tokens in slot order.
+// The transfers are NCCL point-to-point operations in one group per
+// direction (an all-to-all-v), one per (peer, expert) segment, so that the
+// received rows land grouped by expert; the segment sizes come from an
+// all-gather of every rank's per-expert counts, read on the host (one
+// synchronisation of the stream per forward).
+int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int flags,
+			cudaStream_t st, cudaEvent_t *ev)
+{
+	const moe_layer_desc &d = L->d;
+	const int NE = (int)d.n_experts, K = (int)d.top_k, D = (int)d.d_model, F = (int)d.d_ff;
+	const int world = nccl.world, rank = nccl.rank;
+	auto range = [&](int r, int &f, int &n) {
+		f = (int)((int64_t)r * NE / world);
+		n = (int)((int64_t)(r + 1) * NE / world) - f;
+	};
+	int f0, n0;
+	range(rank, f0, n0);
+	if (!nccl.comm || world < 2 || f0 != d.first_expert || n0 != d.n_local)
+		return fail(MOE_ERR_INVALID, "token-sharded forward of %lld tokens: needs moe_ep_init "
+			    "and the layer to own experts [r*NE/world, (r+1)*NE/world)", (long long)T);
+	if (!L->gemm_ok || (uintptr_t)x % 16)
+		return fail(MOE_ERR_UNSUPPORTED, "token-sharded forward of %lld tokens: needs the "
+			    "grouped GEMM (weights and x 16-byte aligned, shapes as it requires)",
+			    (long long)T);
+	cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+	CK(cudaStreamIsCapturing(st, &cap));
+	if (cap != cudaStreamCaptureStatusNone)
+		return fail(MOE_ERR_UNSUPPORTED, "token-sharded forward of %lld tokens reads the "
+			    "transfer sizes on the host: it cannot be captured", (long long)T);
+	const int lanes = (flags & MOE_LANES_AVX2) ? 8 : 16;
+	const int q4 = d.qtype == MOE_Q4_0;
+	const int mode_exact = (flags & MOE_TOPK_EXACT) ? 1 : 0, renorm = (flags & MOE_RENORM) ? 1 : 0;
+	auto record = [&](int i) { return ev ? cudaEventRecord(ev[i], st) : cudaSuccess; };
+	const int64_t P = T * K;
+	// [0] router logits of this rank's tokens
+	if (moe::router_tiled_ok(D, NE))
+		CK(moe::launch_router_tiled(x, d.router_w, (int)T, D, NE, lanes, L->logits, nullptr, q4, st));
+	else
+		CK(moe::launch_router_logits(x, d.router_w, (int)T, D, NE, lanes, L->logits, st));
+	CK(record(1));
+	// [1] top-k and the dispatch of this rank's pairs over every expert
+	if (T <= 256 && moe::route_small_smem((int)T, NE, K) <= 160 * 1024) {
+		CK(moe::launch_route_small(L->logits, d.router_bias, (int)T, NE, K, lanes, mode_exact,
+					   renorm, 0, NE, L->ids, L->wts, L->counts, L->offsets, L->perm,
+					   L->pos_of, L->active, L->n_active, L->err, L->work, st));
+	} else {
+		CK(moe::launch_router_topk(L->logits, d.router_bias, (int)T, NE, K, lanes, mode_exact,
+					   renorm, L->ids, L->wts, nullptr, st));
+		CK(moe::launch_dispatch(L->ids, (int)P, NE, 0, NE, L->counts, L->offsets, L->perm,
+					L->pos_of, L->active, L->n_active, L->err, L->work, st));
+	}
+	// this rank's pairs in expert order as fp16 hi/lo: the send buffer
+	CK(moe::launch_gather_split(x, L->perm, P, D, K, L->x16p, st));
+	// every rank's per-expert counts
+	const size_t mi = (size_t)world * NE + NE + (NE + 1) + NE + 1;
+	if (L->a2a.meta_ints < mi) {
+		CK(cudaStreamSynchronize(st));
+		cudaFree(L->a2a.meta);
+		if (L->a2a.host)
+			cudaFreeHost(L->a2a.host);
+		L->a2a.meta = nullptr;
+		L->a2a.host = nullptr;
+		L->a2a.meta_ints = 0;
+		CK(cudaMalloc(&L->a2a.meta, mi * 4));
+		CK(cudaHostAlloc(&L->a2a.host, mi * 4, cudaHostAllocDefault));
+		L->a2a.meta_ints = mi;
+	}
+	int32_t *allc_d = L->a2a.meta, *allc = L->a2a.host;
+	CK_NCCL(nccl.all_gather(L->counts, allc_d, NE, ncclInt32, nccl.comm, st));
+	CK(cudaMemcpyAsync(allc, allc_d, (size_t)world * NE * 4, cudaMemcpyDeviceToHost, st));
+	CK(cudaStreamSynchronize(st));
+	// the plan: own segments (offsets of this rank's dispatch), and where
+	// rank q's pairs of local expert e land: expert-major, then by rank
+	const int32_t *own = allc + (size_t)rank * NE;
+	std::vector<int64_t> o(NE + 1, 0);
+	for (int e = 0; e < NE; e++)
+		o[e + 1] = o[e] + own[e];
+	int32_t *cnt_l = allc + (size_t)world * NE, *off_l = cnt_l + NE, *act = off_l + NE + 1;
+	int32_t *nact = act + NE;
+	int64_t pl = 0;
+	int na = 0;
+	std::vector<int64_t> rpos((size_t)world * NE, 0);  // [q][e]
+	for (int e = 0; e < NE; e++) {
+		off_l[e] = (int32_t)pl;
+		int64_t c = 0;
+		if (e >= f0 && e < f0 + n0)
+			for (int q = 0; q < world; q++) {
+				rpos[(size_t)q * NE + e] = pl + c;
+				c += allc[(size_t)q * NE + e];
+			}
+		cnt_l[e] = (int32_t)c;
+		if (c > 0)
+			act[na++] = e;
+		pl += c;
+	}
+	off_l[NE] = (int32_t)pl;
+	*nact = na;
+	if (pl > INT32_MAX / 2)
+		return fail(MOE_ERR_INVALID, "token-sharded forward: %lld pairs for one rank", (long long)pl);
+	// receive-side buffers: tokens [pl][2][D], h [pl][2][F] (fp16), rows [pl][D]
+	const size_t bx = align_up((size_t)pl * 2 * D * 2, 256), bh = align_up((size_t)pl * 2 * F * 2, 256);
+	const size_t need = bx + bh + (size_t)pl * D * 4 + 256;
+	if (need > L->a2a.bytes) {
+		cudaFree(L->a2a.buf);
+		L->a2a.buf = nullptr;
+		L->a2a.bytes = 0;
+		CK(cudaMalloc(&L->a2a.buf, need));
+		L->a2a.bytes = need;
+	}
+	__half *xr = (__half *)L->a2a.buf, *hr = (__half *)((char *)L->a2a.buf + bx);
+	float *yr = (float *)((char *)L->a2a.buf + bx + bh);
+	const size_t meta_loc = (size_t)world * NE;
+	CK(cudaMemcpyAsync(allc_d + meta_loc, cnt_l, (mi - meta_loc) * 4, cudaMemcpyHostToDevice, st));
+	const size_t xrow = (size_t)2 * D;  // halves per token row
+	// [2] token rows to the experts' ranks (own experts: a device copy)
+	CK(record(2));
+	for (int e = f0; e < f0 + n0; e++)
+		if (own[e])
+			CK(cudaMemcpyAsync(xr + rpos[(size_t)rank * NE + e] * xrow, L->x16p + o[e] * xrow,
+					   (size_t)own[e] * xrow * 2, cudaMemcpyDeviceToDevice, st));
+	CK_NCCL(nccl.group_start());
+	for (int r = 0; r < world; r++) {
+		if (r == rank)
+			continue;
+		int fr, nr;
+		range(r, fr, nr);
+		for (int e = fr; e < fr + nr; e++)
+			if (own[e])
+				CK_NCCL(nccl.send(L->x16p + o[e] * xrow, (size_t)own[e] * xrow, ncclFloat16, r,
+						  nccl.comm, st));
+		for (int e = f0; e < f0 + n0; e++) {
+			const int32_t c = allc[(size_t)r * NE + e];
+			if (c)
+				CK_NCCL(nccl.recv(xr + rpos[(size_t)r * NE + e] * xrow, (size_t)c * xrow,
+						  ncclFloat16, r, nccl.comm, st));
+		}
+	}
+	CK_NCCL(nccl.group_end());
+	// [3] the grouped GEMMs over the received pairs
+	const size_t mb = moe::weight_map_bytes();
+	moe::GemmArgs gu{};
+	gu.maps1 = L->wmaps;
+	gu.maps2 = (const uint8_t *)L->wmaps + NE * mb;
+	gu.qtype = d.qtype;
+	gu.rows = F;
+	gu.cols = D;
+	gu.n_local = (int)d.n_local;
+	gu.counts = allc_d + meta_loc;
+	gu.offsets = gu.counts + NE;
+	gu.perm = nullptr;
+	gu.active = gu.offsets + NE + 1;
+	gu.n_active = gu.active + NE;
+	gu.out_perm = 0;
+	gu.in16 = xr;
+	gu.out16 = hr;
+	gu.dual = 1;
+	gu.err = L->err;
+	CK(moe::launch_expert_gemm(gu, pl, st));
+	CK(record(3));
+	moe::GemmArgs dn = gu;
+	dn.maps1 = (const uint8_t *)L->wmaps + 2 * NE * mb;
+	dn.maps2 = nullptr;
+	dn.rows = D;
+	dn.cols = F;
+	dn.in16 = hr;
+	dn.out16 = nullptr;
+	dn.out = yr;
+	dn.dual = 0;
+	CK(moe::launch_expert_gemm(dn, pl, st));
+	CK(record(4));
+	// [4] the rows back to the tokens' ranks, at the pairs' dispatch positions
+	for (int e = f0; e < f0 + n0; e++)
+		if (own[e])
+			CK(cudaMemcpyAsync(L->Y + o[e] * D, yr + rpos[(size_t)rank * NE + e] * D,
+					   (size_t)own[e] * D * 4, cudaMemcpyDeviceToDevice, st));
+	CK_NCCL(nccl.group_start());
+	for (int r = 0; r < world; r++) {
+		if (r == rank)
+			continue;
+		int fr, nr;
+		range(r, fr, nr);
+		for (int e = f0; e < f0 + n0; e++) {
+			const int32_t c = allc[(size_t)r * NE + e];
+			if (c)
+				CK_NCCL(nccl.send(yr + rpos[(size_t)r * NE + e] * D, (size_t)c * D, ncclFloat32,
+						  r, nccl.comm, st));
+		}
+		for (int e = fr; e < fr + nr; e++)
+			if (own[e])
+				CK_NCCL(nccl.recv(L->Y + o[e] * D, (size_t)own[e] * D, ncclFloat32, r,
+						  nccl.comm, st));
+	}
+	CK_NCCL(nccl.group_end());
+	CK(moe::launch_combine_pos(L->Y, L->pos_of, L->wts, (int)T, K, D, out, st));
+	CK(record(5));
+	L->last_pairs = P;
 	return MOE_OK;
 }
 
@@ -384,6 +665,9 @@ int moe_shutdown(void)
 	g.resident = 0;
 	if (g.pin)
 		cudaFreeHost(g.pin);
+	if (g.err_pin)
+		cudaFreeHost(g.err_pin);
+	g.err_pin = nullptr;
 	if (g.dev_io)
 		cudaFree(g.dev_io);
 	g.pin = g.dev_io = nullptr;
@@ -449,7 +733,7 @@ int moe_sync(void)
 	if (!g.init)
 		return fail(MOE_ERR_NOT_INIT, "moe_sync: not initialised");
 	CK(cudaStreamSynchronize(g.stream));
-	return MOE_OK;
+	return moe::noalloc_take_error();
 }
 
 // ---------------------------------------------------------------- registry
@@ -636,12 +920,13 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 		}
 	}
 	if (e == cudaSuccess && nl < d.n_experts) {
-		// rows of every (token, slot) pair of a decode batch, twice
+		// rows of every (token, slot) pair of a decode batch, twice; the
+		// counters; every rank's ids and tokens (token-sharded)
 		L->y_half = (int64_t)moe::decode_max_t() * d.top_k * d.d_model;
-		const size_t xb = moe::ep_exchange_bytes(L->y_half);
-		e = cudaMalloc(&L->xbuf, xb);
+		L->xl = moe::ep_layout(L->y_half, d.d_model);
+		e = cudaMalloc(&L->xbuf, L->xl.bytes);
 		if (e == cudaSuccess)
-			e = cudaMemset(L->xbuf, 0, xb);
+			e = cudaMemset(L->xbuf, 0, L->xl.bytes);
 		if (e == cudaSuccess)
 			e = cudaDeviceSynchronize();
 	}
@@ -669,7 +954,14 @@ int moe_layer_destroy(moe_layer *L)
 		cudaIpcCloseMemHandle(p);
 	cudaFree(L->d_ybuf);
 	cudaFree(L->d_inbound);
+	cudaFree(L->d_routed);
+	cudaFree(L->d_xg);
+	cudaFree(L->d_idg);
 	cudaFree(L->xbuf);
+	cudaFree(L->a2a.buf);
+	cudaFree(L->a2a.meta);
+	if (L->a2a.host)
+		cudaFreeHost(L->a2a.host);
 	for (auto &set : L->prof)
 		for (auto ev : set)
 			cudaEventDestroy(ev);
@@ -713,9 +1005,15 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 
 	// decode-sized batch on one GPU: the whole layer in one fused kernel
 	const bool ep_ready = L->ep_world > 1 && L->d_ybuf;
+	// token-sharded expert parallelism: this rank's own tokens
+	const bool shard = (flags & MOE_EP_SHARDED) && d.n_local < d.n_experts;
+	if (shard && !ep_ready && !nccl.comm)
+		return fail(MOE_ERR_INVALID, "moe_layer_forward: MOE_EP_SHARDED needs the ranks "
+			    "connected (moe_layer_set_peers and/or moe_ep_init)");
+	const int64_t world_pairs = shard ? (int64_t)L->ep_world * T * K : T * K;
 	if (!simple && !(flags & (MOE_NO_FUSE | MOE_FORCE_GEMM)) && (d.n_local == d.n_experts || ep_ready) &&
-	    moe::decode_supported(d.qtype, T, D, F, NE, K, (uintptr_t)x, (uintptr_t)d.router_w,
-				  (uintptr_t)out)) {
+	    moe::decode_supported(d.qtype, T, D, F, NE, K, world_pairs, (uintptr_t)x,
+				  (uintptr_t)d.router_w, (uintptr_t)out)) {
 		uint64_t *stamps = nullptr;
 		if (prof && L->prof_used < kStampRecords) {
 			stamps = L->stamps + L->prof_used * moe::sm_count() * moe::decode_stamps();
@@ -754,13 +1052,18 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		a.n_local = (int)d.n_local;
 		a.rank = L->ep_rank;
 		a.world = ep_ready ? L->ep_world : 1;
+		a.shard = shard ? 1 : 0;
 		a.ybuf = L->d_ybuf;
 		a.ybuf_half = L->y_half;
 		a.inbound = L->d_inbound;
-		a.launches = ep_ready ? reinterpret_cast<unsigned long long *>(
-						L->xbuf + 2 * L->y_half * 4 + moe::kMaxEpRanks * moe::kEpFlagStride * 8)
+		a.routed = L->d_routed;
+		a.xg = L->d_xg;
+		a.idg = L->d_idg;
+		a.launches = ep_ready ? reinterpret_cast<unsigned long long *>(L->xbuf + L->xl.launches)
 				      : nullptr;
+		a.ep_wait_ns = L->ep_wait_ns;
 		CK(moe::launch_decode_layer(a, d.qtype, lanes, st));
+		L->last_pairs = world_pairs;
 		return MOE_OK;
 	}
 
@@ -777,6 +1080,9 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		ev = L->prof[L->prof_used++].data();
 		CK(record(ev[0]));
 	}
+	if (shard)
+		return forward_sharded_a2a(L, x, out, T, flags, st, ev);
+	L->last_pairs = T * K;
 	// prefill-sized batches: grouped GEMMs on tcgen05 (the tokens are gathered
 	// into pair order after the dispatch instead of split in token order)
 	const bool gemm = !simple && L->gemm_ok && !(flags & MOE_FORCE_GEMV) &&
@@ -997,7 +1303,9 @@ int moe_layer_set_peers(moe_layer *L, int rank, int world, const void *handles)
 	if (L->d_ybuf)
 		return fail(MOE_ERR_INVALID, "moe_layer_set_peers: peers already set");
 	std::vector<float *> yb(world);
-	std::vector<unsigned long long *> inb(world);
+	std::vector<unsigned long long *> inb(world), rtd(world);
+	std::vector<__half *> xg(world);
+	std::vector<int32_t *> idg(world);
 	const auto *hs = static_cast<const cudaIpcMemHandle_t *>(handles);
 	for (int r = 0; r < world; r++) {
 		void *base = L->xbuf;
@@ -1011,15 +1319,24 @@ int moe_layer_set_peers(moe_layer *L, int rank, int world, const void *handles)
 			}
 			L->opened.push_back(base);
 		}
-		yb[r] = static_cast<float *>(base);
-		inb[r] = reinterpret_cast<unsigned long long *>(static_cast<char *>(base) +
-								 2 * L->y_half * 4);
+		char *cb = static_cast<char *>(base);
+		yb[r] = reinterpret_cast<float *>(cb);
+		inb[r] = reinterpret_cast<unsigned long long *>(cb + L->xl.inbound);
+		rtd[r] = reinterpret_cast<unsigned long long *>(cb + L->xl.routed);
+		idg[r] = reinterpret_cast<int32_t *>(cb + L->xl.idg);
+		xg[r] = reinterpret_cast<__half *>(cb + L->xl.xg);
 	}
-	CK(cudaMalloc(&L->d_ybuf, world * sizeof(float *)));
-	CK(cudaMalloc(&L->d_inbound, world * sizeof(unsigned long long *)));
-	CK(cudaMemcpy(L->d_ybuf, yb.data(), world * sizeof(float *), cudaMemcpyHostToDevice));
-	CK(cudaMemcpy(L->d_inbound, inb.data(), world * sizeof(unsigned long long *),
-		      cudaMemcpyHostToDevice));
+	const size_t pb = world * sizeof(void *);
+	CK(cudaMalloc(&L->d_ybuf, pb));
+	CK(cudaMalloc(&L->d_inbound, pb));
+	CK(cudaMalloc(&L->d_routed, pb));
+	CK(cudaMalloc(&L->d_xg, pb));
+	CK(cudaMalloc(&L->d_idg, pb));
+	CK(cudaMemcpy(L->d_ybuf, yb.data(), pb, cudaMemcpyHostToDevice));
+	CK(cudaMemcpy(L->d_inbound, inb.data(), pb, cudaMemcpyHostToDevice));
+	CK(cudaMemcpy(L->d_routed, rtd.data(), pb, cudaMemcpyHostToDevice));
+	CK(cudaMemcpy(L->d_xg, xg.data(), pb, cudaMemcpyHostToDevice));
+	CK(cudaMemcpy(L->d_idg, idg.data(), pb, cudaMemcpyHostToDevice));
 	L->ep_rank = rank;
 	L->ep_world = world;
 	return MOE_OK;
@@ -1049,26 +1366,11 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 {
 	if (!L)
 		return fail(MOE_ERR_INVALID, "moe_layer_routing: null layer");
-	CK(cudaDeviceSynchronize());  // the forward may have run on a caller stream
 	const int64_t T = L->lastT, K = L->d.top_k, NE = L->d.n_experts;
+	if (int rc = moe_layer_status(L))
+		return rc;
 	if (T == 0)
 		return MOE_OK;
-	int32_t err = 0;
-	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
-	if (err == 2 || err == 3 || err == 4) {
-		// a barrier left half-passed must not poison the next forward
-		CK(cudaMemset(L->gbar, 0, moe::decode_barrier_bytes(moe::sm_count())));
-		CK(cudaDeviceSynchronize());
-	}
-	if (err == 1)
-		return fail(MOE_ERR_INVALID, "dispatch saw an expert id out of range");
-	if (err == 2)
-		return fail(MOE_ERR_TIMEOUT, "an expert kernel's bounded wait expired");
-	if (err == 3)
-		return fail(MOE_ERR_TIMEOUT, "the fused layer kernel's grid barrier expired");
-	if (err == 4)
-		return fail(MOE_ERR_TIMEOUT, "the expert-parallel exchange wait expired (a rank "
-			    "missing or behind)");
 	if (ids)
 		CK(cudaMemcpy(ids, L->ids, T * K * 4, cudaMemcpyDeviceToHost));
 	if (weights)
@@ -1078,7 +1380,42 @@ int moe_layer_routing(moe_layer *L, int32_t *ids, float *weights, int32_t *count
 	if (offsets)
 		CK(cudaMemcpy(offsets, L->offsets, (NE + 1) * 4, cudaMemcpyDeviceToHost));
 	if (perm)
-		CK(cudaMemcpy(perm, L->perm, T * K * 4, cudaMemcpyDeviceToHost));
+		CK(cudaMemcpy(perm, L->perm, L->last_pairs * 4, cudaMemcpyDeviceToHost));
+	return MOE_OK;
+}
+
+int moe_layer_status(moe_layer *L)
+{
+	if (!L)
+		return fail(MOE_ERR_INVALID, "moe_layer_status: null layer");
+	if (!L->err)
+		return MOE_OK;  // no forward has run
+	CK(cudaDeviceSynchronize());  // the forward may have run on a caller stream
+	int32_t err = 0;
+	CK(cudaMemcpy(&err, L->err, 4, cudaMemcpyDeviceToHost));
+	return take_error(L, err);
+}
+
+int moe_layer_set_wait_ms(moe_layer *L, int ms)
+{
+	if (!L || ms <= 0)
+		return fail(MOE_ERR_INVALID, "moe_layer_set_wait_ms: need a layer and ms > 0");
+	L->ep_wait_ns = (uint64_t)ms * 1000000ull;
+	return MOE_OK;
+}
+
+int moe_layer_ep_reset(moe_layer *L)
+{
+	if (!L)
+		return fail(MOE_ERR_INVALID, "moe_layer_ep_reset: null layer");
+	CK(cudaDeviceSynchronize());
+	if (L->xbuf)
+		CK(cudaMemset(L->xbuf + L->xl.inbound, 0, L->xl.idg - L->xl.inbound));
+	if (L->err) {
+		CK(cudaMemset(L->err, 0, 4));
+		CK(cudaMemset(L->gbar, 0, moe::decode_barrier_bytes(moe::sm_count())));
+	}
+	CK(cudaDeviceSynchronize());
 	return MOE_OK;
 }
 
@@ -1372,8 +1709,11 @@ int forward_io(moe_layer *L, const moe_tensor_t *input, moe_tensor_t *output, in
 	if (int rc = moe_layer_forward(L, dx, dy, T, flags, nullptr))
 		return rc;
 	CK(cudaMemcpyAsync(output->data, dy, T * D * 4, cudaMemcpyDeviceToHost, g.stream));
+	// the layer's error word comes back with the output (T == 0 runs nothing)
+	if (T > 0)
+		CK(cudaMemcpyAsync(g.err_pin, L->err, 4, cudaMemcpyDeviceToHost, g.stream));
 	CK(cudaStreamSynchronize(g.stream));
-	return MOE_OK;
+	return T > 0 ? take_error(L, *g.err_pin) : MOE_OK;
 }
 
 int forward_common(const moe_tensor_t *input, moe_tensor_t *output, const moe_tensor_t *gate_inp,

@@ -11,26 +11,33 @@
 
 namespace moe {
 
-// Raise a kernel's dynamic shared-memory limit once per process (the
-// attribute persists), remembering what was set per kernel.
+// Raise a kernel's dynamic shared-memory limit once per device and kernel
+// (the attribute belongs to the device's context and persists), remembering
+// what was set.
 inline cudaError_t ensure_smem_ptr(const void *fn, size_t bytes)
 {
-	static const void *keys[128];
-	static size_t vals[128];
+	static const void *keys[256];
+	static int devs[256];
+	static size_t vals[256];
 	static int used = 0;
+	int dev = 0;
+	cudaError_t e = cudaGetDevice(&dev);
+	if (e != cudaSuccess)
+		return e;
 	int i = 0;
 	for (; i < used; i++)
-		if (keys[i] == fn)
+		if (keys[i] == fn && devs[i] == dev)
 			break;
 	if (i < used && bytes <= vals[i])
 		return cudaSuccess;
-	cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-					     (int)bytes);
+	e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 	if (e != cudaSuccess)
 		return e;
-	if (i == used && used < 128)
-		keys[used++] = fn;
-	if (i < 128)
+	if (i == used && used < 256) {
+		keys[used] = fn;
+		devs[used++] = dev;
+	}
+	if (i < 256)
 		vals[i] = bytes;
 	return cudaSuccess;
 }
@@ -41,17 +48,20 @@ inline cudaError_t ensure_smem(F *fn, size_t bytes)
 	return ensure_smem_ptr(reinterpret_cast<const void *>(fn), bytes);
 }
 
+// SMs of the current device (cached per device)
 inline int sm_count()
 {
-	static int n = 0;
-	if (!n) {
-		int dev = 0;
-		cudaGetDevice(&dev);
-		cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-		if (n <= 0)
-			n = 148;
+	static int n[64];
+	int dev = 0;
+	cudaGetDevice(&dev);
+	if (dev < 0 || dev >= 64)
+		dev = 0;
+	if (!n[dev]) {
+		int v = 0;
+		cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+		n[dev] = v > 0 ? v : 148;
 	}
-	return n;
+	return n[dev];
 }
 
 enum QType { kF32 = 0, kQ8_0 = 1, kQ4_0 = 2 };

@@ -62,8 +62,6 @@ struct RTile {
 	static constexpr int NSLOT = 1;
 };
 
-constexpr int kDecodeMaxT = 64;
-constexpr int kDecodeMaxPairs = 1024;
 // %globaltimer stamps per CTA (thread 0): phase ends and barrier exits
 enum Stamp {
 	kStStart, kStP0, kStB1, kStTopk, kStB1b, kStDispatch, kStP1, kStP2, kStB2, kStP3, kStB3,
@@ -76,23 +74,29 @@ struct DecodeSmem {
 	static constexpr int OFF = EN + kMaxActive * 4;            // int32 [256]
 	static constexpr int PRE_GU = OFF + kMaxActive * 4;        // int32 [260]
 	static constexpr int PRE_DN = PRE_GU + (kMaxActive + 4) * 4;
-	static constexpr int IDS = PRE_DN + (kMaxActive + 4) * 4;  // int32 [1024]
-	static constexpr int WTS = IDS + kDecodeMaxPairs * 4;      // f32   [1024]
-	static constexpr int PERM = WTS + kDecodeMaxPairs * 4;     // int32 [1024]
-	static constexpr int COUNTS = PERM + kDecodeMaxPairs * 4;  // int32 [256]
+	static constexpr int WTS = PRE_DN + (kMaxActive + 4) * 4;  // f32   [1024] own pairs
+	static constexpr int PERM = WTS + kDecodeMaxPairs * 4;     // int32 [2048] all pairs
+	static constexpr int COUNTS = PERM + kDecodeMaxPairsAll * 4;  // int32 [256]
 	static constexpr int OFFSETS = COUNTS + kMaxActive * 4;    // int32 [260]
 	static constexpr int ACTIVE = OFFSETS + (kMaxActive + 4) * 4;  // int32 [256]
 	static constexpr int NACT = ACTIVE + kMaxActive * 4;       // int32 [4]
 	static constexpr int BARS = NACT + 16;                     // u64 bars
 	static constexpr int END = BARS;                           // + bars
+	// during P1 only: the dispatch scratch at the start of the stage ring,
+	// the ids of the dispatched pairs behind it
+	static constexpr int RING_IDS = 16 * 1024;
 };
+// u64 slots after the mbarriers: the router tile barrier, then the peer
+// tables (row destinations of the replicated and the token-sharded
+// exchange, this rank's gathered-token buffer in each rank)
+constexpr int kPtrSlots = 1 + 3 * kMaxEpRanks;
 
 template <int QT, int STAGES>
 constexpr size_t decode_smem_bytes()
 {
 	return (size_t)STAGES * StageLayout<QT>::BYTES + StageLayout<QT>::RED +
 	       StageLayout<QT>::EPI + DecodeSmem::END +
-	       (2 * STAGES + 2 * kRedBufs + 1 + kMaxEpRanks) * 8;  // + router barrier, peer table
+	       (2 * STAGES + 2 * kRedBufs + kPtrSlots) * 8;  // + router barrier, peer tables
 }
 
 // ---------------------------------------------------------------- grid barrier
@@ -113,6 +117,21 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 __device__ __forceinline__ void red_add_release_sys(unsigned long long *p, unsigned long long v)
 {
 	asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// cross-rank arrival wait: until *cnt reaches `want` (acquire, system
+// scope), at most limit_ns; an expired wait records error 4
+__device__ void wait_arrivals(const unsigned long long *cnt, unsigned long long want,
+			      uint64_t limit_ns, int32_t *err)
+{
+	const uint64_t t0 = global_ns();
+	while (ld_acquire_sys(cnt) < want) {
+		if (global_ns() - t0 > limit_ns) {
+			atomicExch(err, 4);
+			return;
+		}
+		__nanosleep(64);
+	}
 }
 
 // Grid barrier: bar[0] counts arrivals since the buffer was zeroed (a
@@ -260,7 +279,6 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	int32_t *off = reinterpret_cast<int32_t *>(tb + DS::OFF);
 	int32_t *pre_gu = reinterpret_cast<int32_t *>(tb + DS::PRE_GU);
 	int32_t *pre_dn = reinterpret_cast<int32_t *>(tb + DS::PRE_DN);
-	int32_t *ids_s = reinterpret_cast<int32_t *>(tb + DS::IDS);
 	float *wts_s = reinterpret_cast<float *>(tb + DS::WTS);
 	int32_t *perm_s = reinterpret_cast<int32_t *>(tb + DS::PERM);
 	int32_t *counts_s = reinterpret_cast<int32_t *>(tb + DS::COUNTS);
@@ -273,8 +291,6 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 	const int T = a.T, D = a.D, F = a.F, NE = a.NE, K = a.K;
 	stamp(a.stamps, kStStart);
-	if (blockIdx.x == 0 && tid == 0)
-		*a.err = 0;
 	const Bars b = init_bars<STAGES>(bars);
 	if (tid == 0)
 		mbar_init(rbar, 1);
@@ -283,12 +299,24 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	// each exchange buffer it writes -- a rank one launch ahead writes the
 	// other half, so it never overwrites rows that are still being combined
 	const bool ep = a.world > 1;
+	const bool shard = ep && a.shard;
 	const unsigned long long epoch = ep ? *reinterpret_cast<volatile unsigned long long *>(a.launches) + 1 : 0;
 	const int64_t half_off = (int64_t)(epoch & 1) * a.ybuf_half;
 	float *Y = ep ? a.ybuf[a.rank] + half_off : a.Y;
-	float **ypeers = reinterpret_cast<float **>(rbar + 1);  // [world - 1] (smem)
-	if (ep && tid < a.world && tid != a.rank)
-		ypeers[tid - (tid > a.rank)] = a.ybuf[tid] + half_off;
+	// peer tables (smem): the other ranks' Y halves (replicated tokens),
+	// every rank's Y half (token-sharded, indexed by rank), and this rank's
+	// rows in every rank's gathered-token buffer (token-sharded)
+	float **ypeers = reinterpret_cast<float **>(rbar + 1);
+	float **yall = ypeers + kMaxEpRanks;
+	__half **xgl = reinterpret_cast<__half **>(yall + kMaxEpRanks);
+	if (ep && tid < a.world) {
+		if (tid != a.rank)
+			ypeers[tid - (tid > a.rank)] = a.ybuf[tid] + half_off;
+		yall[tid] = a.ybuf[tid] + half_off;
+		if (shard)
+			xgl[tid] = a.xg[tid] + (int64_t)a.rank * T * 2 * D;
+	}
+	const uint64_t ep_wait = a.ep_wait_ns ? a.ep_wait_ns : kWaitLimitNs;
 	fence_mbar_init();
 	__syncthreads();
 
@@ -313,15 +341,33 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	}
 	router_tiles<LANES>(a, smem, rbar);
 	{
-		const int64_t total = (int64_t)T * D;
-		for (int64_t i = (int64_t)blockIdx.x * blockDim.x + tid; i < total;
-		     i += (int64_t)gridDim.x * blockDim.x) {
-			const int64_t r = i / D;
-			const int k = (int)(i - r * D);
-			const float v = __ldg(a.x + r * D + (QT == kQ4_0 ? q4_src(k) : k));
-			const __half h = __float2half_rn(v);
-			a.x16[r * 2 * D + k] = h;
-			a.x16[r * 2 * D + D + k] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+		// the fp16 hi/lo split of x that the expert phases read, 8 columns
+		// per thread and 16-byte stores; token-sharded, into this rank's rows
+		// of every rank's gathered-token buffer (over NVLink for the others)
+		__half *xl = shard ? xgl[a.rank] : a.x16;
+		const int64_t groups = (int64_t)T * D / 8;
+		for (int64_t g = (int64_t)blockIdx.x * blockDim.x + tid; g < groups;
+		     g += (int64_t)gridDim.x * blockDim.x) {
+			const int64_t r = g * 8 / D;
+			const int k = (int)(g * 8 - r * D);
+			__align__(16) __half hi[8], lo[8];
+#pragma unroll
+			for (int j = 0; j < 8; j++) {
+				const float v = __ldg(a.x + r * D + (QT == kQ4_0 ? q4_src(k + j) : k + j));
+				hi[j] = __float2half_rn(v);
+				lo[j] = __float2half_rn(__fsub_rn(v, __half2float(hi[j])));
+			}
+			const uint4 vh = *reinterpret_cast<const uint4 *>(hi);
+			const uint4 vl = *reinterpret_cast<const uint4 *>(lo);
+			*reinterpret_cast<uint4 *>(xl + r * 2 * D + k) = vh;
+			*reinterpret_cast<uint4 *>(xl + r * 2 * D + D + k) = vl;
+			if (shard)
+				for (int q = 0; q < a.world; q++)
+					if (q != a.rank) {
+						__half *xp = xgl[q] + r * 2 * D + k;
+						*reinterpret_cast<uint4 *>(xp) = vh;
+						*reinterpret_cast<uint4 *>(xp + D) = vl;
+					}
 		}
 	}
 	__syncthreads();
@@ -344,22 +390,61 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				topk_token<LANES>(lg, a.router_bias, NE, K, a.mode_exact, a.renorm, sel,
 						  reinterpret_cast<int32_t *>(sel + K), a.ids + (int64_t)t * K,
 						  a.wts + (int64_t)t * K, nullptr, nullptr);
+				if (shard) {
+					// this token's ids into every rank's gathered ids: pair
+					// (rank * T + t) * K + slot
+					const int32_t *sid = reinterpret_cast<const int32_t *>(sel + K);
+					for (int q = lane; q < a.world * K; q += 32) {
+						const int r = q / K, sl = q - r * K;
+						a.idg[r][kEpIdsHeader + ((int64_t)a.rank * T + t) * K + sl] = sid[sl];
+					}
+				}
 			}
 		}
+		if (shard && blockIdx.x == 0 && tid < a.world)
+			a.idg[tid][a.rank] = T;  // checked by every rank: the same T everywhere
 		__syncthreads();
 		stamp(a.stamps, kStTopk);
-		if (tid == 0)
+		if (shard) {
+			// every CTA of every rank announces that its tokens and ids are
+			// out (made visible system-wide, then one arrival per CTA on each
+			// rank's counter for this rank); each rank waits for every rank's
+			__threadfence_system();
+			__syncthreads();
+			if (tid == 0)
+				for (int r = 0; r < a.world; r++)
+					red_add_release_sys(a.routed[r] + kEpFlagStride * a.rank, 1ull);
+			if (tid < a.world)
+				wait_arrivals(a.routed[a.rank] + kEpFlagStride * tid, epoch * gridDim.x, ep_wait,
+					      a.err);
+		} else if (tid == 0) {
 			grid_sync(a.gbar, a.err);
-		__syncthreads();
-		stamp(a.stamps, kStB1b);
-		// every CTA: the dispatch of all (token, slot) pairs, in shared memory
-		int32_t *ds = reinterpret_cast<int32_t *>(smem);
-		for (int i = tid; i < T * K; i += blockDim.x) {
-			ids_s[i] = __ldcg(a.ids + i);
-			wts_s[i] = __fdiv_rn(1.0f, __ldcg(a.wts + i));  // 1 / w, the combine's divisor
 		}
 		__syncthreads();
-		dispatch_body(ids_s, T * K, NE, a.first_expert, a.n_local, counts_s, offsets_s, perm_s,
+		stamp(a.stamps, kStB1b);
+		// every CTA: the dispatch of all (token, slot) pairs (token-sharded:
+		// every rank's) into its own shared memory.  The ids sit in the stage
+		// ring behind the dispatch scratch until the experts start.
+		int32_t *ds = reinterpret_cast<int32_t *>(smem);
+		int32_t *ids_all = reinterpret_cast<int32_t *>(smem + DS::RING_IDS);
+		int np = T * K;
+		const int32_t *idsrc = a.ids;
+		if (shard) {
+			const int32_t *hdr = a.idg[a.rank];
+			bool same = true;
+			for (int r = 0; r < a.world; r++)
+				same = same && __ldcg(hdr + r) == T;
+			if (!same && blockIdx.x == 0 && tid == 0)
+				atomicCAS(a.err, 0, 5);  // an expired wait, recorded first, explains it
+			np = same ? a.world * T * K : 0;
+			idsrc = hdr + kEpIdsHeader;
+		}
+		for (int i = tid; i < np; i += blockDim.x)
+			ids_all[i] = __ldcg(idsrc + i);
+		for (int i = tid; i < T * K; i += blockDim.x)
+			wts_s[i] = __fdiv_rn(1.0f, __ldcg(a.wts + i));  // 1 / w, the combine's divisor
+		__syncthreads();
+		dispatch_body(ids_all, np, NE, a.first_expert, a.n_local, counts_s, offsets_s, perm_s,
 			      nullptr, active_s, nact_s, a.err, ds);
 		__syncthreads();
 		stamp(a.stamps, kStDispatch);
@@ -376,7 +461,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			build_prefix_warp(en, n_active, (D + 16 * MT_DN - 1) / (16 * MT_DN), pre_dn);
 		if (blockIdx.x == 0) {
 			// the routing, for the host (moe_layer_routing)
-			for (int i = tid; i < T * K; i += blockDim.x)
+			for (int i = tid; i < np; i += blockDim.x)
 				a.perm[i] = perm_s[i];
 			for (int i = tid; i < NE; i += blockDim.x) {
 				a.counts[i] = counts_s[i];
@@ -397,11 +482,13 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	{
 		const int n_active = *nact_s;
 		const Phase gu{a.dptrs, a.dptrs + NE, F, D, K, en, off, pre_gu, n_active, perm_s, 1, 0,
-			       a.x16, a.h16, nullptr, a.err, nullptr, nullptr, 0};
-		// down stores y per (token, slot) row, also into the other ranks'
-		// exchange buffers; P4 divides by 1 / w and adds
+			       shard ? a.xg[a.rank] : a.x16, a.h16, nullptr, a.err, nullptr, nullptr, 0, 0};
+		// down stores y per (token, slot) row: replicated tokens, here and
+		// into every other rank's exchange buffer; token-sharded, into the
+		// buffer of the rank that owns the token.  P4 divides by 1 / w and adds
 		const Phase dn{a.dptrs + 2 * NE, nullptr, D, F, K, en, off, pre_dn, n_active, perm_s, 0, 1,
-			       a.h16, nullptr, Y, a.err, nullptr, ypeers, ep ? a.world - 1 : 0};
+			       a.h16, nullptr, Y, a.err, nullptr, shard ? yall : ypeers,
+			       (ep && !shard) ? a.world - 1 : 0, shard ? T * K : 0};
 		Pipe pipe;
 		if (warp == kProducerWarp) {
 			core_producer<QT, true, STAGES, WB_GU>(gu, smem, b, pipe, lane);
@@ -449,18 +536,9 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		if (tid == 0)
 			for (int r = 0; r < a.world; r++)
 				red_add_release_sys(a.inbound[r] + kEpFlagStride * a.rank, 1ull);
-		if (tid < a.world) {
-			const unsigned long long *cnt = a.inbound[a.rank] + kEpFlagStride * tid;
-			const unsigned long long want = epoch * gridDim.x;
-			const uint64_t t0 = global_ns();
-			while (ld_acquire_sys(cnt) < want) {
-				if (global_ns() - t0 > kWaitLimitNs) {
-					atomicExch(a.err, 4);
-					break;
-				}
-				__nanosleep(64);
-			}
-		}
+		if (tid < a.world)
+			wait_arrivals(a.inbound[a.rank] + kEpFlagStride * tid, epoch * gridDim.x, ep_wait,
+				      a.err);
 		__syncthreads();
 	}
 	stamp(a.stamps, kStB3);
@@ -495,12 +573,12 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 }
 
 // ---------------------------------------------------------------- launch
-bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr_t x,
-		      uintptr_t router_w, uintptr_t out)
+bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, int64_t world_pairs,
+		      uintptr_t x, uintptr_t router_w, uintptr_t out)
 {
 	const Shape dn = pick_shape(F, false);
 	return (qtype == kQ8_0 || qtype == kQ4_0) && T >= 1 && T <= kDecodeMaxT &&
-	       T * K <= kDecodeMaxPairs && K >= 1 && K <= 32 && NE % 8 == 0 && NE <= kMaxActive &&
+	       T * K <= kDecodeMaxPairs && world_pairs <= kDecodeMaxPairsAll && K >= 1 && K <= 32 && NE % 8 == 0 && NE <= kMaxActive &&
 	       D % 2048 == 0 && dn.wb == 8 && x % 16 == 0 && router_w % 16 == 0 && out % 16 == 0;
 }
 
@@ -526,6 +604,9 @@ static cudaError_t launch_decode_t(const DecodeArgs &a, cudaStream_t st)
 	static_assert(smem <= 227 * 1024, "fused decode kernel exceeds shared memory");
 	static_assert(RTile<LANES>::BYTES <= STAGES * StageLayout<QT>::BYTES,
 		      "the router tile fits in the stage ring");
+	static_assert((2 + kCoreThreads / 32) * kMaxActive * 4 <= DecodeSmem::RING_IDS &&
+			      DecodeSmem::RING_IDS + kDecodeMaxPairsAll * 4 <= STAGES * StageLayout<QT>::BYTES,
+		      "the dispatch scratch and the pair ids fit in the stage ring");
 	auto fn = moe_decode_kernel<QT, LANES, 8, 8, MT_DN, STAGES>;
 	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)

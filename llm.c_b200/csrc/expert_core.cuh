@@ -388,6 +388,11 @@ struct Phase {
 	const float *wdiv;       // single, optional: store y / (1 / wdiv[out row])
 	float *const *peers;     // single, optional: the same rows also go to these
 	int npeers;              // buffers (other GPUs' memory, expert parallelism)
+	// single, token-sharded expert parallelism: out row `orow` belongs to
+	// rank orow / shard_pairs and goes to peers[that rank] at row
+	// orow % shard_pairs (peers then holds every rank's buffer, own one
+	// included, and `out` is unused)
+	int shard_pairs;
 };
 
 struct Bars {
@@ -630,9 +635,15 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 					const int tt = lane >> 2, t = tg + tt;
 					if (t < n) {
 						const int pos = off + t;
-						const int orow = ph.out_perm ? ph.perm[pos] : pos;
+						int orow = ph.out_perm ? ph.perm[pos] : pos;
 						const int rr = (lane & 3) * PER;
-						float *dst = ph.out + (int64_t)orow * ph.rows + r0 + rr;
+						float *obase = ph.out;
+						if (ph.shard_pairs) {
+							const int owner = orow / ph.shard_pairs;
+							obase = ph.peers[owner];
+							orow -= owner * ph.shard_pairs;
+						}
+						float *dst = obase + (int64_t)orow * ph.rows + r0 + rr;
 						const float *src = stg + tt * ROWS + rr;
 						if (nr == ROWS && ph.rows % 4 == 0) {
 #pragma unroll

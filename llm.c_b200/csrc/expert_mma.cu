@@ -94,7 +94,7 @@ static cudaError_t launch_t(const MmaArgs &a, cudaStream_t st)
 	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
-	static int per_sm = 0;  // occupancy of this instantiation (fixed)
+	static int per_sm = 0;  // occupancy of this instantiation (the same on every B200)
 	if (!per_sm) {
 		e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
 		if (e != cudaSuccess)

@@ -188,6 +188,44 @@ cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, 
 	return cudaGetLastError();
 }
 
+// combine of rows stored at the pairs' dispatch positions (token-sharded
+// expert parallelism): out[t] = sum_s Y[pos_of[t*K + s]] / (1 / w[t*K + s])
+// in slot order, the same arithmetic as combine_kernel
+__global__ void combine_pos_kernel(const float *__restrict__ Y, const int32_t *__restrict__ pos_of,
+				   const float *__restrict__ w, int T, int K, int d,
+				   float *__restrict__ out)
+{
+	const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+	const int d4 = d / 4;
+	if (i >= (int64_t)T * d4)
+		return;
+	const int t = (int)(i / d4);
+	const int j4 = (int)(i - (int64_t)t * d4);
+	float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+	for (int s = 0; s < K; s++) {
+		const float inv = __fdiv_rn(1.0f, w[t * K + s]);
+		const int64_t row = pos_of[t * K + s];
+		const float4 y = __ldg(reinterpret_cast<const float4 *>(Y + row * d) + j4);
+		acc.x = __fadd_rn(__fdiv_rn(y.x, inv), acc.x);
+		acc.y = __fadd_rn(__fdiv_rn(y.y, inv), acc.y);
+		acc.z = __fadd_rn(__fdiv_rn(y.z, inv), acc.z);
+		acc.w = __fadd_rn(__fdiv_rn(y.w, inv), acc.w);
+	}
+	reinterpret_cast<float4 *>(out + (int64_t)t * d)[j4] = acc;
+}
+
+cudaError_t launch_combine_pos(const float *Y, const int32_t *pos_of, const float *w, int T, int K,
+			       int d, float *out, cudaStream_t st)
+{
+	const int64_t n4 = (int64_t)T * d / 4;
+	if (n4 == 0)
+		return cudaSuccess;
+	if (d % 4 || (uintptr_t)Y % 16 || (uintptr_t)out % 16)
+		return cudaErrorInvalidValue;
+	combine_pos_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(Y, pos_of, w, T, K, d, out);
+	return cudaGetLastError();
+}
+
 __global__ void add_bias_kernel(float *ret, const float *add, int64_t total, int64_t n_add)
 {
 	const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

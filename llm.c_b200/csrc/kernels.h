@@ -21,7 +21,8 @@ cudaError_t launch_router_tiled(const float *x, const float *w, int T, int d, in
 cudaError_t launch_router_topk(const float *logits, const float *bias, int T, int NE, int K,
 			       int lanes, int mode_exact, int renorm, int32_t *ids, float *wts,
 			       float *probs, cudaStream_t st);
-// dispatch also zeroes *err and work[0..1]
+// dispatch also zeroes work[0..1] (the error word is sticky: the host
+// reads and clears it)
 cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int first, int nlocal,
 			    int32_t *counts, int32_t *offsets, int32_t *perm, int32_t *pos_of,
 			    int32_t *active, int32_t *n_active, int32_t *err, int32_t *work,
@@ -100,36 +101,75 @@ struct DecodeArgs {
 	int mode_exact, renorm;
 	float *logits;             // [T, NE]
 	__half *x16;               // [T, 2, D]
-	__half *h16;               // [T*K, 2, F]
+	__half *h16;               // [pairs, 2, F]
 	float *Y;                  // [T*K, D]
 	float *out;                // [T, D]
 	int32_t *ids;              // [T*K]
 	float *wts;                // [T*K]
 	int32_t *counts, *offsets, *perm, *active, *n_active;
-	int32_t *err;              // 0 ok, 2 bounded mbarrier wait expired, 3 grid barrier expired
+	// sticky error word (the host reads and clears it): 1 expert id out of
+	// range, 2 bounded mbarrier wait expired, 3 grid barrier expired,
+	// 4 expert-parallel exchange wait expired, 5 ranks passed different T
+	int32_t *err;
 	unsigned long long *gbar;  // grid barrier state (decode_barrier_bytes), zero when allocated
 	uint64_t *stamps;          // NULL or [grid][decode_stamps()] phase times (ns)
 	// expert parallelism (world > 1): this GPU computes experts
-	// [first_expert, first_expert + n_local) and writes each of their
-	// (token, slot) rows into every rank's exchange buffer; then every rank
-	// combines all rows in slot order.
+	// [first_expert, first_expert + n_local).
+	//   shard = 0 (replicated tokens): every rank has the same T tokens; each
+	//     (token, slot) row of the local experts goes to every rank's
+	//     exchange buffer and every rank combines all rows in slot order.
+	//   shard = 1 (token-sharded): x holds this rank's own T tokens (every
+	//     rank passes the same T).  Each rank writes its tokens (fp16 hi/lo)
+	//     and top-k ids into every rank's exchange buffer; after the
+	//     cross-rank arrival each rank dispatches the pairs of all world*T
+	//     tokens to its local experts, and every row it produces goes to the
+	//     exchange buffer of the rank that owns the token; each rank then
+	//     combines its own tokens.
 	int first_expert, n_local;
-	int rank, world;
-	float *const *ybuf;        // device [world]: exchange buffers (two halves each)
+	int rank, world, shard;
+	float *const *ybuf;        // device [world]: exchange buffers (two Y halves each)
 	int64_t ybuf_half;         // floats from one half to the other
-	unsigned long long *const *inbound;  // device [world]: rank r's arrival counters
+	unsigned long long *const *inbound;  // device [world]: rank r's row-arrival counters
+	unsigned long long *const *routed;   // device [world]: rank r's routing-arrival counters
+	__half *const *xg;         // device [world]: gathered tokens [world*T][2][D] (shard)
+	int32_t *const *idg;       // device [world]: T of each rank [16], then ids [world*T*K]
 	unsigned long long *launches;        // this rank's count of expert-parallel launches
+	uint64_t ep_wait_ns;       // limit of the cross-rank waits (0: the 2 s default)
 };
 constexpr int kMaxEpRanks = 8;
 constexpr int kEpFlagStride = 16;  // u64s (128 bytes) per counter
-// exchange buffer of one rank: two Y halves of y_half floats, then
-// kMaxEpRanks arrival counters and the launch counter
-inline size_t ep_exchange_bytes(int64_t y_half)
+constexpr int kEpIdsHeader = 16;   // int32 slots before the gathered ids
+// kernel-side limits of the fused decode kernel
+constexpr int kDecodeMaxT = 64;           // tokens per rank
+constexpr int kDecodeMaxPairs = 1024;     // this rank's (token, slot) pairs
+constexpr int kDecodeMaxPairsAll = 2048;  // every rank's pairs (token-sharded)
+// exchange buffer of one rank (one allocation, shared by CUDA IPC):
+//   Y halves      2 * y_half floats
+//   counters      inbound[kMaxEpRanks], routed[kMaxEpRanks], launches
+//                 (one 128-byte line each)
+//   gathered ids  kEpIdsHeader + kMaxEpRanks * kDecodeMaxPairs int32
+//   gathered x    kMaxEpRanks * kDecodeMaxT rows of 2 * D halves
+struct EpLayout {
+	size_t inbound, routed, launches, idg, xg, bytes;
+};
+inline EpLayout ep_layout(int64_t y_half, int64_t D)
 {
-	return (size_t)(2 * y_half) * 4 + (size_t)(kMaxEpRanks + 1) * kEpFlagStride * 8;
+	EpLayout l;
+	const size_t line = (size_t)kEpFlagStride * 8;
+	l.inbound = (size_t)(2 * y_half) * 4;
+	l.inbound = (l.inbound + 255) / 256 * 256;
+	l.routed = l.inbound + kMaxEpRanks * line;
+	l.launches = l.routed + kMaxEpRanks * line;
+	l.idg = l.launches + line;
+	l.xg = l.idg + (size_t)(kEpIdsHeader + kMaxEpRanks * kDecodeMaxPairs) * 4;
+	l.xg = (l.xg + 255) / 256 * 256;
+	l.bytes = l.xg + (size_t)kMaxEpRanks * kDecodeMaxT * 2 * D * 2;
+	return l;
 }
-bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, uintptr_t x,
-		      uintptr_t router_w, uintptr_t out);
+// world_pairs: the (token, slot) pairs of every rank the kernel dispatches
+// (T*K, or world*T*K when token-sharded)
+bool decode_supported(int qtype, int64_t T, int D, int F, int NE, int K, int64_t world_pairs,
+		      uintptr_t x, uintptr_t router_w, uintptr_t out);
 int decode_stamps();
 int decode_max_t();
 size_t decode_barrier_bytes(int ctas);
@@ -169,6 +209,11 @@ cudaError_t launch_gather_split(const float *x, const int32_t *perm, int64_t pai
 // out[t, :] = sum_s Y[t*K + s, :] / (1 / w[t*K + s]) in slot order
 cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, float *out,
 			   cudaStream_t st);
+
+// the same with the rows of Y at the pairs' dispatch positions:
+// Y[pos_of[t*K + s]] (d % 4 == 0, Y and out 16-byte aligned)
+cudaError_t launch_combine_pos(const float *Y, const int32_t *pos_of, const float *w, int T, int K,
+			       int d, float *out, cudaStream_t st);
 
 // ret[i] = ret[i] + add[i % n_add]  (bias of tensor_mma_transposed_2x2)
 cudaError_t launch_add_bias(float *ret, const float *add, int64_t total, int64_t n_add,

@@ -15,12 +15,14 @@
 //   [256, 1 MiB) fp16 hi/lo split of x: m * 2 * cols halves
 // so m * cols <= (1 MiB - 256) / 4 = 262080 elements.
 //
-// Every call rewrites the metadata and the split (the error flag and the
-// work counter start at zero each call).  All calls share the one array:
-// calls that overlap on the GPU (different streams, or host threads)
-// race on it.  The device address of the array is looked up once per
-// device on that device's first call (cudaGetSymbolAddress), so make that
-// first call before any stream capture.
+// Every call rewrites the metadata and the split (the work counter starts at
+// zero each call).  The error flag is sticky: a bounded wait that expires
+// inside the tensor-core kernel sets it, and moe_sync() reports it (and
+// clears it) after synchronising.  All calls share the one array: calls
+// that overlap on the GPU (different streams, or host threads) race on it.
+// The device address of the array is looked up once per device on that
+// device's first call (cudaGetSymbolAddress), so make that first call
+// before any stream capture.
 #include "moe_b200.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -28,8 +30,11 @@
 #include <cstdio>
 
 namespace moe {
-// capi.cu: record a message for moe_last_error(); the library stream
+// capi.cu: record a message for moe_last_error(); initialise the library
+// on the current device if needed (creates its stream, allocates nothing);
+// the library stream
 void set_last_error(const char *msg);
+int ensure_library();
 cudaStream_t library_stream();
 }  // namespace moe
 
@@ -54,6 +59,14 @@ static_assert(sizeof(NoallocMeta) <= kNoallocMeta, "metadata fits its slot");
 
 uint8_t *g_scratch_dev[kMaxDevices];  // device address per device
 
+int cuda_error(cudaError_t e, const char *what)
+{
+	char msg[200];
+	snprintf(msg, sizeof(msg), "moe_gemv_device_noalloc: %s: %s", what, cudaGetErrorString(e));
+	moe::set_last_error(msg);
+	return MOE_ERR_CUDA;
+}
+
 // slot k of a Q4_0 block holds element q4_pick(k) (the order in which the
 // tensor-core kernel pairs 4-bit codes)
 __device__ __forceinline__ int q4_pick(int k)
@@ -71,7 +84,6 @@ __global__ void noalloc_prep_kernel(const void *w, const float *__restrict__ x, 
 		meta->counts[0] = (int32_t)m;
 		meta->offsets[0] = 0;
 		meta->offsets[1] = (int32_t)m;
-		meta->err[0] = 0;
 		meta->active[0] = 0;
 		meta->n_active[0] = 1;
 		meta->work[0] = meta->work[1] = 0;
@@ -119,6 +131,11 @@ extern "C" MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t
 		moe::set_last_error("moe_gemv_device_noalloc: no current CUDA device");
 		return MOE_ERR_CUDA;
 	}
+	// a NULL stream means the library stream, which moe_init creates (a
+	// stream, no memory) on first use
+	if (!stream)
+		if (int rc = moe::ensure_library())
+			return rc;
 	if (!g_scratch_dev[dev]) {
 		// set-up, once per device, with that device current
 		uint8_t *ptr = nullptr;
@@ -146,8 +163,8 @@ extern "C" MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t
 	noalloc_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(w, x, m, (int)cols,
 							      qtype == MOE_Q4_0, meta,
 							      mma ? x16 : nullptr);
-	if (cudaGetLastError() != cudaSuccess)
-		return MOE_ERR_CUDA;
+	if (cudaError_t e = cudaGetLastError())
+		return cuda_error(e, "prep launch");
 	if (mma) {
 		moe::MmaArgs a{};
 		a.w1 = reinterpret_cast<const void *const *>(&meta->w);
@@ -169,7 +186,9 @@ extern "C" MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t
 		a.active = meta->active;
 		a.n_active = meta->n_active;
 		a.work = meta->work;
-		return moe::launch_expert_mma(a, st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+		if (cudaError_t e = moe::launch_expert_mma(a, st))
+			return cuda_error(e, "tensor-core GEMV launch");
+		return MOE_OK;
 	}
 	moe::GemvArgs a{};
 	a.w1 = reinterpret_cast<const void *const *>(&meta->w);
@@ -187,5 +206,33 @@ extern "C" MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t
 	a.in = x;
 	a.out = y;
 	a.dual = 0;
-	return moe::launch_expert_gemv(a, st) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+	if (cudaError_t e = moe::launch_expert_gemv(a, st))
+		return cuda_error(e, "GEMV launch");
+	return MOE_OK;
 }
+
+namespace moe {
+// moe_sync's check of the sticky error flag of this device's noalloc
+// scratch (after the stream is idle): MOE_ERR_TIMEOUT once per expired wait
+int noalloc_take_error()
+{
+	int dev = 0;
+	if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || !g_scratch_dev[dev])
+		return MOE_OK;
+	NoallocMeta *meta = reinterpret_cast<NoallocMeta *>(g_scratch_dev[dev]);
+	int32_t err = 0;
+	cudaError_t e = cudaMemcpy(&err, meta->err, 4, cudaMemcpyDeviceToHost);
+	if (e != cudaSuccess)
+		return cuda_error(e, "reading the error flag");
+	if (!err)
+		return MOE_OK;
+	e = cudaMemset(meta->err, 0, 4);
+	if (e == cudaSuccess)
+		e = cudaDeviceSynchronize();
+	if (e != cudaSuccess)
+		return cuda_error(e, "clearing the error flag");
+	set_last_error("moe_gemv_device_noalloc: a bounded wait of the tensor-core GEMV expired "
+		       "(the output of that call is not valid)");
+	return MOE_ERR_TIMEOUT;
+}
+}  // namespace moe

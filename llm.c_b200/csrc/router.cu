@@ -258,10 +258,8 @@ dispatch_kernel(const int32_t *__restrict__ ids, int npairs, int NE, int first, 
 		int32_t *__restrict__ err, int32_t *__restrict__ work)
 {
 	extern __shared__ int32_t ds[];
-	if (threadIdx.x == 0) {
-		*err = 0;
+	if (threadIdx.x == 0)
 		work[0] = work[1] = 0;
-	}
 	dispatch_body(ids, npairs, NE, first, nlocal, counts, offsets, perm, pos_of, active,
 		      n_active, err, ds);
 }
@@ -284,10 +282,8 @@ route_small_kernel(const float *__restrict__ logits, const float *__restrict__ b
 	float *sel = rs;                                     // [32][2K]
 	int32_t *ids_s = reinterpret_cast<int32_t *>(sel + 64 * K);  // [T*K]
 	int32_t *ds = ids_s + T * K;
-	if (threadIdx.x == 0) {
-		*err = 0;
+	if (threadIdx.x == 0)
 		work[0] = work[1] = 0;
-	}
 	for (int t = warp; t < T; t += 32) {
 		float *sw = sel + warp * 2 * K;
 		topk_token<LANES>(logits + (int64_t)t * NE, bias, NE, K, mode_exact, renorm,

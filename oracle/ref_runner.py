@@ -64,7 +64,7 @@ def main():
                 t0 = time.perf_counter()
                 L.ref_moe_ffn(*args)
                 ts.append(time.perf_counter() - t0)
-            out = dict(seconds=np.array(ts), out=o)
+            out = dict(seconds=np.array(ts), out=o, ids=ids, w=w)
     elif op == "gemm":
         a = np.ascontiguousarray(z["a"], np.float32)
         b = np.ascontiguousarray(z["b"])
