@@ -398,9 +398,10 @@ def run_ours(args, rank, world, local_rank):
         prefill = run_prefill(moe, torch, args, layers, rank, world, d, F, NE, K, stream,
                               torch_stream, dist)
 
-    gemv1 = None
+    gemv1, dense = None, None
     if world == 1 and not args.no_gemv:
         gemv1 = run_config1_gemv(moe, stream, torch_stream)
+        dense = run_dense_gemm(moe, stream, torch_stream)
 
     cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -458,6 +459,7 @@ def run_ours(args, rank, world, local_rank):
         "replicated_tokens": replicated,
         "prefill": prefill,
         "config1_gemv": gemv1,
+        "dense_gemm": dense,
         "sweeps": sweeps,
     }
     if world > 1:
@@ -769,6 +771,52 @@ def run_config1_gemv(moe, stream, torch_stream, copies=8, reps=48):
             "timing": f"CUDA events around {reps * copies} back-to-back eager calls over {copies} "
                       "distinct weight matrices (264 MB > L2), enqueued behind a spin kernel; "
                       "_graph: the same calls replayed from a CUDA graph"}
+
+
+def run_dense_gemm(moe, stream, torch_stream, m=512, reps=20):
+    """The dense quantized projections of a prefill through moe_gemv_device
+    with m = 512 activation rows (the tcgen05 GEMM with the matrix as one
+    expert): config 2's lm_head (50304 x 2048 Q8_0) and an attention
+    projection (2048 x 2048 Q8_0); seeded N(0, 0.02) weights, N(0, 1) rows.
+    CUDA events around `reps` back-to-back calls; tensor roofline on the
+    useful FLOPs (2 m rows cols)."""
+    import torch
+    _, tc_peak, peak_kind = measured_peaks()
+    out = []
+    for name, rows, cols in (("lm_head", 50304, 2048), ("attn_proj", 2048, 2048)):
+        qt = moe.Q8_0
+        tmp = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+        moe.check(moe.lib().moe_synth_gauss(tmp.data_ptr(), 2, 7, 0, rows * cols, 0.02, stream))
+        w = torch.empty(rows * moe.row_bytes(qt, cols), dtype=torch.uint8, device="cuda")
+        moe.check(moe.lib().moe_quantize_device(tmp.data_ptr(), rows, cols, qt, w.data_ptr(),
+                                                stream))
+        del tmp
+        x = torch.empty(m * cols, dtype=torch.float32, device="cuda")
+        moe.check(moe.lib().moe_synth_gauss(x.data_ptr(), 2, 8, 0, m * cols, 1.0, stream))
+        y = torch.empty(m * rows, dtype=torch.float32, device="cuda")
+
+        def call():
+            moe.gemv_device(w.data_ptr(), qt, rows, cols, x.data_ptr(), m, y.data_ptr(), stream)
+
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(torch_stream)
+        for _ in range(reps):
+            call()
+        e1.record(torch_stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        tf = 2.0 * m * rows * cols / (ms / 1e3) / 1e12
+        out.append({"workload": f"{name}: {rows} x {cols} Q8_0, m = {m}", "ms": ms,
+                    "tflops_algorithmic": tf, "frac_of_tensor_peak": tf / tc_peak,
+                    "tflops_executed": 3 * tf, "peak_source": peak_kind + " bf16 (burst)",
+                    "weight_gbs": rows * moe.row_bytes(qt, cols) / (ms / 1e3) / 1e9,
+                    "launches_per_call": 2})
+        del w, x, y
+    return out
 
 
 def run_e2e(moe, args, layers, keep, T, d, F, NE, K, qtype, rank, dist):

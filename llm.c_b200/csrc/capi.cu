@@ -72,6 +72,7 @@ struct Ctx {
 	void *dev_io = nullptr;
 	size_t dev_io_bytes = 0;
 	int32_t *err_pin = nullptr;  // pinned word: a layer's error word read with the output
+	int32_t *gemv_err = nullptr; // device error word of the single-row GEMV (moe_sync reads it)
 	std::map<std::vector<uintptr_t>, moe_layer *> layers;
 	// moe_ffn_forward's repeat calls: (router, gate, up, down host bases,
 	// qtype, experts, d_ff, d_model, top-k) -> the layer in `layers`
@@ -244,6 +245,22 @@ int ensure_pinned(size_t bytes)
 	CK(cudaMallocHost(&g.pin, want));
 	g.pin_bytes = want;
 	return MOE_OK;
+}
+
+// the dense GEMV/GEMM error word (set by an expired bounded wait), read and
+// cleared with the device idle
+int take_gemv_error()
+{
+	if (!g.gemv_err)
+		return MOE_OK;
+	int32_t e = 0;
+	CK(cudaMemcpy(&e, g.gemv_err, 4, cudaMemcpyDeviceToHost));
+	if (!e)
+		return MOE_OK;
+	CK(cudaMemset(g.gemv_err, 0, 4));
+	CK(cudaDeviceSynchronize());
+	return fail(MOE_ERR_TIMEOUT, "moe_gemv_device: a bounded wait expired (the output of that "
+		    "call is not valid)");
 }
 
 int ensure_dev_io(size_t bytes)
@@ -480,8 +497,10 @@ int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int
 	}
 	// this rank's pairs in expert order as fp16 hi/lo: the send buffer
 	CK(moe::launch_gather_split(x, L->perm, P, D, K, L->x16p, st));
-	// every rank's per-expert counts
-	const size_t mi = (size_t)world * NE + NE + (NE + 1) + NE + 1;
+	// every rank's per-expert counts; local counts, offsets, active list,
+	// n_active;
+	// the segment table (up to NE segments of 3 int64)
+	const size_t mi = (size_t)world * NE + 3 * (size_t)NE + 4 + 6 * (size_t)NE + 4;
 	if (L->a2a.meta_ints < mi) {
 		CK(cudaStreamSynchronize(st));
 		cudaFree(L->a2a.meta);
@@ -498,8 +517,12 @@ int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int
 	CK_NCCL(nccl.all_gather(L->counts, allc_d, NE, ncclInt32, nccl.comm, st));
 	CK(cudaMemcpyAsync(allc, allc_d, (size_t)world * NE * 4, cudaMemcpyDeviceToHost, st));
 	CK(cudaStreamSynchronize(st));
-	// the plan: own segments (offsets of this rank's dispatch), and where
-	// rank q's pairs of local expert e land: expert-major, then by rank
+	// the plan.  Own pairs are expert-sorted, so the pairs for rank r are
+	// one contiguous range: one send per peer.  Rank q's pairs arrive as one
+	// contiguous range per source (source-major: by source, then by local
+	// expert), and a segment copy puts them expert-major (by local expert,
+	// then by source), the order the grouped GEMM reads.  The rows go back
+	// the same way reversed and land at the pairs' dispatch positions.
 	const int32_t *own = allc + (size_t)rank * NE;
 	std::vector<int64_t> o(NE + 1, 0);
 	for (int e = 0; e < NE; e++)
@@ -508,7 +531,7 @@ int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int
 	int32_t *nact = act + NE;
 	int64_t pl = 0;
 	int na = 0;
-	std::vector<int64_t> rpos((size_t)world * NE, 0);  // [q][e]
+	std::vector<int64_t> rpos((size_t)world * NE, 0);  // [q][e]: expert-major start
 	for (int e = 0; e < NE; e++) {
 		off_l[e] = (int32_t)pl;
 		int64_t c = 0;
@@ -526,9 +549,31 @@ int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int
 	*nact = na;
 	if (pl > INT32_MAX / 2)
 		return fail(MOE_ERR_INVALID, "token-sharded forward: %lld pairs for one rank", (long long)pl);
-	// receive-side buffers: tokens [pl][2][D], h [pl][2][F] (fp16), rows [pl][D]
+	// source-major starts and the segment table [nseg][3] = (source-major
+	// row, expert-major row, rows)
+	std::vector<int64_t> soff(world + 1, 0);
+	const size_t seg_at = ((size_t)(nact - allc) + 2) & ~(size_t)1;  // even: 8-byte aligned
+	int64_t *seg = reinterpret_cast<int64_t *>(allc + seg_at);
+	int nseg = 0;
+	for (int q = 0; q < world; q++) {
+		int64_t c = soff[q];
+		for (int e = f0; e < f0 + n0; e++) {
+			const int32_t n = allc[(size_t)q * NE + e];
+			if (n) {
+				seg[3 * nseg] = c;
+				seg[3 * nseg + 1] = rpos[(size_t)q * NE + e];
+				seg[3 * nseg + 2] = n;
+				nseg++;
+			}
+			c += n;
+		}
+		soff[q + 1] = c;
+	}
+	// receive-side buffers: tokens source-major and expert-major [pl][2][D],
+	// h [pl][2][F] (fp16), rows expert-major and source-major [pl][D]
 	const size_t bx = align_up((size_t)pl * 2 * D * 2, 256), bh = align_up((size_t)pl * 2 * F * 2, 256);
-	const size_t need = bx + bh + (size_t)pl * D * 4 + 256;
+	const size_t by = align_up((size_t)pl * D * 4, 256);
+	const size_t need = 2 * bx + bh + 2 * by + 256;
 	if (need > L->a2a.bytes) {
 		cudaFree(L->a2a.buf);
 		L->a2a.buf = nullptr;
@@ -536,35 +581,36 @@ int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int
 		CK(cudaMalloc(&L->a2a.buf, need));
 		L->a2a.bytes = need;
 	}
-	__half *xr = (__half *)L->a2a.buf, *hr = (__half *)((char *)L->a2a.buf + bx);
-	float *yr = (float *)((char *)L->a2a.buf + bx + bh);
+	char *ab = (char *)L->a2a.buf;
+	__half *xs = (__half *)ab, *xr = (__half *)(ab + bx), *hr = (__half *)(ab + 2 * bx);
+	float *yr = (float *)(ab + 2 * bx + bh), *ys = (float *)(ab + 2 * bx + bh + by);
 	const size_t meta_loc = (size_t)world * NE;
-	CK(cudaMemcpyAsync(allc_d + meta_loc, cnt_l, (mi - meta_loc) * 4, cudaMemcpyHostToDevice, st));
+	const size_t meta_bytes = (size_t)((char *)(seg + 3 * nseg) - (char *)cnt_l);
+	CK(cudaMemcpyAsync(allc_d + meta_loc, cnt_l, meta_bytes, cudaMemcpyHostToDevice, st));
+	const int64_t *seg_d = reinterpret_cast<const int64_t *>(
+		allc_d + meta_loc + ((int32_t *)seg - cnt_l));
 	const size_t xrow = (size_t)2 * D;  // halves per token row
+	int fr, nr;
 	// [2] token rows to the experts' ranks (own experts: a device copy)
 	CK(record(2));
-	for (int e = f0; e < f0 + n0; e++)
-		if (own[e])
-			CK(cudaMemcpyAsync(xr + rpos[(size_t)rank * NE + e] * xrow, L->x16p + o[e] * xrow,
-					   (size_t)own[e] * xrow * 2, cudaMemcpyDeviceToDevice, st));
+	if (soff[rank + 1] > soff[rank])
+		CK(cudaMemcpyAsync(xs + soff[rank] * xrow, L->x16p + o[f0] * xrow,
+				   (size_t)(soff[rank + 1] - soff[rank]) * xrow * 2,
+				   cudaMemcpyDeviceToDevice, st));
 	CK_NCCL(nccl.group_start());
 	for (int r = 0; r < world; r++) {
 		if (r == rank)
 			continue;
-		int fr, nr;
 		range(r, fr, nr);
-		for (int e = fr; e < fr + nr; e++)
-			if (own[e])
-				CK_NCCL(nccl.send(L->x16p + o[e] * xrow, (size_t)own[e] * xrow, ncclFloat16, r,
-						  nccl.comm, st));
-		for (int e = f0; e < f0 + n0; e++) {
-			const int32_t c = allc[(size_t)r * NE + e];
-			if (c)
-				CK_NCCL(nccl.recv(xr + rpos[(size_t)r * NE + e] * xrow, (size_t)c * xrow,
-						  ncclFloat16, r, nccl.comm, st));
-		}
+		if (o[fr + nr] > o[fr])
+			CK_NCCL(nccl.send(L->x16p + o[fr] * xrow, (size_t)(o[fr + nr] - o[fr]) * xrow,
+					  ncclFloat16, r, nccl.comm, st));
+		if (soff[r + 1] > soff[r])
+			CK_NCCL(nccl.recv(xs + soff[r] * xrow, (size_t)(soff[r + 1] - soff[r]) * xrow,
+					  ncclFloat16, r, nccl.comm, st));
 	}
 	CK_NCCL(nccl.group_end());
+	CK(moe::launch_copy_segments(xs, xr, seg_d, nseg, 0, (int64_t)xrow * 2, st));
 	// [3] the grouped GEMMs over the received pairs
 	const size_t mb = moe::weight_map_bytes();
 	moe::GemmArgs gu{};
@@ -598,26 +644,22 @@ int forward_sharded_a2a(moe_layer *L, const float *x, float *out, int64_t T, int
 	CK(moe::launch_expert_gemm(dn, pl, st));
 	CK(record(4));
 	// [4] the rows back to the tokens' ranks, at the pairs' dispatch positions
-	for (int e = f0; e < f0 + n0; e++)
-		if (own[e])
-			CK(cudaMemcpyAsync(L->Y + o[e] * D, yr + rpos[(size_t)rank * NE + e] * D,
-					   (size_t)own[e] * D * 4, cudaMemcpyDeviceToDevice, st));
+	CK(moe::launch_copy_segments(yr, ys, seg_d, nseg, 1, (int64_t)D * 4, st));
+	if (soff[rank + 1] > soff[rank])
+		CK(cudaMemcpyAsync(L->Y + o[f0] * D, ys + soff[rank] * D,
+				   (size_t)(soff[rank + 1] - soff[rank]) * D * 4, cudaMemcpyDeviceToDevice,
+				   st));
 	CK_NCCL(nccl.group_start());
 	for (int r = 0; r < world; r++) {
 		if (r == rank)
 			continue;
-		int fr, nr;
 		range(r, fr, nr);
-		for (int e = f0; e < f0 + n0; e++) {
-			const int32_t c = allc[(size_t)r * NE + e];
-			if (c)
-				CK_NCCL(nccl.send(yr + rpos[(size_t)r * NE + e] * D, (size_t)c * D, ncclFloat32,
-						  r, nccl.comm, st));
-		}
-		for (int e = fr; e < fr + nr; e++)
-			if (own[e])
-				CK_NCCL(nccl.recv(L->Y + o[e] * D, (size_t)own[e] * D, ncclFloat32, r,
-						  nccl.comm, st));
+		if (soff[r + 1] > soff[r])
+			CK_NCCL(nccl.send(ys + soff[r] * D, (size_t)(soff[r + 1] - soff[r]) * D, ncclFloat32,
+					  r, nccl.comm, st));
+		if (o[fr + nr] > o[fr])
+			CK_NCCL(nccl.recv(L->Y + o[fr] * D, (size_t)(o[fr + nr] - o[fr]) * D, ncclFloat32, r,
+					  nccl.comm, st));
 	}
 	CK_NCCL(nccl.group_end());
 	CK(moe::launch_combine_pos(L->Y, L->pos_of, L->wts, (int)T, K, D, out, st));
@@ -668,6 +710,8 @@ int moe_shutdown(void)
 	if (g.err_pin)
 		cudaFreeHost(g.err_pin);
 	g.err_pin = nullptr;
+	cudaFree(g.gemv_err);
+	g.gemv_err = nullptr;
 	if (g.dev_io)
 		cudaFree(g.dev_io);
 	g.pin = g.dev_io = nullptr;
@@ -733,6 +777,8 @@ int moe_sync(void)
 	if (!g.init)
 		return fail(MOE_ERR_NOT_INIT, "moe_sync: not initialised");
 	CK(cudaStreamSynchronize(g.stream));
+	if (int rc = take_gemv_error())
+		return rc;
 	return moe::noalloc_take_error();
 }
 
@@ -1061,6 +1107,9 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		a.idg = L->d_idg;
 		a.launches = ep_ready ? reinterpret_cast<unsigned long long *>(L->xbuf + L->xl.launches)
 				      : nullptr;
+		a.shard_launches = ep_ready ? reinterpret_cast<unsigned long long *>(
+						      L->xbuf + L->xl.shard_launches)
+					    : nullptr;
 		a.ep_wait_ns = L->ep_wait_ns;
 		CK(moe::launch_decode_layer(a, d.qtype, lanes, st));
 		L->last_pairs = world_pairs;
@@ -1431,15 +1480,22 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 	if (m == 0)
 		return MOE_OK;
 	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
-	// one activation row (decode): the memory-bound GEMV, no scratch
+	if (!g.gemv_err) {
+		CK(cudaMalloc(&g.gemv_err, 4));
+		CK(cudaMemset(g.gemv_err, 0, 4));
+	}
+	// one activation row (decode): the memory-bound GEMV, no scratch; every
+	// path's bounded waits report to the library's GEMV error word (moe_sync)
 	if (m == 1 && moe::gemv1_supported(qtype, rows, cols, (uintptr_t)w, (uintptr_t)x, (uintptr_t)y)) {
-		CK(moe::launch_gemv1(w, qtype, rows, cols, x, y, st));
+		CK(moe::launch_gemv1(w, qtype, rows, cols, x, y, g.gemv_err, st));
 		return MOE_OK;
 	}
 	// one "expert" holding all m rows of x: counts = {m}, offsets = {0, m}.
-	// The metadata and the fp16 split of x live in a per-thread device
-	// buffer, so calls from one thread must be ordered on one stream.
+	// The metadata (and the GEMM's weight tensor map) and the fp16 split of
+	// x live in per-thread device buffers, so calls from one thread must be
+	// ordered on one stream.
 	struct Meta {
+		alignas(64) uint8_t map[128];  // prefill GEMM: the weight matrix's tensor map
 		const void *w;
 		int32_t counts[1], offsets[2], err[1], active[1], n_active[1], work[1];
 	};
@@ -1448,20 +1504,58 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 	static thread_local size_t x16_bytes = 0;
 	if (!dmeta)
 		CK(cudaMalloc(&dmeta, sizeof(Meta)));
-	Meta h{w, {(int32_t)m}, {0, (int32_t)m}, {0}, {0}, {1}, {0}};
+	auto ensure_x16 = [&](size_t need) -> int {
+		if (need <= x16_bytes)
+			return MOE_OK;
+		CK(cudaStreamSynchronize(st));
+		if (x16)
+			cudaFree(x16);
+		x16 = nullptr;
+		x16_bytes = 0;
+		CK(cudaMalloc(&x16, need));
+		x16_bytes = need;
+		return MOE_OK;
+	};
+	Meta h{};
+	h.w = w;
+	h.counts[0] = (int32_t)m;
+	h.offsets[1] = (int32_t)m;
+	h.n_active[0] = 1;
+	// prefill-sized batches (dense projections, lm_head): the tcgen05 GEMM
+	// of the expert layers with one expert; its weight tensor map views the
+	// GGUF rows where they are
+	if (m > moe::decode_max_t() && m <= INT32_MAX / 2 &&
+	    moe::expert_gemm_supported(qtype, (int)rows, (int)cols, 0) && (uintptr_t)w % 16 == 0 &&
+	    (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0 &&
+	    moe::encode_weight_map(h.map, w, qtype, (int)rows, (int)cols)) {
+		CK(cudaMemcpyAsync(dmeta, &h, sizeof(Meta), cudaMemcpyHostToDevice, st));
+		if (int rc = ensure_x16((size_t)m * 2 * cols * sizeof(__half)))
+			return rc;
+		CK(moe::launch_gather_split(x, nullptr, m, (int)cols, 1, x16, st));
+		moe::GemmArgs a{};
+		a.maps1 = dmeta->map;
+		a.qtype = qtype;
+		a.rows = (int)rows;
+		a.cols = (int)cols;
+		a.n_local = 1;
+		a.counts = dmeta->counts;
+		a.offsets = dmeta->offsets;
+		a.perm = nullptr;
+		a.active = dmeta->active;
+		a.n_active = dmeta->n_active;
+		a.out_perm = 0;
+		a.in16 = x16;
+		a.out = y;
+		a.dual = 0;
+		a.err = g.gemv_err;
+		CK(moe::launch_expert_gemm(a, m, st));
+		return MOE_OK;
+	}
 	CK(cudaMemcpyAsync(dmeta, &h, sizeof(Meta), cudaMemcpyHostToDevice, st));
 	const bool mma = moe::expert_mma_supported(qtype, (int)cols) && (uintptr_t)w % 16 == 0;
 	if (mma) {
-		const size_t need = (size_t)m * 2 * cols * sizeof(__half);
-		if (need > x16_bytes) {
-			CK(cudaStreamSynchronize(st));
-			if (x16)
-				cudaFree(x16);
-			x16 = nullptr;
-			x16_bytes = 0;
-			CK(cudaMalloc(&x16, need));
-			x16_bytes = need;
-		}
+		if (int rc = ensure_x16((size_t)m * 2 * cols * sizeof(__half)))
+			return rc;
 		CK(moe::launch_split_f16(x, m, (int)cols, qtype, x16, st));
 		moe::MmaArgs a{};
 		a.w1 = reinterpret_cast<const void *const *>(&dmeta->w);
@@ -1479,7 +1573,7 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 		a.in16 = x16;
 		a.out = y;
 		a.dual = 0;
-		a.err = dmeta->err;
+		a.err = g.gemv_err;
 		a.active = dmeta->active;
 		a.n_active = dmeta->n_active;
 		a.work = dmeta->work;
@@ -1564,6 +1658,8 @@ int moe_tensor_mma_transposed_2x2_status(moe_tensor_t *ret, const moe_tensor_t *
 		CK(moe::launch_add_bias(dy, dadd, m * n, (int64_t)add->totlen, g.stream));
 	CK(cudaMemcpyAsync(g.pin, dy, m * n * 4, cudaMemcpyDeviceToHost, g.stream));
 	CK(cudaStreamSynchronize(g.stream));
+	if (int rc = take_gemv_error())
+		return rc;
 	memcpy(ret->data, g.pin, m * n * 4);
 	return MOE_OK;
 }

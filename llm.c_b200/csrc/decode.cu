@@ -301,6 +301,9 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	const bool ep = a.world > 1;
 	const bool shard = ep && a.shard;
 	const unsigned long long epoch = ep ? *reinterpret_cast<volatile unsigned long long *>(a.launches) + 1 : 0;
+	// the routing arrivals count token-sharded launches only
+	const unsigned long long shard_epoch =
+		shard ? *reinterpret_cast<volatile unsigned long long *>(a.shard_launches) + 1 : 0;
 	const int64_t half_off = (int64_t)(epoch & 1) * a.ybuf_half;
 	float *Y = ep ? a.ybuf[a.rank] + half_off : a.Y;
 	// peer tables (smem): the other ranks' Y halves (replicated tokens),
@@ -415,8 +418,8 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				for (int r = 0; r < a.world; r++)
 					red_add_release_sys(a.routed[r] + kEpFlagStride * a.rank, 1ull);
 			if (tid < a.world)
-				wait_arrivals(a.routed[a.rank] + kEpFlagStride * tid, epoch * gridDim.x, ep_wait,
-					      a.err);
+				wait_arrivals(a.routed[a.rank] + kEpFlagStride * tid, shard_epoch * gridDim.x,
+					      ep_wait, a.err);
 		} else if (tid == 0) {
 			grid_sync(a.gbar, a.err);
 		}
@@ -568,8 +571,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		}
 	}
 	stamp(a.stamps, kStEnd);
-	if (ep && blockIdx.x == 0 && tid == 0)
-		*a.launches = epoch;  // every CTA read it before arriving above
+	if (ep && blockIdx.x == 0 && tid == 0) {
+		*a.launches = epoch;  // every CTA read them before arriving above
+		if (shard)
+			*a.shard_launches = shard_epoch;
+	}
 }
 
 // ---------------------------------------------------------------- launch

@@ -339,8 +339,10 @@ expert_gemm_kernel(GemmArgs a, const __grid_constant__ CUtensorMap xmap)
 	__syncthreads();
 	const int rows = a.rows, cols = a.cols;
 	const int nslice = cols / kGKS;
-	// DUAL: 128 gate rows + the same up rows; single: 256 rows
-	const int rblocks = rows / (DUAL ? kGH : kGR);
+	// DUAL: 128 gate rows + the same up rows; single: 256 rows (a last
+	// block of 128: the weight map reads zeros past the matrix and the
+	// epilogue stores only the rows that exist)
+	const int rblocks = DUAL ? rows / kGH : (rows + kGR - 1) / kGR;
 	if (warp == 0) {
 		// routing tables and the item prefix (32 experts per shuffle scan)
 		int acc = 0;
@@ -532,7 +534,8 @@ expert_gemm_kernel(GemmArgs a, const __grid_constant__ CUtensorMap xmap)
 			} else {
 				const int orow = valid ? (a.out_perm ? a.perm[pos] : pos) : 0;
 				float *o = a.out + (int64_t)orow * rows + w.rb * kGR;
-				for (int c0 = 0; c0 < kGR; c0 += 16) {
+				const int ncols = min(kGR, rows - w.rb * kGR);  // warp-uniform
+				for (int c0 = 0; c0 < ncols; c0 += 16) {
 					float y[16];
 					tmem_ld16(tq + c0, y);
 					if (failed || !valid)
@@ -605,8 +608,9 @@ cudaError_t launch_gemm_t(const GemmArgs &a, int64_t in_rows, cudaStream_t st)
 
 bool expert_gemm_supported(int qtype, int rows, int cols, int dual)
 {
-	// cols % 256: rows of 16-byte multiples for the weight tensor maps
-	return (qtype == kQ8_0 || qtype == kQ4_0) && rows % (dual ? kGH : kGR) == 0 && cols % 256 == 0 &&
+	// cols % 256: rows of 16-byte multiples for the weight tensor maps;
+	// rows % 128 (single: a last item of 128 rows is masked)
+	return (qtype == kQ8_0 || qtype == kQ4_0) && rows % kGH == 0 && cols % 256 == 0 &&
 	       encode_fn() != nullptr;
 }
 
@@ -656,7 +660,8 @@ __global__ void gather_split_kernel(const float *__restrict__ x, const int32_t *
 	     i += (int64_t)gridDim.x * blockDim.x) {
 		const int64_t pos = i / c4;
 		const int k = (int)(i - pos * c4);
-		const float4 v = reinterpret_cast<const float4 *>(x + (int64_t)(perm[pos] / K) * cols)[k];
+		const int64_t src = perm ? perm[pos] / K : pos;  // no perm: rows in order (dense GEMM)
+		const float4 v = reinterpret_cast<const float4 *>(x + src * cols)[k];
 		const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
 		const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
 		__half2 hi[2] = {h0, h1};

@@ -226,6 +226,34 @@ cudaError_t launch_combine_pos(const float *Y, const int32_t *pos_of, const floa
 	return cudaGetLastError();
 }
 
+// rows moved by segment (token-sharded all-to-all): seg[i] = (source-major
+// row, expert-major row, rows); dir 0 copies source-major -> expert-major,
+// dir 1 the reverse.  blockIdx.y = segment, 16-byte chunks.
+__global__ void copy_segments_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
+				     const int64_t *__restrict__ seg, int dir, int64_t row_bytes)
+{
+	const int i = blockIdx.y;
+	const int64_t from = seg[3 * i + (dir ? 1 : 0)], to = seg[3 * i + (dir ? 0 : 1)];
+	const int64_t chunks = seg[3 * i + 2] * row_bytes / 16;
+	const uint4 *s = reinterpret_cast<const uint4 *>(src + from * row_bytes);
+	uint4 *d = reinterpret_cast<uint4 *>(dst + to * row_bytes);
+	for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < chunks;
+	     c += (int64_t)gridDim.x * blockDim.x)
+		d[c] = s[c];
+}
+
+cudaError_t launch_copy_segments(const void *src, void *dst, const int64_t *seg, int nseg, int dir,
+				 int64_t row_bytes, cudaStream_t st)
+{
+	if (nseg <= 0)
+		return cudaSuccess;
+	if (row_bytes % 16 || (uintptr_t)src % 16 || (uintptr_t)dst % 16 || nseg > 65535)
+		return cudaErrorInvalidValue;
+	copy_segments_kernel<<<dim3(32, (unsigned)nseg), 256, 0, st>>>(
+		static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst), seg, dir, row_bytes);
+	return cudaGetLastError();
+}
+
 __global__ void add_bias_kernel(float *ret, const float *add, int64_t total, int64_t n_add)
 {
 	const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

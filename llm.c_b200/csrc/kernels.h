@@ -59,10 +59,12 @@ struct GemvArgs {
 cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st);
 
 // gemv.cu: y[rows] = W[rows, cols] . x[cols] for one activation row (see the
-// file); needs cols % 64 == 0 and 4-byte aligned W (16-byte aligned x)
+// file): the bulk-copy tensor-core kernel for cols % 256 == 0 and 16-byte
+// aligned W, else one warp per row (cols % 64 == 0, 4-byte aligned W);
+// 16-byte aligned x.  err (may be NULL) is set to 2 if a bounded wait expires.
 bool gemv1_supported(int qtype, int64_t rows, int64_t cols, uintptr_t w, uintptr_t x, uintptr_t y);
 cudaError_t launch_gemv1(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
-			 float *y, cudaStream_t st);
+			 float *y, int32_t *err, cudaStream_t st);
 
 // expert_mma.cu: tensor-core grouped expert GEMV (decode).  Same segment
 // semantics as GemvArgs; activations are fp16 hi/lo rows [row][2][cols]
@@ -134,6 +136,7 @@ struct DecodeArgs {
 	__half *const *xg;         // device [world]: gathered tokens [world*T][2][D] (shard)
 	int32_t *const *idg;       // device [world]: T of each rank [16], then ids [world*T*K]
 	unsigned long long *launches;        // this rank's count of expert-parallel launches
+	unsigned long long *shard_launches;  // ... of token-sharded ones (the routing arrivals)
 	uint64_t ep_wait_ns;       // limit of the cross-rank waits (0: the 2 s default)
 };
 constexpr int kMaxEpRanks = 8;
@@ -145,12 +148,12 @@ constexpr int kDecodeMaxPairs = 1024;     // this rank's (token, slot) pairs
 constexpr int kDecodeMaxPairsAll = 2048;  // every rank's pairs (token-sharded)
 // exchange buffer of one rank (one allocation, shared by CUDA IPC):
 //   Y halves      2 * y_half floats
-//   counters      inbound[kMaxEpRanks], routed[kMaxEpRanks], launches
-//                 (one 128-byte line each)
+//   counters      inbound[kMaxEpRanks], routed[kMaxEpRanks], launches,
+//                 token-sharded launches (one 128-byte line each)
 //   gathered ids  kEpIdsHeader + kMaxEpRanks * kDecodeMaxPairs int32
 //   gathered x    kMaxEpRanks * kDecodeMaxT rows of 2 * D halves
 struct EpLayout {
-	size_t inbound, routed, launches, idg, xg, bytes;
+	size_t inbound, routed, launches, shard_launches, idg, xg, bytes;
 };
 inline EpLayout ep_layout(int64_t y_half, int64_t D)
 {
@@ -160,7 +163,8 @@ inline EpLayout ep_layout(int64_t y_half, int64_t D)
 	l.inbound = (l.inbound + 255) / 256 * 256;
 	l.routed = l.inbound + kMaxEpRanks * line;
 	l.launches = l.routed + kMaxEpRanks * line;
-	l.idg = l.launches + line;
+	l.shard_launches = l.launches + line;
+	l.idg = l.shard_launches + line;
 	l.xg = l.idg + (size_t)(kEpIdsHeader + kMaxEpRanks * kDecodeMaxPairs) * 4;
 	l.xg = (l.xg + 255) / 256 * 256;
 	l.bytes = l.xg + (size_t)kMaxEpRanks * kDecodeMaxT * 2 * D * 2;
@@ -214,6 +218,11 @@ cudaError_t launch_combine(const float *Y, const float *w, int T, int K, int d, 
 // Y[pos_of[t*K + s]] (d % 4 == 0, Y and out 16-byte aligned)
 cudaError_t launch_combine_pos(const float *Y, const int32_t *pos_of, const float *w, int T, int K,
 			       int d, float *out, cudaStream_t st);
+
+// rows moved by segment: seg [nseg][3] = (source-major row, expert-major
+// row, rows) on the device; dir 0: source-major -> expert-major, 1: back
+cudaError_t launch_copy_segments(const void *src, void *dst, const int64_t *seg, int nseg, int dir,
+				 int64_t row_bytes, cudaStream_t st);
 
 // ret[i] = ret[i] + add[i % n_add]  (bias of tensor_mma_transposed_2x2)
 cudaError_t launch_add_bias(float *ret, const float *add, int64_t total, int64_t n_add,

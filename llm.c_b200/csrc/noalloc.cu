@@ -155,6 +155,14 @@ extern "C" MOE_API int moe_gemv_device_noalloc(const void *w, int qtype, int64_t
 	__half *x16 = reinterpret_cast<__half *>(base + kNoallocMeta);
 	// NULL = the library stream, as for moe_gemv_device
 	cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : moe::library_stream();
+	// one activation row: the single-row GEMV needs no scratch, only the
+	// error flag
+	if (m == 1 && moe::gemv1_supported(qtype, rows, cols, (uintptr_t)w, (uintptr_t)x,
+					   (uintptr_t)y)) {
+		if (cudaError_t e = moe::launch_gemv1(w, qtype, rows, cols, x, y, meta->err, st))
+			return cuda_error(e, "single-row GEMV launch");
+		return MOE_OK;
+	}
 	const bool mma = moe::expert_mma_supported(qtype, (int)cols) && (uintptr_t)w % 16 == 0;
 
 	int64_t blocks = (m * cols + 255) / 256;

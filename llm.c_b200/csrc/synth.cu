@@ -72,6 +72,36 @@ __device__ __forceinline__ uint16_t f16_trunc(float f)
 	return (uint16_t)(sign | ((uint32_t)e16 << 10) | (man >> 13));
 }
 
+// fp32 -> fp16 bits, round to nearest even (the rounding of the
+// reference's f32_to_f16, quant.c:46-60, and of F16C's _cvtss_sh), in
+// integer arithmetic: normal halves round the 13 dropped mantissa bits,
+// subnormal halves shift the full significand
+__device__ __forceinline__ uint16_t f16_rne(float f)
+{
+	const uint32_t x = __float_as_uint(f);
+	const uint32_t sign = (x >> 16) & 0x8000u;
+	const uint32_t ax = x & 0x7fffffffu;
+	if (ax > 0x7f800000u)
+		return (uint16_t)(sign | 0x7e00u | ((ax >> 13) & 0x3ffu));
+	if (ax >= 0x477ff000u)
+		return (uint16_t)(sign | 0x7c00u);
+	if (ax >= 0x38800000u) {
+		uint32_t r = ax - 0x38000000u;
+		r += 0x0fffu + ((r >> 13) & 1u);
+		return (uint16_t)(sign | (r >> 13));
+	}
+	const uint32_t e = ax >> 23;
+	if (e < 102)
+		return (uint16_t)sign;
+	const uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+	const uint32_t sh = 126 - e;
+	uint32_t q = m >> sh;
+	const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
+	if (rem > half || (rem == half && (q & 1u)))
+		q++;
+	return (uint16_t)(sign | q);
+}
+
 // one thread per 32-element block
 __global__ void quantize_kernel(const float *__restrict__ src, int64_t nblocks, int qtype,
 				uint8_t *__restrict__ dst)
@@ -89,7 +119,7 @@ __global__ void quantize_kernel(const float *__restrict__ src, int64_t nblocks, 
 			uint8_t *o = dst + b * Q8_0_BYTES;
 			const float d = __fdiv_rn(amax, 127.0f);
 			const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-			const uint16_t h = __half_as_ushort(__float2half_rn(d));
+			const uint16_t h = f16_rne(d);
 			o[0] = (uint8_t)(h & 0xff);
 			o[1] = (uint8_t)(h >> 8);
 			for (int j = 0; j < QK; j++)

@@ -149,3 +149,29 @@ def test_gemv_single_row_unaligned_weights(moe, orc, qt):
             b.free()
     assert float(np.abs(got - ref).max()) <= 1e-5
     assert rel_l2(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("qt,rows,cols,m", [(1, 2048, 2048, 512), (1, 384, 2048, 200),
+                                             (2, 256, 14336, 80), (2, 640, 4096, 65),
+                                             (1, 128, 1024, 300)])
+def test_dense_gemm_prefill_sizes(moe, orc, qt, rows, cols, m):
+    """more than 64 activation rows (prefill Q/K/V/O projections, lm_head):
+    the tcgen05 GEMM with the matrix as one expert; rows that end in a
+    128-row block (lm_head's 50304 = 393 x 128) are masked in the epilogue"""
+    w = orc.quantize(qt, orc.gauss(51, 7, rows * cols, 0.02).reshape(rows, cols))
+    x = orc.gauss(51, 8, m * cols, 1.0).reshape(m, cols)
+    ref = orc.gemm_q(x, w, qt, rows)
+    got = moe.gemv(w, qt, rows, cols, x)
+    assert got.shape == ref.shape
+    assert_output_close(got, ref)
+
+
+def test_dense_gemm_drop_in_with_bias(moe, orc):
+    """the tensor_mma_transposed_2x2 drop-in at prefill size (m = 96 > 64)"""
+    m, n, k = 96, 256, 2048
+    lhs = orc.gauss(52, 8, m * k, 1.0).reshape(m, k)
+    rhs = orc.quantize(1, orc.gauss(52, 7, n * k, 0.02).reshape(n, k))
+    add = orc.gauss(52, 9, n, 1.0)
+    got = moe.mma_transposed(lhs, rhs, 1, n, k, add=add)
+    ref = orc.gemm_q(lhs, rhs, 1, n) + add[None, :]
+    assert_output_close(got, ref)

@@ -56,6 +56,7 @@ def local_experts(moe, L, name, first, nl, keep):
 
 
 def _rank_main(rank, world, port, shape, token_counts, sharded, results):
+    """sharded: a bool for every forward, or a list with one per forward"""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -80,17 +81,18 @@ def _rank_main(rank, world, port, shape, token_counts, sharded, results):
         moe.connect_expert_parallel(lay, rank, gather)
         moe.init_expert_parallel_comm(rank, world, gather)
         outs, inputs = [], []
-        for T in token_counts:
-            if sharded:
+        modes = sharded if isinstance(sharded, list) else [sharded] * len(token_counts)
+        for T, shard in zip(token_counts, modes):
+            if shard:
                 x = orc.make_tokens(seed + T, world * T, d)[rank * T:(rank + 1) * T]
             else:
                 x = orc.make_tokens(seed + T, T, d)
             inputs.append(x)
             dist.barrier()
-            outs.append(lay.forward(x, flags=moe.EP_SHARDED if sharded else 0))
+            outs.append(lay.forward(x, flags=moe.EP_SHARDED if shard else 0))
         res = {"outs": outs}
         # this rank's own reference: one GPU with every expert, and the oracle
-        if sharded or rank == 0:
+        if any(modes) or rank == 0:
             full = moe.Layer(d, F, NE, K, qt, L["router_w"], L["gate"], L["up"], L["down"])
             res["single"] = [full.forward(x) for x in inputs]
             res["oracle"] = [orc.moe_ffn(L, x)[0] for x in inputs]
@@ -162,3 +164,25 @@ def test_token_sharded_matches_one_gpu(shape):
             else:
                 assert float(np.abs(got - single).max()) <= 1e-5, (T, r)
             assert_close(got, res[r]["oracle"][i], T)
+
+
+def test_replicated_and_token_sharded_forwards_mixed_on_one_layer():
+    """the two modes keep separate arrival counts: any order of them on one
+    layer stays in step across the ranks"""
+    shape = SHAPES[0]
+    token_counts = [7, 5, 3, 32, 4, 100, 9, 2]
+    modes = [False, True, False, True, True, True, False, True]
+    world, res = run_ranks(shape, token_counts, sharded=modes)
+    for i, (T, shard) in enumerate(zip(token_counts, modes)):
+        for r in range(world):
+            got = res[r]["outs"][i]
+            if shard:
+                single = res[r]["single"][i]
+            else:
+                np.testing.assert_array_equal(got, res[0]["outs"][i])
+                single = res[0]["single"][i]
+            if T <= 64:
+                np.testing.assert_array_equal(got, single)
+            else:
+                assert float(np.abs(got - single).max()) <= 1e-5, (T, r)
+            assert_close(got, res[r]["oracle"][i] if shard else res[0]["oracle"][i], T)

@@ -52,8 +52,9 @@ def test_quantize_device_matches_oracle(moe, orc, qt, rows, cols):
     moe.check(moe.lib().moe_quantize_device(dx.ptr, rows, cols, qt, dq.ptr, None))
     moe.check(moe.lib().moe_sync())
     got = dq.to_numpy(np.uint8, (rows, moe.row_bytes(qt, cols)))
-    ref = orc.quantize(qt, x)
-    np.testing.assert_array_equal(got, ref.reshape(rows, -1))
+    ref = orc.quantize(qt, x).reshape(rows, -1)
+    bad = np.argwhere(got != ref)
+    assert bad.size == 0, [(tuple(i), int(got[tuple(i)]), int(ref[tuple(i)])) for i in bad[:8]]
 
 
 def test_bench_layer_bytes_match_oracle_layer(moe, orc):
