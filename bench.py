@@ -1081,6 +1081,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check at N > 1")
     ap.add_argument("--no-replicated", action="store_true",
                     help="skip the replicated-token leg at N > 1")
+    ap.add_argument("--only", choices=["gemv", "dense"],
+                    help="run one leg alone on one GPU (for profilers) and print its result")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     args.steps = max(args.steps, 1)
@@ -1089,6 +1091,11 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.only:
+        torch, moe, _, torch_stream = init_rank(1, local_rank)
+        leg = run_config1_gemv if args.only == "gemv" else run_dense_gemm
+        print(json.dumps({"only": args.only,
+                          "result": leg(moe, torch_stream.cuda_stream, torch_stream)}), flush=True)
     else:
         run_ours(args, rank, world, local_rank)
 

@@ -324,7 +324,6 @@ struct moe_layer {
 	__half *x16, *h16, *x16p;  // tokens hi/lo (token order), h hi/lo, tokens hi/lo (pair order)
 	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
 	int32_t *active, *n_active, *work;  // [NE], [1], [2]
-	int32_t *ready;                     // [256] per-expert pass counters of the fused kernel
 	unsigned long long *gbar;           // grid barrier arrivals of the fused kernel
 	uint64_t *stamps;                   // [kStampRecords][grid][stamps]
 	// expert parallelism (n_local < n_experts): exchange buffer of this rank
@@ -372,7 +371,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	const int64_t pcap = std::max<int64_t>(cap * K, L->xbuf ? moe::kDecodeMaxPairsAll : 0);
 	size_t o_counts = take(NE * 4), o_offsets = take((NE + 1) * 4), o_perm = take(pcap * 4);
 	size_t o_pos = take(cap * K * 4), o_err = take(4);
-	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8), o_ready = take(256 * 4);
+	size_t o_active = take(NE * 4), o_nact = take(4), o_work = take(8);
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
 	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)pcap * 2 * F * 2);
 	size_t o_x16p = take((size_t)cap * K * 2 * D * 2);
@@ -399,7 +398,6 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->active = (int32_t *)(b + o_active);
 	L->n_active = (int32_t *)(b + o_nact);
 	L->work = (int32_t *)(b + o_work);
-	L->ready = (int32_t *)(b + o_ready);
 	L->h = (float *)(b + o_h);
 	L->Y = (float *)(b + o_Y);
 	L->x16 = (__half *)(b + o_x16);
@@ -1095,7 +1093,6 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		a.n_active = L->n_active;
 		a.err = L->err;
 		a.gbar = L->gbar;
-		a.ready = L->ready;
 		a.stamps = stamps;
 		a.first_expert = (int)d.first_expert;
 		a.n_local = (int)d.n_local;

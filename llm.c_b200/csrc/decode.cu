@@ -342,10 +342,6 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				  reinterpret_cast<int32_t *>(sel + K), dummy, reinterpret_cast<float *>(dummy + K),
 				  nullptr, nullptr);
 	}
-	// per-expert gate/up pass counters of this launch (read after barrier 1)
-	if (blockIdx.x == 0)
-		for (int i = tid; i < kMaxActive; i += blockDim.x)
-			a.ready[i] = 0;
 	router_tiles<LANES>(a, smem, rbar);
 	{
 		// the fp16 hi/lo split of x that the expert phases read, 8 columns
@@ -489,16 +485,13 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	{
 		const int n_active = *nact_s;
 		const Phase gu{a.dptrs, a.dptrs + NE, F, D, K, en, off, pre_gu, n_active, perm_s, 1, 0,
-			       shard ? a.xg[a.rank] : a.x16, a.h16, nullptr, a.err, nullptr, nullptr, 0, 0,
-			       a.ready, 0};
+			       shard ? a.xg[a.rank] : a.x16, a.h16, nullptr, a.err, nullptr, nullptr, 0, 0};
 		// down stores y per (token, slot) row: replicated tokens, here and
 		// into every other rank's exchange buffer; token-sharded, into the
 		// buffer of the rank that owns the token.  P4 divides by 1 / w and adds
-		// down reads an expert's h once all of that expert's gate/up passes
-		// are stored (per-expert counters instead of a grid barrier)
 		const Phase dn{a.dptrs + 2 * NE, nullptr, D, F, K, en, off, pre_dn, n_active, perm_s, 0, 1,
 			       a.h16, nullptr, Y, a.err, nullptr, shard ? yall : ypeers,
-			       (ep && !shard) ? a.world - 1 : 0, shard ? T * K : 0, a.ready, (F + 7) / 8};
+			       (ep && !shard) ? a.world - 1 : 0, shard ? T * K : 0};
 		Pipe pipe;
 		if (warp == kProducerWarp) {
 			core_producer<QT, true, STAGES, WB_GU>(gu, smem, b, pipe, lane);
@@ -511,8 +504,12 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				core_math<QT, true, STAGES, WB_GU, true, 1, true>(gu, smem, red, b, pipe, warp, lane);
 			else
 				core_math<QT, true, STAGES, WB_GU, true>(gu, smem, red, b, pipe, warp, lane);
-			// no grid barrier: each down item waits for its own expert's h
+			// every CTA's h rows must be written before any CTA reads them
+			bar_math_epi();
 			stamp(a.stamps, kStP2);
+			if (tid == 0)
+				grid_sync(a.gbar, a.err);
+			bar_math_epi();
 			stamp(a.stamps, kStB2);
 			if (warp >= kEpiWarp0)
 				core_epilogue<QT, false, MT_DN>(dn, red, stg + (warp - kEpiWarp0) * kEpiStage, b,

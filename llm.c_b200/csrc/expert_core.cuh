@@ -393,14 +393,6 @@ struct Phase {
 	// orow % shard_pairs (peers then holds every rank's buffer, own one
 	// included, and `out` is unused)
 	int shard_pairs;
-	// per-expert readiness instead of a grid barrier between two phases
-	// (device [experts] counters, zero at the start of the first phase):
-	// DUAL phases count each finished pass (item x token tile) of expert e
-	// in ready[e] once its rows are stored; a phase with ready_wait > 0
-	// reads expert e's inputs only after ready[e] reaches ready_wait x its
-	// token tiles (every pass of the phase before for that expert)
-	int32_t *ready;
-	int ready_wait;
 };
 
 struct Bars {
@@ -680,39 +672,8 @@ __device__ void core_epilogue(const Phase &ph, const float4 *red, float *stg, co
 			__syncwarp();
 			if (lane == 0)
 				mbar_arrive(&b.rempty[buf]);
-			if (DUAL && ph.ready) {
-				// this pass's rows are out: release them, then count the pass
-				__threadfence();
-				__syncwarp();
-				if (lane == 0)
-					atomicAdd(&ph.ready[ph.en[ai] & 255], 1);
-			}
 		}
 		seg = seg_end;
-	}
-}
-
-// bounded wait until ready[e] >= want (all lanes of a warp call it); an
-// expired wait records error 3 and returns
-__device__ __forceinline__ void wait_ready(const int32_t *ready, int want, int32_t *err,
-					   bool &failed)
-{
-	int v;
-	asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ready) : "memory");
-	if (v >= want)
-		return;
-	const uint64_t t0 = global_ns();
-	for (;;) {
-		__nanosleep(32);
-		asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ready) : "memory");
-		if (v >= want)
-			return;
-		if (global_ns() - t0 > kWaitLimitNs) {
-			failed = true;
-			if ((threadIdx.x & 31) == 0)
-				atomicExch(err, 3);
-			return;
-		}
 	}
 }
 
@@ -755,11 +716,6 @@ __device__ void core_math(const Phase &ph, const uint8_t *stages, float4 *red,
 			for (int ch = 0; ch < nch; ch++, p.it++) {
 				const int kb0 = ch * (KC / QK) + kq * WB;  // first block (row-global)
 				if (e != x_e || tg != x_tg || ch != x_ch) {
-					// the first read of expert e's inputs waits until the phase
-					// before has produced them (every lane polls: warp-uniform)
-					if (e != x_e && ph.ready_wait > 0 && !p.failed)
-						wait_ready(ph.ready + e, ph.ready_wait * ((n + kTokTile - 1) / kTokTile),
-							   ph.err, p.failed);
 					// token tg+g's activations for this warp's blocks; columns of
 					// tokens past n read the segment's first token (never stored)
 					const int t = tg + g < n ? tg + g : 0;

@@ -20,18 +20,19 @@
 //   stage: Q8_0 as s8, Q4_0 nibbles as u8) multiplies them with x held as
 //   three int8 digit planes per 32-element block: x = s (d1 + d2/254 +
 //   d3/254^2) with s = amax/127, the planes being the MMA's n columns.
-//   Each block's integer sums are exact; they become fp32 with the block's
-//   fp16 weight scale and the plane scales (and, for Q4_0, minus 8 times the
-//   plane's digit sum, the nibble bias).  The three planes carry x to ~2^-17
-//   of the block maximum, so the result is within ~1e-6 relative of the
-//   reference's fp32 arithmetic (dot_f32_q4_0 / dot_f32_q8_0, quant.c:103-155,
-//   which multiplies dequantized weights by fp32 x).  About 37 instructions
-//   per 16 rows x 32 codes instead of ~3 per code with fp32 FMAs, so the
-//   math of a tile takes a fraction of the time its copy does.
-// * The 8 math warps split each tile's blocks (K) eight ways; partial row
+//   Each block's integer sums are exact; they become fp32 through the plane
+//   scales and the block's fp16 weight scale (for Q4_0 a per-block constant
+//   removes the nibble bias: minus 8 times the planes' digit sums).  The
+//   three planes carry x to ~2^-17 of the block maximum, so the result is
+//   within ~1e-6 relative of the reference's fp32 arithmetic (dot_f32_q4_0 /
+//   dot_f32_q8_0, quant.c:103-155, which multiplies dequantized weights by
+//   fp32 x).  About 29 instructions per 16 rows x 32 codes (blocks taken in
+//   pairs, so every code word is one aligned load or a funnel shift of two),
+//   every shared-memory access an explicit 32-bit-addressed ld.shared.
+// * 16 math warps split each tile's blocks (K) sixteen ways; partial row
 //   sums meet in shared memory and are added in warp order.
-// * Every CTA splits x into digits itself (16 KB of x, from L2), while the
-//   first copies are in flight.
+// * Every CTA splits x into digits itself (16 KB of x, from L2, all of a
+//   warp's loads issued at once), while the first copies are in flight.
 //
 // gemv1_kernel (shapes the ring does not fit): one warp per weight row, lane
 // l reading blocks l, l + 32, ... with aligned 32-bit loads, codes made exact
@@ -45,22 +46,29 @@ namespace moe {
 namespace {
 
 // ---------------------------------------------------------------- gemv_tc
-constexpr int kTcMath = 8;                      // math warps
+constexpr int kTcMath = 16;                     // math warps
 constexpr int kTcThreads = (kTcMath + 1) * 32;  // + the copy warp
 constexpr int kTcRows = 16;                     // rows per tile (the MMA's M)
-constexpr int kTcPlanes = 3;                    // int8 digit planes of x
+constexpr int kTcPlanes = 3;                    // int8 digit planes of x (B columns 0..2)
 constexpr int kTcMaxStages = 4;
 constexpr size_t kTcSmemCap = 210 * 1024;
 
-// shared memory after the stage ring, per block of x: digits [3][32] int8,
-// plane scales [4] f32, plane digit sums [4] i32; then 32 zero bytes, the
-// partial sums [2][kTcMath][16] f32 and the mbarriers
-constexpr int kTcXd = kTcPlanes * 32, kTcPerBlock = kTcXd + 16 + 16;
-// bytes between rows in a stage (conflict-free fragment loads)
+// Shared memory after the stage ring, per block of x: the MMA B fragments
+// [4 t][8 g][8 bytes] (lane (g, t) reads its b0, b1 as one 8-byte word;
+// planes g >= 3 are zero) = 256 bytes, and the plane weights [4 t][4]
+// f32 = (weight, 0, nibble correction, 0) = 64 bytes; then the partial
+// sums [2][kTcMath][16] f32 and the mbarriers.  Lane quad t's C columns
+// (2t, 2t + 1) combine in integers as 254 c_2t + c_2t+1 (|.| < 2^27, exact)
+// and take one weight: s2 for planes 0-1, s3 / 254 for plane 2, 0 beyond.
+constexpr int kTcB = 256, kTcW = 64, kTcPerBlock = kTcB + kTcW;
+
+// bytes between rows in a stage: rows of 4096 (Q4_0) or 2048 (Q8_0) columns
+// are multiples of 128 bytes, so unpadded, the eight rows one fragment load
+// touches would all fall in the same shared-memory bank
 __host__ __device__ inline int64_t tc_row_stride(int64_t rb) { return rb + 16; }
 inline size_t tc_smem(int stages, int64_t tile_bytes, int nb)
 {
-	return (size_t)stages * tile_bytes + (size_t)nb * kTcPerBlock + 32 +
+	return (size_t)stages * tile_bytes + (size_t)nb * kTcPerBlock +
 	       2 * kTcMath * kTcRows * 4 + 2 * kTcMaxStages * 8;
 }
 
@@ -79,15 +87,67 @@ __device__ __forceinline__ void imma_16832(int32_t (&d)[4], const uint32_t (&a)[
 			     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-// 4 bytes at p, which lies 0 or 2 bytes past a 4-byte boundary
-__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t *p)
+// shared-memory loads by 32-bit shared address (every access to the stage
+// ring and the x fragments is an explicit ld.shared)
+__device__ __forceinline__ uint2 lds64(uint32_t a)
 {
-	const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-	const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-	return (a & 2) ? __funnelshift_r(w[0], w[1], 16) : w[0];
+	uint2 v;
+	asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+	return v;
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a)
+{
+	float4 v;
+	asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+		     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+		     : "r"(a));
+	return v;
 }
 
-template <int QT>
+constexpr int kTcMaxXb = 12;  // blocks of x per math warp (cols / 32 / kTcMath at most)
+
+// shared-memory loads at a register address plus a compile-time offset
+template <int OFF>
+__device__ __forceinline__ uint32_t lds32o(uint32_t a)
+{
+	uint32_t v;
+	asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+	return v;
+}
+template <int OFF>
+__device__ __forceinline__ float lds_half_o(uint32_t a)
+{
+	unsigned short h;
+	asm volatile("ld.shared.u16 %0, [%1+%2];" : "=h"(h) : "r"(a), "n"(OFF));
+	return __half2float(__ushort_as_half(h));
+}
+
+// A fragments of two adjacent blocks (the pair starting OFF bytes after a
+// 4-byte aligned row position; `a` = that position + 4t for lane quad t):
+// codes 4t..4t+3 (lo) and 16+4t..16+4t+3 (hi) of each block.  Q4_0 (2 x 18
+// bytes): byte j of a block holds code j (low nibble) and code j + 16 (high
+// nibble); the even block's code bytes start 2 bytes past a word, the odd
+// block's on one.  Q8_0 (2 x 34 bytes): int8 codes at the same offsets.
+template <int QT, int OFF>
+__device__ __forceinline__ void pair_codes(uint32_t a, uint32_t (&ev)[2], uint32_t (&od)[2])
+{
+	if (QT == kQ4_0) {
+		const uint32_t e = __funnelshift_r(lds32o<OFF>(a), lds32o<OFF + 4>(a), 16);
+		const uint32_t o = lds32o<OFF + 20>(a);
+		ev[0] = e & 0x0F0F0F0Fu;
+		ev[1] = (e >> 4) & 0x0F0F0F0Fu;
+		od[0] = o & 0x0F0F0F0Fu;
+		od[1] = (o >> 4) & 0x0F0F0F0Fu;
+	} else {
+		ev[0] = __funnelshift_r(lds32o<OFF>(a), lds32o<OFF + 4>(a), 16);
+		ev[1] = __funnelshift_r(lds32o<OFF + 16>(a), lds32o<OFF + 20>(a), 16);
+		od[0] = lds32o<OFF + 36>(a);
+		od[1] = lds32o<OFF + 52>(a);
+	}
+}
+
+// NBW: blocks of a row per math warp (cols / 32 / kTcMath, even)
+template <int QT, int NBW>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	       const float *__restrict__ x, float *__restrict__ y, int32_t *err)
@@ -98,11 +158,9 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	const int64_t rs = tc_row_stride(rb);         // row stride in a stage
 	const int64_t tile_bytes = kTcRows * rs;
 	uint8_t *ring = smem;
-	uint8_t *xd = smem + stages * tile_bytes;     // [nb][3][32] int8
-	float *pw = reinterpret_cast<float *>(xd + (size_t)nb * kTcXd);  // [nb][4]
-	int32_t *psum = reinterpret_cast<int32_t *>(pw + (size_t)nb * 4);  // [nb][4]
-	uint8_t *zero = reinterpret_cast<uint8_t *>(psum + (size_t)nb * 4);  // 32 bytes
-	float *red = reinterpret_cast<float *>(zero + 32);  // [2][kTcMath][16]
+	uint8_t *xfrag = smem + stages * tile_bytes;                 // [nb][kTcB]
+	uint8_t *xw = xfrag + (size_t)nb * kTcB;                      // [nb][kTcW]
+	float *red = reinterpret_cast<float *>(xw + (size_t)nb * kTcW);  // [2][kTcMath][16]
 	uint64_t *full = reinterpret_cast<uint64_t *>(red + 2 * kTcMath * kTcRows);
 	uint64_t *empty = full + kTcMaxStages;
 
@@ -117,8 +175,6 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		}
 		fence_mbar_init();
 	}
-	if (tid < 8)
-		reinterpret_cast<uint32_t *>(zero)[tid] = 0;
 	__syncthreads();
 
 	if (warp == kTcMath) {
@@ -157,55 +213,85 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		return;
 	}
 
-	// ---- math warps: x as three int8 digit planes per block (warp w takes
-	// blocks w, w + 8, ...; lane k = element k of the block)
-	for (int b = warp; b < nb; b += kTcMath) {
-		const float v = __ldg(x + (int64_t)b * 32 + lane);
-		const float amax = warp_max(fabsf(v));
-		const float s1 = amax / 127.0f, s2 = s1 / 254.0f, s3 = s2 / 254.0f;
-		int d1 = 0, d2 = 0, d3 = 0;
-		if (s1 > 0.0f) {
-			d1 = max(-127, min(127, __float2int_rn(v / s1)));
-			const float q1 = __fmaf_rn(-(float)d1, s1, v);
-			if (s2 > 0.0f) {
-				d2 = max(-127, min(127, __float2int_rn(q1 / s2)));
-				const float q2 = __fmaf_rn(-(float)d2, s2, q1);
-				if (s3 > 0.0f)
-					d3 = max(-127, min(127, __float2int_rn(q2 / s3)));
-			}
+	// ---- math warps.  x as three int8 digit planes per block: warp w takes
+	// blocks w, w + 16, ...; lane k = element k.  All of a warp's x loads are
+	// issued before the first is used.
+	{
+		float v[NBW];
+#pragma unroll
+		for (int j = 0; j < NBW; j++) {
+			const int b = warp + j * kTcMath;
+			v[j] = __ldg(x + (int64_t)b * 32 + lane);
 		}
-		int8_t *xb = reinterpret_cast<int8_t *>(xd + (size_t)b * kTcXd);
-		xb[lane] = (int8_t)d1;
-		xb[32 + lane] = (int8_t)d2;
-		xb[64 + lane] = (int8_t)d3;
-		const int t1 = __reduce_add_sync(0xffffffffu, d1);
-		const int t2 = __reduce_add_sync(0xffffffffu, d2);
-		const int t3 = __reduce_add_sync(0xffffffffu, d3);
-		if (lane == 0) {
-			pw[b * 4 + 0] = s1;
-			pw[b * 4 + 1] = s2;
-			pw[b * 4 + 2] = s3;
-			pw[b * 4 + 3] = 0.0f;
-			psum[b * 4 + 0] = t1;
-			psum[b * 4 + 1] = t2;
-			psum[b * 4 + 2] = t3;
-			psum[b * 4 + 3] = 0;
+		const int t_k = (lane & 15) >> 2, hi = lane >= 16 ? 4 : 0;
+#pragma unroll
+		for (int j = 0; j < NBW; j++) {
+			const int b = warp + j * kTcMath;   // < nb = kTcMath * NBW
+			const float amax = warp_max(fabsf(v[j]));
+			float s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+			int d1 = 0, d2 = 0, d3 = 0;
+			if (amax > 0.0f) {
+				// the digits only need s * d to track x: every residual is
+				// taken exactly (fma) against the same s, so products by
+				// rounded reciprocals serve instead of divisions
+				s1 = amax * (1.0f / 127.0f);
+				s2 = s1 * (1.0f / 254.0f);
+				s3 = s2 * (1.0f / 254.0f);
+				const float i1 = __frcp_rn(s1), i2 = i1 * 254.0f, i3 = i2 * 254.0f;
+				d1 = max(-127, min(127, __float2int_rn(v[j] * i1)));
+				const float q1 = __fmaf_rn(-(float)d1, s1, v[j]);
+				d2 = max(-127, min(127, __float2int_rn(q1 * i2)));
+				const float q2 = __fmaf_rn(-(float)d2, s2, q1);
+				d3 = (s3 > 0.0f) ? max(-127, min(127, __float2int_rn(q2 * i3))) : 0;
+			}
+			// B fragment bytes: [t][plane g][b0 (k = 4t..4t+3) | b1 (k = 16+4t..)]
+			int8_t *fb = reinterpret_cast<int8_t *>(xfrag + (size_t)b * kTcB);
+			const int o = t_k * 64 + hi + (lane & 3);
+			fb[o] = (int8_t)d1;
+			fb[o + 8] = (int8_t)d2;
+			fb[o + 16] = (int8_t)d3;
+			constexpr int kZ = 8 - kTcPlanes;  // unused B columns, zero
+			if (lane < 4 * kZ)
+				reinterpret_cast<uint2 *>(fb)[(lane / kZ) * 8 + kTcPlanes + lane % kZ] =
+					make_uint2(0, 0);
+			const int S1 = __reduce_add_sync(0xffffffffu, d1);
+			const int S2 = __reduce_add_sync(0xffffffffu, d2);
+			const int S3 = __reduce_add_sync(0xffffffffu, d3);
+			if (lane < 4) {
+				// (w_2t, w_2t+1, nibble correction, 0): the plane scales of this
+				// lane quad's C columns, and for t = 0 minus 8 x the planes'
+				// digit sums (Q4_0 codes are nib, their values nib - 8)
+				// The MMA's columns are the planes: lane quad 0 holds planes 0
+				// and 1, combined exactly in integers as 254 D0 + D1 with the
+				// weight s2 (= s1 / 254 to fp32 rounding); lane quad 1 holds
+				// plane 2 (and an empty column) as 254 D2 with weight s3 / 254.
+				const float corr = QT == kQ4_0
+							   ? -8.0f * ((float)S1 * s1 + (float)S2 * s2 + (float)S3 * s3)
+							   : 0.0f;
+				reinterpret_cast<float4 *>(xw + (size_t)b * kTcW)[lane] = make_float4(
+					lane == 0 ? s2 : (lane == 1 ? s3 / 254.0f : 0.0f), 0.0f,
+					lane == 0 ? corr : 0.0f, 0.0f);
+			}
 		}
 	}
 	asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
 
 	// MMA fragments: g = lane / 4 (rows g, g + 8; B column = digit plane g),
-	// t = lane % 4 (codes 4t..4t+3 and 16+4t..; C columns 2t, 2t + 1)
+	// t = lane % 4 (codes 4t..4t+3 and 16+4t..; C columns 2t, 2t + 1).  This
+	// warp's blocks [NBW*warp, +NBW): their B fragments and plane weights
+	// stay in registers for every tile.
 	const int g = lane >> 2, t = lane & 3;
-	// B: plane g < 3 of the block's digits, zeros for the unused columns
-	const uint8_t *xbase = g < kTcPlanes ? xd + g * 32 + 4 * t : zero;
-	const int xstride = g < kTcPlanes ? kTcXd : 0;
-	// the plane scales and digit sums of this lane's C columns (2t, 2t + 1;
-	// columns 3..7 are zero)
-	const float *pwb = t < 2 ? pw + 2 * t : reinterpret_cast<const float *>(zero);
-	const int32_t *psb = t < 2 ? psum + 2 * t : reinterpret_cast<const int32_t *>(zero);
-	const int pstride = t < 2 ? 4 : 0;
-	const int b_lo = warp * nb / kTcMath, b_hi = (warp + 1) * nb / kTcMath;
+	const int b0 = warp * NBW;
+	uint2 bfr[NBW];
+	float wx[NBW], wz[NBW];
+#pragma unroll
+	for (int j = 0; j < NBW; j++) {
+		bfr[j] = lds64(smem_addr(xfrag) + (uint32_t)((b0 + j) * kTcB + t * 64 + g * 8));
+		const float4 wv = lds128f(smem_addr(xw) + (uint32_t)((b0 + j) * kTcW + t * 16));
+		wx[j] = wv.x;
+		wz[j] = wv.z;
+	}
+	const uint32_t s_row = smem_addr(ring) + (uint32_t)(g * rs + b0 * BB);
 	bool failed = false;
 	for (int i = 0; i < ntiles; i++) {
 		const int slot = i % stages;
@@ -214,73 +300,56 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 			if (lane == 0 && err)
 				atomicExch(err, 2);
 		}
-		float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // (g, 2t) (g, 2t+1) (g+8, 2t) (g+8, 2t+1)
+		float acc_g = 0.0f, acc_g8 = 0.0f;
 		if (!failed) {
-			const uint8_t *rg = ring + slot * tile_bytes + (int64_t)g * rs;
-			const uint8_t *rg8 = rg + 8 * rs;
-#pragma unroll 4
-			for (int b = b_lo; b < b_hi; b++) {
-				const uint8_t *pg = rg + b * BB, *pg8 = rg8 + b * BB;
-				uint32_t a[4];
-				if (QT == kQ8_0) {
-					a[0] = lds_u32_a2(pg + 2 + 4 * t);
-					a[1] = lds_u32_a2(pg8 + 2 + 4 * t);
-					a[2] = lds_u32_a2(pg + 18 + 4 * t);
-					a[3] = lds_u32_a2(pg8 + 18 + 4 * t);
-				} else {
-					// byte j: code j in the low nibble, code j + 16 in the high
-					const uint32_t wg = lds_u32_a2(pg + 2 + 4 * t);
-					const uint32_t wg8 = lds_u32_a2(pg8 + 2 + 4 * t);
-					a[0] = wg & 0x0F0F0F0Fu;
-					a[1] = wg8 & 0x0F0F0F0Fu;
-					a[2] = (wg >> 4) & 0x0F0F0F0Fu;
-					a[3] = (wg8 >> 4) & 0x0F0F0F0Fu;
-				}
-				const uint8_t *xb = xbase + (size_t)b * xstride;
-				const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xb);
-				const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xb + 16);
-				int32_t dsum[4];
-				imma_16832(dsum, a, b0, b1, QT == kQ4_0);
-				if (QT == kQ4_0) {
-					// codes were nib, values are nib - 8
-					const int2 ps = *reinterpret_cast<const int2 *>(psb + (size_t)b * pstride);
-					dsum[0] -= 8 * ps.x;
-					dsum[1] -= 8 * ps.y;
-					dsum[2] -= 8 * ps.x;
-					dsum[3] -= 8 * ps.y;
-				}
-				const float2 sc = *reinterpret_cast<const float2 *>(pwb + (size_t)b * pstride);
-				const float dg = half_bits_to_float(*reinterpret_cast<const uint16_t *>(pg));
-				const float dg8 = half_bits_to_float(*reinterpret_cast<const uint16_t *>(pg8));
-				acc[0] = __fmaf_rn((float)dsum[0], dg * sc.x, acc[0]);
-				acc[1] = __fmaf_rn((float)dsum[1], dg * sc.y, acc[1]);
-				acc[2] = __fmaf_rn((float)dsum[2], dg8 * sc.x, acc[2]);
-				acc[3] = __fmaf_rn((float)dsum[3], dg8 * sc.y, acc[3]);
-			}
+			// rows g and g + 8 of this stage at this warp's first block
+			const uint32_t rg = s_row + (uint32_t)(slot * tile_bytes);
+			const uint32_t rg8 = rg + (uint32_t)(8 * rs);
+			static_for<NBW / 2>([&](auto J) {
+				constexpr int jp = decltype(J)::value;
+				constexpr int OFF = 2 * jp * BB;
+				uint32_t eg[2], og[2], eg8[2], og8[2];
+				pair_codes<QT, OFF>(rg + 4 * t, eg, og);
+				pair_codes<QT, OFF>(rg8 + 4 * t, eg8, og8);
+				const float dge = lds_half_o<OFF>(rg), dgo = lds_half_o<OFF + BB>(rg);
+				const float d8e = lds_half_o<OFF>(rg8), d8o = lds_half_o<OFF + BB>(rg8);
+				const uint32_t ae[4] = {eg[0], eg8[0], eg[1], eg8[1]};
+				const uint32_t ao[4] = {og[0], og8[0], og[1], og8[1]};
+				int32_t de[4], dd[4];
+				imma_16832(de, ae, bfr[2 * jp].x, bfr[2 * jp].y, QT == kQ4_0);
+				imma_16832(dd, ao, bfr[2 * jp + 1].x, bfr[2 * jp + 1].y, QT == kQ4_0);
+				constexpr int je = 2 * jp, jo = 2 * jp + 1;
+				acc_g = __fmaf_rn(dge, __fmaf_rn((float)(de[0] * 254 + de[1]), wx[je], wz[je]),
+						  acc_g);
+				acc_g8 = __fmaf_rn(d8e, __fmaf_rn((float)(de[2] * 254 + de[3]), wx[je], wz[je]),
+						   acc_g8);
+				acc_g = __fmaf_rn(dgo, __fmaf_rn((float)(dd[0] * 254 + dd[1]), wx[jo], wz[jo]),
+						  acc_g);
+				acc_g8 = __fmaf_rn(d8o, __fmaf_rn((float)(dd[2] * 254 + dd[3]), wx[jo], wz[jo]),
+						   acc_g8);
+			});
 		}
 		__syncwarp();
 		if (lane == 0)
 			mbar_arrive(&empty[slot]);
-		// this warp's share of rows g and g + 8: its columns (planes), then
-		// the four lanes of the row
-		float vg = acc[0] + acc[1], vg8 = acc[2] + acc[3];
-		vg += __shfl_xor_sync(0xffffffffu, vg, 1);
-		vg += __shfl_xor_sync(0xffffffffu, vg, 2);
-		vg8 += __shfl_xor_sync(0xffffffffu, vg8, 1);
-		vg8 += __shfl_xor_sync(0xffffffffu, vg8, 2);
+		// this warp's share of rows g and g + 8: the four lanes of the row
+		acc_g += __shfl_xor_sync(0xffffffffu, acc_g, 1);
+		acc_g += __shfl_xor_sync(0xffffffffu, acc_g, 2);
+		acc_g8 += __shfl_xor_sync(0xffffffffu, acc_g8, 1);
+		acc_g8 += __shfl_xor_sync(0xffffffffu, acc_g8, 2);
 		float *rd = red + (i & 1) * kTcMath * kTcRows + warp * kTcRows;
 		if (t == 0) {
-			rd[g] = vg;
-			rd[g + 8] = vg8;
+			rd[g] = acc_g;
+			rd[g + 8] = acc_g8;
 		}
 		asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
 		if (warp == 0 && lane < kTcRows) {
 			const int r = r0 + i * kTcRows + lane;
-			const float *rs = red + (i & 1) * kTcMath * kTcRows + lane;
+			const float *rsum = red + (i & 1) * kTcMath * kTcRows + lane;
 			float v = 0.0f;
 #pragma unroll
 			for (int q = 0; q < kTcMath; q++)
-				v += rs[q * kTcRows];
+				v += rsum[q * kTcRows];
 			if (r < r1)
 				y[r] = v;
 		}
@@ -393,7 +462,8 @@ gemv1_kernel(const uint8_t *__restrict__ w, int rows, int nb, const float *__res
 static int tc_stages(int qtype, int64_t cols)
 {
 	const int64_t rb = cols / QK * (qtype == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES);
-	if (cols % 256 != 0 || rb % 16 != 0)
+	// an even number of blocks per math warp, at most kTcMaxXb
+	if (cols % (32 * 2 * kTcMath) != 0 || cols / QK > kTcMath * kTcMaxXb || rb % 16 != 0)
 		return 0;
 	for (int s = kTcMaxStages; s >= 2; s--)
 		if (tc_smem(s, kTcRows * tc_row_stride(rb), (int)(cols / QK)) <= kTcSmemCap)
@@ -411,14 +481,12 @@ bool gemv1_supported(int qtype, int64_t rows, int64_t cols, uintptr_t w, uintptr
 	return cols % 64 == 0 && cols / QK * kXPad * 4 <= 200 * 1024 && w % 4 == 0;
 }
 
-template <int QT>
-static cudaError_t launch_tc(const void *w, int64_t rows, int64_t cols, const float *x, float *y,
-			     int32_t *err, int stages, cudaStream_t st)
+template <int QT, int NBW>
+static cudaError_t launch_tc_t(const void *w, int64_t rows, int nb, const float *x, float *y,
+			       int32_t *err, int stages, size_t smem, cudaStream_t st)
 {
-	const int nb = (int)(cols / QK);
-	const int64_t rb = (int64_t)nb * (QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES);
-	const size_t smem = tc_smem(stages, kTcRows * tc_row_stride(rb), nb);
-	cudaError_t e = ensure_smem(gemv_tc_kernel<QT>, smem);
+	auto fn = gemv_tc_kernel<QT, NBW>;
+	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
 	int64_t grid = rows / kTcRows;
@@ -426,9 +494,34 @@ static cudaError_t launch_tc(const void *w, int64_t rows, int64_t cols, const fl
 		grid = sm_count();
 	if (grid < 1)
 		grid = 1;
-	gemv_tc_kernel<QT><<<(unsigned)grid, kTcThreads, smem, st>>>(
-		static_cast<const uint8_t *>(w), (int)rows, nb, stages, x, y, err);
+	fn<<<(unsigned)grid, kTcThreads, smem, st>>>(static_cast<const uint8_t *>(w), (int)rows, nb,
+						       stages, x, y, err);
 	return cudaGetLastError();
+}
+
+template <int QT>
+static cudaError_t launch_tc(const void *w, int64_t rows, int64_t cols, const float *x, float *y,
+			     int32_t *err, int stages, cudaStream_t st)
+{
+	const int nb = (int)(cols / QK);
+	const int64_t rb = (int64_t)nb * (QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES);
+	const size_t smem = tc_smem(stages, kTcRows * tc_row_stride(rb), nb);
+	switch (nb / kTcMath) {
+	case 2:
+		return launch_tc_t<QT, 2>(w, rows, nb, x, y, err, stages, smem, st);
+	case 4:
+		return launch_tc_t<QT, 4>(w, rows, nb, x, y, err, stages, smem, st);
+	case 6:
+		return launch_tc_t<QT, 6>(w, rows, nb, x, y, err, stages, smem, st);
+	case 8:
+		return launch_tc_t<QT, 8>(w, rows, nb, x, y, err, stages, smem, st);
+	case 10:
+		return launch_tc_t<QT, 10>(w, rows, nb, x, y, err, stages, smem, st);
+	case 12:
+		return launch_tc_t<QT, 12>(w, rows, nb, x, y, err, stages, smem, st);
+	default:
+		return cudaErrorInvalidValue;
+	}
 }
 
 cudaError_t launch_gemv1(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,

@@ -114,7 +114,6 @@ struct DecodeArgs {
 	// 4 expert-parallel exchange wait expired, 5 ranks passed different T
 	int32_t *err;
 	unsigned long long *gbar;  // grid barrier state (decode_barrier_bytes), zero when allocated
-	int32_t *ready;            // [256] per-expert gate/up pass counters (zeroed by the kernel)
 	uint64_t *stamps;          // NULL or [grid][decode_stamps()] phase times (ns)
 	// expert parallelism (world > 1): this GPU computes experts
 	// [first_expert, first_expert + n_local).
