@@ -333,6 +333,79 @@ MOE_API int moe_synth_gauss(float *dst, uint64_t seed, uint64_t tag, uint64_t of
 MOE_API int moe_quantize_device(const float *src, int64_t rows, int64_t cols, int qtype,
 			void *dst, void *stream);
 
+/* ------------------------------------------------------------------ */
+/* Whole model on the device (OLMoE, llama / Mixtral)                   */
+/* ------------------------------------------------------------------ */
+
+/* Replaces the forward of models/olmoe/olmoe.c (olmoe_prefill /
+ * olmoe_decode, olmoe.c:504-520) and models/llama/llama.c (llama_prefill /
+ * llama_decode, llama.c:560-576): embedding, RMSNorm, Q/K/V projections,
+ * QK-norm (OLMoE), RoPE, KV cache, causal attention (GQA for llama), output
+ * projection, residuals, the MoE FFN layers of this library (or a dense
+ * SwiGLU FFN), final norm, and lm_head.  The tensors are the GGUF views the
+ * reference's loader makes (olmoe_load / llama_load: gguf_tensor_1d/2d/3d),
+ * copied into HBM by moe_model_create; the model code keeps its own
+ * loading and tokenizer. */
+enum { MOE_ARCH_OLMOE = 0, MOE_ARCH_LLAMA = 1 };
+
+typedef struct moe_model moe_model; /* opaque */
+
+typedef struct moe_model_desc {
+	int arch;                       /* MOE_ARCH_OLMOE or MOE_ARCH_LLAMA   */
+	int64_t n_layers, d_model;
+	int64_t n_heads, n_kv_heads;    /* OLMoE: n_kv_heads = n_heads        */
+	int64_t head_len;               /* 128                                */
+	int64_t vocab, context;
+	int64_t n_experts, top_k, d_ff; /* n_experts 0: dense SwiGLU FFN      */
+	float rope_theta;
+	const moe_tensor_t *token_embd;  /* [vocab, d] F32/Q8_0/Q4_0          */
+	const moe_tensor_t *output;      /* lm_head [vocab, d] Q8_0/Q4_0      */
+	const moe_tensor_t *output_norm; /* [d] F32                           */
+	/* arrays of n_layers tensors (attn_q_norm / attn_k_norm: OLMoE only,
+	 * NULL arrays for llama; ffn_gate_inp: F32 router, MoE only) */
+	const moe_tensor_t *const *attn_norm, *const *attn_q, *const *attn_k, *const *attn_v;
+	const moe_tensor_t *const *attn_q_norm, *const *attn_k_norm, *const *attn_output;
+	const moe_tensor_t *const *ffn_norm, *const *ffn_gate_inp;
+	/* OLMoE: n_layers 3-D expert tensors [n_experts, d_ff, d] / [n_experts,
+	 * d, d_ff]; llama with experts (Mixtral): n_layers * n_experts 2-D
+	 * tensors, layer-major; dense llama: n_layers 2-D tensors */
+	const moe_tensor_t *const *ffn_gate, *const *ffn_up, *const *ffn_down;
+} moe_model_desc;
+
+MOE_API int moe_model_create(moe_model **out, const moe_model_desc *desc);
+MOE_API int moe_model_destroy(moe_model *m);
+/* olmoe_prefill / llama_prefill: T tokens at positions pos (host arrays)
+ * appended to the cache; output (host, may be NULL) receives the T
+ * final-normed rows [T, d].  MOE_ERR_INVALID if the cache would overflow
+ * (the reference only rotates in decode) or a position is outside
+ * [0, context). */
+MOE_API int moe_model_prefill(moe_model *m, const int *tok, const int *pos, size_t T,
+			      float *output);
+/* olmoe_decode / llama_decode: one token; the cache rotates (kvcache.c:
+ * 29-55, keep context/2) when full, and positions past the context are
+ * replaced by the cache size.  output (host, may be NULL): [d]. */
+MOE_API int moe_model_decode(moe_model *m, int tok, int pos, float *output);
+/* logits [vocab] (host) of row `row` of the last prefill/decode output:
+ * tensor_mma_transposed_2x2(logits, row, output.weight) (olmoe.c:563) */
+MOE_API int moe_model_logits(moe_model *m, size_t row, float *logits);
+/* Greedy generation as olmoe_generate / llama_generate with --greedy
+ * (olmoe.c:522-601, main.c:189-193): prefill the prompt at positions
+ * pos.., pick the first maximum of the last row's logits, then decode the
+ * pick and pick again, at most n times, stopping once a pick equals eos
+ * (eos < 0: never).  The decode steps run as one CUDA graph replayed per
+ * token.  tokens (host, n + 1 entries) receives the picks; returns their
+ * number (>= 1) or an error status. */
+MOE_API int moe_model_generate(moe_model *m, const int *prompt, size_t T, int n, int eos,
+			       int *tokens);
+/* empty the KV cache and reset the position (a new sequence) */
+MOE_API int moe_model_reset(moe_model *m);
+/* waits for the device; MOE_OK or the first error a kernel recorded since
+ * the last call (MOE_ERR_INVALID: a token id outside the vocabulary, a
+ * position or cache row out of range; MOE_ERR_TIMEOUT from a MoE layer) */
+MOE_API int moe_model_status(moe_model *m);
+/* the cache size and device bytes the model holds */
+MOE_API int moe_model_info(moe_model *m, int64_t *cache_size, int64_t *pos, size_t *device_bytes);
+
 #ifdef __cplusplus
 }
 #endif

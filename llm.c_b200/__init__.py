@@ -49,6 +49,25 @@ class LayerDesc(C.Structure):
                 ("first_expert", C.c_int64), ("n_local", C.c_int64)]
 
 
+_TPP = C.POINTER(C.POINTER(MoeTensor))
+
+
+class ModelDesc(C.Structure):
+    """moe_model_desc (include/moe_b200.h)"""
+    _fields_ = [("arch", C.c_int), ("n_layers", C.c_int64), ("d_model", C.c_int64),
+                ("n_heads", C.c_int64), ("n_kv_heads", C.c_int64), ("head_len", C.c_int64),
+                ("vocab", C.c_int64), ("context", C.c_int64), ("n_experts", C.c_int64),
+                ("top_k", C.c_int64), ("d_ff", C.c_int64), ("rope_theta", C.c_float),
+                ("token_embd", C.POINTER(MoeTensor)), ("output", C.POINTER(MoeTensor)),
+                ("output_norm", C.POINTER(MoeTensor)),
+                ("attn_norm", _TPP), ("attn_q", _TPP), ("attn_k", _TPP), ("attn_v", _TPP),
+                ("attn_q_norm", _TPP), ("attn_k_norm", _TPP), ("attn_output", _TPP),
+                ("ffn_norm", _TPP), ("ffn_gate_inp", _TPP),
+                ("ffn_gate", _TPP), ("ffn_up", _TPP), ("ffn_down", _TPP)]
+
+
+ARCH_OLMOE, ARCH_LLAMA = 0, 1
+
 _lib = None
 
 # every symbol include/moe_b200.h declares, with (restype, argtypes)
@@ -93,6 +112,15 @@ SIGNATURES = {
     "moe_host_free": (_I, [_P]),
     "moe_synth_gauss": (_I, [_P, _U64, _U64, _U64, _I64, _F, _P]),
     "moe_quantize_device": (_I, [_P, _I64, _I64, _I, _P, _P]),
+    "moe_model_create": (_I, [C.POINTER(_P), C.POINTER(ModelDesc)]),
+    "moe_model_destroy": (_I, [_P]),
+    "moe_model_prefill": (_I, [_P, _P, _P, _SZ, _P]),
+    "moe_model_decode": (_I, [_P, _I, _I, _P]),
+    "moe_model_logits": (_I, [_P, _SZ, _P]),
+    "moe_model_generate": (_I, [_P, _P, _SZ, _I, _I, _P]),
+    "moe_model_reset": (_I, [_P]),
+    "moe_model_status": (_I, [_P]),
+    "moe_model_info": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64), C.POINTER(_SZ)]),
 }
 
 
@@ -420,3 +448,132 @@ def gemv(w: np.ndarray, qtype: int, rows: int, cols: int, x: np.ndarray) -> np.n
     gemv_device(bw.ptr, qtype, rows, cols, bx.ptr, x.shape[0], by.ptr)
     check(lib().moe_sync())
     return by.to_numpy(np.float32, (x.shape[0], rows))
+
+
+# ------------------------------------------------------------------ whole model
+class Model:
+    """A device-resident OLMoE / llama-Mixtral model (moe_model_*): the
+    transformer of models/olmoe/olmoe.c or models/llama/llama.c around this
+    library's MoE layers.  Built from the tensor views of a GGUF file (the
+    reference's loader makes the same views) or of numpy arrays."""
+
+    def __init__(self, desc: ModelDesc, keep):
+        self._keep = keep
+        h = C.c_void_p()
+        check(lib().moe_model_create(C.byref(h), C.byref(desc)))
+        self.h = h
+        self.d_model = desc.d_model
+        self.vocab = desc.vocab
+        self.context = desc.context
+
+    @classmethod
+    def from_gguf(cls, reader) -> "Model":
+        """every tensor the model code asks gguf.c for (olmoe.c:163-183,
+        llama.c:135-175), by name, from a llm.c_b200.gguf.GGUFReader"""
+        kv = reader.kv
+        arch = kv["general.architecture"]
+        a = arch
+        L = kv[f"{a}.block_count"]
+        d = kv[f"{a}.embedding_length"]
+        H = kv[f"{a}.attention.head_count"]
+        kvh = kv.get(f"{a}.attention.head_count_kv", H)
+        ne = kv.get(f"{a}.expert_count", 0)
+        keep = []
+
+        def t(name):
+            arr, dt, dims = reader.tensor(name)
+            mt = tensor(arr, dt, dims)
+            keep.append(mt)
+            return C.pointer(mt)
+
+        def arr(names):
+            ptrs = (C.POINTER(MoeTensor) * len(names))(*[t(n) for n in names])
+            keep.append(ptrs)
+            return C.cast(ptrs, _TPP)
+
+        blk = lambda fmt: [fmt.format(i) for i in range(L)]  # noqa: E731
+        desc = ModelDesc()
+        desc.arch = ARCH_OLMOE if arch == "olmoe" else ARCH_LLAMA
+        desc.n_layers, desc.d_model, desc.n_heads, desc.n_kv_heads = L, d, H, kvh
+        desc.head_len = d // H
+        desc.vocab = len(kv["tokenizer.ggml.tokens"])
+        desc.context = kv[f"{a}.context_length"]
+        desc.n_experts = ne
+        desc.top_k = kv.get(f"{a}.expert_used_count", 0)
+        desc.d_ff = kv[f"{a}.feed_forward_length"]
+        desc.rope_theta = kv[f"{a}.rope.freq_base"]
+        desc.token_embd = t("token_embd.weight")
+        desc.output = t("output.weight")
+        desc.output_norm = t("output_norm.weight")
+        desc.attn_norm = arr(blk("blk.{}.attn_norm.weight"))
+        desc.attn_q = arr(blk("blk.{}.attn_q.weight"))
+        desc.attn_k = arr(blk("blk.{}.attn_k.weight"))
+        desc.attn_v = arr(blk("blk.{}.attn_v.weight"))
+        desc.attn_output = arr(blk("blk.{}.attn_output.weight"))
+        desc.ffn_norm = arr(blk("blk.{}.ffn_norm.weight"))
+        if arch == "olmoe":
+            desc.attn_q_norm = arr(blk("blk.{}.attn_q_norm.weight"))
+            desc.attn_k_norm = arr(blk("blk.{}.attn_k_norm.weight"))
+            for f in ("gate", "up", "down"):
+                setattr(desc, f"ffn_{f}", arr(blk("blk.{}.ffn_" + f + "_exps.weight")))
+        elif ne:
+            for f in ("gate", "up", "down"):
+                setattr(desc, f"ffn_{f}", arr([f"blk.{i}.ffn_{f}.{e}.weight"
+                                               for i in range(L) for e in range(ne)]))
+        else:
+            for f in ("gate", "up", "down"):
+                setattr(desc, f"ffn_{f}", arr(blk("blk.{}.ffn_" + f + ".weight")))
+        if ne:
+            desc.ffn_gate_inp = arr(blk("blk.{}.ffn_gate_inp.weight"))
+        return cls(desc, keep)
+
+    def prefill(self, tokens, positions=None, rows=True):
+        tok = np.ascontiguousarray(tokens, np.int32)
+        pos = (np.arange(tok.size, dtype=np.int32) if positions is None
+               else np.ascontiguousarray(positions, np.int32))
+        out = np.empty((tok.size, self.d_model), np.float32) if rows else None
+        check(lib().moe_model_prefill(self.h, tok.ctypes.data, pos.ctypes.data, tok.size,
+                                      None if out is None else out.ctypes.data))
+        return out
+
+    def decode(self, tok: int, pos: int, row=True):
+        out = np.empty(self.d_model, np.float32) if row else None
+        check(lib().moe_model_decode(self.h, int(tok), int(pos),
+                                     None if out is None else out.ctypes.data))
+        return out
+
+    def logits(self, row: int = 0) -> np.ndarray:
+        out = np.empty(self.vocab, np.float32)
+        check(lib().moe_model_logits(self.h, row, out.ctypes.data))
+        return out
+
+    def generate(self, prompt, n: int, eos: int = -1) -> np.ndarray:
+        tok = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(n + 1, np.int32)
+        made = lib().moe_model_generate(self.h, tok.ctypes.data, tok.size, n, eos,
+                                        out.ctypes.data)
+        if made < 0:
+            check(made)
+        return out[:made]
+
+    def reset(self):
+        check(lib().moe_model_reset(self.h))
+
+    def status(self):
+        return lib().moe_model_status(self.h)
+
+    def info(self):
+        cs, pos, nb = C.c_int64(), C.c_int64(), C.c_size_t()
+        check(lib().moe_model_info(self.h, C.byref(cs), C.byref(pos), C.byref(nb)))
+        return cs.value, pos.value, nb.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().moe_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -350,6 +350,10 @@ struct moe_layer {
 	} a2a;
 };
 
+namespace moe {
+int64_t layer_scratch_rows(const moe_layer *L) { return L ? L->capT : -1; }
+}  // namespace moe
+
 namespace {
 
 constexpr size_t kStampRecords = 64;  // profiled fused forwards kept per layer
@@ -1469,53 +1473,60 @@ int moe_layer_ep_reset(moe_layer *L)
 }
 
 // ---------------------------------------------------------------- dense GEMV
-int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
-		    int64_t m, float *y, void *stream)
+}  // extern "C"
+
+namespace moe {
+// The dense projection behind moe_gemv_device and the model forward: one
+// "expert" holding all m rows of x (counts = {m}, offsets = {0, m}).  The
+// metadata (and the GEMM's weight tensor map) and the fp16 split of x live
+// in the caller's scratch, so calls sharing one scratch must be ordered on
+// one stream.  m == 1 with a supported shape takes the single-row GEMV,
+// which needs no scratch and issues no copy (graph-capturable).
+struct DenseMeta {
+	alignas(64) uint8_t map[128];  // prefill GEMM: the weight matrix's tensor map
+	const void *w;
+	int32_t counts[1], offsets[2], err[1], active[1], n_active[1], work[1];
+};
+
+void dense_scratch_free(DenseScratch &s)
 {
-	if (int rc = ensure_init())
-		return rc;
+	if (s.meta)
+		cudaFree(s.meta);
+	if (s.x16)
+		cudaFree(s.x16);
+	s = DenseScratch{};
+}
+
+int dense_forward(DenseScratch &s, const void *w, int qtype, int64_t rows, int64_t cols,
+		  const float *x, int64_t m, float *y, int32_t *err, cudaStream_t st)
+{
 	if ((qtype != MOE_Q8_0 && qtype != MOE_Q4_0) || cols % QK || rows <= 0 || m < 0)
-		return fail(MOE_ERR_INVALID, "moe_gemv_device: qtype %d rows %lld cols %lld", qtype,
+		return fail(MOE_ERR_INVALID, "dense projection: qtype %d rows %lld cols %lld", qtype,
 			    (long long)rows, (long long)cols);
 	if (m == 0)
 		return MOE_OK;
-	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
-	if (!g.gemv_err) {
-		CK(cudaMalloc(&g.gemv_err, 4));
-		CK(cudaMemset(g.gemv_err, 0, 4));
-	}
-	// one activation row (decode): the memory-bound GEMV, no scratch; every
-	// path's bounded waits report to the library's GEMV error word (moe_sync)
+	// one activation row (decode): the memory-bound GEMV, no scratch
 	if (m == 1 && moe::gemv1_supported(qtype, rows, cols, (uintptr_t)w, (uintptr_t)x, (uintptr_t)y)) {
-		CK(moe::launch_gemv1(w, qtype, rows, cols, x, y, g.gemv_err, st));
+		CK(moe::launch_gemv1(w, qtype, rows, cols, x, y, err, st));
 		return MOE_OK;
 	}
-	// one "expert" holding all m rows of x: counts = {m}, offsets = {0, m}.
-	// The metadata (and the GEMM's weight tensor map) and the fp16 split of
-	// x live in per-thread device buffers, so calls from one thread must be
-	// ordered on one stream.
-	struct Meta {
-		alignas(64) uint8_t map[128];  // prefill GEMM: the weight matrix's tensor map
-		const void *w;
-		int32_t counts[1], offsets[2], err[1], active[1], n_active[1], work[1];
-	};
-	static thread_local Meta *dmeta = nullptr;
-	static thread_local __half *x16 = nullptr;
-	static thread_local size_t x16_bytes = 0;
-	if (!dmeta)
-		CK(cudaMalloc(&dmeta, sizeof(Meta)));
+	using Meta = DenseMeta;
+	if (!s.meta)
+		CK(cudaMalloc(&s.meta, sizeof(Meta)));
+	Meta *dmeta = static_cast<Meta *>(s.meta);
 	auto ensure_x16 = [&](size_t need) -> int {
-		if (need <= x16_bytes)
+		if (need <= s.x16_bytes)
 			return MOE_OK;
 		CK(cudaStreamSynchronize(st));
-		if (x16)
-			cudaFree(x16);
-		x16 = nullptr;
-		x16_bytes = 0;
-		CK(cudaMalloc(&x16, need));
-		x16_bytes = need;
+		if (s.x16)
+			cudaFree(s.x16);
+		s.x16 = nullptr;
+		s.x16_bytes = 0;
+		CK(cudaMalloc(&s.x16, need));
+		s.x16_bytes = need;
 		return MOE_OK;
 	};
+	__half *&x16 = s.x16;
 	Meta h{};
 	h.w = w;
 	h.counts[0] = (int32_t)m;
@@ -1547,7 +1558,7 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 		a.in16 = x16;
 		a.out = y;
 		a.dual = 0;
-		a.err = g.gemv_err;
+		a.err = err;
 		CK(moe::launch_expert_gemm(a, m, st));
 		return MOE_OK;
 	}
@@ -1573,7 +1584,7 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 		a.in16 = x16;
 		a.out = y;
 		a.dual = 0;
-		a.err = g.gemv_err;
+		a.err = err;
 		a.active = dmeta->active;
 		a.n_active = dmeta->n_active;
 		a.work = dmeta->work;
@@ -1598,6 +1609,30 @@ int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const 
 	a.dual = 0;
 	CK(moe::launch_expert_gemv(a, st));
 	return MOE_OK;
+}
+}  // namespace moe
+
+extern "C" {
+
+int moe_gemv_device(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
+		    int64_t m, float *y, void *stream)
+{
+	if (int rc = ensure_init())
+		return rc;
+	if ((qtype != MOE_Q8_0 && qtype != MOE_Q4_0) || cols % QK || rows <= 0 || m < 0)
+		return fail(MOE_ERR_INVALID, "moe_gemv_device: qtype %d rows %lld cols %lld", qtype,
+			    (long long)rows, (long long)cols);
+	if (m == 0)
+		return MOE_OK;
+	cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+	if (!g.gemv_err) {
+		CK(cudaMalloc(&g.gemv_err, 4));
+		CK(cudaMemset(g.gemv_err, 0, 4));
+	}
+	// every path's bounded waits report to the library's GEMV error word
+	// (moe_sync); the scratch is per calling thread
+	static thread_local moe::DenseScratch scratch;
+	return moe::dense_forward(scratch, w, qtype, rows, cols, x, m, y, g.gemv_err, st);
 }
 
 // ---------------------------------------------------------------- drop-ins

@@ -5,6 +5,8 @@
 #include <stdint.h>
 #include <cuda_fp16.h>
 
+struct moe_layer;  // include/moe_b200.h
+
 namespace moe {
 
 // router.cu ------------------------------------------------------------
@@ -227,6 +229,66 @@ cudaError_t launch_copy_segments(const void *src, void *dst, const int64_t *seg,
 // ret[i] = ret[i] + add[i % n_add]  (bias of tensor_mma_transposed_2x2)
 cudaError_t launch_add_bias(float *ret, const float *add, int64_t total, int64_t n_add,
 			    cudaStream_t st);
+
+// capi.cu: the dense projection y[m, rows] = x[m, cols] . W[rows, cols]^T
+// (Q8_0/Q4_0 W) behind moe_gemv_device, with caller-owned scratch; returns
+// a MOE_* status (the message through moe_last_error)
+struct DenseScratch {
+	void *meta = nullptr;
+	__half *x16 = nullptr;
+	size_t x16_bytes = 0;
+};
+int dense_forward(DenseScratch &s, const void *w, int qtype, int64_t rows, int64_t cols,
+		  const float *x, int64_t m, float *y, int32_t *err, cudaStream_t st);
+void dense_scratch_free(DenseScratch &s);
+void set_last_error(const char *msg);
+// rows a MoE layer's scratch holds (it only grows; buffers move when it does)
+int64_t layer_scratch_rows(const ::moe_layer *L);
+int ensure_library();
+cudaStream_t library_stream();
+
+// model.cu: the transformer around the MoE layers --------------------------
+// hidden[t] = dequant(wte row tok[t]); out[t] = rms_norm(hidden[t]) * w
+// (err |= 1 for a token id outside [0, V))
+cudaError_t launch_embed_norm(const void *wte, int wtype, int64_t V, int E, const int32_t *tok,
+			      int T, const float *w, float eps, float *hidden, float *out,
+			      int32_t *err, cudaStream_t st);
+// hidden[t] += delta[t]; out[t] = rms_norm(hidden[t]) * w
+cudaError_t launch_add_norm(float *hidden, const float *delta, const float *w, int T, int E,
+			    float eps, float *out, cudaStream_t st);
+// per token: q (and k) RMS-normed over the whole vector (qk_norm), RoPE on
+// the pairs (2i, 2i+1) of each head from the cos/sin table rope[pos][i];
+// q -> q_out [T, H*HL], k and v -> the layer's cache at rows size + t
+struct QkvArgs {
+	const float *qkv;          // [T, (H + 2 KVH) * HL]
+	const float *q_norm, *k_norm;  // [H*HL], [KVH*HL] or NULL (no QK-norm)
+	const float2 *rope;        // [C][HL/2] (cos, sin)
+	const int32_t *pos;        // [T]
+	const int32_t *size;       // cache rows already filled (device scalar)
+	float *q_out;              // [T, H*HL]
+	float *kc, *vc;            // this layer's cache [KVH][C][HL]
+	int T, H, KVH, HL, C;
+	float eps;
+	int32_t *err;              // err |= 2: position or cache row out of range
+};
+cudaError_t launch_qk_rope(const QkvArgs &a, cudaStream_t st);
+// causal attention of q [T, H*HL] over the cache rows [0, size + T) of this
+// layer (query t sees rows <= size + t); GQA: query head h reads kv head
+// h / (H / KVH).  T == 1 splits the rows into kAttnChunk-row chunks (part:
+// [H][attn_splits(C)][HL + 2] scratch) and merges them.
+constexpr int kAttnChunk = 64;
+inline int attn_splits(int C) { return (C + kAttnChunk - 1) / kAttnChunk; }
+cudaError_t launch_attention(const float *q, const float *kc, const float *vc, const int32_t *size,
+			     int T, int H, int KVH, int HL, int C, float scale_div, float *part,
+			     float *out, cudaStream_t st);
+// greedy pick (main.c:189-193: the first maximum) of logits [V] into
+// state[0] and picks[state[6] % pick_cap] (state[6] counts the picks); with
+// advance, the decode state {tok, pos, size, model_pos} moves one row on
+cudaError_t launch_argmax_advance(const float *logits, int V, int C, int32_t *state,
+				  int32_t *picks, int pick_cap, int advance, cudaStream_t st);
+// cache rows [drop, drop + keep) -> [0, keep) of every layer, head, K and V
+cudaError_t launch_kv_shift(float *kc, float *vc, int L, int KVH, int C, int HL, int keep,
+			    int drop, cudaStream_t st);
 
 // synth.cu -------------------------------------------------------------
 cudaError_t launch_synth_gauss(float *dst, uint64_t stream_seed, uint64_t offset, int64_t n,

@@ -155,13 +155,23 @@ def _vocab(n: int):
     return [f"<t{i}>" for i in range(n)]
 
 
+def _norms(seed: int, norm_sd: float):
+    """RMSNorm weights: ones (norm_sd 0, the usual init), else 1 + N(0,
+    norm_sd) from a stream of their own (the other weights do not move)"""
+    rng = np.random.default_rng(seed + 1000)
+    if norm_sd == 0:
+        return lambda n: np.ones(n, np.float32)
+    return lambda n: (1.0 + rng.normal(0.0, norm_sd, size=n)).astype(np.float32)
+
+
 def write_olmoe(path: str, layers: int, d: int, heads: int, n_exp: int, top_k: int, d_ff: int,
                 vocab: int, seed: int = 2, context: int = 4096, rope_theta: float = 10000.0,
-                sd: float = 0.02, qtype: int = Q8_0):
+                sd: float = 0.02, qtype: int = Q8_0, norm_sd: float = 0.0):
     """random-init OLMoE-architecture model (config 2: 16 layers, d 2048, 16
     heads, 64 experts top-8, d_ff 1024, vocab 50304, Q8_0, seed 2)"""
     rng = np.random.default_rng(seed)
     g = lambda *shape: rng.normal(0.0, sd, size=shape).astype(np.float32)  # noqa: E731
+    nrm = _norms(seed, norm_sd)
     w = GGUFWriter()
     w.add_str("general.architecture", "olmoe")
     for k, v in (("context_length", context), ("embedding_length", d),
@@ -175,15 +185,15 @@ def write_olmoe(path: str, layers: int, d: int, heads: int, n_exp: int, top_k: i
     w.add_u32("tokenizer.ggml.eos_token_id", 2)
     w.add_tensor("token_embd.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
     w.add_tensor("output.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
-    w.add_tensor("output_norm.weight", np.ones(d, np.float32), F32, (d,))
+    w.add_tensor("output_norm.weight", nrm(d), F32, (d,))
     for i in range(layers):
         p = f"blk.{i}."
-        w.add_tensor(p + "attn_norm.weight", np.ones(d, np.float32), F32, (d,))
+        w.add_tensor(p + "attn_norm.weight", nrm(d), F32, (d,))
         for n in ("attn_q", "attn_k", "attn_v", "attn_output"):
             w.add_tensor(p + n + ".weight", quantize(qtype, g(d, d)), qtype, (d, d))
-        w.add_tensor(p + "attn_q_norm.weight", np.ones(d, np.float32), F32, (d,))
-        w.add_tensor(p + "attn_k_norm.weight", np.ones(d, np.float32), F32, (d,))
-        w.add_tensor(p + "ffn_norm.weight", np.ones(d, np.float32), F32, (d,))
+        w.add_tensor(p + "attn_q_norm.weight", nrm(d), F32, (d,))
+        w.add_tensor(p + "attn_k_norm.weight", nrm(d), F32, (d,))
+        w.add_tensor(p + "ffn_norm.weight", nrm(d), F32, (d,))
         w.add_tensor(p + "ffn_gate_inp.weight", g(n_exp, d), F32, (n_exp, d))
         w.add_tensor(p + "ffn_gate_exps.weight", quantize(qtype, g(n_exp, d_ff, d)), qtype,
                      (n_exp, d_ff, d))
@@ -196,12 +206,14 @@ def write_olmoe(path: str, layers: int, d: int, heads: int, n_exp: int, top_k: i
 
 def write_mixtral(path: str, layers: int, d: int, q_heads: int, kv_heads: int, n_exp: int,
                   top_k: int, d_ff: int, vocab: int, seed: int = 3, context: int = 4096,
-                  rope_theta: float = 1e6, sd: float = 0.02, qtype: int = Q4_0):
+                  rope_theta: float = 1e6, sd: float = 0.02, qtype: int = Q4_0,
+                  norm_sd: float = 0.0):
     """random-init Mixtral-architecture model ("llama" with experts; config 3:
     32 layers, d 4096, 32/8 heads, 8 experts top-2, d_ff 14336, vocab 32000,
     Q4_0, seed 3)"""
     rng = np.random.default_rng(seed)
     g = lambda *shape: rng.normal(0.0, sd, size=shape).astype(np.float32)  # noqa: E731
+    nrm = _norms(seed, norm_sd)
     hl = d // q_heads
     w = GGUFWriter()
     w.add_str("general.architecture", "llama")
@@ -216,10 +228,10 @@ def write_mixtral(path: str, layers: int, d: int, q_heads: int, kv_heads: int, n
     w.add_u32("tokenizer.ggml.eos_token_id", 2)
     w.add_tensor("token_embd.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
     w.add_tensor("output.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
-    w.add_tensor("output_norm.weight", np.ones(d, np.float32), F32, (d,))
+    w.add_tensor("output_norm.weight", nrm(d), F32, (d,))
     for i in range(layers):
         p = f"blk.{i}."
-        w.add_tensor(p + "attn_norm.weight", np.ones(d, np.float32), F32, (d,))
+        w.add_tensor(p + "attn_norm.weight", nrm(d), F32, (d,))
         w.add_tensor(p + "attn_q.weight", quantize(qtype, g(q_heads * hl, d)), qtype,
                      (q_heads * hl, d))
         for n in ("attn_k", "attn_v"):
@@ -227,7 +239,7 @@ def write_mixtral(path: str, layers: int, d: int, q_heads: int, kv_heads: int, n
                          (kv_heads * hl, d))
         w.add_tensor(p + "attn_output.weight", quantize(qtype, g(d, q_heads * hl)), qtype,
                      (d, q_heads * hl))
-        w.add_tensor(p + "ffn_norm.weight", np.ones(d, np.float32), F32, (d,))
+        w.add_tensor(p + "ffn_norm.weight", nrm(d), F32, (d,))
         w.add_tensor(p + "ffn_gate_inp.weight", g(n_exp, d), F32, (n_exp, d))
         for e in range(n_exp):
             w.add_tensor(p + f"ffn_gate.{e}.weight", quantize(qtype, g(d_ff, d)), qtype, (d_ff, d))

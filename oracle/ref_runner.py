@@ -13,6 +13,11 @@ runs in its own process and exits when the op is done.  Ops:
   dot      ref_dot_f32_quant  (x, q, qtype, n, rows)
   ffn      ref_fused_ffn_silu (x, gate, up, down, qtype, d_ff)
   bench    times ref_moe_ffn: (same as moe, plus reps) -> seconds per call
+  model    (variant "model": libref_model.so) the reference's own OLMoE /
+           llama-Mixtral forward on a GGUF file: prefill `tokens` at
+           positions 0.., logits of the last row, then `n_decode` steps fed
+           with `forced` tokens (or greedy argmax, main.c:189-193) ->
+           prefill rows, per-step output rows, logits, tokens, seconds
 """
 import ctypes as C
 import os
@@ -80,6 +85,39 @@ def main():
             L.ref_gemm(p(a), m, k, p(b), int(z["qtype"]), n, p(c))
             ts.append(time.perf_counter() - t0)
         out = dict(c=c, seconds=np.array(ts))
+    elif op == "model":
+        L.refm_load.restype = P
+        L.refm_load.argtypes = [C.c_char_p]
+        L.refm_prefill.argtypes = [P, P, P, sz, P]
+        L.refm_decode.argtypes = [P, C.c_int, C.c_int, P]
+        L.refm_logits.argtypes = [P, P, P]
+        h = L.refm_load(str(z["path"]).encode())
+        assert h, "refm_load failed"
+        tok = np.ascontiguousarray(z["tokens"], np.int32)
+        T = tok.size
+        pos = np.arange(T, dtype=np.int32)
+        E, V = int(z["d_model"]), int(z["vocab"])
+        nd = int(z.get("n_decode", 0))
+        forced = z.get("forced")
+        rows = np.empty((T, E), np.float32)
+        t0 = time.perf_counter()
+        assert L.refm_prefill(h, p(tok), p(pos), T, p(rows)) == 0
+        t_prefill = time.perf_counter() - t0
+        logits = np.empty((nd + 1, V), np.float32)
+        drows = np.empty((nd, E), np.float32)
+        toks = np.empty(nd, np.int32)
+        L.refm_logits(h, p(rows[T - 1]), p(logits[0]))
+        t_decode = 0.0
+        for i in range(nd):
+            # greedy: the first maximum (main.c:189-193)
+            nxt = int(forced[i]) if forced is not None else int(np.argmax(logits[i]))
+            toks[i] = nxt
+            t0 = time.perf_counter()
+            L.refm_decode(h, nxt, T + i, p(drows[i]))
+            L.refm_logits(h, p(drows[i]), p(logits[i + 1]))
+            t_decode += time.perf_counter() - t0
+        out = dict(rows=rows, logits=logits, drows=drows, tokens=toks,
+                   prefill_seconds=np.array(t_prefill), decode_seconds=np.array(t_decode))
     elif op == "softmax":
         v = np.array(z["v"], np.float32, copy=True)
         L.ref_softmax.argtypes = [P, sz]
