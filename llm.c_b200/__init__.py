@@ -498,6 +498,8 @@ class Model:
         desc.head_len = d // H
         desc.vocab = len(kv["tokenizer.ggml.tokens"])
         desc.context = kv[f"{a}.context_length"]
+        if arch != "olmoe":
+            desc.context = min(desc.context, 8192)   # llama.c:92-94
         desc.n_experts = ne
         desc.top_k = kv.get(f"{a}.expert_used_count", 0)
         desc.d_ff = kv[f"{a}.feed_forward_length"]

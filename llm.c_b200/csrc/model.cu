@@ -657,7 +657,7 @@ int upload(moe_model *m, const moe_tensor_t *t, int64_t rows, int64_t cols, bool
 	const size_t bytes = (size_t)(rows * row_bytes_of(t->type, cols));
 	void *p;
 	MRC(dalloc(m, &p, bytes));
-	MCK(cudaMemcpy(p, host_ptr(t), bytes, cudaMemcpyHostToDevice));
+	MCK(cudaMemcpy(p, host_ptr(t), bytes, cudaMemcpyDefault));   // host or device views
 	*dev = p;
 	if (type)
 		*type = t->type;
@@ -919,7 +919,7 @@ int create_layers(moe_model *m)
 		int64_t off = 0;
 		for (int i = 0; i < 3; i++) {
 			MCK(cudaMemcpy(static_cast<uint8_t *>(w) + off, host_ptr(qkv[i]),
-				       (size_t)(rows[i] * rb), cudaMemcpyHostToDevice));
+				       (size_t)(rows[i] * rb), cudaMemcpyDefault));
 			off += rows[i] * rb;
 		}
 		ly.wqkv = w;

@@ -117,6 +117,14 @@ class GGUFWriter:
     def add_str(self, key, v):
         self.kv.append((key, T_STR, self._str(v)))
 
+    def add_i32_array(self, key, items):
+        a = np.asarray(items, "<i4")
+        self.kv.append((key, T_ARR, struct.pack("<IQ", T_I32, a.size) + a.tobytes()))
+
+    def add_f32_array(self, key, items):
+        a = np.asarray(items, "<f4")
+        self.kv.append((key, T_ARR, struct.pack("<IQ", T_F32, a.size) + a.tobytes()))
+
     def add_str_array(self, key, items):
         payload = struct.pack("<IQ", T_STR, len(items)) + b"".join(self._str(s) for s in items)
         self.kv.append((key, T_ARR, payload))
@@ -223,7 +231,12 @@ def write_mixtral(path: str, layers: int, d: int, q_heads: int, kv_heads: int, n
                  ("expert_used_count", top_k), ("feed_forward_length", d_ff)):
         w.add_u32("llama." + k, v)
     w.add_f32("llama.rope.freq_base", rope_theta)
+    # llama_load builds the vocabulary tables (llama.c:108 -> vocab.c:323-360):
+    # a SentencePiece ("llama") vocabulary with token types and scores
+    w.add_str("tokenizer.ggml.model", "llama")
     w.add_str_array("tokenizer.ggml.tokens", _vocab(vocab))
+    w.add_i32_array("tokenizer.ggml.token_type", np.ones(vocab, np.int32))
+    w.add_f32_array("tokenizer.ggml.scores", np.zeros(vocab, np.float32))
     w.add_u32("tokenizer.ggml.bos_token_id", 1)
     w.add_u32("tokenizer.ggml.eos_token_id", 2)
     w.add_tensor("token_embd.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
