@@ -425,6 +425,18 @@ def run_ours(args, rank, world, local_rank):
                                       [int(t) for t in args.sweep3.split(",") if t],
                                       cpu_tokens=0 if (world > 1 or args.no_cpu) else 2)
 
+    models = {}
+    if world == 1 and not args.no_model:
+        torch.cuda.synchronize()
+        for lay in layers[1:]:
+            lay.close()
+        del layers[1:], keep[1:]
+        torch.cuda.empty_cache()
+        for cfg in [c for c in args.models.split(",") if c]:
+            models[cfg] = run_model_leg(moe, torch, torch_stream, cfg, with_ref=not args.no_cpu,
+                                        clocks_dev=local_rank)
+            torch.cuda.empty_cache()
+
     line = {
         "metric": "MoE-layer tokens/s (OLMoE config 0, T=%d%s)" % (
             T, " per GPU" if world > 1 else ""),
@@ -461,6 +473,7 @@ def run_ours(args, rank, world, local_rank):
         "config1_gemv": gemv1,
         "dense_gemm": dense,
         "sweeps": sweeps,
+        "models": models,
     }
     if world > 1:
         got = gather_fn(dist, world)((float(np.mean(uniq)), float(np.mean(pairs_local)),
@@ -1057,6 +1070,273 @@ def run_reference(args, rank, world):
                 "d2h_bytes_per_step": 0}}), flush=True)
 
 
+# --------------------------------------------------------------------------- whole model
+# configs 2 and 3: the transformer of olmoe.c / llama.c on the device around
+# the MoE layers (moe_model_*), greedy prefill + decode
+MODEL_CONFIGS = {
+    "config2": dict(arch="olmoe", layers=16, d=2048, heads=16, kv_heads=16, n_exp=64, top_k=8,
+                    d_ff=1024, vocab=50304, q="Q8_0", seed=2, prompt=512, decode=128,
+                    context=4096, theta=1e4, ref_layers=16, ref_tokens=8, ref_decode=2,
+                    name="OLMoE-1B-7B architecture, 16 layers, d 2048, 16 heads, 64 experts "
+                         "top-8, d_ff 1024, vocab 50304, Q8_0"),
+    "config3": dict(arch="mixtral", layers=32, d=4096, heads=32, kv_heads=8, n_exp=8, top_k=2,
+                    d_ff=14336, vocab=32000, q="Q4_0", seed=3, prompt=2048, decode=64,
+                    context=4096, theta=1e6, ref_layers=2, ref_tokens=4, ref_decode=1,
+                    name="Mixtral-8x7B architecture, 32 layers, d 4096, 32/8 heads, 8 experts "
+                         "top-2 (renormalised), d_ff 14336, vocab 32000, Q4_0"),
+}
+
+
+def model_plan(gg, c, layers):
+    if c["arch"] == "olmoe":
+        return gg.olmoe_plan(layers, c["d"], c["heads"], c["n_exp"], c["top_k"], c["d_ff"],
+                             c["vocab"], c["context"], c["theta"])
+    return gg.mixtral_plan(layers, c["d"], c["heads"], c["kv_heads"], c["n_exp"], c["top_k"],
+                           c["d_ff"], c["vocab"], c["context"], c["theta"])
+
+
+def synth_model(moe, torch, gg, c, stream):
+    """every tensor of the config's file plan generated on the device: matrices
+    N(0, 0.02) from generator stream (seed, tag = position in the file) then
+    quantized with the reference quantizer's rounding, routers N(0, 0.02)
+    fp32, RMSNorm weights ones.  name -> (torch tensor, dtype, dims)"""
+    qt = getattr(moe, c["q"])
+    _, ts = model_plan(gg, c, c["layers"])
+    out = {}
+    big = max(int(np.prod(dims)) for _, dims, kind in ts if kind == "mat")
+    tmp = torch.empty(big, dtype=torch.float32, device="cuda")
+    for tag, (name, dims, kind) in enumerate(ts, start=1):
+        n = int(np.prod(dims))
+        if kind == "norm":
+            out[name] = (torch.ones(n, dtype=torch.float32, device="cuda"), moe.F32, dims)
+        elif kind == "router":
+            r = torch.empty(n, dtype=torch.float32, device="cuda")
+            moe.check(moe.lib().moe_synth_gauss(r.data_ptr(), c["seed"], tag, 0, n, 0.02, stream))
+            out[name] = (r, moe.F32, dims)
+        else:
+            cols = dims[-1]
+            rows = n // cols
+            moe.check(moe.lib().moe_synth_gauss(tmp.data_ptr(), c["seed"], tag, 0, n, 0.02,
+                                                stream))
+            q = torch.empty(rows * moe.row_bytes(qt, cols), dtype=torch.uint8, device="cuda")
+            moe.check(moe.lib().moe_quantize_device(tmp.data_ptr(), rows, cols, qt, q.data_ptr(),
+                                                    stream))
+            out[name] = (q, qt, dims)
+    torch.cuda.synchronize()
+    del tmp
+    return out
+
+
+def model_kv(c, layers):
+    a = "olmoe" if c["arch"] == "olmoe" else "llama"
+    kv = {"general.architecture": a, "vocab": c["vocab"],
+          f"{a}.block_count": layers, f"{a}.embedding_length": c["d"],
+          f"{a}.attention.head_count": c["heads"], f"{a}.context_length": c["context"],
+          f"{a}.expert_count": c["n_exp"], f"{a}.expert_used_count": c["top_k"],
+          f"{a}.feed_forward_length": c["d_ff"], f"{a}.rope.freq_base": c["theta"]}
+    if a == "llama":
+        kv[f"{a}.attention.head_count_kv"] = c["kv_heads"]
+    return kv
+
+
+def model_decode_bytes(c, at):
+    """algorithmic HBM bytes of one decode token with `at` cache rows: every
+    layer's attention matrices, router and top_k experts (at most top_k
+    distinct), the K and V rows read, lm_head and one embedding row"""
+    moe = load_package()
+    qt = getattr(moe, c["q"])
+    d, hl = c["d"], c["d"] // c["heads"]
+    nq, nk = c["heads"] * hl, c["kv_heads"] * hl
+    attn = (nq + 2 * nk) * moe.row_bytes(qt, d) + d * moe.row_bytes(qt, nq)
+    expert = 2 * c["d_ff"] * moe.row_bytes(qt, d) + d * moe.row_bytes(qt, c["d_ff"])
+    kv = 2 * at * nk * 4
+    per_layer = attn + c["n_exp"] * d * 4 + c["top_k"] * expert + kv
+    return c["layers"] * per_layer + c["vocab"] * moe.row_bytes(qt, d) + moe.row_bytes(qt, d)
+
+
+def model_prefill_flops(c, T):
+    """algorithmic FLOPs of a T-token prefill: 2 x (attention matrices +
+    router + top_k experts) per token, causal attention scores and values
+    (2 x 2 x T^2/2 x heads x head_len), lm_head of the last row"""
+    d, hl = c["d"], c["d"] // c["heads"]
+    nq, nk = c["heads"] * hl, c["kv_heads"] * hl
+    per_tok = 2 * ((nq + 2 * nk) * d + d * nq + c["n_exp"] * d + c["top_k"] * 3 * c["d_ff"] * d)
+    attn = 2 * 2 * (T * T / 2) * nq
+    return c["layers"] * (T * per_tok + attn) + 2 * c["vocab"] * d
+
+
+def model_reference_sample(moe, torch, gg, c, tensors, model_small):
+    """The reference's own model code (oracle/_ref/libref_model.so: olmoe.c /
+    llama.c) on a GGUF file written from the same device bytes, truncated to
+    ref_layers layers: a ref_tokens-token prefill and ref_decode greedy
+    steps, timed on the host cores, and this library's model of the same
+    layers on the same tokens checked against it."""
+    from oracle import oracle as orc
+    if not orc.ref_available("model") or ref_variant() != "avx512":
+        return None, {"pass": None, "skipped": "oracle/_ref/libref_model.so not built or no "
+                                               "AVX-512 host"}
+    import tempfile
+    L = c["ref_layers"]
+    plan = model_plan(gg, c, L)
+    def fetch(name):
+        t = tensors[name][0]
+        return t.cpu().numpy()
+
+    td = tempfile.mkdtemp(prefix="moe_model_")
+    path = os.path.join(td, "sample.gguf")
+    t0 = time.perf_counter()
+    gg.write_plan_from(path, plan, getattr(moe, c["q"]), fetch)
+    write_s = time.perf_counter() - t0
+    rng = np.random.default_rng(c["seed"] + 100)
+    toks = rng.integers(0, c["vocab"], c["ref_tokens"]).astype(np.int32)
+    try:
+        r = orc.ref_call("model", "model", timeout=1800, path=path, tokens=toks,
+                         n_decode=c["ref_decode"], d_model=c["d"], vocab=c["vocab"])
+    finally:
+        os.unlink(path)
+        os.rmdir(td)
+    # this library, same layers, same tokens, teacher-forced with the
+    # reference's picks
+    model_small.reset()
+    rows = model_small.prefill(toks)
+    errs, rels = [], []
+
+    def cmp(got, want):
+        got = np.asarray(got, np.float64)
+        want = np.asarray(want, np.float64)
+        errs.append(float(np.abs(got - want).max()))
+        rels.append(float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)))
+
+    cmp(rows, r["rows"])
+    cmp(model_small.logits(len(toks) - 1), r["logits"][0])
+    for i, t in enumerate(r["tokens"]):
+        cmp(model_small.decode(int(t), len(toks) + i), r["drows"][i])
+        cmp(model_small.logits(0), r["logits"][i + 1])
+    picks_ok = True
+    model_small.reset()
+    picks = model_small.generate(toks, c["ref_decode"])
+    for i, t in enumerate(r["tokens"]):
+        top2 = np.sort(r["logits"][i])[-2:]
+        if top2[1] - top2[0] < 1e-3:
+            break
+        picks_ok = picks_ok and int(picks[i]) == int(t)
+    model_small.reset()
+    scale = L / c["layers"]
+    pf = float(r["prefill_seconds"])
+    dc = float(r["decode_seconds"])
+    cpu = {"prefill_tok_s": len(toks) / pf * scale, "decode_tok_s": c["ref_decode"] / dc * scale,
+           "unit": "tokens/s", "cores": physical_cores(), "kind": "reference",
+           "sample": f"the reference's olmoe.c/llama.c forward (AVX-512 build, its thread pool "
+                     f"on every core) on {L} of {c['layers']} layers of the same weights: a "
+                     f"{len(toks)}-token prefill ({pf:.2f} s) and {c['ref_decode']} greedy "
+                     f"decode steps with lm_head ({dc:.2f} s); tokens/s scaled by "
+                     f"{L}/{c['layers']} layers",
+           "gguf_write_s": write_s}
+    parity = {"pass": bool(max(errs) <= 2e-3 and max(rels) <= 1e-3 and picks_ok),
+              "max_abs": max(errs), "rel_l2": max(rels), "greedy_picks_match": picks_ok,
+              "against": "the reference's own model code (oracle/_ref/libref_model.so) on a "
+                         f"GGUF of the same bytes, {L} layers",
+              "checked": f"{len(toks)} prefill rows, {c['ref_decode']} decode rows, "
+                         f"{c['ref_decode'] + 1} logit rows, greedy picks",
+              "tolerance": "max-abs 2e-3, rel-L2 1e-3"}
+    return cpu, parity
+
+
+def run_model_leg(moe, torch, torch_stream, cfg_name, runs=3, with_ref=True, clocks_dev=0):
+    """One whole-model config on one GPU: weights generated in HBM, the
+    model built from them (moe_model_create), then greedy generation of the
+    config's decode steps after its prompt, timed by the model's CUDA events
+    (prefill with the first pick; decode steps with lm_head and pick) and,
+    for e2e, by the host clock around the call (host prompt in, host tokens
+    out).  One warm-up generation; `runs` timed ones, median reported."""
+    gg = load_gguf_module()
+    c = MODEL_CONFIGS[cfg_name]
+    stream = torch_stream.cuda_stream
+    t0 = time.perf_counter()
+    tensors = synth_model(moe, torch, gg, c, stream)
+    synth_s = time.perf_counter() - t0
+
+    def get(name):
+        t, dt, dims = tensors[name]
+        return moe.tensor_at(t.data_ptr(), dt, dims)
+
+    small = None
+    if with_ref and c["ref_layers"] < c["layers"]:
+        small = moe.Model.build(model_kv(c, c["ref_layers"]), get)
+    t0 = time.perf_counter()
+    model = moe.Model.build(model_kv(c, c["layers"]), get)
+    create_s = time.perf_counter() - t0
+    cpu, parity = None, None
+    if with_ref:
+        cpu, parity = model_reference_sample(moe, torch, gg, c, tensors, small or model)
+    if small is not None:
+        small.close()
+    del tensors
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    prompt = np.random.default_rng(c["seed"]).integers(0, c["vocab"], c["prompt"]).astype(np.int32)
+    n = c["decode"]
+    model.reset()
+    model.generate(prompt, n)
+    model.reset()
+    clocks = ClockSampler(clocks_dev)
+    clocks.start()
+    pf, dc, wall, made = [], [], [], 0
+    for _ in range(runs):
+        w0 = time.perf_counter()
+        picks = model.generate(prompt, n)
+        wall.append(time.perf_counter() - w0)
+        made = picks.size
+        a, b = model.timing()
+        pf.append(a)
+        dc.append(b)
+        model.reset()
+    clk = clocks.stop()
+    _, _, dev_bytes = model.info()
+    status = model.status()
+    model.close()
+    pf_ms, dc_ms, wall_s = float(np.median(pf)), float(np.median(dc)), float(np.median(wall))
+    steps = made - 1
+    hbm_peak, bf16_peak, peak_kind = measured_peaks()
+    at = c["prompt"] + steps / 2
+    dbytes = model_decode_bytes(c, at)
+    dec_tok_s = steps / (dc_ms / 1e3) if steps else None
+    flops = model_prefill_flops(c, c["prompt"])
+    return {
+        "workload": f"{cfg_name}: {c['name']}; {c['prompt']}-token uniform-random prompt, then "
+                    f"{n} greedy decode steps with KV cache (seed {c['seed']})",
+        "prefill_tok_s": c["prompt"] / (pf_ms / 1e3), "prefill_ms": pf_ms,
+        "decode_tok_s": dec_tok_s, "decode_ms_per_token": dc_ms / max(steps, 1),
+        "decode_steps": steps, "unit": "tokens/s",
+        "e2e": {"tok_s": (c["prompt"] + steps) / wall_s, "seconds": wall_s,
+                "h2d_bytes": int(prompt.nbytes), "d2h_bytes": int(4 * made),
+                "what": "moe_model_generate from host token ids to host picks, host clock"},
+        "decode_roofline": {"bound": "hbm", "bytes_per_token": dbytes,
+                            "achieved_gbs": dbytes * dec_tok_s / 1e9 if dec_tok_s else None,
+                            "peak_gbs": hbm_peak, "frac": (dbytes * dec_tok_s / 1e9 / hbm_peak)
+                            if dec_tok_s else None, "peak_source": peak_kind,
+                            "cache_rows_mean": at},
+        "prefill_roofline": {"bound": "tensor", "flops": flops,
+                             "achieved_tflops": flops / (pf_ms / 1e3) / 1e12,
+                             "peak_tflops": bf16_peak,
+                             "frac": flops / (pf_ms / 1e3) / 1e12 / bf16_peak},
+        "cpu_baseline": cpu, "parity": parity, "clocks": clk,
+        "device_status": "ok" if status == 0 else status,
+        "device_bytes": dev_bytes, "synth_s": synth_s, "create_s": create_s,
+        "timing": f"CUDA events inside moe_model_generate, median of {runs} runs after one "
+                  "warm-up; decode steps replay one CUDA graph each",
+    }
+
+
+def load_gguf_module():
+    import importlib.util
+    p = os.path.join(ROOT, "llm.c_b200", "gguf.py")
+    spec = importlib.util.spec_from_file_location("moe_gguf", p)
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1081,7 +1361,11 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check at N > 1")
     ap.add_argument("--no-replicated", action="store_true",
                     help="skip the replicated-token leg at N > 1")
-    ap.add_argument("--only", choices=["gemv", "dense"],
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the whole-model legs (configs 2 and 3)")
+    ap.add_argument("--models", default="config2,config3",
+                    help="whole-model configs timed at N=1")
+    ap.add_argument("--only", choices=["gemv", "dense", "config2", "config3"],
                     help="run one leg alone on one GPU (for profilers) and print its result")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -1093,9 +1377,13 @@ def main():
         run_reference(args, rank, world)
     elif args.only:
         torch, moe, _, torch_stream = init_rank(1, local_rank)
-        leg = run_config1_gemv if args.only == "gemv" else run_dense_gemm
-        print(json.dumps({"only": args.only,
-                          "result": leg(moe, torch_stream.cuda_stream, torch_stream)}), flush=True)
+        if args.only in MODEL_CONFIGS:
+            res = run_model_leg(moe, torch, torch_stream, args.only, with_ref=not args.no_cpu,
+                                clocks_dev=local_rank)
+        else:
+            leg = run_config1_gemv if args.only == "gemv" else run_dense_gemm
+            res = leg(moe, torch_stream.cuda_stream, torch_stream)
+        print(json.dumps({"only": args.only, "result": res}), flush=True)
     else:
         run_ours(args, rank, world, local_rank)
 

@@ -397,6 +397,10 @@ MOE_API int moe_model_logits(moe_model *m, size_t row, float *logits);
  * number (>= 1) or an error status. */
 MOE_API int moe_model_generate(moe_model *m, const int *prompt, size_t T, int n, int eos,
 			       int *tokens);
+/* device time (CUDA events on the model's stream) of the last
+ * moe_model_generate: the prompt's prefill with the first pick, and the
+ * decode steps with their picks (an eos check adds a host read per step) */
+MOE_API int moe_model_timing(moe_model *m, float *prefill_ms, float *decode_ms);
 /* empty the KV cache and reset the position (a new sequence) */
 MOE_API int moe_model_reset(moe_model *m);
 /* waits for the device; MOE_OK or the first error a kernel recorded since

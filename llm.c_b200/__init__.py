@@ -119,6 +119,7 @@ SIGNATURES = {
     "moe_model_logits": (_I, [_P, _SZ, _P]),
     "moe_model_generate": (_I, [_P, _P, _SZ, _I, _I, _P]),
     "moe_model_reset": (_I, [_P]),
+    "moe_model_timing": (_I, [_P, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "moe_model_status": (_I, [_P]),
     "moe_model_info": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64), C.POINTER(_SZ)]),
 }
@@ -165,6 +166,24 @@ def reset(device: int = 0):
 # ------------------------------------------------------------------ tensors
 def row_bytes(qtype: int, cols: int) -> int:
     return {Q8_0: cols // 32 * 34, Q4_0: cols // 32 * 18, F32: cols * 4}[qtype]
+
+
+def tensor_at(ptr: int, qtype: int, dims) -> MoeTensor:
+    """tensor_t view of a raw (host or device) pointer"""
+    t = MoeTensor()
+    if qtype == F32:
+        t.data = ptr
+    else:
+        t.qdata = ptr
+    t.type = qtype
+    t.ndim = len(dims)
+    n = 1
+    for i, dd in enumerate(dims):
+        t.dim[i] = dd
+        n *= dd
+    t.totlen = n
+    t.maxcap = n
+    return t
 
 
 def tensor(arr: np.ndarray, qtype: int = F32, dims=None) -> MoeTensor:
@@ -470,7 +489,15 @@ class Model:
     def from_gguf(cls, reader) -> "Model":
         """every tensor the model code asks gguf.c for (olmoe.c:163-183,
         llama.c:135-175), by name, from a llm.c_b200.gguf.GGUFReader"""
-        kv = reader.kv
+        def get(name):
+            arr, dt, dims = reader.tensor(name)
+            return tensor(arr, dt, dims)
+        return cls.build(reader.kv, get)
+
+    @classmethod
+    def build(cls, kv: dict, get) -> "Model":
+        """from GGUF metadata `kv` and get(name) -> MoeTensor (host or
+        device payload)"""
         arch = kv["general.architecture"]
         a = arch
         L = kv[f"{a}.block_count"]
@@ -481,8 +508,7 @@ class Model:
         keep = []
 
         def t(name):
-            arr, dt, dims = reader.tensor(name)
-            mt = tensor(arr, dt, dims)
+            mt = get(name)
             keep.append(mt)
             return C.pointer(mt)
 
@@ -496,7 +522,7 @@ class Model:
         desc.arch = ARCH_OLMOE if arch == "olmoe" else ARCH_LLAMA
         desc.n_layers, desc.d_model, desc.n_heads, desc.n_kv_heads = L, d, H, kvh
         desc.head_len = d // H
-        desc.vocab = len(kv["tokenizer.ggml.tokens"])
+        desc.vocab = kv.get("vocab") or len(kv["tokenizer.ggml.tokens"])
         desc.context = kv[f"{a}.context_length"]
         if arch != "olmoe":
             desc.context = min(desc.context, 8192)   # llama.c:92-94
@@ -560,6 +586,12 @@ class Model:
 
     def reset(self):
         check(lib().moe_model_reset(self.h))
+
+    def timing(self):
+        """(prefill ms, decode ms) of the last generate, CUDA events"""
+        a, b = C.c_float(), C.c_float()
+        check(lib().moe_model_timing(self.h, C.byref(a), C.byref(b)))
+        return a.value, b.value
 
     def status(self):
         return lib().moe_model_status(self.h)

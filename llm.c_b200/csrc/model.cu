@@ -619,6 +619,8 @@ struct moe_model {
 	cudaGraphExec_t gexec = nullptr;
 	bool graphable = true;
 	std::vector<int64_t> graph_rows;  // each MoE layer's scratch rows at capture
+	cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // generate: start, first pick, end
+	bool timed = false;
 };
 
 namespace {
@@ -1017,6 +1019,9 @@ void free_model(moe_model *m)
 		cudaFree(p);
 	if (m->hstate)
 		cudaFreeHost(m->hstate);
+	for (cudaEvent_t e : m->ev)
+		if (e)
+			cudaEventDestroy(e);
 	moe::dense_scratch_free(m->ds);
 	delete m;
 }
@@ -1265,6 +1270,11 @@ int moe_model_generate(moe_model *m, const int *prompt, size_t T, int n, int eos
 	std::vector<int> pos(T);
 	for (size_t i = 0; i < T; i++)
 		pos[i] = (int)(m->mpos + (int64_t)i);
+	for (cudaEvent_t &e : m->ev)
+		if (!e)
+			MCK(cudaEventCreate(&e));
+	m->timed = false;
+	MCK(cudaEventRecord(m->ev[0], m->st));
 	MRC(prefill_impl(m, prompt, pos.data(), (int64_t)T));
 	m->mpos += (int64_t)T;
 	// the first pick, from the last prompt row (olmoe.c:559-564)
@@ -1273,6 +1283,7 @@ int moe_model_generate(moe_model *m, const int *prompt, size_t T, int n, int eos
 	MCK(cudaMemsetAsync(m->state + S_STEP, 0, 4, m->st));
 	MCK(moe::launch_argmax_advance(m->logits, (int)m->V, (int)m->C, m->state, m->picks,
 				       (int)m->pick_cap, 0, m->st));
+	MCK(cudaEventRecord(m->ev[1], m->st));
 	int made = 1;
 	int last = -1;
 	auto read_picks = [&](int from, int to) -> int {
@@ -1305,10 +1316,24 @@ int moe_model_generate(moe_model *m, const int *prompt, size_t T, int n, int eos
 		MRC(decode_impl(m, 0, p, false, made == 1));
 		made++;
 	}
+	MCK(cudaEventRecord(m->ev[2], m->st));
 	if (copied < made)
 		MRC(read_picks(copied, made));
 	MRC(take_state_error(m));
+	m->timed = true;
 	return made;
+}
+
+int moe_model_timing(moe_model *m, float *prefill_ms, float *decode_ms)
+{
+	if (!m || !m->timed)
+		return mfail(MOE_ERR_INVALID, "moe_model_timing: no completed moe_model_generate");
+	MCK(cudaEventSynchronize(m->ev[2]));
+	if (prefill_ms)
+		MCK(cudaEventElapsedTime(prefill_ms, m->ev[0], m->ev[1]));
+	if (decode_ms)
+		MCK(cudaEventElapsedTime(decode_ms, m->ev[1], m->ev[2]));
+	return MOE_OK;
 }
 
 int moe_model_status(moe_model *m)

@@ -138,6 +138,16 @@ class GGUFWriter:
             raise ValueError(f"{name}: {len(raw)} bytes for dims {dims}, want {want}")
         self.tensors.append((name, tuple(int(d) for d in dims), _GGML_OF[dtype], raw))
 
+    def add_tensor_lazy(self, name: str, dtype: int, dims, fetch):
+        """a tensor whose bytes fetch() returns when the file is written"""
+        n = int(np.prod(dims))
+        want = n * 4 if dtype == F32 else n // 32 * (34 if dtype == Q8_0 else 18)
+        self.tensors.append((name, tuple(int(d) for d in dims), _GGML_OF[dtype], (want, fetch)))
+
+    @staticmethod
+    def _size(raw):
+        return raw[0] if isinstance(raw, tuple) else len(raw)
+
     def write(self, path: str):
         head = struct.pack("<IIQQ", GGUF_MAGIC, 3, len(self.tensors), len(self.kv))
         for key, t, payload in self.kv:
@@ -145,7 +155,7 @@ class GGUFWriter:
         offs, off = [], 0
         for name, dims, t, raw in self.tensors:
             offs.append(off)
-            off = (off + len(raw) + ALIGN - 1) // ALIGN * ALIGN
+            off = (off + self._size(raw) + ALIGN - 1) // ALIGN * ALIGN
         for (name, dims, t, raw), o in zip(self.tensors, offs):
             ggml_dims = dims[::-1]   # innermost first, as ggml writes them
             head += self._str(name) + struct.pack("<I", len(ggml_dims))
@@ -155,6 +165,11 @@ class GGUFWriter:
         with open(path, "wb") as f:
             f.write(head + b"\0" * pad)
             for (name, dims, t, raw), o in zip(self.tensors, offs):
+                if isinstance(raw, tuple):
+                    want, fetch = raw
+                    raw = np.ascontiguousarray(fetch()).tobytes()
+                    if len(raw) != want:
+                        raise ValueError(f"{name}: {len(raw)} bytes, want {want}")
                 f.write(raw)
                 f.write(b"\0" * ((-len(raw)) % ALIGN))
 
@@ -172,44 +187,120 @@ def _norms(seed: int, norm_sd: float):
     return lambda n: (1.0 + rng.normal(0.0, norm_sd, size=n)).astype(np.float32)
 
 
+def olmoe_plan(layers: int, d: int, heads: int, n_exp: int, top_k: int, d_ff: int, vocab: int,
+               context: int = 4096, rope_theta: float = 10000.0):
+    """(metadata setter, tensors) of an OLMoE-architecture file, in file
+    order: (name, dims outermost first, kind) with kind "mat" (quantized
+    N(0, sd)), "router" (F32 N(0, sd)) or "norm" (F32 RMSNorm weight); the
+    names and shapes olmoe_load asks for (olmoe.c:163-183)"""
+    def meta(w):
+        w.add_str("general.architecture", "olmoe")
+        for k, v in (("context_length", context), ("embedding_length", d),
+                     ("attention.head_count", heads), ("block_count", layers),
+                     ("expert_count", n_exp), ("expert_used_count", top_k),
+                     ("feed_forward_length", d_ff)):
+            w.add_u32("olmoe." + k, v)
+        w.add_f32("olmoe.rope.freq_base", rope_theta)
+        w.add_str_array("tokenizer.ggml.tokens", _vocab(vocab))
+        w.add_u32("tokenizer.ggml.bos_token_id", 1)
+        w.add_u32("tokenizer.ggml.eos_token_id", 2)
+    ts = [("token_embd.weight", (vocab, d), "mat"), ("output.weight", (vocab, d), "mat"),
+          ("output_norm.weight", (d,), "norm")]
+    for i in range(layers):
+        p = f"blk.{i}."
+        ts.append((p + "attn_norm.weight", (d,), "norm"))
+        for n in ("attn_q", "attn_k", "attn_v", "attn_output"):
+            ts.append((p + n + ".weight", (d, d), "mat"))
+        for n in ("attn_q_norm", "attn_k_norm", "ffn_norm"):
+            ts.append((p + n + ".weight", (d,), "norm"))
+        ts.append((p + "ffn_gate_inp.weight", (n_exp, d), "router"))
+        ts.append((p + "ffn_gate_exps.weight", (n_exp, d_ff, d), "mat"))
+        ts.append((p + "ffn_up_exps.weight", (n_exp, d_ff, d), "mat"))
+        ts.append((p + "ffn_down_exps.weight", (n_exp, d, d_ff), "mat"))
+    return meta, ts
+
+
+def mixtral_plan(layers: int, d: int, q_heads: int, kv_heads: int, n_exp: int, top_k: int,
+                 d_ff: int, vocab: int, context: int = 4096, rope_theta: float = 1e6):
+    """the same for the llama architecture with experts (llama.c:92-175)"""
+    hl = d // q_heads
+
+    def meta(w):
+        w.add_str("general.architecture", "llama")
+        for k, v in (("context_length", context), ("embedding_length", d),
+                     ("attention.head_count", q_heads), ("attention.head_count_kv", kv_heads),
+                     ("block_count", layers), ("expert_count", n_exp),
+                     ("expert_used_count", top_k), ("feed_forward_length", d_ff)):
+            w.add_u32("llama." + k, v)
+        w.add_f32("llama.rope.freq_base", rope_theta)
+        # llama_load builds the vocabulary tables (llama.c:108 -> vocab.c:
+        # 323-360): a SentencePiece ("llama") vocabulary with token types
+        # and scores
+        w.add_str("tokenizer.ggml.model", "llama")
+        w.add_str_array("tokenizer.ggml.tokens", _vocab(vocab))
+        w.add_i32_array("tokenizer.ggml.token_type", np.ones(vocab, np.int32))
+        w.add_f32_array("tokenizer.ggml.scores", np.zeros(vocab, np.float32))
+        w.add_u32("tokenizer.ggml.bos_token_id", 1)
+        w.add_u32("tokenizer.ggml.eos_token_id", 2)
+    ts = [("token_embd.weight", (vocab, d), "mat"), ("output.weight", (vocab, d), "mat"),
+          ("output_norm.weight", (d,), "norm")]
+    for i in range(layers):
+        p = f"blk.{i}."
+        ts.append((p + "attn_norm.weight", (d,), "norm"))
+        ts.append((p + "attn_q.weight", (q_heads * hl, d), "mat"))
+        ts.append((p + "attn_k.weight", (kv_heads * hl, d), "mat"))
+        ts.append((p + "attn_v.weight", (kv_heads * hl, d), "mat"))
+        ts.append((p + "attn_output.weight", (d, q_heads * hl), "mat"))
+        ts.append((p + "ffn_norm.weight", (d,), "norm"))
+        ts.append((p + "ffn_gate_inp.weight", (n_exp, d), "router"))
+        for e in range(n_exp):
+            ts.append((p + f"ffn_gate.{e}.weight", (d_ff, d), "mat"))
+            ts.append((p + f"ffn_up.{e}.weight", (d_ff, d), "mat"))
+            ts.append((p + f"ffn_down.{e}.weight", (d, d_ff), "mat"))
+    return meta, ts
+
+
+def write_plan(path: str, plan, qtype: int, seed: int, sd: float = 0.02, norm_sd: float = 0.0):
+    """a random-init file: numpy's PCG64 stream `seed` for the matrices and
+    routers in file order, quantized on the host; RMSNorm weights from
+    _norms"""
+    meta, ts = plan
+    rng = np.random.default_rng(seed)
+    nrm = _norms(seed, norm_sd)
+    w = GGUFWriter()
+    meta(w)
+    for name, dims, kind in ts:
+        if kind == "norm":
+            w.add_tensor(name, nrm(dims[0]), F32, dims)
+        elif kind == "router":
+            w.add_tensor(name, rng.normal(0.0, sd, size=dims).astype(np.float32), F32, dims)
+        else:
+            w.add_tensor(name, quantize(qtype, rng.normal(0.0, sd, size=dims).astype(np.float32)),
+                         qtype, dims)
+    w.write(path)
+
+
+def write_plan_from(path: str, plan, qtype: int, fetch):
+    """a file whose tensor bytes come from fetch(name) (numpy array: fp32
+    values or uint8 blocks), called once per tensor while writing, so that
+    a model held elsewhere (device memory) is written without a host copy
+    of the whole of it"""
+    meta, ts = plan
+    w = GGUFWriter()
+    meta(w)
+    for name, dims, kind in ts:
+        dt = F32 if kind in ("norm", "router") else qtype
+        w.add_tensor_lazy(name, dt, dims, lambda name=name: fetch(name))
+    w.write(path)
+
+
 def write_olmoe(path: str, layers: int, d: int, heads: int, n_exp: int, top_k: int, d_ff: int,
                 vocab: int, seed: int = 2, context: int = 4096, rope_theta: float = 10000.0,
                 sd: float = 0.02, qtype: int = Q8_0, norm_sd: float = 0.0):
     """random-init OLMoE-architecture model (config 2: 16 layers, d 2048, 16
     heads, 64 experts top-8, d_ff 1024, vocab 50304, Q8_0, seed 2)"""
-    rng = np.random.default_rng(seed)
-    g = lambda *shape: rng.normal(0.0, sd, size=shape).astype(np.float32)  # noqa: E731
-    nrm = _norms(seed, norm_sd)
-    w = GGUFWriter()
-    w.add_str("general.architecture", "olmoe")
-    for k, v in (("context_length", context), ("embedding_length", d),
-                 ("attention.head_count", heads), ("block_count", layers),
-                 ("expert_count", n_exp), ("expert_used_count", top_k),
-                 ("feed_forward_length", d_ff)):
-        w.add_u32("olmoe." + k, v)
-    w.add_f32("olmoe.rope.freq_base", rope_theta)
-    w.add_str_array("tokenizer.ggml.tokens", _vocab(vocab))
-    w.add_u32("tokenizer.ggml.bos_token_id", 1)
-    w.add_u32("tokenizer.ggml.eos_token_id", 2)
-    w.add_tensor("token_embd.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
-    w.add_tensor("output.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
-    w.add_tensor("output_norm.weight", nrm(d), F32, (d,))
-    for i in range(layers):
-        p = f"blk.{i}."
-        w.add_tensor(p + "attn_norm.weight", nrm(d), F32, (d,))
-        for n in ("attn_q", "attn_k", "attn_v", "attn_output"):
-            w.add_tensor(p + n + ".weight", quantize(qtype, g(d, d)), qtype, (d, d))
-        w.add_tensor(p + "attn_q_norm.weight", nrm(d), F32, (d,))
-        w.add_tensor(p + "attn_k_norm.weight", nrm(d), F32, (d,))
-        w.add_tensor(p + "ffn_norm.weight", nrm(d), F32, (d,))
-        w.add_tensor(p + "ffn_gate_inp.weight", g(n_exp, d), F32, (n_exp, d))
-        w.add_tensor(p + "ffn_gate_exps.weight", quantize(qtype, g(n_exp, d_ff, d)), qtype,
-                     (n_exp, d_ff, d))
-        w.add_tensor(p + "ffn_up_exps.weight", quantize(qtype, g(n_exp, d_ff, d)), qtype,
-                     (n_exp, d_ff, d))
-        w.add_tensor(p + "ffn_down_exps.weight", quantize(qtype, g(n_exp, d, d_ff)), qtype,
-                     (n_exp, d, d_ff))
-    w.write(path)
+    write_plan(path, olmoe_plan(layers, d, heads, n_exp, top_k, d_ff, vocab, context,
+                                rope_theta), qtype, seed, sd, norm_sd)
 
 
 def write_mixtral(path: str, layers: int, d: int, q_heads: int, kv_heads: int, n_exp: int,
@@ -219,47 +310,8 @@ def write_mixtral(path: str, layers: int, d: int, q_heads: int, kv_heads: int, n
     """random-init Mixtral-architecture model ("llama" with experts; config 3:
     32 layers, d 4096, 32/8 heads, 8 experts top-2, d_ff 14336, vocab 32000,
     Q4_0, seed 3)"""
-    rng = np.random.default_rng(seed)
-    g = lambda *shape: rng.normal(0.0, sd, size=shape).astype(np.float32)  # noqa: E731
-    nrm = _norms(seed, norm_sd)
-    hl = d // q_heads
-    w = GGUFWriter()
-    w.add_str("general.architecture", "llama")
-    for k, v in (("context_length", context), ("embedding_length", d),
-                 ("attention.head_count", q_heads), ("attention.head_count_kv", kv_heads),
-                 ("block_count", layers), ("expert_count", n_exp),
-                 ("expert_used_count", top_k), ("feed_forward_length", d_ff)):
-        w.add_u32("llama." + k, v)
-    w.add_f32("llama.rope.freq_base", rope_theta)
-    # llama_load builds the vocabulary tables (llama.c:108 -> vocab.c:323-360):
-    # a SentencePiece ("llama") vocabulary with token types and scores
-    w.add_str("tokenizer.ggml.model", "llama")
-    w.add_str_array("tokenizer.ggml.tokens", _vocab(vocab))
-    w.add_i32_array("tokenizer.ggml.token_type", np.ones(vocab, np.int32))
-    w.add_f32_array("tokenizer.ggml.scores", np.zeros(vocab, np.float32))
-    w.add_u32("tokenizer.ggml.bos_token_id", 1)
-    w.add_u32("tokenizer.ggml.eos_token_id", 2)
-    w.add_tensor("token_embd.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
-    w.add_tensor("output.weight", quantize(qtype, g(vocab, d)), qtype, (vocab, d))
-    w.add_tensor("output_norm.weight", nrm(d), F32, (d,))
-    for i in range(layers):
-        p = f"blk.{i}."
-        w.add_tensor(p + "attn_norm.weight", nrm(d), F32, (d,))
-        w.add_tensor(p + "attn_q.weight", quantize(qtype, g(q_heads * hl, d)), qtype,
-                     (q_heads * hl, d))
-        for n in ("attn_k", "attn_v"):
-            w.add_tensor(p + n + ".weight", quantize(qtype, g(kv_heads * hl, d)), qtype,
-                         (kv_heads * hl, d))
-        w.add_tensor(p + "attn_output.weight", quantize(qtype, g(d, q_heads * hl)), qtype,
-                     (d, q_heads * hl))
-        w.add_tensor(p + "ffn_norm.weight", nrm(d), F32, (d,))
-        w.add_tensor(p + "ffn_gate_inp.weight", g(n_exp, d), F32, (n_exp, d))
-        for e in range(n_exp):
-            w.add_tensor(p + f"ffn_gate.{e}.weight", quantize(qtype, g(d_ff, d)), qtype, (d_ff, d))
-            w.add_tensor(p + f"ffn_up.{e}.weight", quantize(qtype, g(d_ff, d)), qtype, (d_ff, d))
-            w.add_tensor(p + f"ffn_down.{e}.weight", quantize(qtype, g(d, d_ff)), qtype,
-                         (d, d_ff))
-    w.write(path)
+    write_plan(path, mixtral_plan(layers, d, q_heads, kv_heads, n_exp, top_k, d_ff, vocab,
+                                  context, rope_theta), qtype, seed, sd, norm_sd)
 
 
 # ---------------------------------------------------------------- reader
