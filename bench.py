@@ -1293,6 +1293,7 @@ def run_model_leg(moe, torch, torch_stream, cfg_name, runs=3, with_ref=True, clo
         model.reset()
     clk = clocks.stop()
     _, _, dev_bytes = model.info()
+    mode = model.mode()
     status = model.status()
     model.close()
     pf_ms, dc_ms, wall_s = float(np.median(pf)), float(np.median(dc)), float(np.median(wall))
@@ -1323,6 +1324,7 @@ def run_model_leg(moe, torch, torch_stream, cfg_name, runs=3, with_ref=True, clo
         "cpu_baseline": cpu, "parity": parity, "clocks": clk,
         "device_status": "ok" if status == 0 else status,
         "device_bytes": dev_bytes, "synth_s": synth_s, "create_s": create_s,
+        "decode_step": mode,
         "timing": f"CUDA events inside moe_model_generate, median of {runs} runs after one "
                   "warm-up; decode steps replay one CUDA graph each",
     }

@@ -407,6 +407,10 @@ MOE_API int moe_model_reset(moe_model *m);
  * the last call (MOE_ERR_INVALID: a token id outside the vocabulary, a
  * position or cache row out of range; MOE_ERR_TIMEOUT from a MoE layer) */
 MOE_API int moe_model_status(moe_model *m);
+/* how the decode step runs (bits): 1 a captured CUDA graph (once a decode
+ * step has run), 2 the fused one-row kernels, 4 programmatic dependent
+ * launches; or an error status */
+MOE_API int moe_model_mode(moe_model *m);
 /* the cache size and device bytes the model holds */
 MOE_API int moe_model_info(moe_model *m, int64_t *cache_size, int64_t *pos, size_t *device_bytes);
 

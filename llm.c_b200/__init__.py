@@ -121,6 +121,7 @@ SIGNATURES = {
     "moe_model_reset": (_I, [_P]),
     "moe_model_timing": (_I, [_P, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "moe_model_status": (_I, [_P]),
+    "moe_model_mode": (_I, [_P]),
     "moe_model_info": (_I, [_P, C.POINTER(_I64), C.POINTER(_I64), C.POINTER(_SZ)]),
 }
 
@@ -595,6 +596,12 @@ class Model:
 
     def status(self):
         return lib().moe_model_status(self.h)
+
+    def mode(self) -> dict:
+        v = lib().moe_model_mode(self.h)
+        if v < 0:
+            check(v)
+        return {"graph": bool(v & 1), "fused": bool(v & 2), "pdl": bool(v & 4)}
 
     def info(self):
         cs, pos, nb = C.c_int64(), C.c_int64(), C.c_size_t()

@@ -123,6 +123,18 @@ __device__ __forceinline__ float warp_max(float v)
 	return v;
 }
 
+// Programmatic dependent launch: a kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may start while the
+// kernel before it on the stream is still running; it must not read that
+// kernel's output (or write what it reads) before griddep_wait() returns,
+// which waits for the earlier grid's completion and memory flush.  Without
+// the attribute both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents()
+{
+	asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // silu(g) * u exactly as nn.c:475-478 computes it: g / (1 + exp(-g)) * u,
 // each operation rounded once.
 __device__ __forceinline__ float swiglu(float g, float u)

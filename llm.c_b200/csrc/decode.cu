@@ -40,6 +40,10 @@
 
 namespace moe {
 
+// per-warp scratch of the CTA-local top-k (P1, few tokens): logits [64],
+// weights [32], ids [32]
+constexpr int kLocalTopkBytes = (64 + 32 + 32) * 4;
+
 // router tile of P0: RT tokens x RE experts, whole 2048-column row chunks
 // staged by 16 bulk copies (one per row, issued by 16 lanes at once).
 // Warps 0-3 compute: for 16 SIMD lanes, warp w owns lane quad w and its
@@ -381,11 +385,34 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	stamp(a.stamps, kStB1);
 
 	// ------------------------------------------------ P1: routing
-	// softmax + top-k of token t by warp 0 of CTA (units + t) % grid
+	// softmax + top-k of token t by warp 0 of CTA (units + t) % grid.  A few
+	// tokens on one rank: every CTA ranks every token itself instead (warp t
+	// takes token t), which saves the second grid barrier and a hop through
+	// global memory; CTA 0 writes the routing for the host.
+	const bool local_topk = !shard && T <= (int)(blockDim.x / 32) && NE <= 64;
+	int32_t *ids_all = reinterpret_cast<int32_t *>(smem + DS::RING_IDS);
+	float *wtok = reinterpret_cast<float *>(smem + DS::RING_IDS + kDecodeMaxPairsAll * 4);
 	{
 		float *lg = reinterpret_cast<float *>(smem);                 // [NE]
 		float *sel = lg + kMaxActive;                                // [2K]
-		for (int t = my_token0; t < T; t += gridDim.x) {
+		if (local_topk) {
+			if (warp < T) {
+				float *lgw = reinterpret_cast<float *>(smem + warp * kLocalTopkBytes);
+				float *sw = lgw + 64;
+				int32_t *sid = reinterpret_cast<int32_t *>(sw + 32);
+				for (int e = lane; e < NE; e += 32)
+					lgw[e] = __ldcg(a.logits + (int64_t)warp * NE + e);
+				__syncwarp();
+				topk_token<LANES>(lgw, a.router_bias, NE, K, a.mode_exact, a.renorm, sw, sid,
+						  ids_all + warp * K, wtok + warp * K, nullptr, nullptr);
+				if (blockIdx.x == 0)
+					for (int q = lane; q < K; q += 32) {
+						a.ids[(int64_t)warp * K + q] = ids_all[warp * K + q];
+						a.wts[(int64_t)warp * K + q] = wtok[warp * K + q];
+					}
+			}
+		}
+		for (int t = my_token0; !local_topk && t < T; t += gridDim.x) {
 			if (warp == 0) {
 				for (int e = lane; e < NE; e += 32)
 					lg[e] = __ldcg(a.logits + (int64_t)t * NE + e);
@@ -420,7 +447,7 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			if (tid < a.world)
 				wait_arrivals(a.routed[a.rank] + kEpFlagStride * tid, shard_epoch * gridDim.x,
 					      ep_wait, a.err);
-		} else if (tid == 0) {
+		} else if (tid == 0 && !local_topk) {
 			grid_sync(a.gbar, a.err);
 		}
 		__syncthreads();
@@ -429,7 +456,6 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		// every rank's) into its own shared memory.  The ids sit in the stage
 		// ring behind the dispatch scratch until the experts start.
 		int32_t *ds = reinterpret_cast<int32_t *>(smem);
-		int32_t *ids_all = reinterpret_cast<int32_t *>(smem + DS::RING_IDS);
 		int np = T * K;
 		const int32_t *idsrc = a.ids;
 		if (shard) {
@@ -442,10 +468,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 			np = same ? a.world * T * K : 0;
 			idsrc = hdr + kEpIdsHeader;
 		}
-		for (int i = tid; i < np; i += blockDim.x)
-			ids_all[i] = __ldcg(idsrc + i);
-		for (int i = tid; i < T * K; i += blockDim.x)
-			wts_s[i] = __fdiv_rn(1.0f, __ldcg(a.wts + i));  // 1 / w, the combine's divisor
+		if (!local_topk)
+			for (int i = tid; i < np; i += blockDim.x)
+				ids_all[i] = __ldcg(idsrc + i);
+		for (int i = tid; i < T * K; i += blockDim.x)   // 1 / w, the combine's divisor
+			wts_s[i] = __fdiv_rn(1.0f, local_topk ? wtok[i] : __ldcg(a.wts + i));
 		__syncthreads();
 		dispatch_body(ids_all, np, NE, a.first_expert, a.n_local, counts_s, offsets_s, perm_s,
 			      nullptr, active_s, nact_s, a.err, ds);
@@ -611,7 +638,9 @@ static cudaError_t launch_decode_t(const DecodeArgs &a, cudaStream_t st)
 	static_assert(RTile<LANES>::BYTES <= STAGES * StageLayout<QT>::BYTES,
 		      "the router tile fits in the stage ring");
 	static_assert((2 + kCoreThreads / 32) * kMaxActive * 4 <= DecodeSmem::RING_IDS &&
-			      DecodeSmem::RING_IDS + kDecodeMaxPairsAll * 4 <= STAGES * StageLayout<QT>::BYTES,
+			      (kCoreThreads / 32) * kLocalTopkBytes <= DecodeSmem::RING_IDS &&
+			      DecodeSmem::RING_IDS + kDecodeMaxPairsAll * 4 + (kCoreThreads / 32) * 32 * 4 <=
+				      STAGES * StageLayout<QT>::BYTES,
 		      "the dispatch scratch and the pair ids fit in the stage ring");
 	auto fn = moe_decode_kernel<QT, LANES, 8, 8, MT_DN, STAGES>;
 	cudaError_t e = ensure_smem(fn, smem);

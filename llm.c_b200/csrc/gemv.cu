@@ -150,7 +150,7 @@ __device__ __forceinline__ void pair_codes(uint32_t a, uint32_t (&ev)[2], uint32
 template <int QT, int NBW>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
-	       const float *__restrict__ x, float *__restrict__ y, int32_t *err)
+	       const float *__restrict__ x, float *__restrict__ y, int32_t *err, NormIn nin)
 {
 	constexpr int BB = QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES;
 	extern __shared__ __align__(128) uint8_t smem[];
@@ -176,6 +176,10 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		fence_mbar_init();
 	}
 	__syncthreads();
+	// launched as a dependent (model decode step): the next kernel may start
+	// its own prologue now; this one streams its (constant) weights at once
+	// and waits for the earlier kernel only before reading x
+	griddep_launch_dependents();
 
 	if (warp == kTcMath) {
 		// ---- copy warp: the rows of a tile, lane j copying row j
@@ -218,10 +222,41 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	// issued before the first is used.
 	{
 		float v[NBW];
+		griddep_wait();
+		if (nin.hidden) {
+			// x = rms_norm(hidden + delta) * weight (tensor_add, then
+			// rms_norm, nn.c:7-48); CTA 0 stores hidden + delta
 #pragma unroll
-		for (int j = 0; j < NBW; j++) {
-			const int b = warp + j * kTcMath;
-			v[j] = __ldg(x + (int64_t)b * 32 + lane);
+			for (int j = 0; j < NBW; j++) {
+				const int e = (warp + j * kTcMath) * 32 + lane;
+				v[j] = nin.delta ? __fadd_rn(nin.hidden[e], nin.delta[e]) : nin.hidden[e];
+				if (blockIdx.x == 0)
+					nin.hidden_out[e] = v[j];
+			}
+			float ss = 0.0f;
+#pragma unroll
+			for (int j = 0; j < NBW; j++)
+				ss = fmaf(v[j], v[j], ss);
+			ss = warp_sum(ss);
+			if (lane == 0)
+				red[warp] = ss;
+			asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
+			float tot = 0.0f;
+#pragma unroll
+			for (int q = 0; q < kTcMath; q++)
+				tot += red[q];
+			const float rms = sqrtf(tot / (float)(nb * 32) + nin.eps);
+#pragma unroll
+			for (int j = 0; j < NBW; j++) {
+				const int e = (warp + j * kTcMath) * 32 + lane;
+				v[j] = (v[j] / rms) * nin.weight[e];
+			}
+		} else {
+#pragma unroll
+			for (int j = 0; j < NBW; j++) {
+				const int b = warp + j * kTcMath;
+				v[j] = __ldg(x + (int64_t)b * 32 + lane);
+			}
 		}
 		const int t_k = (lane & 15) >> 2, hi = lane >= 16 ? 4 : 0;
 #pragma unroll
@@ -483,7 +518,8 @@ bool gemv1_supported(int qtype, int64_t rows, int64_t cols, uintptr_t w, uintptr
 
 template <int QT, int NBW>
 static cudaError_t launch_tc_t(const void *w, int64_t rows, int nb, const float *x, float *y,
-			       int32_t *err, int stages, size_t smem, cudaStream_t st)
+			       int32_t *err, int stages, size_t smem, const NormIn &nin, bool pdl,
+			       cudaStream_t st)
 {
 	auto fn = gemv_tc_kernel<QT, NBW>;
 	cudaError_t e = ensure_smem(fn, smem);
@@ -494,43 +530,67 @@ static cudaError_t launch_tc_t(const void *w, int64_t rows, int nb, const float 
 		grid = sm_count();
 	if (grid < 1)
 		grid = 1;
-	fn<<<(unsigned)grid, kTcThreads, smem, st>>>(static_cast<const uint8_t *>(w), (int)rows, nb,
-						       stages, x, y, err);
-	return cudaGetLastError();
+	cudaLaunchConfig_t cfg{};
+	cfg.gridDim = dim3((unsigned)grid);
+	cfg.blockDim = dim3(kTcThreads);
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = pdl ? 1 : 0;
+	return cudaLaunchKernelEx(&cfg, fn, static_cast<const uint8_t *>(w), (int)rows, nb, stages,
+				  x, y, err, nin);
 }
 
 template <int QT>
 static cudaError_t launch_tc(const void *w, int64_t rows, int64_t cols, const float *x, float *y,
-			     int32_t *err, int stages, cudaStream_t st)
+			     int32_t *err, int stages, const NormIn &nin, bool pdl, cudaStream_t st)
 {
 	const int nb = (int)(cols / QK);
 	const int64_t rb = (int64_t)nb * (QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES);
 	const size_t smem = tc_smem(stages, kTcRows * tc_row_stride(rb), nb);
 	switch (nb / kTcMath) {
 	case 2:
-		return launch_tc_t<QT, 2>(w, rows, nb, x, y, err, stages, smem, st);
+		return launch_tc_t<QT, 2>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	case 4:
-		return launch_tc_t<QT, 4>(w, rows, nb, x, y, err, stages, smem, st);
+		return launch_tc_t<QT, 4>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	case 6:
-		return launch_tc_t<QT, 6>(w, rows, nb, x, y, err, stages, smem, st);
+		return launch_tc_t<QT, 6>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	case 8:
-		return launch_tc_t<QT, 8>(w, rows, nb, x, y, err, stages, smem, st);
+		return launch_tc_t<QT, 8>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	case 10:
-		return launch_tc_t<QT, 10>(w, rows, nb, x, y, err, stages, smem, st);
+		return launch_tc_t<QT, 10>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	case 12:
-		return launch_tc_t<QT, 12>(w, rows, nb, x, y, err, stages, smem, st);
+		return launch_tc_t<QT, 12>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	default:
 		return cudaErrorInvalidValue;
 	}
 }
 
+bool gemv_norm_supported(int qtype, int64_t cols, uintptr_t w)
+{
+	return (qtype == kQ8_0 || qtype == kQ4_0) && tc_stages(qtype, cols) && w % 16 == 0;
+}
+
+cudaError_t launch_gemv_norm(const void *w, int qtype, int64_t rows, int64_t cols,
+			     const NormIn &nin, float *y, int32_t *err, bool pdl, cudaStream_t st)
+{
+	const int stages = tc_stages(qtype, cols);
+	if (!stages || (uintptr_t)w % 16 || !nin.hidden || !nin.weight || !nin.hidden_out)
+		return cudaErrorNotSupported;
+	return qtype == kQ8_0 ? launch_tc<kQ8_0>(w, rows, cols, nullptr, y, err, stages, nin, pdl, st)
+			      : launch_tc<kQ4_0>(w, rows, cols, nullptr, y, err, stages, nin, pdl, st);
+}
+
 cudaError_t launch_gemv1(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
-			 float *y, int32_t *err, cudaStream_t st)
+			 float *y, int32_t *err, cudaStream_t st, bool pdl)
 {
 	const int stages = tc_stages(qtype, cols);
 	if (stages && (uintptr_t)w % 16 == 0)
-		return qtype == kQ8_0 ? launch_tc<kQ8_0>(w, rows, cols, x, y, err, stages, st)
-				      : launch_tc<kQ4_0>(w, rows, cols, x, y, err, stages, st);
+		return qtype == kQ8_0 ? launch_tc<kQ8_0>(w, rows, cols, x, y, err, stages, NormIn{}, pdl, st)
+				      : launch_tc<kQ4_0>(w, rows, cols, x, y, err, stages, NormIn{}, pdl, st);
 	const int nb = (int)(cols / QK);
 	const size_t smem = (size_t)nb * kXPad * 4;
 	int64_t grid = (rows + kG1Threads / 32 - 1) / (kG1Threads / 32);

@@ -65,8 +65,21 @@ cudaError_t launch_expert_gemv(const GemvArgs &a, cudaStream_t st);
 // aligned W, else one warp per row (cols % 64 == 0, 4-byte aligned W);
 // 16-byte aligned x.  err (may be NULL) is set to 2 if a bounded wait expires.
 bool gemv1_supported(int qtype, int64_t rows, int64_t cols, uintptr_t w, uintptr_t x, uintptr_t y);
+// pdl: launched as a programmatic dependent of the kernel before it (the
+// weights stream at once; x is read after that kernel completes)
 cudaError_t launch_gemv1(const void *w, int qtype, int64_t rows, int64_t cols, const float *x,
-			 float *y, int32_t *err, cudaStream_t st);
+			 float *y, int32_t *err, cudaStream_t st, bool pdl = false);
+// the tensor-core GEMV with its x made in the prologue from the residual
+// stream: h = hidden + delta (delta may be NULL), x = rms_norm(h) * weight;
+// CTA 0 stores h into hidden_out (not hidden: the other CTAs still read it)
+struct NormIn {
+	const float *hidden = nullptr, *delta = nullptr, *weight = nullptr;
+	float *hidden_out = nullptr;
+	float eps = 1e-5f;
+};
+bool gemv_norm_supported(int qtype, int64_t cols, uintptr_t w);
+cudaError_t launch_gemv_norm(const void *w, int qtype, int64_t rows, int64_t cols,
+			     const NormIn &nin, float *y, int32_t *err, bool pdl, cudaStream_t st);
 
 // expert_mma.cu: tensor-core grouped expert GEMV (decode).  Same segment
 // semantics as GemvArgs; activations are fp16 hi/lo rows [row][2][cols]
@@ -252,10 +265,10 @@ cudaStream_t library_stream();
 // (err |= 1 for a token id outside [0, V))
 cudaError_t launch_embed_norm(const void *wte, int wtype, int64_t V, int E, const int32_t *tok,
 			      int T, const float *w, float eps, float *hidden, float *out,
-			      int32_t *err, cudaStream_t st);
+			      int32_t *err, cudaStream_t st, bool pdl = false);
 // hidden[t] += delta[t]; out[t] = rms_norm(hidden[t]) * w
 cudaError_t launch_add_norm(float *hidden, const float *delta, const float *w, int T, int E,
-			    float eps, float *out, cudaStream_t st);
+			    float eps, float *out, cudaStream_t st, bool pdl = false);
 // per token: q (and k) RMS-normed over the whole vector (qk_norm), RoPE on
 // the pairs (2i, 2i+1) of each head from the cos/sin table rope[pos][i];
 // q -> q_out [T, H*HL], k and v -> the layer's cache at rows size + t
@@ -278,14 +291,38 @@ cudaError_t launch_qk_rope(const QkvArgs &a, cudaStream_t st);
 // [H][attn_splits(C)][HL + 2] scratch) and merges them.
 constexpr int kAttnChunk = 64;
 inline int attn_splits(int C) { return (C + kAttnChunk - 1) / kAttnChunk; }
+// CTAs per head of the one-launch decode step (balanced row ranges)
+inline int attn_step_splits(int C) { return C < 16 ? C : 16; }
 cudaError_t launch_attention(const float *q, const float *kc, const float *vc, const int32_t *size,
 			     int T, int H, int KVH, int HL, int C, float scale_div, float *part,
 			     float *out, cudaStream_t st);
+// T = 1: QK-norm + RoPE of the step's q and k, the new cache row and the
+// split attention with the merge by each head's last CTA, in one launch
+struct AttnStepArgs {
+	const float *qkv;              // [(H + 2 KVH) * HL]
+	const float *q_norm, *k_norm;  // or NULL
+	const float2 *rope;
+	const int32_t *pos, *size;     // device scalars
+	float *kc, *vc;                // this layer's cache
+	float *part;                   // [H][attn_step_splits(C)][HL + 2]
+	int32_t *cnt;                  // [H] arrival counters, zero between launches
+	float *out;                    // [H * HL]
+	int H, KVH, C;
+	float eps, scale_div;
+	int32_t *err;
+};
+cudaError_t launch_attn_step(const AttnStepArgs &a, cudaStream_t st);
+// launch with programmatic stream serialization (see griddep_wait), unless
+// MOE_PDL=0 in the environment
+bool pdl_enabled();
+
 // greedy pick (main.c:189-193: the first maximum) of logits [V] into
 // state[0] and picks[state[6] % pick_cap] (state[6] counts the picks); with
 // advance, the decode state {tok, pos, size, model_pos} moves one row on
+// (scratch: device, at least 4 KB, zero before the first call)
 cudaError_t launch_argmax_advance(const float *logits, int V, int C, int32_t *state,
-				  int32_t *picks, int pick_cap, int advance, cudaStream_t st);
+				  int32_t *picks, int pick_cap, int advance, float *scratch,
+				  cudaStream_t st, bool pdl = false);
 // cache rows [drop, drop + keep) -> [0, keep) of every layer, head, K and V
 cudaError_t launch_kv_shift(float *kc, float *vc, int L, int KVH, int C, int HL, int keep,
 			    int drop, cudaStream_t st);

@@ -14,6 +14,7 @@
 #include "kernels.h"
 
 #include <float.h>
+#include <stdlib.h>
 
 namespace moe {
 
@@ -73,41 +74,112 @@ __device__ __forceinline__ void norm_row(const float *h, const float *w, float *
 		out[j] = (h[j] / rms) * w[j];
 }
 
+// the rows of the tokens' ids (tensor_pick_rows, tensor.c:263-293) and
+// their rms_norm; d_model <= 16 * 256 (REG): the row's loads all issued into
+// registers first
+template <bool REG>
 __global__ void __launch_bounds__(kNormThreads)
-embed_norm_kernel(const uint8_t *wte, int wtype, int64_t V, int E, const int32_t *tok,
-		  const float *w, float eps, float *hidden, float *out, int32_t *err)
+embed_norm_kernel(const uint8_t *__restrict__ wte, int wtype, int64_t V, int E,
+		  const int32_t *tok, const float *__restrict__ w, float eps,
+		  float *__restrict__ hidden, float *__restrict__ out, int32_t *err)
 {
 	__shared__ float red[32];
+	griddep_wait();
+	griddep_launch_dependents();
 	const int t = blockIdx.x;
 	const int id = tok[t];
 	float *h = hidden + (int64_t)t * E;
-	if (id < 0 || id >= V) {
-		if (threadIdx.x == 0 && err)
-			atomicOr(err, 1);
-		for (int j = threadIdx.x; j < E; j += blockDim.x)
-			h[j] = 0.0f;
+	const bool ok = id >= 0 && id < V;
+	if (!ok && threadIdx.x == 0 && err)
+		atomicOr(err, 1);
+	const int64_t rb = wtype == 0 ? (int64_t)E * 4
+			   : (int64_t)E / 32 * (wtype == 1 ? Q8_0_BYTES : Q4_0_BYTES);
+	const uint8_t *row = wte + (ok ? (int64_t)id * rb : 0);
+	if (REG) {
+		float v[16];
+#pragma unroll
+		for (int k = 0; k < 16; k++) {
+			const int j = threadIdx.x + k * kNormThreads;
+			v[k] = (ok && j < E) ? dequant_at(row, wtype, j) : 0.0f;
+		}
+		float ss = 0.0f;
+#pragma unroll
+		for (int k = 0; k < 16; k++) {
+			const int j = threadIdx.x + k * kNormThreads;
+			if (j < E)
+				h[j] = v[k];
+			ss = fmaf(v[k], v[k], ss);
+		}
+		const float rms = sqrtf(block_sum(ss, red) / (float)E + eps);
+#pragma unroll
+		for (int k = 0; k < 16; k++) {
+			const int j = threadIdx.x + k * kNormThreads;
+			if (j < E)
+				out[(int64_t)t * E + j] = (v[k] / rms) * w[j];
+		}
 	} else {
-		const int64_t rb = wtype == 0 ? (int64_t)E * 4
-				   : (int64_t)E / 32 * (wtype == 1 ? Q8_0_BYTES : Q4_0_BYTES);
-		const uint8_t *row = wte + (int64_t)id * rb;
 		for (int j = threadIdx.x; j < E; j += blockDim.x)
-			h[j] = dequant_at(row, wtype, j);
+			h[j] = ok ? dequant_at(row, wtype, j) : 0.0f;
+		__syncthreads();
+		norm_row(h, w, out + (int64_t)t * E, E, eps, red);
 	}
-	__syncthreads();
-	norm_row(h, w, out + (int64_t)t * E, E, eps, red);
 }
 
-// tensor_add (tensor.c:334-353) then rms_norm
+// tensor_add (tensor.c:334-353) then rms_norm.  d_model <= 16 * 256 and a
+// multiple of 4 (VEC): four float4 per thread, every load issued before the
+// first use (a strided loop would wait for each load in turn)
+template <bool VEC>
 __global__ void __launch_bounds__(kNormThreads)
-add_norm_kernel(float *hidden, const float *delta, const float *w, int E, float eps, float *out)
+add_norm_kernel(float *__restrict__ hidden, const float *__restrict__ delta,
+		const float *__restrict__ w, int E, float eps, float *__restrict__ out)
 {
 	__shared__ float red[32];
+	griddep_wait();
+	griddep_launch_dependents();
 	const int64_t o = (int64_t)blockIdx.x * E;
 	float *h = hidden + o;
-	for (int j = threadIdx.x; j < E; j += blockDim.x)
-		h[j] = h[j] + delta[o + j];
-	__syncthreads();
-	norm_row(h, w, out + o, E, eps, red);
+	if (VEC) {
+		const int n4 = E / 4;
+		float4 x[4], dl[4], wv[4];
+#pragma unroll
+		for (int k = 0; k < 4; k++) {
+			const int i = threadIdx.x + k * kNormThreads;
+			const bool in = i < n4;
+			const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+			x[k] = in ? reinterpret_cast<const float4 *>(h)[i] : z;
+			dl[k] = in && delta ? reinterpret_cast<const float4 *>(delta + o)[i] : z;
+			wv[k] = in ? reinterpret_cast<const float4 *>(w)[i] : z;
+		}
+		float s = 0.0f;
+#pragma unroll
+		for (int k = 0; k < 4; k++) {
+			x[k].x = __fadd_rn(x[k].x, dl[k].x);
+			x[k].y = __fadd_rn(x[k].y, dl[k].y);
+			x[k].z = __fadd_rn(x[k].z, dl[k].z);
+			x[k].w = __fadd_rn(x[k].w, dl[k].w);
+			s = fmaf(x[k].x, x[k].x, s);
+			s = fmaf(x[k].y, x[k].y, s);
+			s = fmaf(x[k].z, x[k].z, s);
+			s = fmaf(x[k].w, x[k].w, s);
+			const int i = threadIdx.x + k * kNormThreads;
+			if (i < n4)
+				reinterpret_cast<float4 *>(h)[i] = x[k];
+		}
+		const float rms = sqrtf(block_sum(s, red) / (float)E + eps);
+#pragma unroll
+		for (int k = 0; k < 4; k++) {
+			const int i = threadIdx.x + k * kNormThreads;
+			if (i < n4)
+				reinterpret_cast<float4 *>(out + o)[i] =
+					make_float4((x[k].x / rms) * wv[k].x, (x[k].y / rms) * wv[k].y,
+						    (x[k].z / rms) * wv[k].z, (x[k].w / rms) * wv[k].w);
+		}
+	} else {
+		for (int j = threadIdx.x; j < E; j += blockDim.x)
+			h[j] = h[j] + (delta ? delta[o + j] : 0.0f);
+		__syncthreads();
+		norm_row(h, w, out + o, E, eps, red);
+	}
 }
 
 // blockIdx.y: 0 = q, 1 = k, 2 = v of token blockIdx.x
@@ -247,6 +319,186 @@ attn_merge_kernel(const float *part, const int32_t *size, int C, int nsplit, flo
 	out[(int64_t)h * HL + e] = acc / L;
 }
 
+// Sum of squares of n floats (n % 4 == 0, n <= 16 * blockDim.x) with all
+// loads issued before the first use: four float4 per thread
+__device__ __forceinline__ float sumsq4(const float *__restrict__ v, int n, float *red)
+{
+	const int n4 = n / 4;
+	float4 x[4];
+#pragma unroll
+	for (int k = 0; k < 4; k++) {
+		const int i = threadIdx.x + k * blockDim.x;
+		x[k] = i < n4 ? reinterpret_cast<const float4 *>(v)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+	}
+	float s = 0.0f;
+#pragma unroll
+	for (int k = 0; k < 4; k++) {
+		s = fmaf(x[k].x, x[k].x, s);
+		s = fmaf(x[k].y, x[k].y, s);
+		s = fmaf(x[k].z, x[k].z, s);
+		s = fmaf(x[k].w, x[k].w, s);
+	}
+	return block_sum(s, red);
+}
+
+// One decode step (T = 1) of a layer's attention in one launch: grid (H,
+// kStepSplits), 8 warps.  CTA c of head h takes cache rows
+// [c AT / S, (c + 1) AT / S) of the AT = size + 1 rows.  Every CTA
+// normalises (QK-norm over the whole vector, olmoe.c:455-459) and rotates
+// (nn.c:192-219) its head's query; the CTA holding the new row (row `size`)
+// does the same for its KV head's key, stores key and value into the cache
+// and uses them from registers.  Each CTA's online-softmax partial goes to
+// part[h][c]; the head's last CTA to finish (arrival counter cnt[h], reset by
+// that CTA) merges them into out[h].  Rows are taken four at a time per
+// warp with their loads issued first.
+constexpr int kStepThreads = 256, kStepWarps = kStepThreads / 32;
+
+__global__ void __launch_bounds__(kStepThreads) attn_step_kernel(AttnStepArgs a)
+{
+	constexpr int HL = 128;
+	__shared__ float4 so[kStepWarps][32];
+	__shared__ float sml[kStepWarps][2];
+	__shared__ float red[32];
+	__shared__ int merge_here;
+	griddep_wait();   // qkv comes from the projection launched before
+	griddep_launch_dependents();
+	const int h = blockIdx.x, c = blockIdx.y, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+	const int S = gridDim.y;
+	const int size = *a.size, pos = *a.pos;
+	if (size < 0 || size >= a.C || pos < 0 || pos >= a.C) {
+		if (threadIdx.x == 0 && h == 0 && c == 0 && a.err)
+			atomicOr(a.err, 2);
+		return;
+	}
+	const int AT = size + 1;
+	const int r0 = (int)((int64_t)c * AT / S), r1 = (int)((int64_t)(c + 1) * AT / S);
+	const bool tail = c == S - 1;   // r1 == AT: this chunk holds the new row
+	const int group = a.H / a.KVH, kvh = h / group;
+	const int nq = a.H * HL, nk = a.KVH * HL;
+	const float *qs = a.qkv, *ks = a.qkv + nq, *vs = a.qkv + nq + nk;
+	float rq = 1.0f, rk = 1.0f;
+	if (a.q_norm) {
+		rq = sqrtf(sumsq4(qs, nq, red) / (float)nq + a.eps);
+		if (tail)
+			rk = sqrtf(sumsq4(ks, nk, red) / (float)nk + a.eps);
+	}
+	// lane owns elements 4 lane .. 4 lane + 3 of a head: pairs 2 lane, 2 lane + 1
+	const float2 c0 = a.rope[(int64_t)pos * (HL / 2) + 2 * lane];
+	const float2 c1 = a.rope[(int64_t)pos * (HL / 2) + 2 * lane + 1];
+	auto norm_rope = [&](const float *src, const float *nw, float r, int base) {
+		float4 v = reinterpret_cast<const float4 *>(src + base)[lane];
+		if (nw) {
+			const float4 w = reinterpret_cast<const float4 *>(nw + base)[lane];
+			v.x = (v.x / r) * w.x;
+			v.y = (v.y / r) * w.y;
+			v.z = (v.z / r) * w.z;
+			v.w = (v.w / r) * w.w;
+		}
+		return make_float4(v.x * c0.x - v.y * c0.y, v.x * c0.y + v.y * c0.x,
+				   v.z * c1.x - v.w * c1.y, v.z * c1.y + v.w * c1.x);
+	};
+	const float4 qv = norm_rope(qs, a.q_norm, rq, h * HL);
+	float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
+	const float *kb = a.kc + (int64_t)kvh * a.C * HL, *vb = a.vc + (int64_t)kvh * a.C * HL;
+	if (tail) {
+		knew = norm_rope(ks, a.k_norm, rk, kvh * HL);
+		vnew = reinterpret_cast<const float4 *>(vs + kvh * HL)[lane];
+		if (warp == 0 && h % group == 0) {
+			reinterpret_cast<float4 *>(a.kc + ((int64_t)kvh * a.C + size) * HL)[lane] = knew;
+			reinterpret_cast<float4 *>(a.vc + ((int64_t)kvh * a.C + size) * HL)[lane] = vnew;
+		}
+	}
+	float m = -FLT_MAX, l = 0.0f;
+	float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+	constexpr int U = 4;
+	for (int rb = r0 + warp; rb < r1; rb += kStepWarps * U) {
+		float4 kk[U], vv[U];
+#pragma unroll
+		for (int u = 0; u < U; u++) {
+			const int r = rb + u * kStepWarps;
+			const bool in = r < r1, fresh = r == size;
+			kk[u] = !in ? make_float4(0.f, 0.f, 0.f, 0.f)
+			       : fresh ? knew : reinterpret_cast<const float4 *>(kb + (int64_t)r * HL)[lane];
+			vv[u] = !in ? make_float4(0.f, 0.f, 0.f, 0.f)
+			       : fresh ? vnew : reinterpret_cast<const float4 *>(vb + (int64_t)r * HL)[lane];
+		}
+#pragma unroll
+		for (int u = 0; u < U; u++) {
+			if (rb + u * kStepWarps >= r1)
+				break;
+			float s = qv.x * kk[u].x;
+			s = fmaf(qv.y, kk[u].y, s);
+			s = fmaf(qv.z, kk[u].z, s);
+			s = fmaf(qv.w, kk[u].w, s);
+			s = warp_sum(s) / a.scale_div;
+			const float mn = fmaxf(m, s);
+			const float f = expf(m - mn), p = expf(s - mn);
+			l = fmaf(l, f, p);
+			o.x = fmaf(o.x, f, p * vv[u].x);
+			o.y = fmaf(o.y, f, p * vv[u].y);
+			o.z = fmaf(o.z, f, p * vv[u].z);
+			o.w = fmaf(o.w, f, p * vv[u].w);
+			m = mn;
+		}
+	}
+	if (lane == 0) {
+		sml[warp][0] = m;
+		sml[warp][1] = l;
+	}
+	__syncthreads();
+	float M = -FLT_MAX;
+	for (int w = 0; w < kStepWarps; w++)
+		if (sml[w][1] > 0.0f)
+			M = fmaxf(M, sml[w][0]);
+	const float fw = (l > 0.0f) ? expf(m - M) : 0.0f;
+	so[warp][lane] = make_float4(o.x * fw, o.y * fw, o.z * fw, o.w * fw);
+	__syncthreads();
+	float *pp = a.part + ((int64_t)h * S + c) * (HL + 2);
+	if (threadIdx.x < HL) {
+		const float *sf = reinterpret_cast<const float *>(so);
+		float acc = 0.0f;
+		for (int w = 0; w < kStepWarps; w++)
+			acc += sf[w * HL + threadIdx.x];
+		pp[threadIdx.x] = acc;
+	}
+	if (threadIdx.x == 0) {
+		float L = 0.0f;
+		for (int w = 0; w < kStepWarps; w++)
+			if (sml[w][1] > 0.0f)
+				L = fmaf(sml[w][1], expf(sml[w][0] - M), L);
+		pp[HL] = M;
+		pp[HL + 1] = L;   // 0 for a CTA without rows
+	}
+	// the head's last CTA merges (release: partial, then the count)
+	__threadfence();
+	__syncthreads();
+	if (threadIdx.x == 0)
+		merge_here = atomicAdd(a.cnt + h, 1) == S - 1;
+	__syncthreads();
+	if (!merge_here)
+		return;
+	__threadfence();
+	const float *hp = a.part + (int64_t)h * S * (HL + 2);
+	float Mx = -FLT_MAX;
+	for (int q = 0; q < S; q++)
+		if (__ldcg(hp + q * (HL + 2) + HL + 1) > 0.0f)
+			Mx = fmaxf(Mx, __ldcg(hp + q * (HL + 2) + HL));
+	float Ls = 0.0f, acc = 0.0f;
+	for (int q = 0; q < S; q++) {
+		const float Lq = __ldcg(hp + q * (HL + 2) + HL + 1);
+		if (Lq > 0.0f) {
+			const float f = expf(__ldcg(hp + q * (HL + 2) + HL) - Mx);
+			Ls = fmaf(Lq, f, Ls);
+			if (threadIdx.x < HL)
+				acc = fmaf(__ldcg(hp + q * (HL + 2) + threadIdx.x), f, acc);
+		}
+	}
+	if (threadIdx.x < HL)
+		a.out[(int64_t)h * HL + threadIdx.x] = acc / Ls;
+	if (threadIdx.x == 0)
+		a.cnt[h] = 0;   // ready for the next launch
+}
+
 // prefill: 16 query rows of one head per CTA against 64-row tiles of the
 // cache, online softmax (the reference forms the full masked score matrix,
 // olmoe.c:300-312: scores / sqrt(head_len), -1e4 above the diagonal, which
@@ -360,29 +612,20 @@ attn_prefill_kernel(const float *q, const float *kc, const float *vc, const int3
 // state = {tok, pos, size, model_pos}: the pick of this step becomes the next
 // step's token; olmoe_decode (olmoe.c:510-520): the cache grows by one row,
 // positions past the context are replaced by the cache size
-constexpr int kArgThreads = 1024;
+constexpr int kArgCtas = 64, kArgThreads = 256;
 
-__global__ void __launch_bounds__(kArgThreads)
-argmax_advance_kernel(const float *logits, int V, int C, int32_t *state, int32_t *picks,
-		      int pick_cap, int advance)
+__device__ __forceinline__ bool pick_better(float v, int i, float w, int j)
 {
-	__shared__ float bv[32];
-	__shared__ int bi[32];
-	float best = -FLT_MAX;
-	int idx = -1;
-	for (int i = threadIdx.x; i < V; i += blockDim.x)
-		if (idx < 0 || logits[i] > best) {
-			best = logits[i];
-			idx = i;
-		}
-	// the first maximum: larger value, or the same value at a lower index
-	auto better = [](float v, int i, float w, int j) {
-		return j >= 0 && (i < 0 || w > v || (w == v && j < i));
-	};
+	// the first maximum: a larger value, or the same value at a lower index
+	return j >= 0 && (i < 0 || w > v || (w == v && j < i));
+}
+
+__device__ __forceinline__ void block_argmax(float &best, int &idx, float *bv, int *bi)
+{
 	for (int off = 16; off; off >>= 1) {
 		const float w = __shfl_xor_sync(0xffffffffu, best, off);
 		const int j = __shfl_xor_sync(0xffffffffu, idx, off);
-		if (better(best, idx, w, j)) {
+		if (pick_better(best, idx, w, j)) {
 			best = w;
 			idx = j;
 		}
@@ -399,22 +642,79 @@ argmax_advance_kernel(const float *logits, int V, int C, int32_t *state, int32_t
 		for (int off = 16; off; off >>= 1) {
 			const float w = __shfl_xor_sync(0xffffffffu, best, off);
 			const int j = __shfl_xor_sync(0xffffffffu, idx, off);
-			if (better(best, idx, w, j)) {
+			if (pick_better(best, idx, w, j)) {
 				best = w;
 				idx = j;
 			}
 		}
-		if (lane == 0) {
-			const int tok = idx < 0 ? 0 : idx;
-			state[0] = tok;
-			picks[state[6] % pick_cap] = tok;
-			state[6] += 1;
-			if (advance) {
-				const int size = state[2] + 1, mpos = state[3] + 1;
-				state[2] = size;
-				state[3] = mpos;
-				state[1] = mpos >= C ? size : mpos;
+	}
+}
+
+// kArgCtas CTAs take contiguous slices of the logits (four loads per
+// thread in flight); the last CTA to finish (counter cnt, reset by it)
+// reduces their partial maxima in slice order and updates the state
+__global__ void __launch_bounds__(kArgThreads)
+argmax_advance_kernel(const float *logits, int V, int C, int32_t *state, int32_t *picks,
+		      int pick_cap, int advance, float *pv, int32_t *pi, int32_t *cnt)
+{
+	__shared__ float bv[32];
+	__shared__ int bi[32];
+	__shared__ int last;
+	griddep_wait();
+	const int chunk = (V + gridDim.x - 1) / gridDim.x;
+	const int b0 = blockIdx.x * chunk, b1 = min(V, b0 + chunk);
+	float best = -FLT_MAX;
+	int idx = -1;
+	for (int i0 = b0 + threadIdx.x; i0 < b1; i0 += 4 * kArgThreads) {
+		float v[4];
+#pragma unroll
+		for (int u = 0; u < 4; u++) {
+			const int i = i0 + u * kArgThreads;
+			v[u] = i < b1 ? logits[i] : -FLT_MAX;
+		}
+#pragma unroll
+		for (int u = 0; u < 4; u++) {
+			const int i = i0 + u * kArgThreads;
+			if (i < b1 && (idx < 0 || v[u] > best)) {
+				best = v[u];
+				idx = i;
 			}
+		}
+	}
+	block_argmax(best, idx, bv, bi);
+	if (threadIdx.x == 0) {
+		pv[blockIdx.x] = best;
+		pi[blockIdx.x] = idx;
+		__threadfence();
+		last = atomicAdd(cnt, 1) == (int)gridDim.x - 1;
+	}
+	__syncthreads();
+	if (!last)
+		return;
+	__threadfence();
+	best = -FLT_MAX;
+	idx = -1;
+	for (int c = threadIdx.x; c < (int)gridDim.x; c += blockDim.x) {
+		const float w = __ldcg(pv + c);
+		const int j = __ldcg(pi + c);
+		if (pick_better(best, idx, w, j)) {
+			best = w;
+			idx = j;
+		}
+	}
+	__syncthreads();
+	block_argmax(best, idx, bv, bi);
+	if (threadIdx.x == 0) {
+		*cnt = 0;
+		const int tok = idx < 0 ? 0 : idx;
+		state[0] = tok;
+		picks[state[6] % pick_cap] = tok;
+		state[6] += 1;
+		if (advance) {
+			const int size = state[2] + 1, mpos = state[3] + 1;
+			state[2] = size;
+			state[3] = mpos;
+			state[1] = mpos >= C ? size : mpos;
 		}
 	}
 }
@@ -431,26 +731,49 @@ __global__ void kv_shift_kernel(float *kc, float *vc, int C, int HL, int from, i
 		base[(int64_t)to * HL + i] = base[(int64_t)from * HL + i];
 }
 
+template <typename... P, typename... A>
+cudaError_t launch_k(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+		     bool pdl, A... args)
+{
+	cudaLaunchConfig_t cfg{};
+	cfg.gridDim = grid;
+	cfg.blockDim = block;
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = pdl ? 1 : 0;
+	return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace
 
 cudaError_t launch_embed_norm(const void *wte, int wtype, int64_t V, int E, const int32_t *tok,
 			      int T, const float *w, float eps, float *hidden, float *out,
-			      int32_t *err, cudaStream_t st)
+			      int32_t *err, cudaStream_t st, bool pdl)
 {
 	if (T <= 0)
 		return cudaSuccess;
-	embed_norm_kernel<<<T, kNormThreads, 0, st>>>(static_cast<const uint8_t *>(wte), wtype, V, E,
-						       tok, w, eps, hidden, out, err);
-	return cudaGetLastError();
+	if (E <= 16 * kNormThreads)
+		return launch_k(embed_norm_kernel<true>, dim3(T), dim3(kNormThreads), 0, st, pdl,
+				static_cast<const uint8_t *>(wte), wtype, V, E, tok, w, eps, hidden, out,
+				err);
+	return launch_k(embed_norm_kernel<false>, dim3(T), dim3(kNormThreads), 0, st, pdl,
+			static_cast<const uint8_t *>(wte), wtype, V, E, tok, w, eps, hidden, out, err);
 }
 
 cudaError_t launch_add_norm(float *hidden, const float *delta, const float *w, int T, int E,
-			    float eps, float *out, cudaStream_t st)
+			    float eps, float *out, cudaStream_t st, bool pdl)
 {
 	if (T <= 0)
 		return cudaSuccess;
-	add_norm_kernel<<<T, kNormThreads, 0, st>>>(hidden, delta, w, E, eps, out);
-	return cudaGetLastError();
+	if (E % 4 == 0 && E <= 16 * kNormThreads)
+		return launch_k(add_norm_kernel<true>, dim3(T), dim3(kNormThreads), 0, st, pdl, hidden,
+				delta, w, E, eps, out);
+	return launch_k(add_norm_kernel<false>, dim3(T), dim3(kNormThreads), 0, st, pdl, hidden,
+			delta, w, E, eps, out);
 }
 
 cudaError_t launch_qk_rope(const QkvArgs &a, cudaStream_t st)
@@ -493,12 +816,44 @@ cudaError_t launch_attention(const float *q, const float *kc, const float *vc, c
 	return cudaGetLastError();
 }
 
-cudaError_t launch_argmax_advance(const float *logits, int V, int C, int32_t *state,
-				  int32_t *picks, int pick_cap, int advance, cudaStream_t st)
+bool pdl_enabled()
 {
-	argmax_advance_kernel<<<1, kArgThreads, 0, st>>>(logits, V, C, state, picks, pick_cap,
-							 advance);
-	return cudaGetLastError();
+	static const bool on = [] {
+		const char *e = getenv("MOE_PDL");
+		return !(e && e[0] == '0');
+	}();
+	return on;
+}
+
+cudaError_t launch_attn_step(const AttnStepArgs &a, cudaStream_t st)
+{
+	if (a.KVH <= 0 || a.H % a.KVH)
+		return cudaErrorInvalidValue;
+	if (a.H * 128 > 16 * kStepThreads || a.KVH * 128 > 16 * kStepThreads)
+		return cudaErrorInvalidValue;   // sumsq4's reach
+	cudaLaunchConfig_t cfg{};
+	cfg.gridDim = dim3(a.H, attn_step_splits(a.C));
+	cfg.blockDim = dim3(kStepThreads);
+	cfg.dynamicSmemBytes = 0;
+	cfg.stream = st;
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = pdl_enabled() ? 1 : 0;
+	return cudaLaunchKernelEx(&cfg, attn_step_kernel, a);
+}
+
+cudaError_t launch_argmax_advance(const float *logits, int V, int C, int32_t *state,
+				  int32_t *picks, int pick_cap, int advance, float *scratch,
+				  cudaStream_t st, bool pdl)
+{
+	// scratch: kArgCtas floats, kArgCtas ints, one counter (zero)
+	float *pv = scratch;
+	int32_t *pi = reinterpret_cast<int32_t *>(scratch + kArgCtas);
+	int32_t *cnt = pi + kArgCtas;
+	return launch_k(argmax_advance_kernel, dim3(kArgCtas), dim3(kArgThreads), 0, st, pdl, logits,
+			V, C, state, picks, pick_cap, advance, pv, pi, cnt);
 }
 
 cudaError_t launch_kv_shift(float *kc, float *vc, int L, int KVH, int C, int HL, int keep,
@@ -525,6 +880,7 @@ cudaError_t launch_kv_shift(float *kc, float *vc, int L, int KVH, int C, int HL,
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <utility>
 #include <vector>
 
 namespace {
@@ -603,6 +959,9 @@ struct moe_model {
 	int64_t cap = 0;
 	float *hidden = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr,
 	      *proj = nullptr, *ffn = nullptr, *gate = nullptr, *up = nullptr;
+	float *hidden2 = nullptr;        // the decode step's second residual buffer
+	int32_t *attn_cnt = nullptr;     // [H] arrival counters of the fused attention
+	bool fused_step = false;         // T = 1 through the fused kernels
 	int32_t *tok = nullptr, *pos = nullptr;
 	std::vector<void *> act;         // the activation buffers (regrown)
 	float *part = nullptr;           // decode attention partials
@@ -610,6 +969,7 @@ struct moe_model {
 	int32_t *state = nullptr;        // device S_WORDS
 	int32_t *hstate = nullptr;       // pinned mirror
 	int32_t *picks = nullptr;        // greedy picks, ring of pick_cap
+	float *argbuf = nullptr;         // the pick's partial maxima and counter
 	int64_t pick_cap = 0;
 	int64_t logits_row = -1;         // row of xn whose logits m->logits holds
 	int64_t size = 0, mpos = 0;      // host mirrors of the cache size and model position
@@ -705,6 +1065,7 @@ int ensure_act(moe_model *m, int64_t T)
 		return MOE_OK;
 	};
 	MRC(get(&m->hidden, T * E * 4));
+	MRC(get(&m->hidden2, T * E * 4));
 	MRC(get(&m->xn, T * E * 4));
 	MRC(get(&m->qkv, T * nqkv * 4));
 	MRC(get(&m->q, T * m->nq * 4));
@@ -725,11 +1086,68 @@ int ensure_act(moe_model *m, int64_t T)
 
 namespace {
 
+// The decode step (T = 1) through the fused kernels, each launched as a
+// programmatic dependent of the one before: per layer the QKV GEMV takes the
+// residual add and attn_norm into its prologue (the residual stream moves
+// between two buffers), one launch does QK-norm + RoPE + cache row +
+// attention, then the O GEMV, the add + ffn_norm, and the MoE layer.
+int forward_step(moe_model *m, const int32_t *tok_d, const int32_t *pos_d)
+{
+	const int E = (int)m->E;
+	const float eps = 1e-5f;
+	const bool pdl = moe::pdl_enabled();
+	int32_t *size_d = m->state + S_SIZE, *err = m->state + S_ERR, *perr = m->state + S_PERR;
+	MCK(moe::launch_embed_norm(m->wte, m->wte_t, m->V, E, tok_d, 1, m->layers[0].attn_norm, eps,
+				   m->hidden, m->xn, err, m->st, pdl));
+	const int64_t nqkv = m->nq + 2 * m->nk;
+	const size_t per_layer = (size_t)(m->KVH * m->C * m->HL);
+	float *R = m->hidden, *R2 = m->hidden2;
+	const float *D = nullptr;
+	for (int64_t l = 0; l < m->L; l++) {
+		const moe_model::Layer &ly = m->layers[l];
+		moe::NormIn nin;
+		nin.hidden = R;
+		nin.delta = D;
+		nin.weight = ly.attn_norm;
+		nin.hidden_out = R2;
+		nin.eps = eps;
+		MCK(moe::launch_gemv_norm(ly.wqkv, ly.qkv_t, nqkv, E, nin, m->qkv, perr, pdl, m->st));
+		std::swap(R, R2);
+		moe::AttnStepArgs a{};
+		a.qkv = m->qkv;
+		a.q_norm = ly.q_norm;
+		a.k_norm = ly.k_norm;
+		a.rope = m->rope;
+		a.pos = pos_d;
+		a.size = size_d;
+		a.kc = m->kc + l * per_layer;
+		a.vc = m->vc + l * per_layer;
+		a.part = m->part;
+		a.cnt = m->attn_cnt;
+		a.out = m->att;
+		a.H = (int)m->H;
+		a.KVH = (int)m->KVH;
+		a.C = (int)m->C;
+		a.eps = eps;
+		a.scale_div = m->scale_div;
+		a.err = err;
+		MCK(moe::launch_attn_step(a, m->st));
+		MCK(moe::launch_gemv1(ly.wo, ly.o_t, E, m->nq, m->att, m->proj, perr, m->st, pdl));
+		MCK(moe::launch_add_norm(R, m->proj, ly.ffn_norm, 1, E, eps, m->xn, m->st, pdl));
+		MRC(moe_layer_forward(ly.moe, m->xn, m->ffn, 1, m->renorm ? MOE_RENORM : 0, m->st));
+		D = m->ffn;
+	}
+	MCK(moe::launch_add_norm(R, D, m->out_norm, 1, E, eps, m->xn, m->st, pdl));
+	return MOE_OK;
+}
+
 // One forward over T tokens (olmoe.c:409-502 / llama.c:459-558) on m->st:
 // tok_d/pos_d are device arrays of T ids and positions, the cache grows
 // from state[S_SIZE].  Leaves the final-normed rows in m->xn.
 int forward(moe_model *m, int64_t T, const int32_t *tok_d, const int32_t *pos_d)
 {
+	if (T == 1 && m->fused_step)
+		return forward_step(m, tok_d, pos_d);
 	const int E = (int)m->E;
 	const float eps = 1e-5f;
 	int32_t *size_d = m->state + S_SIZE, *err = m->state + S_ERR, *perr = m->state + S_PERR;
@@ -803,10 +1221,15 @@ int rotate(moe_model *m)
 int decode_step_body(moe_model *m)
 {
 	MRC(forward(m, 1, m->state + S_TOK, m->state + S_POS));
-	MRC(moe::dense_forward(m->ds, m->lm, m->lm_t, m->V, m->E, m->xn, 1, m->logits,
-			       m->state + S_PERR, m->st));
+	const bool pdl = m->fused_step && moe::pdl_enabled();
+	if (m->fused_step)
+		MCK(moe::launch_gemv1(m->lm, m->lm_t, m->V, m->E, m->xn, m->logits, m->state + S_PERR,
+				      m->st, pdl));
+	else
+		MRC(moe::dense_forward(m->ds, m->lm, m->lm_t, m->V, m->E, m->xn, 1, m->logits,
+				       m->state + S_PERR, m->st));
 	MCK(moe::launch_argmax_advance(m->logits, (int)m->V, (int)m->C, m->state, m->picks,
-				       (int)m->pick_cap, 1, m->st));
+				       (int)m->pick_cap, 1, m->argbuf, m->st, pdl));
 	return MOE_OK;
 }
 
@@ -836,16 +1259,23 @@ int capture(moe_model *m)
 	MCK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
 	const int rc = decode_step_body(m);
 	cudaGraph_t g = nullptr;
-	const cudaError_t e = cudaStreamEndCapture(m->st, &g);
+	cudaError_t e = cudaStreamEndCapture(m->st, &g);
 	if (rc != MOE_OK) {
 		if (g)
 			cudaGraphDestroy(g);
 		return rc;
 	}
-	if (e != cudaSuccess)
-		return mcuda(e, "moe_model: decode graph capture");
-	m->graph = g;
-	MCK(cudaGraphInstantiate(&m->gexec, g, 0));
+	if (e == cudaSuccess) {
+		m->graph = g;
+		e = cudaGraphInstantiate(&m->gexec, g, 0);
+	}
+	if (e != cudaSuccess) {
+		// a step that cannot be captured runs eagerly (same launches)
+		cudaGetLastError();
+		drop_graph(m);
+		m->graphable = false;
+		return MOE_OK;
+	}
 	m->graph_rows.clear();
 	for (const auto &ly : m->layers)
 		m->graph_rows.push_back(moe::layer_scratch_rows(ly.moe));
@@ -1071,12 +1501,12 @@ int decode_impl(moe_model *m, int tok, int64_t pos, bool host_tok, bool sync_sta
 	MRC(ensure_act(m, 1));
 	if (host_tok || sync_state || rotated)
 		MRC(write_state(m, pos, host_tok ? tok : -1));
-	if (m->graphable) {
+	if (m->graphable)
 		MRC(capture(m));
+	if (m->gexec)
 		MCK(cudaGraphLaunch(m->gexec, m->st));
-	} else {
+	else
 		MRC(decode_step_body(m));
-	}
 	m->size += 1;
 	m->mpos += 1;
 	m->last_T = 1;
@@ -1156,13 +1586,21 @@ int moe_model_create(moe_model **out, const moe_model_desc *desc)
 	if (rc == MOE_OK && step(dalloc(m, &v, cache)))
 		m->vc = static_cast<float *>(v);
 	if (rc == MOE_OK && step(build_rope(m)) &&
-	    step(dalloc(m, &v, (size_t)(m->H * moe::attn_splits((int)m->C) * (m->HL + 2)) * 4)))
+	    step(dalloc(m, &v, (size_t)(m->H * std::max(moe::attn_splits((int)m->C),
+						       moe::attn_step_splits((int)m->C)) *
+					(m->HL + 2)) * 4)))
 		m->part = static_cast<float *>(v);
 	if (rc == MOE_OK && step(dalloc(m, &v, (size_t)m->V * 4)))
 		m->logits = static_cast<float *>(v);
 	m->pick_cap = 4096;
 	if (rc == MOE_OK && step(dalloc(m, &v, (size_t)m->pick_cap * 4)))
 		m->picks = static_cast<int32_t *>(v);
+	if (rc == MOE_OK && step(dalloc(m, &v, 4096))) {
+		m->argbuf = static_cast<float *>(v);
+		const cudaError_t e = cudaMemset(v, 0, 4096);
+		if (e != cudaSuccess)
+			step(mcuda(e, "moe_model_create: pick scratch"));
+	}
 	if (rc == MOE_OK && step(dalloc(m, &v, S_WORDS * 4))) {
 		m->state = static_cast<int32_t *>(v);
 		cudaError_t e = cudaMemset(v, 0, S_WORDS * 4);
@@ -1184,6 +1622,27 @@ int moe_model_create(moe_model **out, const moe_model_desc *desc)
 			       moe::gemv1_supported(ly.qkv_t, m->nq + 2 * m->nk, m->E,
 						    (uintptr_t)ly.wqkv, al, al) &&
 			       moe::gemv1_supported(ly.o_t, m->E, m->nq, (uintptr_t)ly.wo, al, al);
+	// the fused decode step: tensor-core GEMVs for every one-row projection
+	// (the QKV one with the norm in its prologue)
+	m->fused_step = m->graphable && moe::gemv_norm_supported(m->lm_t, m->E, (uintptr_t)m->lm);
+	for (const auto &ly : m->layers)
+		m->fused_step = m->fused_step &&
+				moe::gemv_norm_supported(ly.qkv_t, m->E, (uintptr_t)ly.wqkv) &&
+				moe::gemv_norm_supported(ly.o_t, m->nq, (uintptr_t)ly.wo);
+	if (m->fused_step) {
+		void *c = nullptr;
+		rc = dalloc(m, &c, (size_t)m->H * 4);
+		if (rc == MOE_OK) {
+			const cudaError_t e = cudaMemset(c, 0, (size_t)m->H * 4);
+			if (e != cudaSuccess)
+				rc = mcuda(e, "moe_model_create: counters");
+		}
+		m->attn_cnt = static_cast<int32_t *>(c);
+		if (rc != MOE_OK) {
+			free_model(m);
+			return rc;
+		}
+	}
 	// one eager decode step on token 0 into the empty cache: every layer's
 	// one-row scratch and every kernel attribute exist before a capture
 	rc = ensure_act(m, 1);
@@ -1282,7 +1741,7 @@ int moe_model_generate(moe_model *m, const int *prompt, size_t T, int n, int eos
 			       m->logits, m->state + S_PERR, m->st));
 	MCK(cudaMemsetAsync(m->state + S_STEP, 0, 4, m->st));
 	MCK(moe::launch_argmax_advance(m->logits, (int)m->V, (int)m->C, m->state, m->picks,
-				       (int)m->pick_cap, 0, m->st));
+				       (int)m->pick_cap, 0, m->argbuf, m->st));
 	MCK(cudaEventRecord(m->ev[1], m->st));
 	int made = 1;
 	int last = -1;
@@ -1341,6 +1800,14 @@ int moe_model_status(moe_model *m)
 	if (!m)
 		return mfail(MOE_ERR_INVALID, "moe_model_status: null model");
 	return take_state_error(m);
+}
+
+int moe_model_mode(moe_model *m)
+{
+	if (!m)
+		return mfail(MOE_ERR_INVALID, "moe_model_mode: null model");
+	return (m->gexec ? 1 : 0) | (m->fused_step ? 2 : 0) |
+	       (m->fused_step && moe::pdl_enabled() ? 4 : 0);
 }
 
 int moe_model_info(moe_model *m, int64_t *cache_size, int64_t *pos, size_t *device_bytes)

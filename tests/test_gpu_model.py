@@ -151,3 +151,30 @@ def test_model_errors(moe, tmp_path):
         model.logits(5)                        # no such row
     model.prefill([1, 2, 3], rows=False)       # still usable
     assert model.status() == 0
+
+
+@pytest.mark.parametrize("arch", ["olmoe", "mixtral"])
+def test_fused_decode_step_matches_reference(moe, orc, tmp_path, arch):
+    """d_model 2048: the decode step takes the fused kernels (QKV GEMV with
+    the residual add and RMSNorm in its prologue, one-launch QK-norm + RoPE +
+    cache row + split attention with the merge by the last CTA of each head,
+    programmatic dependent launches) inside the CUDA graph"""
+    gg = gguf_module()
+    path = str(tmp_path / f"{arch}.gguf")
+    if arch == "olmoe":
+        gg.write_olmoe(path, 2, 2048, 16, 8, 2, 256, 512, seed=31, context=256, norm_sd=0.1)
+    else:
+        gg.write_mixtral(path, 2, 2048, 16, 4, 4, 2, 512, 512, seed=32, context=256,
+                         norm_sd=0.1)
+    prompt = np.random.default_rng(10).integers(0, 512, 70)
+    ref = ref_model(orc, path, prompt, 8, 2048, 512)
+    model = moe.Model.from_gguf(gg.GGUFReader(path))
+    close(model.prefill(prompt), ref["rows"], "prefill rows")
+    for i, t in enumerate(ref["tokens"]):
+        close(model.decode(int(t), 70 + i), ref["drows"][i], f"decode row {i}")
+        close(model.logits(0), ref["logits"][i + 1], f"decode logits {i}")
+    model.reset()
+    picks = model.generate(prompt, 8)
+    want = np.concatenate([ref["tokens"], [int(np.argmax(ref["logits"][-1]))]])
+    same_greedy(picks, want, ref["logits"])
+    assert model.status() == 0
