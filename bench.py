@@ -433,8 +433,9 @@ def run_ours(args, rank, world, local_rank):
         del layers[1:], keep[1:]
         torch.cuda.empty_cache()
         for cfg in [c for c in args.models.split(",") if c]:
-            models[cfg] = run_model_leg(moe, torch, torch_stream, cfg, with_ref=not args.no_cpu,
-                                        clocks_dev=local_rank)
+            models[cfg] = run_model_leg(moe, torch, torch_stream, cfg, runs=args.model_runs,
+                                        with_ref=not args.no_cpu, clocks_dev=local_rank,
+                                        n_decode=args.model_decode)
             torch.cuda.empty_cache()
 
     line = {
@@ -1242,7 +1243,8 @@ def model_reference_sample(moe, torch, gg, c, tensors, model_small):
     return cpu, parity
 
 
-def run_model_leg(moe, torch, torch_stream, cfg_name, runs=3, with_ref=True, clocks_dev=0):
+def run_model_leg(moe, torch, torch_stream, cfg_name, runs=3, with_ref=True, clocks_dev=0,
+                  n_decode=0):
     """One whole-model config on one GPU: weights generated in HBM, the
     model built from them (moe_model_create), then greedy generation of the
     config's decode steps after its prompt, timed by the model's CUDA events
@@ -1275,7 +1277,7 @@ def run_model_leg(moe, torch, torch_stream, cfg_name, runs=3, with_ref=True, clo
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     prompt = np.random.default_rng(c["seed"]).integers(0, c["vocab"], c["prompt"]).astype(np.int32)
-    n = c["decode"]
+    n = n_decode or c["decode"]
     model.reset()
     model.generate(prompt, n)
     model.reset()
@@ -1367,6 +1369,9 @@ def main():
                     help="skip the whole-model legs (configs 2 and 3)")
     ap.add_argument("--models", default="config2,config3",
                     help="whole-model configs timed at N=1")
+    ap.add_argument("--model-decode", type=int, default=0,
+                    help="decode steps of the model legs (0: the config's)")
+    ap.add_argument("--model-runs", type=int, default=3, help="timed generations per model leg")
     ap.add_argument("--only", choices=["gemv", "dense", "config2", "config3"],
                     help="run one leg alone on one GPU (for profilers) and print its result")
     args = ap.parse_args()
@@ -1380,8 +1385,9 @@ def main():
     elif args.only:
         torch, moe, _, torch_stream = init_rank(1, local_rank)
         if args.only in MODEL_CONFIGS:
-            res = run_model_leg(moe, torch, torch_stream, args.only, with_ref=not args.no_cpu,
-                                clocks_dev=local_rank)
+            res = run_model_leg(moe, torch, torch_stream, args.only, runs=args.model_runs,
+                                with_ref=not args.no_cpu, clocks_dev=local_rank,
+                                n_decode=args.model_decode)
         else:
             leg = run_config1_gemv if args.only == "gemv" else run_dense_gemm
             res = leg(moe, torch_stream.cuda_stream, torch_stream)

@@ -335,7 +335,9 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	const int units = ((T + RTile<LANES>::RT - 1) / RTile<LANES>::RT) * (NE / RTile<LANES>::RE);
 	const int topk_first = units % (int)gridDim.x;  // CTA of token 0
 	const int my_token0 = ((int)blockIdx.x - topk_first + (int)gridDim.x) % (int)gridDim.x;
-	if ((int)blockIdx.x >= units && my_token0 < T && warp == 0) {
+	// few tokens on one rank: P1 ranks every token on every CTA (see there)
+	const bool local_topk = !shard && T <= (int)(blockDim.x / 32) && NE <= 64;
+	if (!local_topk && (int)blockIdx.x >= units && my_token0 < T && warp == 0) {
 		float *lg = reinterpret_cast<float *>(smem);
 		float *sel = lg + kMaxActive;
 		int32_t *dummy = reinterpret_cast<int32_t *>(sel + 2 * K);
@@ -389,7 +391,6 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	// tokens on one rank: every CTA ranks every token itself instead (warp t
 	// takes token t), which saves the second grid barrier and a hop through
 	// global memory; CTA 0 writes the routing for the host.
-	const bool local_topk = !shard && T <= (int)(blockDim.x / 32) && NE <= 64;
 	int32_t *ids_all = reinterpret_cast<int32_t *>(smem + DS::RING_IDS);
 	float *wtok = reinterpret_cast<float *>(smem + DS::RING_IDS + kDecodeMaxPairsAll * 4);
 	{
@@ -572,6 +573,12 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		__syncthreads();
 	}
 	stamp(a.stamps, kStB3);
+
+	// a kernel launched as a programmatic dependent of this one (the next
+	// projection of a model's decode step) may start streaming its weights
+	// on SMs this kernel leaves; it reads this layer's output only after
+	// this grid completes
+	griddep_launch_dependents();
 
 	// ------------------------------------------------ P4: combine
 	// one output element per thread; the rows of 8 slots are loaded before

@@ -226,12 +226,22 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		if (nin.hidden) {
 			// x = rms_norm(hidden + delta) * weight (tensor_add, then
 			// rms_norm, nn.c:7-48); CTA 0 stores hidden + delta
+			// every load before the first store (hidden_out might alias
+			// them as far as the compiler knows)
+			float dl[NBW], wn[NBW];
 #pragma unroll
 			for (int j = 0; j < NBW; j++) {
 				const int e = (warp + j * kTcMath) * 32 + lane;
-				v[j] = nin.delta ? __fadd_rn(nin.hidden[e], nin.delta[e]) : nin.hidden[e];
+				v[j] = nin.hidden[e];
+				dl[j] = nin.delta ? nin.delta[e] : 0.0f;
+				wn[j] = nin.weight[e];
+			}
+#pragma unroll
+			for (int j = 0; j < NBW; j++) {
+				if (nin.delta)
+					v[j] = __fadd_rn(v[j], dl[j]);
 				if (blockIdx.x == 0)
-					nin.hidden_out[e] = v[j];
+					nin.hidden_out[(warp + j * kTcMath) * 32 + lane] = v[j];
 			}
 			float ss = 0.0f;
 #pragma unroll
@@ -247,10 +257,8 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 				tot += red[q];
 			const float rms = sqrtf(tot / (float)(nb * 32) + nin.eps);
 #pragma unroll
-			for (int j = 0; j < NBW; j++) {
-				const int e = (warp + j * kTcMath) * 32 + lane;
-				v[j] = (v[j] / rms) * nin.weight[e];
-			}
+			for (int j = 0; j < NBW; j++)
+				v[j] = (v[j] / rms) * wn[j];
 		} else {
 #pragma unroll
 			for (int j = 0; j < NBW; j++) {

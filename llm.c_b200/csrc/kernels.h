@@ -292,7 +292,7 @@ cudaError_t launch_qk_rope(const QkvArgs &a, cudaStream_t st);
 constexpr int kAttnChunk = 64;
 inline int attn_splits(int C) { return (C + kAttnChunk - 1) / kAttnChunk; }
 // CTAs per head of the one-launch decode step (balanced row ranges)
-inline int attn_step_splits(int C) { return C < 16 ? C : 16; }
+inline int attn_step_splits(int C) { return C < 16 ? C : 16; }   // <= 16: the merge's reach
 cudaError_t launch_attention(const float *q, const float *kc, const float *vc, const int32_t *size,
 			     int T, int H, int KVH, int HL, int C, float scale_div, float *part,
 			     float *out, cudaStream_t st);

@@ -479,20 +479,28 @@ __global__ void __launch_bounds__(kStepThreads) attn_step_kernel(AttnStepArgs a)
 		return;
 	__threadfence();
 	const float *hp = a.part + (int64_t)h * S * (HL + 2);
-	float Mx = -FLT_MAX;
-	for (int q = 0; q < S; q++)
-		if (__ldcg(hp + q * (HL + 2) + HL + 1) > 0.0f)
-			Mx = fmaxf(Mx, __ldcg(hp + q * (HL + 2) + HL));
-	float Ls = 0.0f, acc = 0.0f;
-	for (int q = 0; q < S; q++) {
-		const float Lq = __ldcg(hp + q * (HL + 2) + HL + 1);
-		if (Lq > 0.0f) {
-			const float f = expf(__ldcg(hp + q * (HL + 2) + HL) - Mx);
-			Ls = fmaf(Lq, f, Ls);
-			if (threadIdx.x < HL)
-				acc = fmaf(__ldcg(hp + q * (HL + 2) + threadIdx.x), f, acc);
-		}
+	// every partial's loads first (S <= 16), then the merge
+	float Mq[16], Lq[16], Oq[16];
+#pragma unroll
+	for (int q = 0; q < 16; q++) {
+		const bool in = q < S;
+		Mq[q] = in ? __ldcg(hp + q * (HL + 2) + HL) : -FLT_MAX;
+		Lq[q] = in ? __ldcg(hp + q * (HL + 2) + HL + 1) : 0.0f;
+		Oq[q] = in && threadIdx.x < HL ? __ldcg(hp + q * (HL + 2) + threadIdx.x) : 0.0f;
 	}
+	float Mx = -FLT_MAX;
+#pragma unroll
+	for (int q = 0; q < 16; q++)
+		if (Lq[q] > 0.0f)
+			Mx = fmaxf(Mx, Mq[q]);
+	float Ls = 0.0f, acc = 0.0f;
+#pragma unroll
+	for (int q = 0; q < 16; q++)
+		if (Lq[q] > 0.0f) {
+			const float f = expf(Mq[q] - Mx);
+			Ls = fmaf(Lq[q], f, Ls);
+			acc = fmaf(Oq[q], f, acc);
+		}
 	if (threadIdx.x < HL)
 		a.out[(int64_t)h * HL + threadIdx.x] = acc / Ls;
 	if (threadIdx.x == 0)
