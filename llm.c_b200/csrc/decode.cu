@@ -6,15 +6,19 @@
 // renormalisation) compute, phase by phase:
 //
 //   P0  router logits (matmul.c:91-131 lane order, exact) by tiles of
-//       8 or 16 tokens x 8 experts spread over the CTAs, each tile staged
-//       into shared memory by bulk copies; every CTA also writes its share
-//       of the fp16 hi/lo split of x that the expert phases read.
+//       8 or 16 tokens x 8 experts spread over the CTAs (up to 8 tokens: one
+//       expert per CTA), each tile staged into shared memory by bulk
+//       copies; every CTA also writes its share of the fp16 hi/lo split of
+//       x that the expert phases read.
 //   --  grid barrier
 //   P1  CTA t computes softmax + top-k (nn.c:221-308) of token t; grid
 //       barrier; then every CTA reads the selected (token, slot) pairs and
 //       computes their stable dispatch by expert into its own shared
 //       memory (redundant, but cheaper than another barrier); CTA 0 writes
-//       the dispatch to global memory for the host.
+//       the dispatch to global memory for the host.  Up to 11 tokens on one
+//       rank, every CTA ranks every token itself (one thread per (token,
+//       expert) up to 5 tokens) and no second barrier is needed; up to 32
+//       pairs, one warp dispatches them.
 //   P2  gate/up + SwiGLU over (active expert, 8-row) items — the expert
 //       pipeline of expert_core.cuh, writing h as fp16 hi/lo rows.
 //   --  grid barrier among the math and epilogue warps.  The producer warp
@@ -268,6 +272,78 @@ __device__ void router_tiles(const DecodeArgs &a, uint8_t *buf, uint64_t *rbar)
 	}
 }
 
+// P0 for a few tokens (T <= 8): one expert per CTA (CTAs NE.. idle), so the
+// router's latency is one 2048-column chunk of one row per CTA instead of
+// eight.  The T token rows and the expert's row are staged by bulk copies;
+// warp t computes token t: lane quad q (lane q < LANES / 4) carries the
+// reference's SIMD lanes 4q..4q+3 (the same fp32 chains as router_tiles,
+// matmul.c:91-105 with LANES lanes), and the halving tree over the lanes
+// runs in lane 0 (the same additions in the same order).
+constexpr int kSmallRouterT = 8;
+
+template <int LANES>
+__device__ void router_small(const DecodeArgs &a, uint8_t *buf, uint64_t *rbar)
+{
+	constexpr int CH = 2048, RS = CH * 4 + 16, LQ = LANES / 4;
+	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+	const int e = blockIdx.x;
+	if (e >= a.NE)
+		return;
+	const int nch = a.D / CH;
+	float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+	bool failed = false;
+	for (int c = 0; c < nch; c++) {
+		if (warp == 0) {
+			// rows 0..T-1: tokens, row T: the expert
+			if (lane == 0)
+				mbar_arrive_expect_tx(rbar, (uint32_t)((a.T + 1) * CH * 4));
+			__syncwarp();
+			if (lane <= a.T) {
+				const float *src = lane < a.T ? a.x + (int64_t)lane * a.D
+							      : a.router_w + (int64_t)e * a.D;
+				fence_proxy_async();
+				bulk_g2s(buf + lane * RS, src + (int64_t)c * CH, CH * 4, rbar);
+			}
+		}
+		if (!mbar_wait(rbar, c & 1)) {
+			failed = true;
+			atomicExch(a.err, 2);
+		}
+		if (!failed && warp < a.T && lane < LQ) {
+			const float *xs = reinterpret_cast<const float *>(buf + warp * RS);
+			const float *ws = reinterpret_cast<const float *>(buf + a.T * RS);
+#pragma unroll 8
+			for (int st = 0; st < CH / LANES; st++) {
+				const int col = st * LANES + lane * 4;
+				const float4 xv = *reinterpret_cast<const float4 *>(xs + col);
+				const float4 wv = *reinterpret_cast<const float4 *>(ws + col);
+				acc[0] = __fmaf_rn(xv.x, wv.x, acc[0]);
+				acc[1] = __fmaf_rn(xv.y, wv.y, acc[1]);
+				acc[2] = __fmaf_rn(xv.z, wv.z, acc[2]);
+				acc[3] = __fmaf_rn(xv.w, wv.w, acc[3]);
+			}
+		}
+		__syncthreads();  // the buffer is free again
+		if (failed)
+			break;
+	}
+	if (warp < a.T && !failed) {
+		// lane j of the reference's LANES sits in lane j / 4, slot j % 4
+		float l[LANES];
+#pragma unroll
+		for (int j = 0; j < LANES; j++)
+			l[j] = __shfl_sync(0xffffffffu, acc[j % 4], j / 4);
+		if (lane == 0) {
+#pragma unroll
+			for (int h = LANES / 2; h >= 1; h /= 2)
+#pragma unroll
+				for (int j = 0; j < h; j++)
+					l[j] = __fadd_rn(l[j], l[j + h]);
+			a.logits[(int64_t)warp * a.NE + e] = __fadd_rn(0.0f, l[0]);
+		}
+	}
+}
+
 // ---------------------------------------------------------------- the kernel
 template <int QT, int LANES, int WB_GU, int WB_DN, int MT_DN, int STAGES>
 __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs a)
@@ -332,7 +408,11 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	// normally a CTA without router work.  Such a CTA first runs the top-k
 	// once on dummy logits, so that its code is in the SM's instruction cache
 	// (it is otherwise fetched cold, from memory, when the result is needed).
-	const int units = ((T + RTile<LANES>::RT - 1) / RTile<LANES>::RT) * (NE / RTile<LANES>::RE);
+	// a few tokens and enough CTAs: one expert per CTA (router_small)
+	const bool small_router = T <= kSmallRouterT && NE <= (int)gridDim.x;
+	const int units = small_router
+				  ? NE
+				  : ((T + RTile<LANES>::RT - 1) / RTile<LANES>::RT) * (NE / RTile<LANES>::RE);
 	const int topk_first = units % (int)gridDim.x;  // CTA of token 0
 	const int my_token0 = ((int)blockIdx.x - topk_first + (int)gridDim.x) % (int)gridDim.x;
 	// few tokens on one rank: P1 ranks every token on every CTA (see there)
@@ -348,7 +428,10 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 				  reinterpret_cast<int32_t *>(sel + K), dummy, reinterpret_cast<float *>(dummy + K),
 				  nullptr, nullptr);
 	}
-	router_tiles<LANES>(a, smem, rbar);
+	if (small_router)
+		router_small<LANES>(a, smem, rbar);
+	else
+		router_tiles<LANES>(a, smem, rbar);
 	{
 		// the fp16 hi/lo split of x that the expert phases read, 8 columns
 		// per thread and 16-byte stores; token-sharded, into this rank's rows
@@ -396,7 +479,13 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 	{
 		float *lg = reinterpret_cast<float *>(smem);                 // [NE]
 		float *sel = lg + kMaxActive;                                // [2K]
-		if (local_topk) {
+		if (local_topk && T * 64 <= (int)blockDim.x) {
+			// one thread per (token, expert)
+			topk_tokens_cta<LANES>(a.logits, a.router_bias, T, NE, K, a.mode_exact, a.renorm,
+					       reinterpret_cast<float *>(smem), ids_all, wtok,
+					       blockIdx.x == 0 ? a.ids : nullptr,
+					       blockIdx.x == 0 ? a.wts : nullptr);
+		} else if (local_topk) {
 			if (warp < T) {
 				float *lgw = reinterpret_cast<float *>(smem + warp * kLocalTopkBytes);
 				float *sw = lgw + 64;
@@ -475,8 +564,14 @@ __global__ void __launch_bounds__(kCoreThreads, 1) moe_decode_kernel(DecodeArgs 
 		for (int i = tid; i < T * K; i += blockDim.x)   // 1 / w, the combine's divisor
 			wts_s[i] = __fdiv_rn(1.0f, local_topk ? wtok[i] : __ldcg(a.wts + i));
 		__syncthreads();
-		dispatch_body(ids_all, np, NE, a.first_expert, a.n_local, counts_s, offsets_s, perm_s,
-			      nullptr, active_s, nact_s, a.err, ds);
+		if (local_topk && np <= 32) {
+			if (warp == 0)
+				dispatch_warp(ids_all, np, NE, a.first_expert, a.n_local, counts_s, offsets_s,
+					      perm_s, active_s, nact_s, a.err);
+		} else {
+			dispatch_body(ids_all, np, NE, a.first_expert, a.n_local, counts_s, offsets_s,
+				      perm_s, nullptr, active_s, nact_s, a.err, ds);
+		}
 		__syncthreads();
 		stamp(a.stamps, kStDispatch);
 		const int n_active = *nact_s;

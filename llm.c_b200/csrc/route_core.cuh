@@ -201,6 +201,124 @@ static __device__ __noinline__ void topk_token_j(const float *__restrict__ lr, c
 	__syncwarp();
 }
 
+// The same softmax + top-k for T <= blockDim.x / 64 tokens at once, one
+// thread per (token, expert) (NE <= 64), for the few-token decode batches
+// where a single warp's serial shuffle chain would be the latency: the max,
+// the exponentials, the LANES-chain sum with its halving tree and the tail,
+// the divisions and the ranks (reference mode or exact) are the same
+// operations in the same order as topk_token_j, spread over the CTA.  Every
+// thread of the CTA calls it (it synchronises the CTA).  lg: [T][NE]
+// logits (global); scr: shared scratch of T * (64 + LANES + 1 + 2 * K)
+// words; ids_s/w_s: [T][K] outputs in slot order (shared); ids_g/w_g: the
+// same to global memory (or NULL).
+template <int LANES>
+static __device__ void topk_tokens_cta(const float *__restrict__ lg, const float *__restrict__ bias,
+				       int T, int NE, int K, int mode_exact, int renorm, float *scr,
+				       int32_t *ids_s, float *w_s, int32_t *ids_g, float *w_g)
+{
+	float *P = scr;                          // [T][64]
+	float *CS = P + T * 64;                  // [T][LANES]
+	float *SUM = CS + T * LANES;             // [T]
+	int32_t *SID = reinterpret_cast<int32_t *>(SUM + T);  // [T][K]
+	float *SW = reinterpret_cast<float *>(SID + T * K);   // [T][K]
+	const int tid = threadIdx.x, t = tid / 64, e = tid % 64;
+	const bool act = t < T && e < NE;
+	float l = 0.0f;
+	if (act) {
+		l = __ldcg(lg + (int64_t)t * NE + e);
+		if (bias)
+			l = __fadd_rn(l, bias[e]);
+		P[t * 64 + e] = l;
+	}
+	__syncthreads();
+	float v = 0.0f;
+	if (act) {
+		float mx = -INFINITY;
+		for (int i = 0; i < NE; i++)
+			mx = fmaxf(mx, P[t * 64 + i]);
+		v = exp_rn(__fsub_rn(l, mx));
+	}
+	__syncthreads();
+	if (act)
+		P[t * 64 + e] = v;
+	__syncthreads();
+	// nn.c:236-250: lane c sums elements c, c + LANES, ... of the vector part
+	// in order; the halving tree over the lanes; the scalar tail in order
+	const int nv = NE - NE % LANES;
+	if (t < T && e < LANES) {
+		float s = 0.0f;
+		for (int m = 0; m < nv / LANES; m++)
+			s = __fadd_rn(s, P[t * 64 + e + LANES * m]);
+		CS[t * LANES + e] = s;
+	}
+	__syncthreads();
+	if (t < T && e == 0) {
+		float c[LANES];
+#pragma unroll
+		for (int j = 0; j < LANES; j++)
+			c[j] = CS[t * LANES + j];
+#pragma unroll
+		for (int h = LANES / 2; h >= 1; h /= 2)
+#pragma unroll
+			for (int j = 0; j < h; j++)
+				c[j] = __fadd_rn(c[j], c[j + h]);
+		float s = c[0];
+		for (int i = nv; i < NE; i++)
+			s = __fadd_rn(s, P[t * 64 + i]);
+		SUM[t] = s;
+	}
+	__syncthreads();
+	const float p = act ? __fdiv_rn(v, SUM[t]) : 0.0f;
+	__syncthreads();
+	if (act)
+		P[t * 64 + e] = p;
+	__syncthreads();
+	// ranks by (value desc, index asc); reference mode (nn.c:276-308 seeds
+	// every slot with element 0): elements not above p0 fall behind its k
+	// copies, which fill the slots from r0 = #{i >= 1 : p_i > p0} on
+	if (act) {
+		const float p0 = P[t * 64];
+		if (mode_exact || e != 0) {
+			int rank = (!mode_exact && p0 >= p) ? K : 0;
+			for (int i = 0; i < NE; i++) {
+				const float o = P[t * 64 + i];
+				rank += (mode_exact || i != 0) && (o > p || (o == p && i < e));
+			}
+			if (rank < K) {
+				SID[t * K + K - 1 - rank] = e;
+				SW[t * K + K - 1 - rank] = p;
+			}
+		} else {
+			int r0 = 0;
+			for (int i = 1; i < NE; i++)
+				r0 += P[t * 64 + i] > p0;
+			for (int c = r0; c < K; c++) {
+				SID[t * K + K - 1 - c] = 0;
+				SW[t * K + K - 1 - c] = p0;
+			}
+		}
+	}
+	__syncthreads();
+	if (renorm && t < T && e == 0) {
+		// llama.c:422-427: sequential sum in slot order, then divide
+		float sum = 0.0f;
+		for (int q = 0; q < K; q++)
+			sum = __fadd_rn(sum, SW[t * K + q]);
+		for (int q = 0; q < K; q++)
+			SW[t * K + q] = __fdiv_rn(SW[t * K + q], sum);
+	}
+	__syncthreads();
+	if (t < T && e < K) {
+		ids_s[t * K + e] = SID[t * K + e];
+		w_s[t * K + e] = SW[t * K + e];
+		if (ids_g) {
+			ids_g[(int64_t)t * K + e] = SID[t * K + e];
+			w_g[(int64_t)t * K + e] = SW[t * K + e];
+		}
+	}
+	__syncthreads();
+}
+
 // NE <= 32 * MAXJ elements per token: the smallest register file that fits.
 // topk_token_j is kept out of line so that its register arrays stay in
 // registers inside large kernels as well.
@@ -231,6 +349,57 @@ static __device__ void topk_token(const float *__restrict__ lr, const float *__r
 // of the CTA must call it (it synchronises the CTA).
 // smem: cnt[NE], run[NE], wcnt[warps][NE]; blockDim.x a multiple of 32
 // ---------------------------------------------------------------------
+// The same dispatch for at most 32 pairs, by one warp (lane p holds pair p):
+// a pair's position is the number of pairs with a smaller expert id plus
+// the earlier pairs with its own, which is dispatch_body's stable order.
+// Called by one warp; the caller synchronises the CTA after it.
+static __device__ void dispatch_warp(const int32_t *ids, int npairs, int NE, int first, int nlocal,
+				     int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+				     int32_t *__restrict__ perm, int32_t *__restrict__ active,
+				     int32_t *__restrict__ n_active, int32_t *__restrict__ err)
+{
+	constexpr unsigned FULL = 0xffffffffu;
+	const int lane = threadIdx.x % 32;
+	int e = lane < npairs ? ids[lane] : -1;
+	if (lane < npairs && (e < 0 || e >= NE)) {
+		atomicExch(err, 1);
+		e = -1;
+	}
+	int below = 0, same_before = 0;
+	for (int q = 0; q < 32; q++) {
+		const int eq = __shfl_sync(FULL, e, q);
+		below += eq >= 0 && eq < e;
+		same_before += eq == e && q < lane;
+	}
+	if (e >= 0)
+		perm[below + same_before] = lane;
+	int na = 0;
+	for (int base = 0; base < NE; base += 32) {
+		const int x = base + lane;
+		int c = 0, o = 0;
+		for (int q = 0; q < 32; q++) {
+			const int eq = __shfl_sync(FULL, e, q);
+			c += eq == x;
+			o += eq >= 0 && eq < x;
+		}
+		if (x < NE) {
+			counts[x] = c;
+			offsets[x] = o;
+		}
+		const bool act = x < NE && c > 0 && x >= first && x < first + nlocal;
+		const unsigned m = __ballot_sync(FULL, act);
+		if (act)
+			active[na + __popc(m & ((1u << lane) - 1u))] = x;
+		na += __popc(m);
+	}
+	const unsigned valid = __ballot_sync(FULL, e >= 0);
+	if (lane == 0) {
+		offsets[NE] = __popc(valid);
+		*n_active = na;
+	}
+	__syncwarp();
+}
+
 static __device__ void dispatch_body(const int32_t *ids, int npairs, int NE, int first, int nlocal,
 			      int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
 			      int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,

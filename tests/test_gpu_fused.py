@@ -122,3 +122,23 @@ def test_beyond_fused_limit_takes_five_launch_path(moe, orc, olmoe):
     assert_routing(orc, x, olmoe, 16, ids, w, ids_ref, w_ref)
     assert_output_close(got, ref)
     lay.close()
+
+
+@pytest.mark.parametrize("T", [1, 3, 5])
+@pytest.mark.parametrize("flags,lanes,mode", [(0, 16, 0), (1, 16, 1), (4, 8, 0), (5, 8, 1)])
+def test_fused_few_tokens_modes(moe, orc, q4_layer, T, flags, lanes, mode):
+    """up to 8 tokens: one router expert per CTA; up to 5: the CTA-parallel
+    top-k; up to 32 pairs: the one-warp dispatch (both lane orders, reference
+    and exact top-k)"""
+    check(moe, orc, q4_layer, orc.make_tokens(70 + T, T, 2048), flags=flags, lanes=lanes,
+          mode=mode)
+
+
+@pytest.mark.parametrize("bias0", [8.0, 1.5])
+def test_fused_few_tokens_quirk(moe, orc, q4_layer, bias0):
+    """the index-0 seeding quirk through the CTA-parallel top-k"""
+    L = dict(q4_layer)
+    bias = np.zeros(16, np.float32)
+    bias[0] = bias0
+    L["router_bias"] = bias
+    check(moe, orc, L, orc.make_tokens(80, 4, 2048))
