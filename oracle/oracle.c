@@ -279,6 +279,10 @@ size_t orc_row_bytes(int type, size_t cols)
 		return cols / QK * 34;
 	if (type == ORC_Q4_0)
 		return cols / QK * 18;
+	if (type == ORC_Q4_K)
+		return cols / 256 * 144;
+	if (type == ORC_Q6_K)
+		return cols / 256 * 210;
 	return cols * 4;
 }
 
@@ -360,12 +364,180 @@ static float dot_q4_0(const float *x, const uint8_t *row, size_t n, int lanes)
 	return lane_reduce(acc, lanes);
 }
 
+/* ------------------------------------------------------------------ */
+/* K-quants                                                             */
+/* ------------------------------------------------------------------ */
+
+/* get_scale_min_k4 (quant.h:62-71): 6-bit scale and min of sub-block j */
+static void scale_min_k4(int j, const uint8_t *q, int *d, int *m)
+{
+	if (j < 4) {
+		*d = q[j] & 63;
+		*m = q[j + 4] & 63;
+	} else {
+		*d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+		*m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+	}
+}
+
+/* quant.c:200-236: element e of a Q4_K block, value (d*sc)*q - dmin*m with
+ * the two products rounded, lanes of fused multiply-adds */
+static float dot_q4_K(const float *x, const uint8_t *row, size_t n, int lanes)
+{
+	float acc[16] = { 0 };
+	for (size_t b = 0; b < n / 256; b++) {
+		const uint8_t *blk = row + b * 144;
+		const float d = orc_f16_to_f32(get_u16(blk)), dmin = orc_f16_to_f32(get_u16(blk + 2));
+		const uint8_t *sc = blk + 4, *q = blk + 16;
+		for (int j = 0; j < 4; j++) {
+			int s1, m1, s2, m2;
+			scale_min_k4(2 * j, sc, &s1, &m1);
+			scale_min_k4(2 * j + 1, sc, &s2, &m2);
+			const float d1 = d * (float)s1, n1 = dmin * (float)m1;
+			const float d2 = d * (float)s2, n2 = dmin * (float)m2;
+			for (int k = 0; k < 32; k++) {
+				const size_t e = b * 256 + j * 64 + k;
+				const float v = d1 * (float)(q[j * 32 + k] & 15) - n1;
+				acc[e % lanes] = fmaf(v, x[e], acc[e % lanes]);
+			}
+			for (int k = 0; k < 32; k++) {
+				const size_t e = b * 256 + j * 64 + 32 + k;
+				const float v = d2 * (float)(q[j * 32 + k] >> 4) - n2;
+				acc[e % lanes] = fmaf(v, x[e], acc[e % lanes]);
+			}
+		}
+	}
+	return lane_reduce(acc, lanes);
+}
+
+/* Q6_K element e of a block: 6-bit value minus 32 (quant.c:305-410) and
+ * its 8-bit scale */
+static int q6_value(const uint8_t *blk, int e, int *scale)
+{
+	const int half = e / 128, r = e % 128, g = r / 32, k = r % 32;
+	const uint8_t *ql = blk + half * 64, *qh = blk + 128 + half * 32;
+	const int lo = g & 1 ? ql[32 + k] : ql[k];
+	const int nib = g < 2 ? (lo & 15) : (lo >> 4);
+	*scale = (int8_t)blk[192 + e / 16];
+	return (nib | (((qh[k] >> (2 * g)) & 3) << 4)) - 32;
+}
+
+/* quant.c:305-410: (float)(q - 32) * (d * scale), lanes of fused
+ * multiply-adds */
+static float dot_q6_K(const float *x, const uint8_t *row, size_t n, int lanes)
+{
+	float acc[16] = { 0 };
+	for (size_t b = 0; b < n / 256; b++) {
+		const uint8_t *blk = row + b * 210;
+		const float d = orc_f16_to_f32(get_u16(blk + 208));
+		for (int e = 0; e < 256; e++) {
+			int sc;
+			const int q = q6_value(blk, e, &sc);
+			const float v = (float)q * (d * (float)sc);
+			const size_t i = b * 256 + e;
+			acc[i % lanes] = fmaf(v, x[i], acc[i % lanes]);
+		}
+	}
+	return lane_reduce(acc, lanes);
+}
+
+/* quant.c:627-654: per 256 values, the first value of largest magnitude
+ * sets iscale = -127 / mval; q = min(127, roundf(iscale * x)); d = 1 /
+ * iscale; bsums over each 16 */
+void orc_quantize_row_q8K(const float *x, void *blocks, size_t n)
+{
+	uint8_t *out = blocks;
+	for (size_t i = 0; i < n / 256; i++) {
+		const float *xb = x + i * 256;
+		uint8_t *y = out + i * ORC_Q8K_BYTES;
+		float amax = 0.0f, mval = 0.0f;
+		for (int j = 0; j < 256; j++) {
+			const float a = fabsf(xb[j]);
+			if (a > amax) {
+				amax = a;
+				mval = xb[j];
+			}
+		}
+		memset(y, 0, ORC_Q8K_BYTES);
+		if (amax == 0.0f)
+			continue;
+		const float iscale = -127.0f / mval;
+		const float d = 1.0f / iscale;
+		memcpy(y, &d, 4);
+		int8_t *qs = (int8_t *)(y + 4);
+		for (int j = 0; j < 256; j++) {
+			const int v = (int)roundf(iscale * xb[j]);
+			qs[j] = (int8_t)(v < 127 ? v : 127);
+		}
+		for (int j = 0; j < 16; j++) {
+			int16_t s = 0;
+			for (int k = 0; k < 16; k++)
+				s = (int16_t)(s + qs[j * 16 + k]);
+			memcpy(y + 260 + 2 * j, &s, 2);
+		}
+	}
+}
+
+/* quant_avx2.h: the integer sums are exact; per block acc += d * S (and,
+ * for Q4_K, acc_m += dmin * M with M = sum_s m_s * (bsum_2s + bsum_2s+1),
+ * added after the blocks), d = d8 * d_block, dmin = -d8 * dmin_block.  The
+ * reference build contracts `acc += d * S` into a fused multiply-add. */
+float orc_dot_q8K(const void *q8, const void *qdata, int type, size_t row, size_t n)
+{
+	const uint8_t *base = (const uint8_t *)qdata + row * orc_row_bytes(type, n);
+	const uint8_t *y8 = q8;
+	float acc = 0.0f, acc_m = 0.0f;
+	for (size_t b = 0; b < n / 256; b++) {
+		const uint8_t *y = y8 + b * ORC_Q8K_BYTES;
+		float d8;
+		memcpy(&d8, y, 4);
+		const int8_t *qs = (const int8_t *)(y + 4);
+		int16_t bs[16];
+		memcpy(bs, y + 260, 32);
+		if (type == ORC_Q4_K) {
+			const uint8_t *blk = base + b * 144;
+			const float d = d8 * orc_f16_to_f32(get_u16(blk));
+			const float dmin = -d8 * orc_f16_to_f32(get_u16(blk + 2));
+			int S = 0, M = 0;
+			for (int s = 0; s < 8; s++) {
+				int sc, m;
+				scale_min_k4(s, blk + 4, &sc, &m);
+				M += m * (bs[2 * s] + bs[2 * s + 1]);
+				int t = 0;
+				const int j = s / 2, hi = s & 1;
+				for (int k = 0; k < 32; k++) {
+					const int q = hi ? blk[16 + j * 32 + k] >> 4 : blk[16 + j * 32 + k] & 15;
+					t += q * qs[s * 32 + k];
+				}
+				S += sc * t;
+			}
+			acc_m = fmaf(dmin, (float)M, acc_m);
+			acc = fmaf(d, (float)S, acc);
+		} else {
+			const uint8_t *blk = base + b * 210;
+			const float d = d8 * orc_f16_to_f32(get_u16(blk + 208));
+			int S = 0;
+			for (int e = 0; e < 256; e++) {
+				int sc;
+				const int q = q6_value(blk, e, &sc);
+				S += sc * q * qs[e];
+			}
+			acc = fmaf(d, (float)S, acc);
+		}
+	}
+	return acc + acc_m;
+}
+
 float orc_dot_f32_quant(const float *x, const void *qdata, int type, size_t row,
 			size_t n, int lanes)
 {
 	const uint8_t *base = (const uint8_t *)qdata + row * orc_row_bytes(type, n);
 	if (type == ORC_Q8_0)
 		return dot_q8_0(x, base, n, lanes);
+	if (type == ORC_Q4_K)
+		return dot_q4_K(x, base, n, lanes);
+	if (type == ORC_Q6_K)
+		return dot_q6_K(x, base, n, lanes);
 	return dot_q4_0(x, base, n, lanes);
 }
 
@@ -515,14 +687,23 @@ void orc_fused_ffn_silu(const float *x, size_t d, size_t d_ff, int type,
 			const void *gate_w, const void *up_w, const void *down_w,
 			int lanes, float *hidden, float *out)
 {
+	const int tg = ORC_QTYPE_GU(type), td = ORC_QTYPE_DN(type);
+	/* Q8_DOT (nn.c:525-531, quant.c:656-668): K-quant gate/up rows take the
+	 * integer dot against x quantized to Q8_K; every other type the fp32 dot */
+	uint8_t *q8 = NULL;
+	if ((tg == ORC_Q4_K || tg == ORC_Q6_K) && d % 256 == 0) {
+		q8 = malloc(d / 256 * ORC_Q8K_BYTES);
+		orc_quantize_row_q8K(x, q8, d);
+	}
 	for (size_t j = 0; j < d_ff; j++) {
-		float g = orc_dot_f32_quant(x, gate_w, type, j, d, lanes);
-		float u = orc_dot_f32_quant(x, up_w, type, j, d, lanes);
+		float g = q8 ? orc_dot_q8K(q8, gate_w, tg, j, d) : orc_dot_f32_quant(x, gate_w, tg, j, d, lanes);
+		float u = q8 ? orc_dot_q8K(q8, up_w, tg, j, d) : orc_dot_f32_quant(x, up_w, tg, j, d, lanes);
 		float sg = g / (1.0f + expf(-g));
 		hidden[j] = sg * u;
 	}
+	free(q8);
 	for (size_t j = 0; j < d; j++)
-		out[j] = orc_dot_f32_quant(hidden, down_w, type, j, d_ff, lanes);
+		out[j] = orc_dot_f32_quant(hidden, down_w, td, j, d_ff, lanes);
 }
 
 /* matmul.c:270-324 with a quantized rhs.  With k % 256 == 0 (the Q8_DOT

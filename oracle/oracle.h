@@ -28,7 +28,11 @@ extern "C" {
 #endif
 
 /* tensor_dtype values of the reference (tensor.h:10-17) */
-enum { ORC_F32 = 0, ORC_Q8_0 = 1, ORC_Q4_0 = 2 };
+enum { ORC_F32 = 0, ORC_Q8_0 = 1, ORC_Q4_0 = 2, ORC_Q4_K = 3, ORC_Q6_K = 5 };
+/* a layer's weight types: gate/up in the low byte, down in the next (0:
+ * the same as gate/up) */
+#define ORC_QTYPE_GU(t) ((t) & 0xFF)
+#define ORC_QTYPE_DN(t) (((t) >> 8) & 0xFF ? ((t) >> 8) & 0xFF : (t) & 0xFF)
 
 /* top-k selection rule */
 enum {
@@ -69,6 +73,15 @@ float orc_dot_f32_quant(const float *x, const void *qdata, int type, size_t row,
 			size_t n, int lanes);
 float orc_dot_f32_f32(const float *x, const float *y, size_t n, int lanes);
 
+/* ---- K-quants: Q8_K activations and the integer dots of the Q8_DOT build
+ * (quant.c:627-668, quant_avx2.h), which both of the reference's x86 builds
+ * select (__AVX2__) ---------------------------------------------------- */
+/* sizeof(block_q8_K) = 4 + 256 + 32 */
+#define ORC_Q8K_BYTES 292
+void orc_quantize_row_q8K(const float *x, void *blocks, size_t n);
+/* row `row` of a Q4_K / Q6_K matrix against Q8_K activations */
+float orc_dot_q8K(const void *q8, const void *qdata, int type, size_t row, size_t n);
+
 /* ---- router pieces --------------------------------------------------- */
 /* logits[T,NE] = X[T,d] . Wr[NE,d]^T (matmul.c:91-131,169-245) */
 void orc_router_logits(const float *x, size_t T, size_t d, const float *wr,
@@ -95,7 +108,7 @@ void orc_gemm_q(const float *a, size_t m, size_t k, const void *b, int type,
 /* ---- the MoE layer (olmoe.c:343-407, llama.c:393-457) --------------- */
 typedef struct {
 	size_t d_model, d_ff, n_experts, top_k;
-	int qtype;      /* ORC_Q8_0 or ORC_Q4_0 */
+	int qtype;      /* ORC_Q8_0 / ORC_Q4_0, or K-quants as ORC_QTYPE_GU / _DN */
 	int renorm;     /* 1 = Mixtral renormalisation (llama.c:422-427) */
 	int topk_mode;  /* ORC_TOPK_REF / ORC_TOPK_EXACT */
 	int lanes;      /* 16 (AVX-512 build) or 8 (AVX2 build) */

@@ -20,8 +20,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 
-F32, Q8_0, Q4_0 = 0, 1, 2
+F32, Q8_0, Q4_0, Q4_K, Q6_K = 0, 1, 2, 3, 5
 TOPK_REF, TOPK_EXACT = 0, 1
+Q8K_BYTES = 292   # sizeof(block_q8_K)
+
+
+def qtype2(gate_up: int, down: int) -> int:
+    """a layer's weight types: gate/up in the low byte, down in the next"""
+    return gate_up | (down << 8)
 
 _lib = None
 
@@ -69,6 +75,9 @@ def lib():
         L.orc_gemm_q.argtypes = [P, sz, sz, P, C.c_int, sz, C.c_int, P]
         L.orc_moe_ffn.argtypes = [C.POINTER(MoeLayer), P, sz, P, P, P, P]
         L.orc_moe_slot_terms.argtypes = [C.POINTER(MoeLayer), P, sz, sz, sz, P, P, P]
+        L.orc_quantize_row_q8K.argtypes = [P, P, sz]
+        L.orc_dot_q8K.restype = C.c_float
+        L.orc_dot_q8K.argtypes = [P, P, C.c_int, sz, sz]
         _lib = L
     return _lib
 
@@ -107,7 +116,44 @@ def zipf_bias(seed: int, n: int, s: float = 1.1) -> np.ndarray:
 
 # ---------------------------------------------------------------- quant
 def row_bytes(qtype: int, cols: int) -> int:
-    return {Q8_0: cols // 32 * 34, Q4_0: cols // 32 * 18, F32: cols * 4}[qtype]
+    return {Q8_0: cols // 32 * 34, Q4_0: cols // 32 * 18, Q4_K: cols // 256 * 144,
+            Q6_K: cols // 256 * 210, F32: cols * 4}[qtype & 0xFF]
+
+
+def random_kquant(qtype: int, rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    """valid Q4_K / Q6_K rows (quant.h:30-57) with random codes and scales,
+    sized so the weights look like N(0, 0.02) ones: uint8 [rows, row_bytes].
+    The reference has no K-quant quantizer; the parity tests need only
+    well-formed blocks."""
+    nb = rows * cols // 256
+    if qtype == Q4_K:
+        blk = np.empty((nb, 144), np.uint8)
+        d = (1e-4 * rng.uniform(0.5, 1.5, nb)).astype(np.float16)
+        dmin = (1e-3 * rng.uniform(0.5, 1.5, nb)).astype(np.float16)
+        blk[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+        blk[:, 2:4] = dmin.view(np.uint8).reshape(nb, 2)
+        blk[:, 4:16] = rng.integers(0, 256, (nb, 12), dtype=np.uint8)
+        blk[:, 16:] = rng.integers(0, 256, (nb, 128), dtype=np.uint8)
+    else:
+        blk = np.empty((nb, 210), np.uint8)
+        blk[:, :192] = rng.integers(0, 256, (nb, 192), dtype=np.uint8)
+        blk[:, 192:208] = rng.integers(-60, 61, (nb, 16), dtype=np.int8).view(np.uint8)
+        d = (5e-5 * rng.uniform(0.5, 1.5, nb)).astype(np.float16)
+        blk[:, 208:210] = d.view(np.uint8).reshape(nb, 2)
+    return blk.reshape(rows, -1)
+
+
+def quantize_q8K(x: np.ndarray) -> np.ndarray:
+    """quant.c:627-654: fp32 [n] (n % 256 == 0) -> block_q8_K bytes"""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.size // 256 * Q8K_BYTES, np.uint8)
+    lib().orc_quantize_row_q8K(_p(x), _p(out), x.size)
+    return out
+
+
+def dot_q8K(q8: np.ndarray, q: np.ndarray, qtype: int, row: int, n: int) -> float:
+    return lib().orc_dot_q8K(_p(np.ascontiguousarray(q8)), _p(np.ascontiguousarray(q)), qtype,
+                             row, n)
 
 
 def quantize(qtype: int, x: np.ndarray) -> np.ndarray:
@@ -247,6 +293,19 @@ def make_layer(seed: int, d: int, F: int, NE: int, K: int, qtype: int = Q8_0,
     if zipf:
         layer["router_bias"] = zipf_bias(seed, NE, 1.1)
     return layer
+
+
+def make_layer_kquant(seed: int, d: int, F: int, NE: int, K: int, gate_up: int = Q4_K,
+                      down: int = Q6_K, renorm: bool = False) -> dict:
+    """A MoE layer with K-quant experts (random well-formed blocks; gate/up
+    and down types as in the reference's Q4_K_M files) and a seeded router"""
+    rng = np.random.default_rng(seed)
+    wr = gauss(seed, 1, NE * d, 0.02).reshape(NE, d)
+    gate = random_kquant(gate_up, rng, NE * F, d).reshape(NE, F, -1)
+    up = random_kquant(gate_up, rng, NE * F, d).reshape(NE, F, -1)
+    dn = random_kquant(down, rng, NE * d, F).reshape(NE, d, -1)
+    return dict(router_w=wr, gate=gate, up=up, down=dn, qtype=qtype2(gate_up, down),
+                d_model=d, d_ff=F, n_experts=NE, top_k=K, renorm=int(renorm))
 
 
 def make_tokens(seed: int, T: int, d: int) -> np.ndarray:

@@ -35,9 +35,24 @@ static void view_2d(tensor_t *t, float *data, void *qdata, enum tensor_dtype typ
 
 static size_t qrow_bytes(int type, size_t cols)
 {
-	return type == TENSOR_Q8_0 ? cols / 32 * sizeof(block_q8_0)
-				   : cols / 32 * sizeof(block_q4_0);
+	switch (type) {
+	case TENSOR_Q8_0:
+		return cols / 32 * sizeof(block_q8_0);
+	case TENSOR_Q4_0:
+		return cols / 32 * sizeof(block_q4_0);
+	case TENSOR_Q4_K:
+		return cols / QK_K * sizeof(block_q4_K);
+	case TENSOR_Q6_K:
+		return cols / QK_K * sizeof(block_q6_K);
+	default:
+		return cols * sizeof(float);
+	}
 }
+
+/* a layer's weight types: gate/up in the low byte, down in the next byte
+ * (0: the same) */
+#define TYPE_GU(t) ((t) & 0xFF)
+#define TYPE_DN(t) (((t) >> 8) & 0xFF ? ((t) >> 8) & 0xFF : (t) & 0xFF)
 
 /* Same call sequence as moe_ffn.  Experts are 3-D [NE, rows, cols] tensors
  * (OLMoE) addressed like tensor_at_q; renorm = 1 adds the Mixtral weight
@@ -67,8 +82,9 @@ int ref_moe_ffn(const float *x, size_t T, size_t d, const float *router_w,
 			for (size_t e = 0; e < NE; e++)
 				logits->data[t * NE + e] += router_bias[e];
 
-	size_t gsz = d_ff * qrow_bytes(qtype, d);
-	size_t dsz = d * qrow_bytes(qtype, d_ff);
+	const int tg = TYPE_GU(qtype), td = TYPE_DN(qtype);
+	size_t gsz = d_ff * qrow_bytes(tg, d);
+	size_t dsz = d * qrow_bytes(td, d_ff);
 
 	for (size_t t = 0; t < T; t++) {
 		tensor_t tl;
@@ -89,9 +105,9 @@ int ref_moe_ffn(const float *x, size_t T, size_t d, const float *router_w,
 		tensor_reshape_2d(&tok_in, 1, d);
 		for (size_t e = 0; e < topk; e++) {
 			tensor_t gw, uw, dw;
-			view_2d(&gw, NULL, (char *)gate + ids[e] * gsz, qtype, d_ff, d);
-			view_2d(&uw, NULL, (char *)up + ids[e] * gsz, qtype, d_ff, d);
-			view_2d(&dw, NULL, (char *)down + ids[e] * dsz, qtype, d, d_ff);
+			view_2d(&gw, NULL, (char *)gate + ids[e] * gsz, tg, d_ff, d);
+			view_2d(&uw, NULL, (char *)up + ids[e] * gsz, tg, d_ff, d);
+			view_2d(&dw, NULL, (char *)down + ids[e] * dsz, td, d, d_ff);
 			if (!fused_ffn_silu(&tok_in, eo, eg, &gw, eu, &uw, &dw)) {
 				tensor_mma_transposed_2x2(eg, &tok_in, &gw, NULL);
 				tensor_mma_transposed_2x2(eu, &tok_in, &uw, NULL);
@@ -166,6 +182,18 @@ void ref_quantize_row_q8_0(const float *x, void *y, size_t n)
 	quantize_row_q8_0(x, (block_q8_0 *)y, n);
 }
 
+/* Q8_K activations (quant.c:627-654) and the integer K-quant dot against
+ * them (quant.c:656-668 -> quant_avx2.h) */
+void ref_quantize_row_q8K(const float *x, void *y, size_t n)
+{
+	quantize_row_q8(x, (block_q8_K *)y, n);
+}
+
+float ref_dot_q8K(const void *q8, const void *q, int type, size_t row, size_t n)
+{
+	return dot_q8_quant((const block_q8_K *)q8, NULL, q, type, row, n);
+}
+
 float ref_dot_f32_quant(const float *x, const void *q, int type, size_t row, size_t n)
 {
 	return dot_f32_quant(x, q, type, row, n);
@@ -185,9 +213,9 @@ int ref_fused_ffn_silu(const float *x, size_t d, size_t d_ff, int type, const vo
 	tensor_t *u = tensor_new_zero(2, 1, d_ff);
 	tensor_t tg, tu, td;
 	memcpy(in->data, x, d * sizeof(float));
-	view_2d(&tg, NULL, (void *)gw, type, d_ff, d);
-	view_2d(&tu, NULL, (void *)uw, type, d_ff, d);
-	view_2d(&td, NULL, (void *)dw, type, d, d_ff);
+	view_2d(&tg, NULL, (void *)gw, TYPE_GU(type), d_ff, d);
+	view_2d(&tu, NULL, (void *)uw, TYPE_GU(type), d_ff, d);
+	view_2d(&td, NULL, (void *)dw, TYPE_DN(type), d, d_ff);
 	int ok = fused_ffn_silu(in, o, g, &tg, u, &tu, &td);
 	memcpy(out, o->data, d * sizeof(float));
 	tensor_free(in);

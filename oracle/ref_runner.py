@@ -13,6 +13,8 @@ runs in its own process and exits when the op is done.  Ops:
   dot      ref_dot_f32_quant  (x, q, qtype, n, rows)
   ffn      ref_fused_ffn_silu (x, gate, up, down, qtype, d_ff)
   bench    times ref_moe_ffn: (same as moe, plus reps) -> seconds per call
+  q8k      ref_quantize_row_q8K (x [n])
+  dotq8k   ref_dot_q8K        (q8, q, qtype, n, rows)
   model    (variant "model": libref_model.so) the reference's own OLMoE /
            llama-Mixtral forward on a GGUF file: prefill `tokens` at
            positions 0.., logits of the last row, then `n_decode` steps fed
@@ -133,6 +135,20 @@ def main():
         for r in range(v.shape[0]):
             L.ref_top_k(v[r].ctypes.data, v.shape[1], ids[r].ctypes.data, vals[r].ctypes.data, k)
         out = dict(ids=ids, vals=vals)
+    elif op == "q8k":
+        x = np.ascontiguousarray(z["x"], np.float32)
+        q = np.empty(x.size // 256 * 292, np.uint8)
+        L.ref_quantize_row_q8K.argtypes = [P, P, sz]
+        L.ref_quantize_row_q8K(p(x), p(q), x.size)
+        out = dict(q=q)
+    elif op == "dotq8k":
+        q8 = np.ascontiguousarray(z["q8"])
+        q = np.ascontiguousarray(z["q"])
+        n, rows = int(z["n"]), int(z["rows"])
+        L.ref_dot_q8K.restype = C.c_float
+        L.ref_dot_q8K.argtypes = [P, P, C.c_int, sz, sz]
+        out = dict(y=np.array([L.ref_dot_q8K(p(q8), p(q), int(z["qtype"]), r, n)
+                               for r in range(rows)], np.float32))
     elif op == "q8":
         x = np.ascontiguousarray(z["x"], np.float32)
         rows, n = x.shape

@@ -80,3 +80,58 @@ def test_fused_ffn_bit_exact(orc, qt):
     r = orc.ref_call("ffn", x=x, gate=g, up=u, down=dn, qtype=qt, d_ff=F)
     assert int(r["ok"]) == 1
     np.testing.assert_array_equal(out, r["out"])
+
+
+# ---------------------------------------------------------------- K-quants
+def test_q8K_quantizer_bit_exact(orc):
+    """quant.c:627-654 (Q8_K activations), zeros and a first-of-ties maximum"""
+    need_ref(orc, "avx512")
+    rng = np.random.default_rng(11)
+    x = rng.normal(0, 1, 1024).astype(np.float32)
+    x[256:512] = 0.0                       # an all-zero block
+    x[600], x[700] = 3.5, -3.5             # equal magnitudes: the first sets the sign
+    r = orc.ref_call("q8k", "avx512", x=x)
+    np.testing.assert_array_equal(orc.quantize_q8K(x), r["q"])
+
+
+@pytest.mark.parametrize("qt", [3, 5])
+def test_kquant_integer_dot_bit_exact(orc, qt):
+    """quant_avx2.h: Q4_K / Q6_K rows against Q8_K activations"""
+    need_ref(orc, "avx512")
+    rng = np.random.default_rng(12 + qt)
+    d = 2048
+    x = rng.normal(0, 1, d).astype(np.float32)
+    q8 = orc.quantize_q8K(x)
+    w = orc.random_kquant(qt, rng, 24, d)
+    mine = np.array([orc.dot_q8K(q8, w, qt, r, d) for r in range(24)], np.float32)
+    ref = orc.ref_call("dotq8k", "avx512", q8=q8, q=w, qtype=qt, n=d, rows=24)["y"]
+    np.testing.assert_array_equal(mine, ref)
+
+
+@pytest.mark.parametrize("variant,lanes", VARIANTS)
+@pytest.mark.parametrize("qt", [3, 5])
+def test_kquant_f32_dot_bit_exact(orc, variant, lanes, qt):
+    """quant.c:198-418: fp32 activations against Q4_K / Q6_K rows, lane order"""
+    need_ref(orc, variant)
+    rng = np.random.default_rng(13 + qt)
+    d = 1024
+    x = rng.normal(0, 1, d).astype(np.float32)
+    w = orc.random_kquant(qt, rng, 16, d)
+    mine = np.array([orc.dot_f32_quant(x, w, qt, r, d, lanes) for r in range(16)], np.float32)
+    ref = orc.ref_call("dot", variant, x=x, q=w, qtype=qt, n=d, rows=16)["y"]
+    np.testing.assert_array_equal(mine, ref)
+
+
+@pytest.mark.parametrize("variant,lanes", VARIANTS)
+@pytest.mark.parametrize("gu,dn", [(3, 5), (3, 3), (5, 5)])
+def test_kquant_layer_bit_exact(orc, variant, lanes, gu, dn):
+    """a MoE layer with K-quant experts: gate/up by the integer dots against
+    Q8_K activations, down by the fp32 dot on h (nn.c:449-539, Q8_DOT)"""
+    need_ref(orc, variant)
+    L = orc.make_layer_kquant(14, 512, 256, 8, 2, gu, dn)
+    x = orc.make_tokens(14, 5, 512)
+    out, ids, w, _ = orc.moe_ffn(L, x, lanes=lanes)
+    r = orc.ref_call("moe", variant, x=x, router_w=L["router_w"], gate=L["gate"], up=L["up"],
+                     down=L["down"], qtype=L["qtype"], d_ff=256, top_k=2, renorm=0)
+    np.testing.assert_array_equal(ids, r["ids"])
+    np.testing.assert_array_equal(out, r["out"])
