@@ -50,8 +50,14 @@ typedef struct moe_tensor {
 	size_t scratch_size;
 } moe_tensor_t;
 
-/* enum tensor_dtype (tensor.h:10-17); only these three are supported */
-enum { MOE_F32 = 0, MOE_Q8_0 = 1, MOE_Q4_0 = 2 };
+/* enum tensor_dtype (tensor.h:10-17); Q5_K (4) is not supported.  The
+ * K-quants (Q4_K, Q6_K) serve the MoE experts: a layer's qtype is one type,
+ * or gate/up and down types as MOE_QTYPE2 (the reference's Q4_K_M files
+ * keep some down matrices in Q6_K). */
+enum { MOE_F32 = 0, MOE_Q8_0 = 1, MOE_Q4_0 = 2, MOE_Q4_K = 3, MOE_Q6_K = 5 };
+#define MOE_QTYPE2(gate_up, down) ((gate_up) | ((down) << 8))
+#define MOE_QTYPE_GU(t) ((t) & 0xFF)
+#define MOE_QTYPE_DN(t) (((t) >> 8) & 0xFF ? ((t) >> 8) & 0xFF : (t) & 0xFF)
 
 enum moe_status {
 	MOE_OK = 0,
@@ -178,7 +184,9 @@ typedef struct moe_layer moe_layer; /* opaque */
 
 typedef struct moe_layer_desc {
 	int64_t d_model, d_ff, n_experts, top_k;
-	int qtype;                   /* MOE_Q8_0 or MOE_Q4_0              */
+	int qtype;                   /* MOE_Q8_0, MOE_Q4_0; K-quants: Q4_K /
+				      * Q6_K or MOE_QTYPE2 of them (CUDA-
+				      * core GEMVs, one GPU)               */
 	int flags;                   /* default flags for forward calls   */
 	const float *router_w;       /* device [n_experts, d_model] fp32  */
 	const float *router_bias;    /* device [n_experts] or NULL        */

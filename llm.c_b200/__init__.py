@@ -17,7 +17,12 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
 
-F32, Q8_0, Q4_0 = 0, 1, 2
+F32, Q8_0, Q4_0, Q4_K, Q6_K = 0, 1, 2, 3, 5
+
+
+def qtype2(gate_up: int, down: int) -> int:
+    """MOE_QTYPE2: a layer's gate/up and down weight types"""
+    return gate_up | (down << 8)
 TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE, SIMPLE = (
     0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40, 0x80)
 NO_FUSE = 0x100
@@ -166,7 +171,8 @@ def reset(device: int = 0):
 
 # ------------------------------------------------------------------ tensors
 def row_bytes(qtype: int, cols: int) -> int:
-    return {Q8_0: cols // 32 * 34, Q4_0: cols // 32 * 18, F32: cols * 4}[qtype]
+    return {Q8_0: cols // 32 * 34, Q4_0: cols // 32 * 18, Q4_K: cols // 256 * 144,
+            Q6_K: cols // 256 * 210, F32: cols * 4}[qtype]
 
 
 def tensor_at(ptr: int, qtype: int, dims) -> MoeTensor:
@@ -403,9 +409,10 @@ def ffn_forward(x, router_w, gate, up, down, qtype, top_k, flags=0):
     out = np.zeros((T, d), np.float32)
     ti, to = tensor(x), tensor(out)
     tr = tensor(np.ascontiguousarray(router_w, np.float32))
-    tg = tensor(gate, qtype, (NE, F, d))
-    tu = tensor(up, qtype, (NE, F, d))
-    td = tensor(down, qtype, (NE, d, F))
+    qg, qd = qtype & 0xFF, (qtype >> 8) or (qtype & 0xFF)
+    tg = tensor(gate, qg, (NE, F, d))
+    tu = tensor(up, qg, (NE, F, d))
+    td = tensor(down, qd, (NE, d, F))
     check(lib().moe_ffn_forward(C.byref(ti), C.byref(to), C.byref(tr), C.byref(tg),
                                 C.byref(tu), C.byref(td), top_k, flags))
     return out

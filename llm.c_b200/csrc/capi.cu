@@ -166,8 +166,15 @@ int64_t qrow_bytes(int type, int64_t cols)
 		return cols / QK * Q8_0_BYTES;
 	if (type == MOE_Q4_0)
 		return cols / QK * Q4_0_BYTES;
+	if (type == MOE_Q4_K)
+		return cols / 256 * 144;
+	if (type == MOE_Q6_K)
+		return cols / 256 * 210;
 	return cols * 4;
 }
+
+bool legacy_type(int t) { return t == MOE_Q8_0 || t == MOE_Q4_0; }
+bool ktype(int t) { return t == MOE_Q4_K || t == MOE_Q6_K; }
 
 // bytes of a tensor's payload from its dims (innermost dim = columns)
 size_t tensor_bytes(const moe_tensor_t *t)
@@ -321,6 +328,8 @@ struct moe_layer {
 	void *wmaps = nullptr;  // device [3][NE] weight tensor maps: gate, up, down
 	// slices of scratch
 	float *logits, *wts, *h, *Y;
+	uint8_t *q8k = nullptr;    // K-quant experts: the tokens as Q8_K blocks
+	int qt_gu = 0, qt_dn = 0;  // the experts' gate/up and down types
 	__half *x16, *h16, *x16p;  // tokens hi/lo (token order), h hi/lo, tokens hi/lo (pair order)
 	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
 	int32_t *active, *n_active, *work;  // [NE], [1], [2]
@@ -379,6 +388,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	size_t o_h = take((size_t)cap * K * F * 4), o_Y = take((size_t)cap * K * D * 4);
 	size_t o_x16 = take((size_t)cap * 2 * D * 2), o_h16 = take((size_t)pcap * 2 * F * 2);
 	size_t o_x16p = take((size_t)cap * K * 2 * D * 2);
+	size_t o_q8k = take(D % 256 == 0 ? (size_t)cap * (D / 256) * 292 : 0);
 	const size_t gbar_bytes = moe::decode_barrier_bytes(moe::sm_count());
 	size_t o_gbar = take(gbar_bytes);
 	size_t o_stamps = take((size_t)kStampRecords * moe::sm_count() * moe::decode_stamps() * 8);
@@ -407,6 +417,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->x16 = (__half *)(b + o_x16);
 	L->x16p = (__half *)(b + o_x16p);
 	L->h16 = (__half *)(b + o_h16);
+	L->q8k = (uint8_t *)(b + o_q8k);
 	L->gbar = (unsigned long long *)(b + o_gbar);
 	L->stamps = (uint64_t *)(b + o_stamps);
 	CK(cudaMemset(L->gbar, 0, gbar_bytes));
@@ -908,9 +919,14 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 	if (int rc = ensure_init())
 		return rc;
 	const moe_layer_desc &d = *desc;
-	if (d.qtype != MOE_Q8_0 && d.qtype != MOE_Q4_0)
-		return fail(MOE_ERR_UNSUPPORTED, "moe_layer_create: qtype %d (Q8_0/Q4_0 only)",
-			    d.qtype);
+	const int qt_gu = MOE_QTYPE_GU(d.qtype), qt_dn = MOE_QTYPE_DN(d.qtype);
+	const bool kq = ktype(qt_gu) || ktype(qt_dn);
+	if (!(kq ? (ktype(qt_gu) && ktype(qt_dn)) : (d.qtype == MOE_Q8_0 || d.qtype == MOE_Q4_0)))
+		return fail(MOE_ERR_UNSUPPORTED, "moe_layer_create: qtype %d (Q8_0 / Q4_0, or Q4_K / "
+			    "Q6_K for gate/up and down)", d.qtype);
+	if (kq && (d.d_model % 256 || d.d_ff % 256))
+		return fail(MOE_ERR_INVALID, "moe_layer_create: K-quant experts need d_model and d_ff "
+			    "multiples of 256");
 	if (d.d_model <= 0 || d.d_ff <= 0 || d.d_model % QK || d.d_ff % QK)
 		return fail(MOE_ERR_INVALID, "moe_layer_create: d_model %lld / d_ff %lld must be "
 			    "positive multiples of 32", (long long)d.d_model, (long long)d.d_ff);
@@ -930,9 +946,13 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 		if (!d.gate[e] || !d.up[e] || !d.down[e])
 			return fail(MOE_ERR_INVALID, "moe_layer_create: expert %lld has no weights",
 				    (long long)e);
+	if (kq && nl < d.n_experts)
+		return fail(MOE_ERR_UNSUPPORTED, "moe_layer_create: K-quant experts on one GPU only");
 	moe_layer *L = new moe_layer();
 	L->d = d;
-	L->mma_ok = moe::expert_mma_supported(d.qtype, (int)d.d_model) &&
+	L->qt_gu = qt_gu;
+	L->qt_dn = qt_dn;
+	L->mma_ok = !kq && moe::expert_mma_supported(d.qtype, (int)d.d_model) &&
 		    moe::expert_mma_supported(d.qtype, (int)d.d_ff);
 	for (int64_t e = first; e < first + nl; e++)
 		L->mma_ok = L->mma_ok && ((uintptr_t)d.gate[e] % 16 == 0) &&
@@ -951,7 +971,7 @@ int moe_layer_create(moe_layer **out, const moe_layer_desc *desc)
 		e = cudaMemcpy(L->dptrs, host.data(), host.size() * sizeof(void *),
 			       cudaMemcpyHostToDevice);
 	const int qt = (int)d.qtype, D = (int)d.d_model, F = (int)d.d_ff;
-	L->gemm_ok = L->mma_ok && moe::expert_gemm_supported(qt, F, D, 1) &&
+	L->gemm_ok = !kq && L->mma_ok && moe::expert_gemm_supported(qt, F, D, 1) &&
 		     moe::expert_gemm_supported(qt, D, F, 0);
 	if (e == cudaSuccess && L->gemm_ok) {
 		// tensor maps of every local expert matrix for the prefill GEMM
@@ -1060,6 +1080,53 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 	if (shard && !ep_ready && !nccl.comm)
 		return fail(MOE_ERR_INVALID, "moe_layer_forward: MOE_EP_SHARDED needs the ranks "
 			    "connected (moe_layer_set_peers and/or moe_ep_init)");
+	if (ktype(L->qt_gu)) {
+		// K-quant experts (kquant.cu): router, routing, tokens to Q8_K, the
+		// gate/up and down GEMVs, combine
+		L->last_pairs = T * K;
+		if (moe::router_tiled_ok(D, NE))
+			CK(moe::launch_router_tiled(x, d.router_w, (int)T, D, NE, lanes, L->logits, nullptr,
+						    0, st));
+		else
+			CK(moe::launch_router_logits(x, d.router_w, (int)T, D, NE, lanes, L->logits, st));
+		if (T <= 256 && moe::route_small_smem((int)T, NE, K) <= 160 * 1024) {
+			CK(moe::launch_route_small(L->logits, d.router_bias, (int)T, NE, K, lanes, mode_exact,
+						   renorm, 0, NE, L->ids, L->wts, L->counts, L->offsets,
+						   L->perm, L->pos_of, L->active, L->n_active, L->err, L->work,
+						   st));
+		} else {
+			CK(moe::launch_router_topk(L->logits, d.router_bias, (int)T, NE, K, lanes,
+						   mode_exact, renorm, L->ids, L->wts, nullptr, st));
+			CK(moe::launch_dispatch(L->ids, (int)(T * K), NE, 0, NE, L->counts, L->offsets,
+						L->perm, L->pos_of, L->active, L->n_active, L->err, L->work,
+						st));
+		}
+		CK(moe::launch_quantize_q8k(x, (int)T, D, L->q8k, st));
+		moe::KqArgs ka{};
+		ka.w1 = L->dptrs;
+		ka.w2 = L->dptrs + NE;
+		ka.rows = F;
+		ka.cols = D;
+		ka.K = K;
+		ka.first_expert = 0;
+		ka.n_local = NE;
+		ka.counts = L->counts;
+		ka.offsets = L->offsets;
+		ka.perm = L->perm;
+		ka.x8 = L->q8k;
+		ka.h = L->h;
+		CK(moe::launch_kq_gate_up(ka, L->qt_gu, st));
+		moe::KqArgs kd = ka;
+		kd.w1 = L->dptrs + 2 * NE;
+		kd.w2 = nullptr;
+		kd.rows = D;
+		kd.cols = F;
+		kd.hin = L->h;
+		kd.out = L->Y;
+		CK(moe::launch_kq_down(kd, L->qt_dn, st));
+		CK(moe::launch_combine(L->Y, L->wts, (int)T, K, D, out, st));
+		return MOE_OK;
+	}
 	const int64_t world_pairs = shard ? (int64_t)L->ep_world * T * K : T * K;
 	if (!simple && !(flags & (MOE_NO_FUSE | MOE_FORCE_GEMM)) && (d.n_local == d.n_experts || ep_ready) &&
 	    moe::decode_supported(d.qtype, T, D, F, NE, K, world_pairs, (uintptr_t)x,
@@ -1915,17 +1982,19 @@ int moe_ffn_forward(const moe_tensor_t *input, moe_tensor_t *output, const moe_t
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: null expert tensor");
 	if (gate_exps->ndim != 3 || up_exps->ndim != 3 || down_exps->ndim != 3)
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: expert tensors must be 3-D");
-	const int qt = gate_exps->type;
-	if (up_exps->type != qt || down_exps->type != qt)
+	// gate/up share a type; down may differ (K-quant files mix Q4_K and Q6_K)
+	const int tgu = gate_exps->type, tdn = down_exps->type;
+	if (up_exps->type != tgu || (tdn != tgu && !(ktype(tgu) && ktype(tdn))))
 		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward: mixed expert dtypes");
+	const int qt = tdn == tgu ? tgu : MOE_QTYPE2(tgu, tdn);
 	const int64_t NE = (int64_t)gate_exps->dim[0], F = (int64_t)gate_exps->dim[1];
 	const int64_t D = (int64_t)gate_exps->dim[2];
 	if ((int64_t)up_exps->dim[0] != NE || (int64_t)up_exps->dim[1] != F ||
 	    (int64_t)up_exps->dim[2] != D || (int64_t)down_exps->dim[0] != NE ||
 	    (int64_t)down_exps->dim[1] != D || (int64_t)down_exps->dim[2] != F)
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward: expert shapes disagree");
-	if (qt != MOE_Q8_0 && qt != MOE_Q4_0)
-		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward: expert dtype %d", qt);
+	if (!legacy_type(tgu) && !ktype(tgu))
+		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward: expert dtype %d", tgu);
 	// repeat call with the same tensors: the cached layer, without
 	// resolving every expert's view again (~200 lookups and a 198-entry key)
 	const std::array<uintptr_t, 9> fk{(uintptr_t)(gate_inp ? gate_inp->data : nullptr),
@@ -1941,7 +2010,7 @@ int moe_ffn_forward(const moe_tensor_t *input, moe_tensor_t *output, const moe_t
 		}
 	}
 	// tensor_at_q (olmoe.c:20-60): expert e starts e*rows*(cols/32)*bsz bytes in
-	const size_t gb = (size_t)(F * qrow_bytes(qt, D)), db = (size_t)(D * qrow_bytes(qt, F));
+	const size_t gb = (size_t)(F * qrow_bytes(tgu, D)), db = (size_t)(D * qrow_bytes(tdn, F));
 	if (int rc = ensure_init())
 		return rc;
 	const void *tmp;
@@ -1973,14 +2042,16 @@ int moe_ffn_forward_split(const moe_tensor_t *input, moe_tensor_t *output,
 {
 	if (!gate_exp || !up_exp || !down_exp || n_experts == 0)
 		return fail(MOE_ERR_INVALID, "moe_ffn_forward_split: no experts");
-	const int qt = gate_exp[0]->type;
+	const int tgu = gate_exp[0]->type, tdn = down_exp[0] ? down_exp[0]->type : tgu;
 	const int64_t F = (int64_t)gate_exp[0]->dim[0], D = (int64_t)gate_exp[0]->dim[1];
-	if (qt != MOE_Q8_0 && qt != MOE_Q4_0)
-		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward_split: expert dtype %d", qt);
+	if ((!legacy_type(tgu) && !ktype(tgu)) || (tdn != tgu && !(ktype(tgu) && ktype(tdn))))
+		return fail(MOE_ERR_UNSUPPORTED, "moe_ffn_forward_split: expert dtypes %d/%d", tgu,
+			    tdn);
+	const int qt = tdn == tgu ? tgu : MOE_QTYPE2(tgu, tdn);
 	std::vector<const void *> hg(n_experts), hu(n_experts), hd(n_experts);
 	for (size_t e = 0; e < n_experts; e++) {
 		const moe_tensor_t *a = gate_exp[e], *b = up_exp[e], *c = down_exp[e];
-		if (!a || !b || !c || a->type != qt || b->type != qt || c->type != qt ||
+		if (!a || !b || !c || a->type != tgu || b->type != tgu || c->type != tdn ||
 		    (int64_t)a->dim[0] != F || (int64_t)a->dim[1] != D || (int64_t)b->dim[0] != F ||
 		    (int64_t)b->dim[1] != D || (int64_t)c->dim[0] != D || (int64_t)c->dim[1] != F)
 			return fail(MOE_ERR_INVALID, "moe_ffn_forward_split: expert %zu shape/type", e);
@@ -1988,7 +2059,7 @@ int moe_ffn_forward_split(const moe_tensor_t *input, moe_tensor_t *output,
 		hu[e] = b->qdata;
 		hd[e] = c->qdata;
 	}
-	const size_t gb = (size_t)(F * qrow_bytes(qt, D)), db = (size_t)(D * qrow_bytes(qt, F));
+	const size_t gb = (size_t)(F * qrow_bytes(tgu, D)), db = (size_t)(D * qrow_bytes(tdn, F));
 	return forward_common(input, output, gate_inp, qt, (int64_t)n_experts, F, D, hg, hu, hd, gb,
 			      db, topk, flags, nullptr);
 }

@@ -64,7 +64,7 @@ inline int sm_count()
 	return n[dev];
 }
 
-enum QType { kF32 = 0, kQ8_0 = 1, kQ4_0 = 2 };
+enum QType { kF32 = 0, kQ8_0 = 1, kQ4_0 = 2, kQ4_K = 3, kQ6_K = 5 };
 
 __host__ __device__ inline int64_t block_bytes(int qtype)
 {

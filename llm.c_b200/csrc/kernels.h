@@ -243,6 +243,23 @@ cudaError_t launch_copy_segments(const void *src, void *dst, const int64_t *seg,
 cudaError_t launch_add_bias(float *ret, const float *add, int64_t total, int64_t n_add,
 			    cudaStream_t st);
 
+// kquant.cu: K-quant experts (Q4_K = 3, Q6_K = 5, the reference's tensor
+// dtype values) over the dispatch's expert segments
+struct KqArgs {
+	const void *const *w1, *const *w2;  // device arrays [NE] of expert matrices
+	int rows, cols;                     // the matrices' shape (cols % 256 == 0)
+	int K, first_expert, n_local;
+	const int32_t *counts, *offsets, *perm;
+	const uint8_t *x8;                  // gate/up: tokens as Q8_K [T][cols/256]
+	const float *hin;                   // down: h rows [pairs][cols]
+	float *h;                           // gate/up: h rows [pairs][rows] (pair order)
+	float *out;                         // down: Y rows [pairs by t*K + slot][rows]
+};
+bool kquant_type(int qtype);
+cudaError_t launch_quantize_q8k(const float *x, int T, int D, uint8_t *y, cudaStream_t st);
+cudaError_t launch_kq_gate_up(const KqArgs &a, int qtype, cudaStream_t st);
+cudaError_t launch_kq_down(const KqArgs &a, int qtype, cudaStream_t st);
+
 // capi.cu: the dense projection y[m, rows] = x[m, cols] . W[rows, cols]^T
 // (Q8_0/Q4_0 W) behind moe_gemv_device, with caller-owned scratch; returns
 // a MOE_* status (the message through moe_last_error)
