@@ -349,9 +349,12 @@ __device__ __forceinline__ float sumsq4(const float *__restrict__ v, int n, floa
 // does the same for its KV head's key, stores key and value into the cache
 // and uses them from registers.  Each CTA's online-softmax partial goes to
 // part[h][c]; the head's last CTA to finish (arrival counter cnt[h], reset by
-// that CTA) merges them into out[h].  Rows are taken four at a time per
-// warp with their loads issued first.
+// that CTA) merges them into out[h].  Each warp's first kStepU rows, the
+// rope factors and the raw q (k, v) are loaded before the norm reductions,
+// which would otherwise stand between dependent round trips; further rows
+// go four at a time with their loads issued first.
 constexpr int kStepThreads = 256, kStepWarps = kStepThreads / 32;
+constexpr int kStepU = 8;   // cache rows per warp loaded before the norms
 
 __global__ void __launch_bounds__(kStepThreads) attn_step_kernel(AttnStepArgs a)
 {
@@ -376,6 +379,29 @@ __global__ void __launch_bounds__(kStepThreads) attn_step_kernel(AttnStepArgs a)
 	const int group = a.H / a.KVH, kvh = h / group;
 	const int nq = a.H * HL, nk = a.KVH * HL;
 	const float *qs = a.qkv, *ks = a.qkv + nq, *vs = a.qkv + nq + nk;
+	const float *kb = a.kc + (int64_t)kvh * a.C * HL, *vb = a.vc + (int64_t)kvh * a.C * HL;
+	const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+	// every load that does not wait for the norms goes out first: this
+	// warp's first kStepU cache rows, the rope factors, the head's raw q (and
+	// for the new row k, v) with their norm weights
+	float4 kk[kStepU], vv[kStepU];
+#pragma unroll
+	for (int u = 0; u < kStepU; u++) {
+		const int r = r0 + warp + u * kStepWarps;
+		const bool in = r < r1 && r != size;
+		kk[u] = in ? reinterpret_cast<const float4 *>(kb + (int64_t)r * HL)[lane] : z4;
+		vv[u] = in ? reinterpret_cast<const float4 *>(vb + (int64_t)r * HL)[lane] : z4;
+	}
+	const float2 c0 = a.rope[(int64_t)pos * (HL / 2) + 2 * lane];
+	const float2 c1 = a.rope[(int64_t)pos * (HL / 2) + 2 * lane + 1];
+	const float4 qraw = reinterpret_cast<const float4 *>(qs + h * HL)[lane];
+	const float4 qw = a.q_norm ? reinterpret_cast<const float4 *>(a.q_norm + h * HL)[lane] : z4;
+	float4 kraw = z4, kw = z4, vnew = z4;
+	if (tail) {
+		kraw = reinterpret_cast<const float4 *>(ks + kvh * HL)[lane];
+		kw = a.k_norm ? reinterpret_cast<const float4 *>(a.k_norm + kvh * HL)[lane] : z4;
+		vnew = reinterpret_cast<const float4 *>(vs + kvh * HL)[lane];
+	}
 	float rq = 1.0f, rk = 1.0f;
 	if (a.q_norm) {
 		rq = sqrtf(sumsq4(qs, nq, red) / (float)nq + a.eps);
@@ -383,12 +409,8 @@ __global__ void __launch_bounds__(kStepThreads) attn_step_kernel(AttnStepArgs a)
 			rk = sqrtf(sumsq4(ks, nk, red) / (float)nk + a.eps);
 	}
 	// lane owns elements 4 lane .. 4 lane + 3 of a head: pairs 2 lane, 2 lane + 1
-	const float2 c0 = a.rope[(int64_t)pos * (HL / 2) + 2 * lane];
-	const float2 c1 = a.rope[(int64_t)pos * (HL / 2) + 2 * lane + 1];
-	auto norm_rope = [&](const float *src, const float *nw, float r, int base) {
-		float4 v = reinterpret_cast<const float4 *>(src + base)[lane];
-		if (nw) {
-			const float4 w = reinterpret_cast<const float4 *>(nw + base)[lane];
+	auto norm_rope = [&](float4 v, float4 w, bool norm, float r) {
+		if (norm) {
 			v.x = (v.x / r) * w.x;
 			v.y = (v.y / r) * w.y;
 			v.z = (v.z / r) * w.z;
@@ -397,48 +419,53 @@ __global__ void __launch_bounds__(kStepThreads) attn_step_kernel(AttnStepArgs a)
 		return make_float4(v.x * c0.x - v.y * c0.y, v.x * c0.y + v.y * c0.x,
 				   v.z * c1.x - v.w * c1.y, v.z * c1.y + v.w * c1.x);
 	};
-	const float4 qv = norm_rope(qs, a.q_norm, rq, h * HL);
-	float4 knew = make_float4(0.f, 0.f, 0.f, 0.f), vnew = knew;
-	const float *kb = a.kc + (int64_t)kvh * a.C * HL, *vb = a.vc + (int64_t)kvh * a.C * HL;
+	const float4 qv = norm_rope(qraw, qw, a.q_norm != nullptr, rq);
+	float4 knew = z4;
 	if (tail) {
-		knew = norm_rope(ks, a.k_norm, rk, kvh * HL);
-		vnew = reinterpret_cast<const float4 *>(vs + kvh * HL)[lane];
+		knew = norm_rope(kraw, kw, a.k_norm != nullptr, rk);
 		if (warp == 0 && h % group == 0) {
 			reinterpret_cast<float4 *>(a.kc + ((int64_t)kvh * a.C + size) * HL)[lane] = knew;
 			reinterpret_cast<float4 *>(a.vc + ((int64_t)kvh * a.C + size) * HL)[lane] = vnew;
 		}
 	}
 	float m = -FLT_MAX, l = 0.0f;
-	float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-	constexpr int U = 4;
-	for (int rb = r0 + warp; rb < r1; rb += kStepWarps * U) {
-		float4 kk[U], vv[U];
+	float4 o = z4;
+	auto take = [&](float4 k4, float4 v4) {
+		float s = qv.x * k4.x;
+		s = fmaf(qv.y, k4.y, s);
+		s = fmaf(qv.z, k4.z, s);
+		s = fmaf(qv.w, k4.w, s);
+		s = warp_sum(s) / a.scale_div;
+		const float mn = fmaxf(m, s);
+		const float f = expf(m - mn), p = expf(s - mn);
+		l = fmaf(l, f, p);
+		o.x = fmaf(o.x, f, p * v4.x);
+		o.y = fmaf(o.y, f, p * v4.y);
+		o.z = fmaf(o.z, f, p * v4.z);
+		o.w = fmaf(o.w, f, p * v4.w);
+		m = mn;
+	};
 #pragma unroll
-		for (int u = 0; u < U; u++) {
+	for (int u = 0; u < kStepU; u++) {
+		const int r = r0 + warp + u * kStepWarps;
+		if (r < r1)
+			take(r == size ? knew : kk[u], r == size ? vnew : vv[u]);
+	}
+	// rows past the first batch (long caches): four at a time, loads first
+	for (int rb = r0 + warp + kStepU * kStepWarps; rb < r1; rb += kStepWarps * 4) {
+		float4 k4[4], v4[4];
+#pragma unroll
+		for (int u = 0; u < 4; u++) {
 			const int r = rb + u * kStepWarps;
-			const bool in = r < r1, fresh = r == size;
-			kk[u] = !in ? make_float4(0.f, 0.f, 0.f, 0.f)
-			       : fresh ? knew : reinterpret_cast<const float4 *>(kb + (int64_t)r * HL)[lane];
-			vv[u] = !in ? make_float4(0.f, 0.f, 0.f, 0.f)
-			       : fresh ? vnew : reinterpret_cast<const float4 *>(vb + (int64_t)r * HL)[lane];
+			const bool in = r < r1 && r != size;
+			k4[u] = in ? reinterpret_cast<const float4 *>(kb + (int64_t)r * HL)[lane] : z4;
+			v4[u] = in ? reinterpret_cast<const float4 *>(vb + (int64_t)r * HL)[lane] : z4;
 		}
 #pragma unroll
-		for (int u = 0; u < U; u++) {
-			if (rb + u * kStepWarps >= r1)
-				break;
-			float s = qv.x * kk[u].x;
-			s = fmaf(qv.y, kk[u].y, s);
-			s = fmaf(qv.z, kk[u].z, s);
-			s = fmaf(qv.w, kk[u].w, s);
-			s = warp_sum(s) / a.scale_div;
-			const float mn = fmaxf(m, s);
-			const float f = expf(m - mn), p = expf(s - mn);
-			l = fmaf(l, f, p);
-			o.x = fmaf(o.x, f, p * vv[u].x);
-			o.y = fmaf(o.y, f, p * vv[u].y);
-			o.z = fmaf(o.z, f, p * vv[u].z);
-			o.w = fmaf(o.w, f, p * vv[u].w);
-			m = mn;
+		for (int u = 0; u < 4; u++) {
+			const int r = rb + u * kStepWarps;
+			if (r < r1)
+				take(r == size ? knew : k4[u], r == size ? vnew : v4[u]);
 		}
 	}
 	if (lane == 0) {
