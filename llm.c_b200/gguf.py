@@ -260,6 +260,33 @@ def mixtral_plan(layers: int, d: int, q_heads: int, kv_heads: int, n_exp: int, t
     return meta, ts
 
 
+def llama_dense_plan(layers: int, d: int, q_heads: int, kv_heads: int, d_ff: int, vocab: int,
+                     context: int = 4096, rope_theta: float = 5e5):
+    """the llama architecture without experts (llama.c:86-94: one dense
+    SwiGLU FFN per layer, blk.L.ffn_{gate,up,down}.weight)"""
+    meta0, _ = mixtral_plan(layers, d, q_heads, kv_heads, 1, 1, d_ff, vocab, context, rope_theta)
+    hl = d // q_heads
+
+    def meta(w):
+        meta0(w)
+        # no experts: drop the expert keys the MoE plan wrote
+        w.kv = [kv for kv in w.kv if kv[0] not in ("llama.expert_count", "llama.expert_used_count")]
+    ts = [("token_embd.weight", (vocab, d), "mat"), ("output.weight", (vocab, d), "mat"),
+          ("output_norm.weight", (d,), "norm")]
+    for i in range(layers):
+        p = f"blk.{i}."
+        ts.append((p + "attn_norm.weight", (d,), "norm"))
+        ts.append((p + "attn_q.weight", (q_heads * hl, d), "mat"))
+        ts.append((p + "attn_k.weight", (kv_heads * hl, d), "mat"))
+        ts.append((p + "attn_v.weight", (kv_heads * hl, d), "mat"))
+        ts.append((p + "attn_output.weight", (d, q_heads * hl), "mat"))
+        ts.append((p + "ffn_norm.weight", (d,), "norm"))
+        ts.append((p + "ffn_gate.weight", (d_ff, d), "mat"))
+        ts.append((p + "ffn_up.weight", (d_ff, d), "mat"))
+        ts.append((p + "ffn_down.weight", (d, d_ff), "mat"))
+    return meta, ts
+
+
 def write_plan(path: str, plan, qtype: int, seed: int, sd: float = 0.02, norm_sd: float = 0.0):
     """a random-init file: numpy's PCG64 stream `seed` for the matrices and
     routers in file order, quantized on the host; RMSNorm weights from

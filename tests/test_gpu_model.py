@@ -178,3 +178,25 @@ def test_fused_decode_step_matches_reference(moe, orc, tmp_path, arch):
     want = np.concatenate([ref["tokens"], [int(np.argmax(ref["logits"][-1]))]])
     same_greedy(picks, want, ref["logits"])
     assert model.status() == 0
+
+
+@pytest.mark.parametrize("d,d_ff", [(512, 768), (2048, 1024)])
+def test_dense_llama_match_reference(moe, orc, tmp_path, d, d_ff):
+    """llama without experts (llama.c's dense_ffn, llama.c:365-391): the FFN
+    runs as one expert that every token takes with weight 1"""
+    gg = gguf_module()
+    path = str(tmp_path / "dense.gguf")
+    plan = gg.llama_dense_plan(2, d, d // 128, 2, d_ff, 600, context=64)
+    gg.write_plan(path, plan, gg.Q8_0, seed=23, norm_sd=0.1)
+    prompt = np.random.default_rng(11).integers(0, 600, 12)
+    ref = ref_model(orc, path, prompt, 4, d, 600)
+    model = moe.Model.from_gguf(gg.GGUFReader(path))
+    close(model.prefill(prompt), ref["rows"], "prefill rows")
+    for i, t in enumerate(ref["tokens"]):
+        close(model.decode(int(t), 12 + i), ref["drows"][i], f"decode row {i}")
+        close(model.logits(0), ref["logits"][i + 1], f"decode logits {i}")
+    model.reset()
+    picks = model.generate(prompt, 4)
+    want = np.concatenate([ref["tokens"], [int(np.argmax(ref["logits"][-1]))]])
+    same_greedy(picks, want, ref["logits"])
+    assert model.status() == 0
