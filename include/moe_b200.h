@@ -93,6 +93,10 @@ enum moe_status {
                              /* own tokens and out receives their outputs    */
                              /* (tokens travel to the experts' ranks and the */
                              /* rows back); see moe_layer_set_peers          */
+#define MOE_NO_T1       0x400 /* one token: keep it on the fused layer kernel */
+                             /* instead of the single-token expert GEMVs     */
+#define MOE_FORCE_T1    0x800 /* one token: the single-token expert GEMVs for */
+                             /* any expert type (default: Q4_0 experts)      */
 
 /* ------------------------------------------------------------------ */
 /* Library lifetime                                                     */

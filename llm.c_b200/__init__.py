@@ -27,6 +27,8 @@ TOPK_EXACT, DEVICE_IO, LANES_AVX2, RENORM, FORCE_GEMV, FORCE_GEMM, PROFILE, SIMP
     0x1, 0x2, 0x4, 0x8, 0x10, 0x20, 0x40, 0x80)
 NO_FUSE = 0x100
 EP_SHARDED = 0x200
+NO_T1 = 0x400
+FORCE_T1 = 0x800
 
 ERRORS = {0: "MOE_OK", -1: "MOE_ERR_INVALID", -2: "MOE_ERR_UNSUPPORTED", -3: "MOE_ERR_CUDA",
           -4: "MOE_ERR_NOMEM", -5: "MOE_ERR_NOT_INIT", -6: "MOE_ERR_COMM", -7: "MOE_ERR_TIMEOUT"}

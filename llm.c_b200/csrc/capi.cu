@@ -334,6 +334,7 @@ struct moe_layer {
 	int32_t *ids, *counts, *offsets, *perm, *pos_of, *err;
 	int32_t *active, *n_active, *work;  // [NE], [1], [2]
 	unsigned long long *gbar;           // grid barrier arrivals of the fused kernel
+	unsigned *t1cnt;                    // arrivals of the single-token router
 	uint64_t *stamps;                   // [kStampRecords][grid][stamps]
 	// expert parallelism (n_local < n_experts): exchange buffer of this rank
 	// (moe::ep_layout: two Y halves, counters, gathered ids and tokens),
@@ -367,6 +368,19 @@ namespace {
 
 constexpr size_t kStampRecords = 64;  // profiled fused forwards kept per layer
 
+// single-token layers of these expert types take the single-row GEMV path;
+// MOE_T1=0 / MOE_T1=1 in the environment turn it off / on for both types
+bool t1_on(int qtype)
+{
+	static const int mode = [] {
+		const char *e = getenv("MOE_T1");
+		return e ? (e[0] == '0' ? 0 : 1) : -1;
+	}();
+	if (mode >= 0)
+		return mode == 1;
+	return qtype == MOE_Q4_0;
+}
+
 int layer_scratch(moe_layer *L, int64_t T)
 {
 	if (T <= L->capT)
@@ -390,7 +404,7 @@ int layer_scratch(moe_layer *L, int64_t T)
 	size_t o_x16p = take((size_t)cap * K * 2 * D * 2);
 	size_t o_q8k = take(D % 256 == 0 ? (size_t)cap * (D / 256) * 292 : 0);
 	const size_t gbar_bytes = moe::decode_barrier_bytes(moe::sm_count());
-	size_t o_gbar = take(gbar_bytes);
+	size_t o_gbar = take(gbar_bytes), o_t1cnt = take(4);
 	size_t o_stamps = take((size_t)kStampRecords * moe::sm_count() * moe::decode_stamps() * 8);
 	if (L->scratch) {
 		CK(cudaStreamSynchronize(g.stream));
@@ -419,8 +433,10 @@ int layer_scratch(moe_layer *L, int64_t T)
 	L->h16 = (__half *)(b + o_h16);
 	L->q8k = (uint8_t *)(b + o_q8k);
 	L->gbar = (unsigned long long *)(b + o_gbar);
+	L->t1cnt = (unsigned *)(b + o_t1cnt);
 	L->stamps = (uint64_t *)(b + o_stamps);
 	CK(cudaMemset(L->gbar, 0, gbar_bytes));
+	CK(cudaMemset(L->t1cnt, 0, 4));
 	CK(cudaDeviceSynchronize());  // ordered before launches on any stream
 	L->capT = cap;
 	return MOE_OK;
@@ -1128,7 +1144,14 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 		return MOE_OK;
 	}
 	const int64_t world_pairs = shard ? (int64_t)L->ep_world * T * K : T * K;
-	if (!simple && !(flags & (MOE_NO_FUSE | MOE_FORCE_GEMM)) && (d.n_local == d.n_experts || ep_ready) &&
+	// one token on one GPU: its K experts through the single-row GEMV
+	// (gemv.cu), when that is the faster kernel for the expert type
+	const bool t1 = T == 1 && !simple && ((flags & MOE_FORCE_T1) || t1_on(d.qtype)) &&
+			!(flags & (MOE_NO_FUSE | MOE_FORCE_GEMM | MOE_NO_T1)) &&
+			d.n_local == d.n_experts && !ep_ready && !shard && (uintptr_t)x % 16 == 0 &&
+			(uintptr_t)d.router_w % 16 == 0 && moe::router_t1_ok(D, NE, K) &&
+			moe::expert_t1_chunks(d.qtype, D, F, K) > 0;
+	if (!simple && !t1 && !(flags & (MOE_NO_FUSE | MOE_FORCE_GEMM)) && (d.n_local == d.n_experts || ep_ready) &&
 	    moe::decode_supported(d.qtype, T, D, F, NE, K, world_pairs, (uintptr_t)x,
 				  (uintptr_t)d.router_w, (uintptr_t)out)) {
 		uint64_t *stamps = nullptr;
@@ -1203,6 +1226,26 @@ int moe_layer_forward(moe_layer *L, const float *x, float *out, int64_t T, int f
 	if (shard)
 		return forward_sharded_a2a(L, x, out, T, flags, st, ev);
 	L->last_pairs = T * K;
+	if (t1) {
+		// [0] + [1] router, top-k and dispatch in one launch; gate/up rows
+		// of the K experts -> L->h ([2K][F]); down in column chunks -> L->Y
+		// ([chunks][K][D]); combine
+		CK(moe::launch_router_t1(x, d.router_w, d.router_bias, D, NE, K, lanes, mode_exact,
+					 renorm, L->logits, L->ids, L->wts, L->counts, L->offsets,
+					 L->perm, L->pos_of, L->active, L->n_active, L->err, L->work,
+					 L->t1cnt, st));
+		if (prof) {
+			CK(record(ev[1]));
+			CK(record(ev[2]));
+		}
+		for (int stage = 0; stage < 3; stage++) {
+			CK(moe::launch_expert_t1(stage, L->dptrs, L->ids, L->wts, d.qtype, D, F, NE, K, x,
+						 L->h, L->Y, out, L->err, st));
+			if (prof)
+				CK(record(ev[3 + stage]));
+		}
+		return MOE_OK;
+	}
 	// prefill-sized batches: grouped GEMMs on tcgen05 (the tokens are gathered
 	// into pair order after the dispatch instead of split in token order)
 	const bool gemm = !simple && L->gemm_ok && !(flags & MOE_FORCE_GEMV) &&

@@ -146,11 +146,31 @@ __device__ __forceinline__ void pair_codes(uint32_t a, uint32_t (&ev)[2], uint32
 	}
 }
 
+// Expert segments (SegMap with wtab set): the grid is split into units
+// (column chunk, activation row), the CTAs of a unit into row ranges of its
+// segments placed end to end.  Row r of a unit: segment r / rows, row
+// r % rows of that matrix, its chunk `c` of nb blocks.
+struct SegPos {
+	int c, xi;     // column chunk, activation row (down: the slot)
+	int nseg;      // segments of the unit (gate/up: 2K, down: 1)
+};
+
+__device__ __forceinline__ const uint8_t *seg_row(const SegMap &sm, const SegPos &p, int rows,
+						  int r, int64_t rb)
+{
+	const int sl = r / rows, rr = r - sl * rows;
+	const int slot = sm.down ? p.xi : (sl < sm.K ? sl : sl - sm.K);
+	const int kind = sm.down ? 2 : (sl < sm.K ? 0 : 1);
+	const uint8_t *base = static_cast<const uint8_t *>(sm.wtab[kind * sm.NE + sm.ids[slot]]);
+	return base + (int64_t)rr * sm.rb_full + (int64_t)p.c * rb;
+}
+
 // NBW: blocks of a row per math warp (cols / 32 / kTcMath, even)
 template <int QT, int NBW>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
-	       const float *__restrict__ x, float *__restrict__ y, int32_t *err, NormIn nin)
+	       const float *__restrict__ x, float *__restrict__ y, int32_t *err, NormIn nin,
+	       SegMap sm)
 {
 	constexpr int BB = QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES;
 	extern __shared__ __align__(128) uint8_t smem[];
@@ -165,8 +185,32 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	uint64_t *empty = full + kTcMaxStages;
 
 	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-	const int r0 = (int)((int64_t)blockIdx.x * rows / gridDim.x);
-	const int r1 = (int)((int64_t)(blockIdx.x + 1) * rows / gridDim.x);
+	int r0 = (int)((int64_t)blockIdx.x * rows / gridDim.x);
+	int r1 = (int)((int64_t)(blockIdx.x + 1) * rows / gridDim.x);
+	SegPos sp{0, 0, 1};
+	if (sm.wtab) {
+		// this CTA's unit and its row range in the unit's segments
+		const int nx = sm.down ? sm.K : 1, U = sm.nchunks * nx, G = (int)gridDim.x;
+		const int u = (int)((int64_t)blockIdx.x * U / G);
+		const int b0u = (int)(((int64_t)u * G + U - 1) / U);
+		const int b1u = (int)(((int64_t)(u + 1) * G + U - 1) / U);
+		sp.c = u % sm.nchunks;
+		sp.xi = u / sm.nchunks;
+		sp.nseg = sm.down ? 1 : 2 * sm.K;
+		const int64_t R = (int64_t)sp.nseg * rows;
+		const int i = (int)blockIdx.x - b0u, n = b1u - b0u;
+		r0 = (int)(i * R / n);
+		r1 = (int)((i + 1) * R / n);
+		// a slot's expert out of range: flag it, compute nothing
+		bool bad = false;
+		for (int k = 0; k < sm.K; k++)
+			bad |= (unsigned)sm.ids[k] >= (unsigned)sm.NE;
+		if (bad) {
+			if (tid == 0 && err)
+				atomicExch(err, 1);
+			return;
+		}
+	}
 	const int ntiles = (r1 - r0 + kTcRows - 1) / kTcRows;
 	if (tid == 0) {
 		for (int i = 0; i < stages; i++) {
@@ -200,9 +244,10 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 				mbar_arrive_expect_tx(&full[slot], (uint32_t)(n * rb));
 			__syncwarp();
 			if (lane < n) {
+				const uint8_t *src = sm.wtab ? seg_row(sm, sp, rows, r + lane, rb)
+							     : w + (int64_t)(r + lane) * rb;
 				fence_proxy_async();
-				bulk_g2s(ring + slot * tile_bytes + lane * rs, w + (int64_t)(r + lane) * rb,
-					 (uint32_t)rb, &full[slot]);
+				bulk_g2s(ring + slot * tile_bytes + lane * rs, src, (uint32_t)rb, &full[slot]);
 			}
 		}
 		// no copy may still be landing when the CTA ends: wait for the last
@@ -259,11 +304,27 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 #pragma unroll
 			for (int j = 0; j < NBW; j++)
 				v[j] = (v[j] / rms) * wn[j];
-		} else {
+		} else if (sm.wtab && sm.down) {
+			// h of this unit's slot: swiglu(gate row, up row) (nn.c:475-478)
+			const int64_t cols = (int64_t)sm.nchunks * nb * 32;
+			const float *g = sm.gu + (int64_t)sp.xi * cols + (int64_t)sp.c * nb * 32;
+			const float *u = g + (int64_t)sm.K * cols;
+			float gv[NBW], uv[NBW];
 #pragma unroll
 			for (int j = 0; j < NBW; j++) {
 				const int b = warp + j * kTcMath;
-				v[j] = __ldg(x + (int64_t)b * 32 + lane);
+				gv[j] = __ldcg(g + (int64_t)b * 32 + lane);
+				uv[j] = __ldcg(u + (int64_t)b * 32 + lane);
+			}
+#pragma unroll
+			for (int j = 0; j < NBW; j++)
+				v[j] = swiglu(gv[j], uv[j]);
+		} else {
+			const float *xc = x + (int64_t)sp.c * nb * 32;
+#pragma unroll
+			for (int j = 0; j < NBW; j++) {
+				const int b = warp + j * kTcMath;
+				v[j] = __ldg(xc + (int64_t)b * 32 + lane);
 			}
 		}
 		const int t_k = (lane & 15) >> 2, hi = lane >= 16 ? 4 : 0;
@@ -393,8 +454,16 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 #pragma unroll
 			for (int q = 0; q < kTcMath; q++)
 				v += rsum[q * kTcRows];
-			if (r < r1)
-				y[r] = v;
+			if (r < r1) {
+				if (sm.wtab) {
+					const int sl = r / rows, rr = r - sl * rows;
+					const int s_ = sm.down ? sp.xi : sl;
+					const int nsg = sm.down ? sm.K : 2 * sm.K;
+					sm.part[((int64_t)sp.c * nsg + s_) * rows + rr] = v;
+				} else {
+					y[r] = v;
+				}
+			}
 		}
 	}
 }
@@ -549,7 +618,7 @@ static cudaError_t launch_tc_t(const void *w, int64_t rows, int nb, const float 
 	cfg.attrs = at;
 	cfg.numAttrs = pdl ? 1 : 0;
 	return cudaLaunchKernelEx(&cfg, fn, static_cast<const uint8_t *>(w), (int)rows, nb, stages,
-				  x, y, err, nin);
+				  x, y, err, nin, SegMap{});
 }
 
 template <int QT>
@@ -575,6 +644,117 @@ static cudaError_t launch_tc(const void *w, int64_t rows, int64_t cols, const fl
 	default:
 		return cudaErrorInvalidValue;
 	}
+}
+
+// ---------------------------------------------------------------- one token's experts
+template <int QT, int NBW>
+static cudaError_t launch_seg_t(int rows, int nb, const float *x, int32_t *err, int stages,
+				size_t smem, const SegMap &sm, cudaStream_t st)
+{
+	auto fn = gemv_tc_kernel<QT, NBW>;
+	cudaError_t e = ensure_smem(fn, smem);
+	if (e != cudaSuccess)
+		return e;
+	fn<<<(unsigned)sm_count(), kTcThreads, smem, st>>>(nullptr, rows, nb, stages, x, nullptr, err,
+							   NormIn{}, sm);
+	return cudaGetLastError();
+}
+
+template <int QT>
+static cudaError_t launch_seg(int rows, int64_t cols, const float *x, int32_t *err,
+			      const SegMap &sm, cudaStream_t st)
+{
+	const int stages = tc_stages(QT, cols);
+	if (!stages)
+		return cudaErrorNotSupported;
+	const int nb = (int)(cols / QK);
+	const int64_t rb = (int64_t)nb * (QT == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES);
+	const size_t smem = tc_smem(stages, kTcRows * tc_row_stride(rb), nb);
+	switch (nb / kTcMath) {
+	case 2:
+		return launch_seg_t<QT, 2>(rows, nb, x, err, stages, smem, sm, st);
+	case 4:
+		return launch_seg_t<QT, 4>(rows, nb, x, err, stages, smem, sm, st);
+	case 6:
+		return launch_seg_t<QT, 6>(rows, nb, x, err, stages, smem, sm, st);
+	case 8:
+		return launch_seg_t<QT, 8>(rows, nb, x, err, stages, smem, sm, st);
+	case 10:
+		return launch_seg_t<QT, 10>(rows, nb, x, err, stages, smem, sm, st);
+	case 12:
+		return launch_seg_t<QT, 12>(rows, nb, x, err, stages, smem, sm, st);
+	default:
+		return cudaErrorInvalidValue;
+	}
+}
+
+// out = sum over slots k (in slot order) of y_k / (1 / w_k), y_k the sum of
+// its column chunks' partial rows in chunk order (the combine of
+// olmoe.c:387-405 with the reciprocal division of the other paths)
+__global__ void t1_combine_kernel(const float *__restrict__ part, const float *__restrict__ w,
+				  int nchunks, int K, int D, float *__restrict__ out)
+{
+	const int j = blockIdx.x * blockDim.x + threadIdx.x;
+	if (j >= D)
+		return;
+	float acc = 0.0f;
+	for (int k = 0; k < K; k++) {
+		float y = part[(int64_t)k * D + j];
+		for (int c = 1; c < nchunks; c++)
+			y = __fadd_rn(y, part[((int64_t)c * K + k) * D + j]);
+		acc = __fadd_rn(__fdiv_rn(y, __fdiv_rn(1.0f, w[k])), acc);
+	}
+	out[j] = acc;
+}
+
+int expert_t1_chunks(int qtype, int64_t D, int64_t F, int K)
+{
+	if ((qtype != kQ8_0 && qtype != kQ4_0) || K < 1 || K > 32 || !tc_stages(qtype, D) ||
+	    F > INT32_MAX / 2 || D > INT32_MAX / 2)
+		return 0;
+	// the largest chunk of whole 1024-column groups that the ring fits
+	for (int64_t n = 1; n <= 64; n++) {
+		if (F % n != 0 || (F / n) % 1024 != 0)
+			continue;
+		if (tc_stages(qtype, F / n))
+			return n * K <= sm_count() ? (int)n : 0;
+	}
+	return 0;
+}
+
+cudaError_t launch_expert_t1(int stage, const void *const *wtab, const int32_t *ids,
+			     const float *w, int qtype, int64_t D, int64_t F, int NE, int K,
+			     const float *x, float *gu, float *part, float *out, int32_t *err,
+			     cudaStream_t st)
+{
+	const int nch = expert_t1_chunks(qtype, D, F, K);
+	if (!nch)
+		return cudaErrorNotSupported;
+	const int BB = qtype == kQ8_0 ? Q8_0_BYTES : Q4_0_BYTES;
+	SegMap a;
+	a.wtab = wtab;
+	a.ids = ids;
+	a.NE = NE;
+	a.K = K;
+	if (stage == 0) {
+		a.down = 0;
+		a.nchunks = 1;
+		a.rb_full = D / QK * BB;
+		a.part = gu;
+		return qtype == kQ8_0 ? launch_seg<kQ8_0>((int)F, D, x, err, a, st)
+				      : launch_seg<kQ4_0>((int)F, D, x, err, a, st);
+	}
+	if (stage == 1) {
+		a.down = 1;
+		a.nchunks = nch;
+		a.rb_full = F / QK * BB;
+		a.gu = gu;
+		a.part = part;
+		return qtype == kQ8_0 ? launch_seg<kQ8_0>((int)D, F / nch, nullptr, err, a, st)
+				      : launch_seg<kQ4_0>((int)D, F / nch, nullptr, err, a, st);
+	}
+	t1_combine_kernel<<<(unsigned)((D + 255) / 256), 256, 0, st>>>(part, w, nch, K, (int)D, out);
+	return cudaGetLastError();
 }
 
 bool gemv_norm_supported(int qtype, int64_t cols, uintptr_t w)

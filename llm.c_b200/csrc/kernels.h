@@ -29,6 +29,14 @@ cudaError_t launch_dispatch(const int32_t *ids, int npairs, int NE, int first, i
 			    int32_t *counts, int32_t *offsets, int32_t *perm, int32_t *pos_of,
 			    int32_t *active, int32_t *n_active, int32_t *err, int32_t *work,
 			    cudaStream_t st);
+// one token: logits (one CTA per expert), then top-k and dispatch by the
+// last CTA; cnt is a zeroed device counter (left zero)
+bool router_t1_ok(int d, int NE, int K);
+cudaError_t launch_router_t1(const float *x, const float *w, const float *bias, int d, int NE,
+			     int K, int lanes, int mode_exact, int renorm, float *logits,
+			     int32_t *ids, float *wts, int32_t *counts, int32_t *offsets,
+			     int32_t *perm, int32_t *pos_of, int32_t *active, int32_t *n_active,
+			     int32_t *err, int32_t *work, unsigned *cnt, cudaStream_t st);
 // top-k + dispatch in one CTA (needs route_small_smem(T, NE, K) <= ~200 KB)
 size_t route_small_smem(int T, int NE, int K);
 cudaError_t launch_route_small(const float *logits, const float *bias, int T, int NE, int K,
@@ -78,6 +86,31 @@ struct NormIn {
 	float eps = 1e-5f;
 };
 bool gemv_norm_supported(int qtype, int64_t cols, uintptr_t w);
+
+// gemv.cu: the experts of ONE token (moe_layer_forward at T = 1) through the
+// single-row GEMV: the matrices of the token's K slots are row segments of
+// one launch, read in column chunks.  gate/up: segments gate of slots
+// 0..K-1 then up of slots 0..K-1, all against the token x; down: segment k
+// = the down matrix of slot k against h_k = swiglu(gate_k, up_k).
+struct SegMap {
+	const void *const *wtab = nullptr;  // NULL: a plain GEMV; else device [3][NE]
+	const int32_t *ids = nullptr;       // device [K]: the token's experts, slot order
+	int NE = 0, K = 0, down = 0;
+	int nchunks = 1;                    // column chunks per row
+	int64_t rb_full = 0;                // bytes of a whole matrix row
+	const float *gu = nullptr;          // down: gate/up results [2K][cols]
+	float *part = nullptr;              // [nchunks][segments][rows] partial row sums
+};
+// 0 when the shapes (d_model D, d_ff F) do not fit; else the down matrix's
+// column chunks
+int expert_t1_chunks(int qtype, int64_t D, int64_t F, int K);
+// ids (the token's K experts) and w (their weights) on the device; gu:
+// [2K][F] and part: [chunks][K][D] scratch; out: [D].  stage 0: gate/up
+// (gu), 1: down (part), 2: combine (out)
+cudaError_t launch_expert_t1(int stage, const void *const *wtab, const int32_t *ids,
+			     const float *w, int qtype, int64_t D, int64_t F, int NE, int K,
+			     const float *x, float *gu, float *part, float *out, int32_t *err,
+			     cudaStream_t st);
 cudaError_t launch_gemv_norm(const void *w, int qtype, int64_t rows, int64_t cols,
 			     const NormIn &nin, float *y, int32_t *err, bool pdl, cudaStream_t st);
 

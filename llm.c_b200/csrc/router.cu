@@ -295,9 +295,119 @@ route_small_kernel(const float *__restrict__ logits, const float *__restrict__ b
 		      n_active, err, ds);
 }
 
+// One token (T = 1): the router logit of expert blockIdx.x by one warp (the
+// same LANES-lane chains and halving tree as the kernels above, both rows
+// staged in shared memory by the whole CTA first), then the last CTA to
+// finish ranks the token's experts (topk_tokens_cta) and dispatches its K
+// pairs (dispatch_warp).  cnt: an arrival counter, zero at launch and
+// reset by the last CTA.  smem: x [d], the expert's row [d], top-k scratch.
+constexpr int kT1Threads = 64;
+
+template <int LANES>
+__global__ void __launch_bounds__(kT1Threads)
+router_t1_kernel(const float *__restrict__ x, const float *__restrict__ w,
+		 const float *__restrict__ bias, int d, int NE, int K, int mode_exact, int renorm,
+		 float *__restrict__ logits, int32_t *__restrict__ ids, float *__restrict__ wts,
+		 int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+		 int32_t *__restrict__ perm, int32_t *__restrict__ pos_of,
+		 int32_t *__restrict__ active, int32_t *__restrict__ n_active,
+		 int32_t *__restrict__ err, int32_t *__restrict__ work, unsigned *cnt)
+{
+	extern __shared__ __align__(16) float rs[];
+	__shared__ int last;
+	const int tid = threadIdx.x, e = blockIdx.x;
+	const float4 *x4 = reinterpret_cast<const float4 *>(x);
+	const float4 *w4 = reinterpret_cast<const float4 *>(w + (int64_t)e * d);
+	float4 *sx = reinterpret_cast<float4 *>(rs), *sw = reinterpret_cast<float4 *>(rs + d);
+	for (int i = tid; i < d / 4; i += blockDim.x) {
+		sx[i] = __ldg(x4 + i);
+		sw[i] = __ldg(w4 + i);
+	}
+	__syncthreads();
+	if (tid < 32) {
+		// lane q < LANES / 4 carries SIMD lanes 4q..4q+3: element
+		// st * LANES + 4q + c goes to chain 4q + c, in order of st
+		constexpr int Q = LANES / 4;
+		float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+		if (tid < Q) {
+#pragma unroll 8
+			for (int st = 0; st < d / LANES; st++) {
+				const float4 xv = sx[st * Q + tid], wv = sw[st * Q + tid];
+				a0 = __fmaf_rn(xv.x, wv.x, a0);
+				a1 = __fmaf_rn(xv.y, wv.y, a1);
+				a2 = __fmaf_rn(xv.z, wv.z, a2);
+				a3 = __fmaf_rn(xv.w, wv.w, a3);
+			}
+		}
+		float l[LANES];
+#pragma unroll
+		for (int q = 0; q < Q; q++) {
+			l[4 * q] = __shfl_sync(0xffffffffu, a0, q);
+			l[4 * q + 1] = __shfl_sync(0xffffffffu, a1, q);
+			l[4 * q + 2] = __shfl_sync(0xffffffffu, a2, q);
+			l[4 * q + 3] = __shfl_sync(0xffffffffu, a3, q);
+		}
+#pragma unroll
+		for (int h = LANES / 2; h >= 1; h /= 2)
+#pragma unroll
+			for (int j = 0; j < h; j++)
+				l[j] = __fadd_rn(l[j], l[j + h]);
+		if (tid == 0)
+			logits[e] = __fadd_rn(0.0f, l[0]);
+	}
+	if (tid == 0) {
+		__threadfence();
+		last = atomicAdd(cnt, 1u) == (unsigned)NE - 1;
+	}
+	__syncthreads();
+	if (!last)
+		return;
+	__threadfence();
+	float *scr = rs + 2 * d;                                      // 64 + LANES + 1 + 2K
+	int32_t *ids_s = reinterpret_cast<int32_t *>(scr + 64 + LANES + 1 + 2 * K);  // [K]
+	float *w_s = reinterpret_cast<float *>(ids_s + K);            // [K]
+	topk_tokens_cta<LANES>(logits, bias, 1, NE, K, mode_exact, renorm, scr, ids_s, w_s, ids, wts);
+	__syncthreads();
+	if (tid < 32) {
+		dispatch_warp(ids_s, K, NE, 0, NE, counts, offsets, perm, active, n_active, err);
+		if (tid < K) {
+			const int p = perm[tid];
+			if (p >= 0 && p < K)
+				pos_of[p] = tid;
+		}
+	}
+	if (tid == 0) {
+		work[0] = work[1] = 0;
+		*cnt = 0u;
+	}
+}
+
 // ---------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------
+bool router_t1_ok(int d, int NE, int K)
+{
+	return d % 64 == 0 && d <= 16384 && NE >= 1 && NE <= 64 && K >= 1 && K <= NE && K <= 32;
+}
+
+cudaError_t launch_router_t1(const float *x, const float *w, const float *bias, int d, int NE,
+			     int K, int lanes, int mode_exact, int renorm, float *logits,
+			     int32_t *ids, float *wts, int32_t *counts, int32_t *offsets,
+			     int32_t *perm, int32_t *pos_of, int32_t *active, int32_t *n_active,
+			     int32_t *err, int32_t *work, unsigned *cnt, cudaStream_t st)
+{
+	if (!router_t1_ok(d, NE, K))
+		return cudaErrorNotSupported;
+	const size_t smem = ((size_t)2 * d + 64 + 16 + 1 + 4 * K) * sizeof(float);
+	auto fn = lanes == 8 ? router_t1_kernel<8> : router_t1_kernel<16>;
+	cudaError_t e = ensure_smem(fn, smem);
+	if (e != cudaSuccess)
+		return e;
+	fn<<<NE, kT1Threads, smem, st>>>(x, w, bias, d, NE, K, mode_exact, renorm, logits, ids, wts,
+					 counts, offsets, perm, pos_of, active, n_active, err, work,
+					 cnt);
+	return cudaGetLastError();
+}
 template <int LANES, int TQ, int EQ, int TT, int CH>
 static cudaError_t run_tiled(const float *x, const float *w, float *logits, int T, int d, int NE,
 			     __half *x16, int q4, cudaStream_t st)

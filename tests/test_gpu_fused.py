@@ -37,7 +37,7 @@ def check(moe, orc, L, x, flags=0, lanes=16, mode=0):
     T = x.shape[0]
     ref, ids_ref, w_ref, _ = orc.moe_ffn(L, x, lanes=lanes, topk_mode=mode)
     lay = build(moe, L, flags=moe.RENORM if L.get("renorm") else 0)
-    got = lay.forward(x, flags=flags)
+    got = lay.forward(x, flags=flags | moe.NO_T1)
     ids, w, counts, offsets, perm = lay.routing(T)
     assert_routing(orc, x, L, lanes, ids, w, ids_ref, w_ref)
     assert_dispatch(orc, ids, counts, offsets, perm, L["n_experts"])
