@@ -104,7 +104,8 @@ __device__ __forceinline__ float4 lds128f(uint32_t a)
 	return v;
 }
 
-constexpr int kTcMaxXb = 12;  // blocks of x per math warp (cols / 32 / kTcMath at most)
+constexpr int kTcMaxXb = 14;  // blocks of x per math warp (cols / 32 / kTcMath at most)
+
 
 // shared-memory loads at a register address plus a compile-time offset
 template <int OFF>
@@ -201,6 +202,11 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		const int i = (int)blockIdx.x - b0u, n = b1u - b0u;
 		r0 = (int)(i * R / n);
 		r1 = (int)((i + 1) * R / n);
+		if (rows % 2 == 0) {
+			// even bounds: a row pair never spans two matrices
+			r0 &= ~1;
+			r1 = i + 1 == n ? (int)R : (r1 & ~1);
+		}
 		// a slot's expert out of range: flag it, compute nothing
 		bool bad = false;
 		for (int k = 0; k < sm.K; k++)
@@ -212,6 +218,13 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		}
 	}
 	const int ntiles = (r1 - r0 + kTcRows - 1) / kTcRows;
+	// rows adjacent in memory (not a column chunk of a wider matrix): one
+	// bulk copy per row pair (2 rb bytes, pair j at j (2 rb + 16) in the
+	// stage), MMA rows g and g + 8 being the tile's rows 2g and 2g + 1; the
+	// copy engine takes a request every ~0.1 us per SM, which bounded the
+	// stream at one request per row.  Else one copy per row at j rs.
+	const bool pairs = !sm.wtab || sm.nchunks == 1;
+	const int64_t ps = 2 * rb + 16;  // pair stride
 	if (tid == 0) {
 		for (int i = 0; i < stages; i++) {
 			mbar_init(&full[i], 1);
@@ -243,7 +256,16 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 			if (lane == 0)
 				mbar_arrive_expect_tx(&full[slot], (uint32_t)(n * rb));
 			__syncwarp();
-			if (lane < n) {
+			if (pairs) {
+				if (2 * lane < n) {
+					const int nr = min(2, n - 2 * lane);
+					const uint8_t *src = sm.wtab ? seg_row(sm, sp, rows, r + 2 * lane, rb)
+								     : w + (int64_t)(r + 2 * lane) * rb;
+					fence_proxy_async();
+					bulk_g2s(ring + slot * tile_bytes + lane * ps, src, (uint32_t)(nr * rb),
+						 &full[slot]);
+				}
+			} else if (lane < n) {
 				const uint8_t *src = sm.wtab ? seg_row(sm, sp, rows, r + lane, rb)
 							     : w + (int64_t)(r + lane) * rb;
 				fence_proxy_async();
@@ -395,7 +417,9 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		wx[j] = wv.x;
 		wz[j] = wv.z;
 	}
-	const uint32_t s_row = smem_addr(ring) + (uint32_t)(g * rs + b0 * BB);
+	const uint32_t s_row =
+		smem_addr(ring) + (uint32_t)((pairs ? g * ps : g * rs) + b0 * BB);
+	const uint32_t d8 = (uint32_t)(pairs ? rb : 8 * rs);  // MMA row g + 8 from row g
 	bool failed = false;
 	for (int i = 0; i < ntiles; i++) {
 		const int slot = i % stages;
@@ -408,7 +432,7 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		if (!failed) {
 			// rows g and g + 8 of this stage at this warp's first block
 			const uint32_t rg = s_row + (uint32_t)(slot * tile_bytes);
-			const uint32_t rg8 = rg + (uint32_t)(8 * rs);
+			const uint32_t rg8 = rg + d8;
 			static_for<NBW / 2>([&](auto J) {
 				constexpr int jp = decltype(J)::value;
 				constexpr int OFF = 2 * jp * BB;
@@ -448,7 +472,9 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		}
 		asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
 		if (warp == 0 && lane < kTcRows) {
-			const int r = r0 + i * kTcRows + lane;
+			// MMA row `lane` -> its tile row
+			const int tr = pairs ? (lane < 8 ? 2 * lane : 2 * lane - 15) : lane;
+			const int r = r0 + i * kTcRows + tr;
 			const float *rsum = red + (i & 1) * kTcMath * kTcRows + lane;
 			float v = 0.0f;
 #pragma unroll
@@ -641,6 +667,8 @@ static cudaError_t launch_tc(const void *w, int64_t rows, int64_t cols, const fl
 		return launch_tc_t<QT, 10>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	case 12:
 		return launch_tc_t<QT, 12>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
+	case 14:
+		return launch_tc_t<QT, 14>(w, rows, nb, x, y, err, stages, smem, nin, pdl, st);
 	default:
 		return cudaErrorInvalidValue;
 	}
@@ -683,6 +711,8 @@ static cudaError_t launch_seg(int rows, int64_t cols, const float *x, int32_t *e
 		return launch_seg_t<QT, 10>(rows, nb, x, err, stages, smem, sm, st);
 	case 12:
 		return launch_seg_t<QT, 12>(rows, nb, x, err, stages, smem, sm, st);
+	case 14:
+		return launch_seg_t<QT, 14>(rows, nb, x, err, stages, smem, sm, st);
 	default:
 		return cudaErrorInvalidValue;
 	}
