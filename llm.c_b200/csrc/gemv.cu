@@ -190,6 +190,9 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	int r1 = (int)((int64_t)(blockIdx.x + 1) * rows / gridDim.x);
 	SegPos sp{0, 0, 1};
 	if (sm.wtab) {
+		// the slots' experts (and the weights they select) come from the
+		// kernel before: launched as its dependent, wait for it first
+		griddep_wait();
 		// this CTA's unit and its row range in the unit's segments
 		const int nx = sm.down ? sm.K : 1, U = sm.nchunks * nx, G = (int)gridDim.x;
 		const int u = (int)((int64_t)blockIdx.x * U / G);
@@ -683,9 +686,20 @@ static cudaError_t launch_seg_t(int rows, int nb, const float *x, int32_t *err, 
 	cudaError_t e = ensure_smem(fn, smem);
 	if (e != cudaSuccess)
 		return e;
-	fn<<<(unsigned)sm_count(), kTcThreads, smem, st>>>(nullptr, rows, nb, stages, x, nullptr, err,
-							   NormIn{}, sm);
-	return cudaGetLastError();
+	// a programmatic dependent of the kernel before (it waits for it before
+	// reading the experts, x or h)
+	cudaLaunchConfig_t cfg{};
+	cfg.gridDim = dim3((unsigned)sm_count());
+	cfg.blockDim = dim3(kTcThreads);
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = pdl_enabled() ? 1 : 0;
+	return cudaLaunchKernelEx(&cfg, fn, static_cast<const uint8_t *>(nullptr), rows, nb, stages, x,
+				  static_cast<float *>(nullptr), err, NormIn{}, sm);
 }
 
 template <int QT>
@@ -724,6 +738,8 @@ static cudaError_t launch_seg(int rows, int64_t cols, const float *x, int32_t *e
 __global__ void t1_combine_kernel(const float *__restrict__ part, const float *__restrict__ w,
 				  int nchunks, int K, int D, float *__restrict__ out)
 {
+	griddep_launch_dependents();
+	griddep_wait();
 	const int j = blockIdx.x * blockDim.x + threadIdx.x;
 	if (j >= D)
 		return;
@@ -783,8 +799,17 @@ cudaError_t launch_expert_t1(int stage, const void *const *wtab, const int32_t *
 		return qtype == kQ8_0 ? launch_seg<kQ8_0>((int)D, F / nch, nullptr, err, a, st)
 				      : launch_seg<kQ4_0>((int)D, F / nch, nullptr, err, a, st);
 	}
-	t1_combine_kernel<<<(unsigned)((D + 255) / 256), 256, 0, st>>>(part, w, nch, K, (int)D, out);
-	return cudaGetLastError();
+	cudaLaunchConfig_t cfg{};
+	cfg.gridDim = dim3((unsigned)((D + 255) / 256));
+	cfg.blockDim = dim3(256);
+	cfg.stream = st;
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = pdl_enabled() ? 1 : 0;
+	return cudaLaunchKernelEx(&cfg, t1_combine_kernel, static_cast<const float *>(part), w, nch, K,
+				  (int)D, out);
 }
 
 bool gemv_norm_supported(int qtype, int64_t cols, uintptr_t w)

@@ -315,6 +315,9 @@ router_t1_kernel(const float *__restrict__ x, const float *__restrict__ w,
 {
 	extern __shared__ __align__(16) float rs[];
 	__shared__ int last;
+	// the expert GEMVs after it may start their set-up (they wait for the
+	// routing before reading it)
+	griddep_launch_dependents();
 	const int tid = threadIdx.x, e = blockIdx.x;
 	const float4 *x4 = reinterpret_cast<const float4 *>(x);
 	const float4 *w4 = reinterpret_cast<const float4 *>(w + (int64_t)e * d);
