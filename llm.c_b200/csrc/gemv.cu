@@ -26,13 +26,20 @@
 //   three planes carry x to ~2^-17 of the block maximum, so the result is
 //   within ~1e-6 relative of the reference's fp32 arithmetic (dot_f32_q4_0 /
 //   dot_f32_q8_0, quant.c:103-155, which multiplies dequantized weights by
-//   fp32 x).  About 29 instructions per 16 rows x 32 codes (blocks taken in
-//   pairs, so every code word is one aligned load or a funnel shift of two),
-//   every shared-memory access an explicit 32-bit-addressed ld.shared.
+//   fp32 x).  Blocks are taken in pairs: every code word is one aligned
+//   load or a funnel shift of two, and the odd block's planes sit in B
+//   columns 4-6 (the even block's in 0-2), so its MMA accumulates onto the
+//   even block's and one C tile, one conversion and one scale FMA per lane
+//   and row serve both blocks (about 17 instructions per 16 rows x 32
+//   codes); every shared-memory access is an explicit 32-bit-addressed
+//   ld.shared.
 // * 16 math warps split each tile's blocks (K) sixteen ways; partial row
 //   sums meet in shared memory and are added in warp order.
-// * Every CTA splits x into digits itself (16 KB of x, from L2, all of a
-//   warp's loads issued at once), while the first copies are in flight.
+// * Every CTA splits x into digits itself (16 KB of x, from L2) while its
+//   first copies are in flight: each thread takes a quarter block (the 8
+//   elements of one lane quad's B fragment), so the block maximum and the
+//   digit sums are two shuffles and the 8 elements give the scheduler
+//   independent work.
 //
 // gemv1_kernel (shapes the ring does not fit): one warp per weight row, lane
 // l reading blocks l, l + 32, ... with aligned 32-bit loads, codes made exact
@@ -55,11 +62,12 @@ constexpr size_t kTcSmemCap = 210 * 1024;
 
 // Shared memory after the stage ring, per block of x: the MMA B fragments
 // [4 t][8 g][8 bytes] (lane (g, t) reads its b0, b1 as one 8-byte word;
-// planes g >= 3 are zero) = 256 bytes, and the plane weights [4 t][4]
-// f32 = (weight, 0, nibble correction, 0) = 64 bytes; then the partial
-// sums [2][kTcMath][16] f32 and the mbarriers.  Lane quad t's C columns
-// (2t, 2t + 1) combine in integers as 254 c_2t + c_2t+1 (|.| < 2^27, exact)
-// and take one weight: s2 for planes 0-1, s3 / 254 for plane 2, 0 beyond.
+// planes in columns 0-2 for an even block, 4-6 for an odd one, the other
+// columns zero) = 256 bytes, and the plane weights [4 t][4] f32 = (weight,
+// 0, nibble correction, 0) = 64 bytes; then the partial sums
+// [2][kTcMath][16] f32 and the mbarriers.  Lane quad t's C columns (2t,
+// 2t + 1) combine in integers as 254 c_2t + c_2t+1 (|.| < 2^27, exact) and
+// take one weight: s2 for planes 0-1, s3 / 254 for plane 2.
 constexpr int kTcB = 256, kTcW = 64, kTcPerBlock = kTcB + kTcW;
 
 // bytes between rows in a stage: rows of 4096 (Q4_0) or 2048 (Q8_0) columns
@@ -85,6 +93,22 @@ __device__ __forceinline__ void imma_16832(int32_t (&d)[4], const uint32_t (&a)[
 			     "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
 			     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
 			     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// the same product added onto d
+__device__ __forceinline__ void imma_16832_acc(int32_t (&d)[4], const uint32_t (&a)[4],
+					       uint32_t b0, uint32_t b1, bool a_unsigned)
+{
+	if (a_unsigned)
+		asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+			     "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+			     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+			     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+	else
+		asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+			     "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+			     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+			     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // shared-memory loads by 32-bit shared address (every access to the stage
@@ -287,36 +311,69 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		return;
 	}
 
-	// ---- math warps.  x as three int8 digit planes per block: warp w takes
-	// blocks w, w + 16, ...; lane k = element k.  All of a warp's x loads are
-	// issued before the first is used.
+	// ---- math warps.  x as three int8 digit planes per block.  Thread q of
+	// the math warps takes quarter q % 4 of block q / 4 (and q + 512, ...):
+	// elements 4 (q % 4) + {0..3} and 16 + 4 (q % 4) + {0..3}, which are
+	// exactly the 8 bytes of each plane's B fragment for lane quad q % 4,
+	// so every plane leaves as one 8-byte store.  The block maximum and the
+	// digit sums are two shuffles among the block's 4 (adjacent) threads, and
+	// a thread's 8 elements are independent, so the prologue is short and
+	// issues densely (a whole warp per block, with a warp-wide reduction
+	// between dependent steps, took ~0.4 us per block).
 	{
-		float v[NBW];
+		constexpr int QPT = (NBW + 7) / 8;  // quarters per thread: nb * 4 = 64 NBW over 512
+		const int nq = nb * 4;              // a multiple of 64: whole warps active or not
+		float va[QPT][8];
 		griddep_wait();
+		// this thread's elements of quarter it: e0 + {0..3}, e0 + 16 + {0..3}
+		auto ld8 = [&](const float *p, int e0, float (&o)[8], bool coherent) {
+			if (((uintptr_t)p & 15) == 0) {
+				const float4 u0 = coherent ? __ldcg(reinterpret_cast<const float4 *>(p + e0))
+							   : __ldg(reinterpret_cast<const float4 *>(p + e0));
+				const float4 u1 = coherent ? __ldcg(reinterpret_cast<const float4 *>(p + e0 + 16))
+							   : __ldg(reinterpret_cast<const float4 *>(p + e0 + 16));
+				o[0] = u0.x; o[1] = u0.y; o[2] = u0.z; o[3] = u0.w;
+				o[4] = u1.x; o[5] = u1.y; o[6] = u1.z; o[7] = u1.w;
+			} else {
+#pragma unroll
+				for (int e = 0; e < 8; e++)
+					o[e] = coherent ? __ldcg(p + e0 + (e & 3) + (e >> 2) * 16)
+							: __ldg(p + e0 + (e & 3) + (e >> 2) * 16);
+			}
+		};
 		if (nin.hidden) {
 			// x = rms_norm(hidden + delta) * weight (tensor_add, then
-			// rms_norm, nn.c:7-48); CTA 0 stores hidden + delta
-			// every load before the first store (hidden_out might alias
-			// them as far as the compiler knows)
-			float dl[NBW], wn[NBW];
+			// rms_norm, nn.c:7-48); CTA 0 stores hidden + delta.  Every
+			// load comes before the first store (hidden_out might alias
+			// them as far as the compiler knows).
+			float dl[QPT][8], wn[QPT][8];
 #pragma unroll
-			for (int j = 0; j < NBW; j++) {
-				const int e = (warp + j * kTcMath) * 32 + lane;
-				v[j] = nin.hidden[e];
-				dl[j] = nin.delta ? nin.delta[e] : 0.0f;
-				wn[j] = nin.weight[e];
-			}
-#pragma unroll
-			for (int j = 0; j < NBW; j++) {
-				if (nin.delta)
-					v[j] = __fadd_rn(v[j], dl[j]);
-				if (blockIdx.x == 0)
-					nin.hidden_out[(warp + j * kTcMath) * 32 + lane] = v[j];
+			for (int it = 0; it < QPT; it++) {
+				const int q = tid + it * kTcMath * 32;
+				if (q < nq) {
+					const int e0 = (q >> 2) * 32 + 4 * (q & 3);
+					ld8(nin.hidden, e0, va[it], true);
+					if (nin.delta)
+						ld8(nin.delta, e0, dl[it], true);
+					ld8(nin.weight, e0, wn[it], false);
+				}
 			}
 			float ss = 0.0f;
 #pragma unroll
-			for (int j = 0; j < NBW; j++)
-				ss = fmaf(v[j], v[j], ss);
+			for (int it = 0; it < QPT; it++) {
+				const int q = tid + it * kTcMath * 32;
+				if (q < nq) {
+					const int e0 = (q >> 2) * 32 + 4 * (q & 3);
+#pragma unroll
+					for (int e = 0; e < 8; e++) {
+						if (nin.delta)
+							va[it][e] = __fadd_rn(va[it][e], dl[it][e]);
+						if (blockIdx.x == 0)
+							nin.hidden_out[e0 + (e & 3) + (e >> 2) * 16] = va[it][e];
+						ss = fmaf(va[it][e], va[it][e], ss);
+					}
+				}
+			}
 			ss = warp_sum(ss);
 			if (lane == 0)
 				red[warp] = ss;
@@ -327,80 +384,117 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 				tot += red[q];
 			const float rms = sqrtf(tot / (float)(nb * 32) + nin.eps);
 #pragma unroll
-			for (int j = 0; j < NBW; j++)
-				v[j] = (v[j] / rms) * wn[j];
+			for (int it = 0; it < QPT; it++)
+#pragma unroll
+				for (int e = 0; e < 8; e++)
+					va[it][e] = (va[it][e] / rms) * wn[it][e];
 		} else if (sm.wtab && sm.down) {
 			// h of this unit's slot: swiglu(gate row, up row) (nn.c:475-478)
 			const int64_t cols = (int64_t)sm.nchunks * nb * 32;
-			const float *g = sm.gu + (int64_t)sp.xi * cols + (int64_t)sp.c * nb * 32;
-			const float *u = g + (int64_t)sm.K * cols;
-			float gv[NBW], uv[NBW];
+			const float *gp = sm.gu + (int64_t)sp.xi * cols + (int64_t)sp.c * nb * 32;
+			const float *up = gp + (int64_t)sm.K * cols;
 #pragma unroll
-			for (int j = 0; j < NBW; j++) {
-				const int b = warp + j * kTcMath;
-				gv[j] = __ldcg(g + (int64_t)b * 32 + lane);
-				uv[j] = __ldcg(u + (int64_t)b * 32 + lane);
+			for (int it = 0; it < QPT; it++) {
+				const int q = tid + it * kTcMath * 32;
+				if (q < nq) {
+					const int e0 = (q >> 2) * 32 + 4 * (q & 3);
+					float gv[8], uv[8];
+					ld8(gp, e0, gv, true);
+					ld8(up, e0, uv, true);
+#pragma unroll
+					for (int e = 0; e < 8; e++)
+						va[it][e] = swiglu(gv[e], uv[e]);
+				}
 			}
-#pragma unroll
-			for (int j = 0; j < NBW; j++)
-				v[j] = swiglu(gv[j], uv[j]);
 		} else {
 			const float *xc = x + (int64_t)sp.c * nb * 32;
 #pragma unroll
-			for (int j = 0; j < NBW; j++) {
-				const int b = warp + j * kTcMath;
-				v[j] = __ldg(xc + (int64_t)b * 32 + lane);
+			for (int it = 0; it < QPT; it++) {
+				const int q = tid + it * kTcMath * 32;
+				if (q < nq)
+					ld8(xc, (q >> 2) * 32 + 4 * (q & 3), va[it], false);
 			}
 		}
-		const int t_k = (lane & 15) >> 2, hi = lane >= 16 ? 4 : 0;
 #pragma unroll
-		for (int j = 0; j < NBW; j++) {
-			const int b = warp + j * kTcMath;   // < nb = kTcMath * NBW
-			const float amax = warp_max(fabsf(v[j]));
+		for (int it = 0; it < QPT; it++) {
+			const int q = tid + it * kTcMath * 32;
+			if (q >= nq)
+				continue;   // whole warps (nq is a multiple of 64)
+			const int b = q >> 2, tq = q & 3;
+			float am = 0.0f;
+#pragma unroll
+			for (int e = 0; e < 8; e++)
+				am = fmaxf(am, fabsf(va[it][e]));
+			am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+			const float amax = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
 			float s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-			int d1 = 0, d2 = 0, d3 = 0;
+			int d1[8], d2[8], d3[8];
+#pragma unroll
+			for (int e = 0; e < 8; e++)
+				d1[e] = d2[e] = d3[e] = 0;
 			if (amax > 0.0f) {
 				// the digits only need s * d to track x: every residual is
-				// taken exactly (fma) against the same s, so products by
-				// rounded reciprocals serve instead of divisions
+				// taken exactly (fma) against the same s, so an approximate
+				// reciprocal serves instead of a division (a digit that
+				// rounds the other way leaves a residual the next plane
+				// takes; the clamps keep every digit in range)
 				s1 = amax * (1.0f / 127.0f);
 				s2 = s1 * (1.0f / 254.0f);
 				s3 = s2 * (1.0f / 254.0f);
-				const float i1 = __frcp_rn(s1), i2 = i1 * 254.0f, i3 = i2 * 254.0f;
-				d1 = max(-127, min(127, __float2int_rn(v[j] * i1)));
-				const float q1 = __fmaf_rn(-(float)d1, s1, v[j]);
-				d2 = max(-127, min(127, __float2int_rn(q1 * i2)));
-				const float q2 = __fmaf_rn(-(float)d2, s2, q1);
-				d3 = (s3 > 0.0f) ? max(-127, min(127, __float2int_rn(q2 * i3))) : 0;
+				const float i1 = __fdividef(1.0f, s1), i2 = i1 * 254.0f, i3 = i2 * 254.0f;
+#pragma unroll
+				for (int e = 0; e < 8; e++) {
+					const float v = va[it][e];
+					d1[e] = max(-127, min(127, __float2int_rn(v * i1)));
+					const float q1 = __fmaf_rn(-(float)d1[e], s1, v);
+					d2[e] = max(-127, min(127, __float2int_rn(q1 * i2)));
+					const float q2 = __fmaf_rn(-(float)d2[e], s2, q1);
+					d3[e] = (s3 > 0.0f) ? max(-127, min(127, __float2int_rn(q2 * i3))) : 0;
+				}
 			}
-			// B fragment bytes: [t][plane g][b0 (k = 4t..4t+3) | b1 (k = 16+4t..)]
-			int8_t *fb = reinterpret_cast<int8_t *>(xfrag + (size_t)b * kTcB);
-			const int o = t_k * 64 + hi + (lane & 3);
-			fb[o] = (int8_t)d1;
-			fb[o + 8] = (int8_t)d2;
-			fb[o + 16] = (int8_t)d3;
-			constexpr int kZ = 8 - kTcPlanes;  // unused B columns, zero
-			if (lane < 4 * kZ)
-				reinterpret_cast<uint2 *>(fb)[(lane / kZ) * 8 + kTcPlanes + lane % kZ] =
-					make_uint2(0, 0);
-			const int S1 = __reduce_add_sync(0xffffffffu, d1);
-			const int S2 = __reduce_add_sync(0xffffffffu, d2);
-			const int S3 = __reduce_add_sync(0xffffffffu, d3);
-			if (lane < 4) {
-				// (w_2t, w_2t+1, nibble correction, 0): the plane scales of this
-				// lane quad's C columns, and for t = 0 minus 8 x the planes'
-				// digit sums (Q4_0 codes are nib, their values nib - 8)
-				// The MMA's columns are the planes: lane quad 0 holds planes 0
-				// and 1, combined exactly in integers as 254 D0 + D1 with the
-				// weight s2 (= s1 / 254 to fp32 rounding); lane quad 1 holds
-				// plane 2 (and an empty column) as 254 D2 with weight s3 / 254.
-				const float corr = QT == kQ4_0
-							   ? -8.0f * ((float)S1 * s1 + (float)S2 * s2 + (float)S3 * s3)
-							   : 0.0f;
-				reinterpret_cast<float4 *>(xw + (size_t)b * kTcW)[lane] = make_float4(
-					lane == 0 ? s2 : (lane == 1 ? s3 / 254.0f : 0.0f), 0.0f,
-					lane == 0 ? corr : 0.0f, 0.0f);
+			// each plane's 8 digits as the two words b0 (elements 4tq..) and
+			// b1 (16 + 4tq..) of its B fragment
+			auto pack = [](const int (&d)[8], int o) {
+				return __byte_perm(__byte_perm(d[o], d[o + 1], 0x0040),
+						   __byte_perm(d[o + 2], d[o + 3], 0x0040), 0x5410);
+			};
+			const uint2 w1 = make_uint2(pack(d1, 0), pack(d1, 4));
+			const uint2 w2 = make_uint2(pack(d2, 0), pack(d2, 4));
+			const uint2 w3 = make_uint2(pack(d3, 0), pack(d3, 4));
+			// B fragment bytes: [t][column g][b0 | b1].  An even block's
+			// planes are columns 0-2, an odd block's columns 4-6 (the other
+			// columns zero), so the MMA of an odd block can accumulate onto
+			// its even neighbour's and both leave one C tile.
+			const int cb = (b & 1) * 4;
+			uint2 *fb = reinterpret_cast<uint2 *>(xfrag + (size_t)b * kTcB + tq * 64);
+#pragma unroll
+			for (int c = 0; c < 8; c++) {
+				const int pl = (c - cb) & 7;   // plane of column c (none past the planes)
+				fb[c] = pl >= kTcPlanes ? make_uint2(0, 0) : pl == 0 ? w1 : pl == 1 ? w2 : w3;
 			}
+			// digit sums of the planes over the block (signed bytes)
+			int S1 = __dp4a((int)w1.x, 0x01010101, __dp4a((int)w1.y, 0x01010101, 0));
+			int S2 = __dp4a((int)w2.x, 0x01010101, __dp4a((int)w2.y, 0x01010101, 0));
+			int S3 = __dp4a((int)w3.x, 0x01010101, __dp4a((int)w3.y, 0x01010101, 0));
+			S1 += __shfl_xor_sync(0xffffffffu, S1, 1);
+			S2 += __shfl_xor_sync(0xffffffffu, S2, 1);
+			S3 += __shfl_xor_sync(0xffffffffu, S3, 1);
+			S1 += __shfl_xor_sync(0xffffffffu, S1, 2);
+			S2 += __shfl_xor_sync(0xffffffffu, S2, 2);
+			S3 += __shfl_xor_sync(0xffffffffu, S3, 2);
+			// entry tq = (w_2t, 0, nibble correction, 0): the weight of lane
+			// quad t's combined C columns and, once per block, minus 8 x the
+			// planes' digit sums (Q4_0 codes are nib, their values nib - 8).
+			// Quads 0-1 read an even block's entries, quads 2-3 an odd
+			// block's: the first of its quads holds planes 0 and 1, combined
+			// exactly in integers as 254 D0 + D1 with the weight s2 (= s1 /
+			// 254 to fp32 rounding); the second holds plane 2 (and an empty
+			// column) as 254 D2 with the weight s3 / 254.
+			const float corr =
+				QT == kQ4_0 ? -8.0f * ((float)S1 * s1 + (float)S2 * s2 + (float)S3 * s3) : 0.0f;
+			const int qq = tq - (b & 1) * 2;   // 0, 1: this block's quads
+			reinterpret_cast<float4 *>(xw + (size_t)b * kTcW)[tq] = make_float4(
+				qq == 0 ? s2 : (qq == 1 ? s3 / 254.0f : 0.0f), 0.0f, qq == 0 ? corr : 0.0f, 0.0f);
 		}
 	}
 	asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
@@ -412,17 +506,22 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	const int g = lane >> 2, t = lane & 3;
 	const int b0 = warp * NBW;
 	uint2 bfr[NBW];
-	float wx[NBW], wz[NBW];
+	// quads 0-1 weigh the even block of each pair, quads 2-3 the odd one
+	float wx[NBW / 2], wz[NBW / 2];
 #pragma unroll
-	for (int j = 0; j < NBW; j++) {
+	for (int j = 0; j < NBW; j++)
 		bfr[j] = lds64(smem_addr(xfrag) + (uint32_t)((b0 + j) * kTcB + t * 64 + g * 8));
-		const float4 wv = lds128f(smem_addr(xw) + (uint32_t)((b0 + j) * kTcW + t * 16));
-		wx[j] = wv.x;
-		wz[j] = wv.z;
+#pragma unroll
+	for (int jp = 0; jp < NBW / 2; jp++) {
+		const float4 wv =
+			lds128f(smem_addr(xw) + (uint32_t)((b0 + 2 * jp + (t >> 1)) * kTcW + t * 16));
+		wx[jp] = wv.x;
+		wz[jp] = wv.z;
 	}
 	const uint32_t s_row =
 		smem_addr(ring) + (uint32_t)((pairs ? g * ps : g * rs) + b0 * BB);
 	const uint32_t d8 = (uint32_t)(pairs ? rb : 8 * rs);  // MMA row g + 8 from row g
+	const uint32_t so = (uint32_t)((t >> 1) * BB);        // this quad's block scale
 	bool failed = false;
 	for (int i = 0; i < ntiles; i++) {
 		const int slot = i % stages;
@@ -442,21 +541,18 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 				uint32_t eg[2], og[2], eg8[2], og8[2];
 				pair_codes<QT, OFF>(rg + 4 * t, eg, og);
 				pair_codes<QT, OFF>(rg8 + 4 * t, eg8, og8);
-				const float dge = lds_half_o<OFF>(rg), dgo = lds_half_o<OFF + BB>(rg);
-				const float d8e = lds_half_o<OFF>(rg8), d8o = lds_half_o<OFF + BB>(rg8);
+				// the scale of this quad's block (even: quads 0-1, odd: 2-3)
+				const float dg = lds_half_o<OFF>(rg + so), d8 = lds_half_o<OFF>(rg8 + so);
 				const uint32_t ae[4] = {eg[0], eg8[0], eg[1], eg8[1]};
 				const uint32_t ao[4] = {og[0], og8[0], og[1], og8[1]};
-				int32_t de[4], dd[4];
-				imma_16832(de, ae, bfr[2 * jp].x, bfr[2 * jp].y, QT == kQ4_0);
-				imma_16832(dd, ao, bfr[2 * jp + 1].x, bfr[2 * jp + 1].y, QT == kQ4_0);
-				constexpr int je = 2 * jp, jo = 2 * jp + 1;
-				acc_g = __fmaf_rn(dge, __fmaf_rn((float)(de[0] * 254 + de[1]), wx[je], wz[je]),
+				// the odd block's sums (columns 4-7) accumulate onto the even
+				// block's (columns 0-3): one C tile holds both blocks
+				int32_t c[4];
+				imma_16832(c, ae, bfr[2 * jp].x, bfr[2 * jp].y, QT == kQ4_0);
+				imma_16832_acc(c, ao, bfr[2 * jp + 1].x, bfr[2 * jp + 1].y, QT == kQ4_0);
+				acc_g = __fmaf_rn(dg, __fmaf_rn((float)(c[0] * 254 + c[1]), wx[jp], wz[jp]),
 						  acc_g);
-				acc_g8 = __fmaf_rn(d8e, __fmaf_rn((float)(de[2] * 254 + de[3]), wx[je], wz[je]),
-						   acc_g8);
-				acc_g = __fmaf_rn(dgo, __fmaf_rn((float)(dd[0] * 254 + dd[1]), wx[jo], wz[jo]),
-						  acc_g);
-				acc_g8 = __fmaf_rn(d8o, __fmaf_rn((float)(dd[2] * 254 + dd[3]), wx[jo], wz[jo]),
+				acc_g8 = __fmaf_rn(d8, __fmaf_rn((float)(c[2] * 254 + c[3]), wx[jp], wz[jp]),
 						   acc_g8);
 			});
 		}
