@@ -59,13 +59,14 @@ constexpr int kTcRows = 16;                     // rows per tile (the MMA's M)
 constexpr int kTcPlanes = 3;                    // int8 digit planes of x (B columns 0..2)
 constexpr int kTcMaxStages = 4;
 constexpr size_t kTcSmemCap = 210 * 1024;
+constexpr int kTcRedTiles = 8;                  // tiles per reduction of the partial row sums
 
 // Shared memory after the stage ring, per block of x: the MMA B fragments
 // [4 t][8 g][8 bytes] (lane (g, t) reads its b0, b1 as one 8-byte word;
 // planes in columns 0-2 for an even block, 4-6 for an odd one, the other
 // columns zero) = 256 bytes, and the plane weights [4 t][4] f32 = (weight,
 // 0, nibble correction, 0) = 64 bytes; then the partial sums
-// [2][kTcMath][16] f32 and the mbarriers.  Lane quad t's C columns (2t,
+// [kTcRedTiles][kTcMath][16] f32 and the mbarriers.  Lane quad t's C columns (2t,
 // 2t + 1) combine in integers as 254 c_2t + c_2t+1 (|.| < 2^27, exact) and
 // take one weight: s2 for planes 0-1, s3 / 254 for plane 2.
 constexpr int kTcB = 256, kTcW = 64, kTcPerBlock = kTcB + kTcW;
@@ -77,7 +78,7 @@ __host__ __device__ inline int64_t tc_row_stride(int64_t rb) { return rb + 16; }
 inline size_t tc_smem(int stages, int64_t tile_bytes, int nb)
 {
 	return (size_t)stages * tile_bytes + (size_t)nb * kTcPerBlock +
-	       2 * kTcMath * kTcRows * 4 + 2 * kTcMaxStages * 8;
+	       kTcRedTiles * kTcMath * kTcRows * 4 + 2 * kTcMaxStages * 8;
 }
 
 __device__ __forceinline__ void imma_16832(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -205,8 +206,8 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 	uint8_t *ring = smem;
 	uint8_t *xfrag = smem + stages * tile_bytes;                 // [nb][kTcB]
 	uint8_t *xw = xfrag + (size_t)nb * kTcB;                      // [nb][kTcW]
-	float *red = reinterpret_cast<float *>(xw + (size_t)nb * kTcW);  // [2][kTcMath][16]
-	uint64_t *full = reinterpret_cast<uint64_t *>(red + 2 * kTcMath * kTcRows);
+	float *red = reinterpret_cast<float *>(xw + (size_t)nb * kTcW);  // [kTcRedTiles][kTcMath][16]
+	uint64_t *full = reinterpret_cast<uint64_t *>(red + kTcRedTiles * kTcMath * kTcRows);
 	uint64_t *empty = full + kTcMaxStages;
 
 	const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -564,31 +565,40 @@ gemv_tc_kernel(const uint8_t *__restrict__ w, int rows, int nb, int stages,
 		acc_g += __shfl_xor_sync(0xffffffffu, acc_g, 2);
 		acc_g8 += __shfl_xor_sync(0xffffffffu, acc_g8, 1);
 		acc_g8 += __shfl_xor_sync(0xffffffffu, acc_g8, 2);
-		float *rd = red + (i & 1) * kTcMath * kTcRows + warp * kTcRows;
+		// partial sums of up to kTcRedTiles tiles wait in shared memory; the
+		// math warps meet once per chunk of tiles (not once per tile) and
+		// then add the chunk's rows in warp order, one row per thread
+		const int ct = i % kTcRedTiles;
+		float *rd = red + (ct * kTcMath + warp) * kTcRows;
 		if (t == 0) {
 			rd[g] = acc_g;
 			rd[g + 8] = acc_g8;
 		}
-		asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
-		if (warp == 0 && lane < kTcRows) {
-			// MMA row `lane` -> its tile row
-			const int tr = pairs ? (lane < 8 ? 2 * lane : 2 * lane - 15) : lane;
-			const int r = r0 + i * kTcRows + tr;
-			const float *rsum = red + (i & 1) * kTcMath * kTcRows + lane;
-			float v = 0.0f;
+		if (ct == kTcRedTiles - 1 || i == ntiles - 1) {
+			asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
+			const int n = (ct + 1) * kTcRows;   // rows of this chunk
+			if (tid < n) {
+				const int m = tid % kTcRows;    // MMA row -> its tile row
+				const int tr = pairs ? (m < 8 ? 2 * m : 2 * m - 15) : m;
+				const int r = r0 + (i - ct + tid / kTcRows) * kTcRows + tr;
+				const float *rsum = red + (tid / kTcRows) * kTcMath * kTcRows + m;
+				float v = 0.0f;
 #pragma unroll
-			for (int q = 0; q < kTcMath; q++)
-				v += rsum[q * kTcRows];
-			if (r < r1) {
-				if (sm.wtab) {
-					const int sl = r / rows, rr = r - sl * rows;
-					const int s_ = sm.down ? sp.xi : sl;
-					const int nsg = sm.down ? sm.K : 2 * sm.K;
-					sm.part[((int64_t)sp.c * nsg + s_) * rows + rr] = v;
-				} else {
-					y[r] = v;
+				for (int q = 0; q < kTcMath; q++)
+					v += rsum[q * kTcRows];
+				if (r < r1) {
+					if (sm.wtab) {
+						const int sl = r / rows, rr = r - sl * rows;
+						const int s_ = sm.down ? sp.xi : sl;
+						const int nsg = sm.down ? sm.K : 2 * sm.K;
+						sm.part[((int64_t)sp.c * nsg + s_) * rows + rr] = v;
+					} else {
+						y[r] = v;
+					}
 				}
 			}
+			// the next chunk overwrites these partial sums
+			asm volatile("bar.sync 1, %0;" ::"n"(kTcMath * 32) : "memory");
 		}
 	}
 }
